@@ -1,0 +1,206 @@
+/*
+ * slimkv_b200 — C ABI of the B200 (sm_100a) SlimKV decode path.
+ *
+ * Plain pointers, element strides and sizes; no framework types.  All
+ * tensors are device pointers unless stated otherwise; bf16 tensors are
+ * passed as `const void*` (IEEE bfloat16 storage).  `stream` is a
+ * `cudaStream_t` passed as `void*`.  Every entry point validates its
+ * arguments on the host before launching anything and returns
+ * SLIMKV_OK (0) or a positive SLIMKV_ERR_* code; nothing is launched on
+ * error.  No entry point allocates device memory: callers pass any
+ * workspace they need, sized by the matching *_workspace_size query, so the
+ * calls can be captured in CUDA graphs.  Kernels that wait on TMA copies
+ * give up after a bounded time, set bits in a per-device status word and
+ * return; read it with slimkv_device_status().
+ */
+#ifndef SLIMKV_B200_H
+#define SLIMKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SLIMKV_API __attribute__((visibility("default")))
+#else
+#define SLIMKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SLIMKV_OK 0
+#define SLIMKV_ERR_INVALID_ARGUMENT 1
+#define SLIMKV_ERR_UNSUPPORTED_SHAPE 2
+#define SLIMKV_ERR_ALIGNMENT 3
+#define SLIMKV_ERR_WORKSPACE 4
+#define SLIMKV_ERR_CUDA 5
+#define SLIMKV_ERR_TENSOR_MAP 6
+
+/* Device status bits written by kernels (slimkv_device_status). */
+#define SLIMKV_DEVICE_TIMEOUT 0x1u
+#define SLIMKV_DEVICE_BAD_LENGTH 0x2u
+
+/* Library version as 10000*major + 100*minor + patch. */
+SLIMKV_API int slimkv_version(void);
+
+/* Human-readable text of the last host-side error on this thread. */
+SLIMKV_API const char* slimkv_last_error(void);
+
+/*
+ * Read (and optionally clear) the device status word of the current device.
+ * Synchronises the device.  Returns SLIMKV_OK or SLIMKV_ERR_CUDA.
+ */
+SLIMKV_API int slimkv_device_status(unsigned int* status, int clear);
+
+/* ------------------------------------------------------------------------
+ * Split-KV decode attention — drop-in for the reference extension
+ * `slimkv_fa2_decode_320.forward(q, k, v, softmax_scale, causal=False,
+ * num_splits=0, pack_q=True, cache_seqlens=None)`
+ * (kernels/fa2_decode/binding.cpp:35-121, bound at 123-130).
+ *
+ * BSHD layouts with element strides {batch, seq, head}; the last dimension is
+ * contiguous.  q [B, Q, H, D], k [B, N, Hkv, D], v [B, N, Hkv, Dv]; a batch
+ * stride of 0 for k/v (one cache shared by every row) is allowed.  H % Hkv
+ * == 0, Q in {1, 2}.  D, Dv <= 320 and multiples of 8.  Row strides must be
+ * multiples of 8 elements and pointers 16-byte aligned (TMA).
+ * out [B, Q, H, Dv] bf16, lse [B, H, Q] fp32 contiguous (natural log).
+ * `causal` is bottom-right aligned.  Rows that see no key get zero output
+ * and lse = +inf when `lse_masked_positive` (the reference extension's
+ * convention) else -inf.  `cache_seqlens` (optional, int32 [B], device)
+ * limits each row's keys.  `num_splits` 0 picks the split count.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    const void* q;
+    int64_t q_stride[3];
+    const void* k;
+    int64_t k_stride[3];
+    const void* v;
+    int64_t v_stride[3];
+    void* out;
+    int64_t out_stride[3];
+    float* lse;
+    const int32_t* cache_seqlens;
+    int batch, queries, heads, kv_heads, keys, head_dim, value_dim;
+    float scale;
+    int causal;
+    int num_splits;
+    int lse_masked_positive;
+} slimkv_attention_args;
+
+SLIMKV_API size_t slimkv_attention_workspace_size(const slimkv_attention_args* args);
+SLIMKV_API int slimkv_attention_forward(const slimkv_attention_args* args, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Fused latent decode step — replaces steps 3-8 of the reference decode
+ * `slimkv.llama3.fa2_decode.decode` (slimkv/llama3/fa2_decode.py:77-166):
+ * BF16-exact RoPE of q and of the new raw key, cache append of the new raw
+ * K/V and Beacon latents (llama3/memory.py:233-278, static_decode.py:156-171),
+ * raw-branch grouped attention, q-absorb into Beacon-K latent space, latent
+ * split-KV attention (causal on a Beacon-insertion row), V up-projection,
+ * up-projection biases and the LSE merge.  Writes the attention output
+ * [B, L, H*D] that feeds o_proj.
+ *
+ * Cache layout (per layer, this library's native HBM layout):
+ *   raw_k_rot / raw_v : [B, raw_capacity, Hkv, D] bf16 token-major, strides
+ *                       {raw_stride_batch, raw_stride_token} elements (head
+ *                       stride D).  Rows 0..S-1 sinks, then the open window's
+ *                       raw tail, then the current token.  raw_k_rot holds
+ *                       keys already rotated at their compressed positions.
+ *   raw_k_pre         : optional pre-RoPE copy of the keys (same layout).
+ *   lat_k / lat_v     : [B, lat_capacity, Rk] / [B, lat_capacity, Rv] bf16,
+ *                       strides {lat_stride_batch, lat_stride_row}; rows are
+ *                       history latents then open-window latents.
+ * Per-step metadata (int32 device arrays [B]):
+ *   raw_len    : raw keys incl. the current token (its row is raw_len-1)
+ *   latent_len : latents incl. a Beacon inserted this step (row latent_len-1)
+ *   query_len  : 1, or 2 when this row inserts a Beacon (optional; NULL
+ *                means `length` for every row)
+ *   qpos       : [B, length] compressed positions of the queries
+ * New entries this step (bf16, pre-RoPE): new_k / new_v [B, Hkv*D] from
+ * k_proj/v_proj; new_lat_k [B, Rk] / new_lat_v [B, Rv] from the Beacon
+ * down-projections (read only for rows whose query_len is 2).  Any of the
+ * new_* pointers may be NULL to skip that append.
+ * q [B, L, H, D] pre-RoPE (element strides {batch, seq, head}).
+ * uk / uv: up-projection weights [Hkv*D, Rk] / [Hkv*D, Rv] (nn.Linear
+ * weights), optional biases uk_bias / uv_bias [Hkv*D].
+ * cos / sin: fp32 tables [rope_positions, D].
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    int batch, length, heads, kv_heads, head_dim, rank_k, rank_v;
+    float scale;
+    const void* q;
+    int64_t q_stride[3];
+    void* raw_k_rot;
+    void* raw_v;
+    void* raw_k_pre;
+    int64_t raw_stride_batch, raw_stride_token;
+    int raw_capacity;
+    void* lat_k;
+    void* lat_v;
+    int64_t lat_stride_batch, lat_stride_row;
+    int lat_capacity;
+    const int32_t* raw_len;
+    const int32_t* latent_len;
+    const int32_t* query_len;
+    const int32_t* qpos;
+    const void* new_k;
+    const void* new_v;
+    const void* new_lat_k;
+    const void* new_lat_v;
+    const void* uk;
+    const void* uv;
+    const void* uk_bias;
+    const void* uv_bias;
+    const float* cos;
+    const float* sin;
+    int rope_positions;
+    void* out;
+    int64_t out_stride[2];
+    /* Host-side upper bounds of latent_len / raw_len used to plan the split
+     * counts (0 = the capacities).  Lengths above them are still handled. */
+    int latent_len_max;
+    int raw_len_max;
+    /* Split counts (0 = chosen from the byte volume and the SM count). */
+    int latent_splits;
+    int raw_splits;
+} slimkv_latent_decode_args;
+
+SLIMKV_API size_t slimkv_latent_decode_workspace_size(const slimkv_latent_decode_args* args);
+SLIMKV_API int slimkv_latent_decode(const slimkv_latent_decode_args* args, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * BF16-exact decode RoPE — drop-in for `decode_ops.fused_rope`
+ * (slimkv/llama3/decode_ops.py:14-31, kernel decode_kernels.py:8-51).
+ * q [B, H, Q, D] rotated at qpos [B, Q] (row stride qpos_stride); k
+ * [B, Hkv, K, D] where key s < sink sits at position s, key s in
+ * [sink, K-1) at raw_idx[s-sink] + sink + history and key K-1 at qpos[b][0].
+ * Element strides {batch, head, seq}; outputs contiguous [B,H,Q,D] and
+ * [B,Hkv,K,D].  raw_idx is int64 [K-1-sink] (may be NULL when K-1 == sink).
+ * ---------------------------------------------------------------------- */
+SLIMKV_API int slimkv_rope_decode(const void* q, const int64_t q_stride[3], const void* k,
+                       const int64_t k_stride[3], const float* cos, const float* sin,
+                       int rope_positions, const int64_t* qpos, int64_t qpos_stride,
+                       const int64_t* raw_idx, int sink, int history, int batch, int heads,
+                       int kv_heads, int queries, int keys, int head_dim, void* q_out,
+                       void* k_out, void* stream);
+
+/* ------------------------------------------------------------------------
+ * LSE merge — drop-in for `decode_ops.fused_merge`
+ * (slimkv/llama3/decode_ops.py:34-48, kernel decode_kernels.py:54-76).
+ * raw/latent [B, H, Q, D] bf16 (strides {batch, head, seq}), lse fp32
+ * [B, H, Q] (strides {batch, head, seq}); out contiguous [B, H, Q, D] bf16.
+ * ---------------------------------------------------------------------- */
+SLIMKV_API int slimkv_merge(const void* raw, const int64_t raw_stride[3], const float* raw_lse,
+                 const int64_t raw_lse_stride[3], const void* latent,
+                 const int64_t latent_stride[3], const float* latent_lse,
+                 const int64_t latent_lse_stride[3], int batch, int heads, int queries,
+                 int head_dim, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SLIMKV_B200_H */

@@ -1,0 +1,115 @@
+"""ctypes binding of the C ABI in ``include/slimkv_b200.h``.
+
+The shared library ``libslimkv_b200.so`` is built in-tree by
+``slimkv_b200.build``.  There is deliberately no fallback: if the library is
+missing or fails to load, every entry point raises, so no CPU or eager path
+can silently stand in for the CUDA kernels.
+"""
+import ctypes
+import os
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get('SLIMKV_B200_LIB', _PKG / 'libslimkv_b200.so'))
+
+SLIMKV_OK = 0
+ERRORS = {1: 'invalid argument', 2: 'unsupported shape', 3: 'alignment', 4: 'workspace',
+          5: 'CUDA error', 6: 'tensor map'}
+DEVICE_TIMEOUT = 0x1
+DEVICE_BAD_LENGTH = 0x2
+
+I64x3 = ctypes.c_int64 * 3
+I64x2 = ctypes.c_int64 * 2
+
+
+class AttentionArgs(ctypes.Structure):
+    _fields_ = [
+        ('q', ctypes.c_void_p), ('q_stride', I64x3),
+        ('k', ctypes.c_void_p), ('k_stride', I64x3),
+        ('v', ctypes.c_void_p), ('v_stride', I64x3),
+        ('out', ctypes.c_void_p), ('out_stride', I64x3),
+        ('lse', ctypes.c_void_p), ('cache_seqlens', ctypes.c_void_p),
+        ('batch', ctypes.c_int), ('queries', ctypes.c_int), ('heads', ctypes.c_int),
+        ('kv_heads', ctypes.c_int), ('keys', ctypes.c_int), ('head_dim', ctypes.c_int),
+        ('value_dim', ctypes.c_int), ('scale', ctypes.c_float), ('causal', ctypes.c_int),
+        ('num_splits', ctypes.c_int), ('lse_masked_positive', ctypes.c_int),
+    ]
+
+
+class LatentDecodeArgs(ctypes.Structure):
+    _fields_ = [
+        ('batch', ctypes.c_int), ('length', ctypes.c_int), ('heads', ctypes.c_int),
+        ('kv_heads', ctypes.c_int), ('head_dim', ctypes.c_int), ('rank_k', ctypes.c_int),
+        ('rank_v', ctypes.c_int), ('scale', ctypes.c_float),
+        ('q', ctypes.c_void_p), ('q_stride', I64x3),
+        ('raw_k_rot', ctypes.c_void_p), ('raw_v', ctypes.c_void_p), ('raw_k_pre', ctypes.c_void_p),
+        ('raw_stride_batch', ctypes.c_int64), ('raw_stride_token', ctypes.c_int64),
+        ('raw_capacity', ctypes.c_int),
+        ('lat_k', ctypes.c_void_p), ('lat_v', ctypes.c_void_p),
+        ('lat_stride_batch', ctypes.c_int64), ('lat_stride_row', ctypes.c_int64),
+        ('lat_capacity', ctypes.c_int),
+        ('raw_len', ctypes.c_void_p), ('latent_len', ctypes.c_void_p),
+        ('query_len', ctypes.c_void_p), ('qpos', ctypes.c_void_p),
+        ('new_k', ctypes.c_void_p), ('new_v', ctypes.c_void_p),
+        ('new_lat_k', ctypes.c_void_p), ('new_lat_v', ctypes.c_void_p),
+        ('uk', ctypes.c_void_p), ('uv', ctypes.c_void_p),
+        ('uk_bias', ctypes.c_void_p), ('uv_bias', ctypes.c_void_p),
+        ('cos', ctypes.c_void_p), ('sin', ctypes.c_void_p), ('rope_positions', ctypes.c_int),
+        ('out', ctypes.c_void_p), ('out_stride', I64x2),
+        ('latent_len_max', ctypes.c_int), ('raw_len_max', ctypes.c_int),
+        ('latent_splits', ctypes.c_int), ('raw_splits', ctypes.c_int),
+    ]
+
+
+# Exported symbols and their ctypes signatures; the CPU test suite checks
+# that the built library exports every one of them.
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+SIGNATURES = {
+    'slimkv_version': (_I, []),
+    'slimkv_last_error': (ctypes.c_char_p, []),
+    'slimkv_device_status': (_I, [ctypes.POINTER(ctypes.c_uint), _I]),
+    'slimkv_attention_workspace_size': (ctypes.c_size_t, [ctypes.POINTER(AttentionArgs)]),
+    'slimkv_attention_forward': (_I, [ctypes.POINTER(AttentionArgs), _P, ctypes.c_size_t, _P]),
+    'slimkv_latent_decode_workspace_size': (ctypes.c_size_t, [ctypes.POINTER(LatentDecodeArgs)]),
+    'slimkv_latent_decode': (_I, [ctypes.POINTER(LatentDecodeArgs), _P, ctypes.c_size_t, _P]),
+    'slimkv_rope_decode': (_I, [_P, ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _P, _P,
+                                _I, _P, ctypes.c_int64, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
+    'slimkv_merge': (_I, [_P, ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _P,
+                          ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I,
+                          _I, _P, _P]),
+}
+
+_lib = None
+
+
+def load():
+    """Load the shared library once; raises if it is missing."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f'{LIB_PATH} is missing; build it with `python -m slimkv_b200.build` '
+                              '(no CPU fallback exists)')
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+class SlimKVError(RuntimeError):
+    pass
+
+
+def check(rc):
+    if rc != SLIMKV_OK:
+        msg = load().slimkv_last_error().decode(errors='replace')
+        raise SlimKVError(f'slimkv_b200: {ERRORS.get(rc, rc)}: {msg}')
+
+
+def device_status(clear=False):
+    value = ctypes.c_uint(0)
+    check(load().slimkv_device_status(ctypes.byref(value), int(clear)))
+    return value.value

@@ -1,0 +1,492 @@
+// Fused SlimKV latent decode step (C ABI slimkv_latent_decode).
+//
+// Replaces steps 3-8 of the reference `fa2_decode.decode`
+// (slimkv/llama3/fa2_decode.py:77-166) with three launches:
+//   1. prologue  — BF16-exact RoPE of q (decode_kernels.py:8-51), q-absorb
+//                  into Beacon-K latent space (fa2_decode.py:41-46), and the
+//                  append of the new raw K (rotated and pre-RoPE) / V and of a
+//                  new Beacon latent pair (llama3/memory.py:233-278);
+//   2. attention — one launch whose first CTAs stream the latent cache (one
+//                  shared latent "head", all H query heads per CTA, causal on
+//                  Beacon-insertion rows) and whose remaining CTAs stream the
+//                  raw sink+tail per KV head (fa2_decode.py:146-154);
+//   3. merge     — split combine of both branches, V up-projection with its
+//                  bias (fa2_decode.py:49-54, 157-163), the K-bias LSE shift
+//                  and the LSE merge (fa2_decode.py:57-66).
+#include <algorithm>
+
+#include "attn_body.cuh"
+#include "host_utils.h"
+
+namespace slimkv {
+
+int make_bshd_map(CUtensorMap* map, const void* base, int batch, int keys, int kv_heads, int dim,
+                  const int64_t stride[3], int* bcast);
+
+struct PrologueArgs {
+    const __nv_bfloat16* q;
+    int64_t q_sb, q_sl, q_sh;
+    int length, heads, kv_heads, dim, rank_k, rank_v, width, group;
+    const int32_t* qpos;
+    const int32_t* qlens;
+    const float* cos;
+    const float* sin;
+    int rope_positions;
+    const __nv_bfloat16* uk;
+    __nv_bfloat16* q_rot;   // [B, L, H, D]
+    __nv_bfloat16* q_lat;   // [B, L, H, width]
+    const __nv_bfloat16* new_k;
+    const __nv_bfloat16* new_v;
+    __nv_bfloat16* raw_k_rot;
+    __nv_bfloat16* raw_v;
+    __nv_bfloat16* raw_k_pre;
+    int64_t raw_sb, raw_st;
+    const int32_t* raw_len;
+    int raw_capacity;
+    const __nv_bfloat16* new_lat_k;
+    const __nv_bfloat16* new_lat_v;
+    __nv_bfloat16* lat_k;
+    __nv_bfloat16* lat_v;
+    int64_t lat_sb, lat_sr;
+    const int32_t* latent_len;
+    int lat_capacity;
+    unsigned int* status;
+};
+
+// out = bf16(bf16(x * bf16(cos)) + bf16(rotate_half(x) * bf16(sin))), the
+// reference's per-operation BF16 rounding (decode_kernels.py:40-51).
+__device__ __forceinline__ float rope_one(float x, float partner, int d, int half, float c, float s) {
+    const float rot = d < half ? -partner : partner;
+    const float cb = bf16_round(c), sb = bf16_round(s);
+    const float first = bf16_round(__fmul_rn(x, cb));
+    const float second = bf16_round(__fmul_rn(rot, sb));
+    return bf16_round(__fadd_rn(first, second));
+}
+
+constexpr int kMaxRows = 16;   // query rows per KV head handled by prologue/merge
+
+__global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
+    extern __shared__ float qs[];                      // [rows][dim]
+    const int g = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const int qlen = a.qlens ? a.qlens[b] : a.length;
+    const int rows = qlen * a.group;
+    const int half = a.dim / 2;
+    // ---- RoPE of this KV head's query rows ----
+    for (int idx = tid; idx < rows * a.dim; idx += blockDim.x) {
+        const int r = idx / a.dim, d = idx - r * a.dim;
+        const int l = r / a.group, h = g * a.group + (r - l * a.group);
+        int pos = a.qpos[b * a.length + l];
+        if (pos < 0 || pos >= a.rope_positions) {
+            report(a.status, SLIMKV_DEVICE_BAD_LENGTH);
+            pos = 0;
+        }
+        const __nv_bfloat16* src = a.q + b * a.q_sb + l * a.q_sl + h * a.q_sh;
+        const float v = rope_one(__bfloat162float(src[d]), __bfloat162float(src[(d + half) % a.dim]), d, half,
+                                 a.cos[(int64_t)pos * a.dim + d], a.sin[(int64_t)pos * a.dim + d]);
+        a.q_rot[(((int64_t)b * a.length + l) * a.heads + h) * a.dim + d] = __float2bfloat16_rn(v);
+        qs[r * a.dim + d] = v;
+    }
+    __syncthreads();
+    // ---- q-absorb: q_lat[r, c] = sum_d q_rot[r, d] * U_k[g*D + d, c] ----
+    for (int c = tid; c < a.width; c += blockDim.x) {
+        float acc[kMaxRows];
+#pragma unroll
+        for (int r = 0; r < kMaxRows; ++r) acc[r] = 0.f;
+        if (c < a.rank_k) {
+            const __nv_bfloat16* u = a.uk + (int64_t)g * a.dim * a.rank_k + c;
+            for (int d = 0; d < a.dim; ++d) {
+                const float w = __bfloat162float(u[(int64_t)d * a.rank_k]);
+#pragma unroll
+                for (int r = 0; r < kMaxRows; ++r)
+                    if (r < rows) acc[r] = fmaf(qs[r * a.dim + d], w, acc[r]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < kMaxRows; ++r) {
+            if (r >= rows) break;
+            const int l = r / a.group, h = g * a.group + (r - l * a.group);
+            a.q_lat[(((int64_t)b * a.length + l) * a.heads + h) * a.width + c] = __float2bfloat16_rn(acc[r]);
+        }
+    }
+    // ---- append the new raw token of this KV head ----
+    if (a.new_k) {
+        const int row = a.raw_len[b] - 1;
+        if (row < 0 || row >= a.raw_capacity) {
+            if (tid == 0) report(a.status, SLIMKV_DEVICE_BAD_LENGTH);
+        } else {
+            int pos = a.qpos[b * a.length];
+            if (pos < 0 || pos >= a.rope_positions) pos = 0;
+            const __nv_bfloat16* k = a.new_k + ((int64_t)b * a.kv_heads + g) * a.dim;
+            const __nv_bfloat16* v = a.new_v + ((int64_t)b * a.kv_heads + g) * a.dim;
+            const int64_t dst = b * a.raw_sb + row * a.raw_st + (int64_t)g * a.dim;
+            for (int d = tid; d < a.dim; d += blockDim.x) {
+                const float x = __bfloat162float(k[d]);
+                const float rv = rope_one(x, __bfloat162float(k[(d + half) % a.dim]), d, half,
+                                          a.cos[(int64_t)pos * a.dim + d], a.sin[(int64_t)pos * a.dim + d]);
+                a.raw_k_rot[dst + d] = __float2bfloat16_rn(rv);
+                a.raw_v[dst + d] = v[d];
+                if (a.raw_k_pre) a.raw_k_pre[dst + d] = k[d];
+            }
+        }
+    }
+    // ---- append the Beacon latent pair inserted by this row ----
+    if (g == 0 && a.new_lat_k && qlen == 2) {
+        const int row = a.latent_len[b] - 1;
+        if (row < 0 || row >= a.lat_capacity) {
+            if (tid == 0) report(a.status, SLIMKV_DEVICE_BAD_LENGTH);
+        } else {
+            for (int c = tid; c < a.rank_k; c += blockDim.x)
+                a.lat_k[b * a.lat_sb + row * a.lat_sr + c] = a.new_lat_k[(int64_t)b * a.rank_k + c];
+            for (int c = tid; c < a.rank_v; c += blockDim.x)
+                a.lat_v[b * a.lat_sb + row * a.lat_sr + c] = a.new_lat_v[(int64_t)b * a.rank_v + c];
+        }
+    }
+}
+
+// One launch: CTAs [0, n_latent) take latent work items, the rest raw ones.
+template <int WL, int MTL>
+__global__ void __launch_bounds__(kThreads, 1)
+decode_attention_kernel(const __grid_constant__ CUtensorMap lk, const __grid_constant__ CUtensorMap lv,
+                        const __grid_constant__ CUtensorMap rk, const __grid_constant__ CUtensorMap rv,
+                        AttnJob jl, AttnJob jr, int latent_row_blocks, int n_latent) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    int idx = blockIdx.x;
+    if (idx < n_latent) {
+        if (threadIdx.x == 0) { tma_prefetch_desc(&lk); tma_prefetch_desc(&lv); }
+        jl.kmap = &lk;
+        jl.vmap = &lv;
+        const int split = idx % jl.splits;
+        const int rest = idx / jl.splits;
+        attn_body<WL, MTL>(jl, rest / latent_row_blocks, 0, split, rest % latent_row_blocks, smem);
+    } else {
+        idx -= n_latent;
+        if (threadIdx.x == 0) { tma_prefetch_desc(&rk); tma_prefetch_desc(&rv); }
+        jr.kmap = &rk;
+        jr.vmap = &rv;
+        const int split = idx % jr.splits;
+        const int bg = idx / jr.splits;
+        attn_body<128, 1>(jr, bg / jr.kv_heads, bg % jr.kv_heads, split, 0, smem);
+    }
+}
+
+struct MergeArgs {
+    const float* lat_o; const float* lat_lse; int lat_splits, lat_rows, lat_width;
+    const float* raw_o; const float* raw_lse; int raw_splits, raw_rows;
+    const __nv_bfloat16* q_rot;
+    const __nv_bfloat16* uv; const __nv_bfloat16* uk_bias; const __nv_bfloat16* uv_bias;
+    const int32_t* qlens;
+    int length, heads, kv_heads, dim, rank_v, group;
+    float scale;
+    __nv_bfloat16* out; int64_t o_sb, o_sl;
+};
+
+// Combine `splits` normalised partials of one row into dst[0..width).
+__device__ void combine_row(const float* o, const float* lse, int splits, int64_t row_pitch, int width,
+                            int lane, float* dst, float* lse_dst) {
+    float m = -INFINITY;
+    for (int s = lane; s < splits; s += 32) m = fmaxf(m, lse[s * row_pitch]);
+#pragma unroll
+    for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    float total = 0.f;
+    if (m != -INFINITY)
+        for (int s = lane; s < splits; s += 32) total += expf(lse[s * row_pitch] - m);
+#pragma unroll
+    for (int off = 16; off; off >>= 1) total += __shfl_xor_sync(0xffffffffu, total, off);
+    const float inv = total > 0.f ? 1.f / total : 0.f;
+    for (int c = lane; c < width; c += 32) {
+        float acc = 0.f;
+        if (m != -INFINITY)
+            for (int s = 0; s < splits; ++s)
+                acc += expf(lse[s * row_pitch] - m) * o[s * row_pitch * width + c];
+        dst[c] = acc * inv;
+    }
+    if (lane == 0) *lse_dst = m == -INFINITY ? -INFINITY : m + logf(total);
+}
+
+__global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
+    extern __shared__ float sm[];
+    const int g = blockIdx.x, b = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int qlen = a.qlens ? a.qlens[b] : a.length;
+    const int rows = qlen * a.group;
+    float* olat = sm;                                   // [kMaxRows][lat_width]
+    float* oraw = olat + kMaxRows * a.lat_width;        // [kMaxRows][dim]
+    float* llat = oraw + kMaxRows * a.dim;              // [kMaxRows]
+    float* lraw = llat + kMaxRows;
+    for (int r = warp; r < rows; r += 8) {
+        const int l = r / a.group, h = g * a.group + (r - l * a.group);
+        const int rl = l * a.heads + h;                 // row in the latent job
+        const int64_t lat_base = (int64_t)b * a.lat_splits * a.lat_rows + rl;
+        combine_row(a.lat_o + lat_base * a.lat_width, a.lat_lse + lat_base, a.lat_splits, a.lat_rows,
+                    a.lat_width, lane, olat + r * a.lat_width, llat + r);
+        const int64_t raw_base = ((int64_t)(b * a.kv_heads + g) * a.raw_splits) * a.raw_rows + r;
+        combine_row(a.raw_o + raw_base * a.dim, a.raw_lse + raw_base, a.raw_splits, a.raw_rows, a.dim, lane,
+                    oraw + r * a.dim, lraw + r);
+        if (a.uk_bias) {
+            // Latent LSE shift by scale * q . b_k (fa2_decode.py:157-160).
+            const __nv_bfloat16* q = a.q_rot + (((int64_t)b * a.length + l) * a.heads + h) * a.dim;
+            const __nv_bfloat16* bk = a.uk_bias + (int64_t)g * a.dim;
+            float dot = 0.f;
+            for (int d = lane; d < a.dim; d += 32) dot += __bfloat162float(q[d]) * __bfloat162float(bk[d]);
+#pragma unroll
+            for (int off = 16; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+            __syncwarp();
+            if (lane == 0 && llat[r] != -INFINITY) llat[r] += dot * a.scale;
+        }
+    }
+    __syncthreads();
+    // ---- V up-projection, bias and LSE merge: thread owns column d ----
+    for (int d = tid; d < a.dim; d += blockDim.x) {
+        float acc[kMaxRows];
+#pragma unroll
+        for (int r = 0; r < kMaxRows; ++r) acc[r] = 0.f;
+        const __nv_bfloat16* u = a.uv + ((int64_t)g * a.dim + d) * a.rank_v;
+        for (int c = 0; c < a.rank_v; c += 8) {
+            const uint4 pk = *reinterpret_cast<const uint4*>(u + c);
+            const __nv_bfloat16* w8 = reinterpret_cast<const __nv_bfloat16*>(&pk);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float w = __bfloat162float(w8[e]);
+#pragma unroll
+                for (int r = 0; r < kMaxRows; ++r)
+                    if (r < rows) acc[r] = fmaf(olat[r * a.lat_width + c + e], w, acc[r]);
+            }
+        }
+        const float bv = a.uv_bias ? __bfloat162float(a.uv_bias[(int64_t)g * a.dim + d]) : 0.f;
+#pragma unroll
+        for (int r = 0; r < kMaxRows; ++r) {
+            if (r >= rows) break;
+            const int l = r / a.group, h = g * a.group + (r - l * a.group);
+            const float lr = lraw[r], ll = llat[r];
+            float value;
+            if (lr == -INFINITY && ll == -INFINITY) {
+                value = 0.f;
+            } else {
+                const float mx = fmaxf(lr, ll);
+                const float total = mx + log1pf(expf(-fabsf(lr - ll)));
+                const float wr = lr == -INFINITY ? 0.f : expf(lr - total);
+                const float wl = ll == -INFINITY ? 0.f : expf(ll - total);
+                value = wr * oraw[r * a.dim + d] + wl * (acc[r] + bv);
+            }
+            a.out[b * a.o_sb + l * a.o_sl + (int64_t)h * a.dim + d] = __float2bfloat16_rn(value);
+        }
+    }
+}
+
+namespace {
+
+struct DecodePlan {
+    int wl = 0, mtl = 0, lat_row_blocks = 0, lat_rows = 0, lat_splits = 0, lat_tps = 0;
+    int raw_rows = 0, raw_splits = 0, raw_tps = 0, group = 0;
+    size_t q_rot = 0, q_lat = 0, lat_o = 0, lat_lse = 0, raw_o = 0, raw_lse = 0;
+};
+
+int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
+    if (!a) return fail(SLIMKV_ERR_INVALID_ARGUMENT, "null arguments");
+    if (a->batch <= 0 || a->heads <= 0 || a->kv_heads <= 0 || a->heads % a->kv_heads)
+        return fail(SLIMKV_ERR_INVALID_ARGUMENT, "invalid head counts");
+    if (a->length != 1 && a->length != 2) return fail(SLIMKV_ERR_INVALID_ARGUMENT, "length must be 1 or 2");
+    if (a->head_dim != 128) return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "fused decode needs head_dim 128");
+    if (a->rank_k <= 0 || a->rank_k > 320 || a->rank_k % 8 || a->rank_v <= 0 || a->rank_v > 320 || a->rank_v % 8)
+        return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "latent ranks must be multiples of 8 in [8, 320]");
+    if (a->raw_capacity <= 0 || a->lat_capacity <= 0) return fail(SLIMKV_ERR_INVALID_ARGUMENT, "empty cache");
+    p.group = a->heads / a->kv_heads;
+    if (p.group * a->length > kMaxRows)
+        return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "at most %d query rows per KV head", kMaxRows);
+    p.wl = (std::max(a->rank_k, a->rank_v) + 63) / 64 * 64;
+    p.wl = std::max(p.wl, 128);
+    const int lat_rows = a->heads * a->length;
+    p.mtl = lat_rows <= 32 ? 2 : 4;
+    p.lat_row_blocks = (lat_rows + 16 * p.mtl - 1) / (16 * p.mtl);
+    p.lat_rows = p.lat_row_blocks * 16 * p.mtl;
+    p.raw_rows = 16;
+    const int lat_len = a->latent_len_max > 0 ? std::min(a->latent_len_max, a->lat_capacity) : a->lat_capacity;
+    const int raw_len = a->raw_len_max > 0 ? std::min(a->raw_len_max, a->raw_capacity) : a->raw_capacity;
+    const int lat_tiles = std::max(1, (lat_len + kTile - 1) / kTile);
+    const int raw_tiles = std::max(1, (raw_len + kTile - 1) / kTile);
+    // Balance bytes: one CTA per SM, each streaming about the same volume.
+    const double lat_tile_bytes = double(kTile) * (a->rank_k + a->rank_v) * 2;
+    const double raw_tile_bytes = double(kTile) * a->head_dim * 2 * 2;
+    const double total = a->batch * (p.lat_row_blocks * lat_tiles * lat_tile_bytes +
+                                     a->kv_heads * raw_tiles * raw_tile_bytes);
+    const double per_cta = total / std::max(device_info().sm_count, 1);
+    int ls = a->latent_splits > 0 ? a->latent_splits
+                                  : int(std::ceil(lat_tiles * lat_tile_bytes / std::max(per_cta, 1.0)));
+    int rs = a->raw_splits > 0 ? a->raw_splits : int(std::ceil(raw_tiles * raw_tile_bytes / std::max(per_cta, 1.0)));
+    ls = std::max(1, std::min(ls, lat_tiles));
+    rs = std::max(1, std::min(rs, raw_tiles));
+    p.lat_tps = (lat_tiles + ls - 1) / ls;
+    p.lat_splits = (lat_tiles + p.lat_tps - 1) / p.lat_tps;
+    p.raw_tps = (raw_tiles + rs - 1) / rs;
+    p.raw_splits = (raw_tiles + p.raw_tps - 1) / p.raw_tps;
+    const size_t B = a->batch, L = a->length, H = a->heads;
+    p.q_rot = B * L * H * a->head_dim;
+    p.q_lat = B * L * H * p.wl;
+    p.lat_o = B * p.lat_splits * p.lat_rows * p.wl;
+    p.lat_lse = B * p.lat_splits * p.lat_rows;
+    p.raw_o = B * a->kv_heads * p.raw_splits * p.raw_rows * 128;
+    p.raw_lse = B * a->kv_heads * p.raw_splits * p.raw_rows;
+    return SLIMKV_OK;
+}
+
+struct Buffers {
+    __nv_bfloat16 *q_rot, *q_lat;
+    float *lat_o, *lat_lse, *raw_o, *raw_lse;
+};
+
+Buffers carve(Carver& c, const DecodePlan& p) {
+    Buffers w;
+    w.q_rot = c.take<__nv_bfloat16>(p.q_rot);
+    w.q_lat = c.take<__nv_bfloat16>(p.q_lat);
+    w.lat_o = c.take<float>(p.lat_o);
+    w.lat_lse = c.take<float>(p.lat_lse);
+    w.raw_o = c.take<float>(p.raw_o);
+    w.raw_lse = c.take<float>(p.raw_lse);
+    return w;
+}
+
+template <int WL, int MTL>
+int launch_decode_attention(const CUtensorMap& lk, const CUtensorMap& lv, const CUtensorMap& rk,
+                            const CUtensorMap& rv, const AttnJob& jl, const AttnJob& jr, int row_blocks,
+                            int n_latent, int n_raw, cudaStream_t stream) {
+    constexpr int smem = std::max(AttnCfg<WL, MTL>::SMEM, AttnCfg<128, 1>::SMEM);
+    auto kernel = decode_attention_kernel<WL, MTL>;
+    static bool configured[64] = {};
+    const int dev = device_info().device;
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return fail(SLIMKV_ERR_CUDA, "cudaFuncSetAttribute failed");
+        configured[dev] = true;
+    }
+    kernel<<<n_latent + n_raw, kThreads, smem, stream>>>(lk, lv, rk, rv, jl, jr, row_blocks, n_latent);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "decode attention launch failed: %s", cudaGetErrorString(e));
+    return SLIMKV_OK;
+}
+
+template <int WL>
+int launch_wl(int mtl, const CUtensorMap& lk, const CUtensorMap& lv, const CUtensorMap& rk, const CUtensorMap& rv,
+              const AttnJob& jl, const AttnJob& jr, int rb, int nl, int nr, cudaStream_t s) {
+    if (mtl == 2) return launch_decode_attention<WL, 2>(lk, lv, rk, rv, jl, jr, rb, nl, nr, s);
+    return launch_decode_attention<WL, 4>(lk, lv, rk, rv, jl, jr, rb, nl, nr, s);
+}
+
+}  // namespace
+}  // namespace slimkv
+
+using namespace slimkv;
+
+extern "C" size_t slimkv_latent_decode_workspace_size(const slimkv_latent_decode_args* a) {
+    DecodePlan p;
+    if (plan_decode(a, p) != SLIMKV_OK) return 0;
+    Carver c(nullptr, 0);
+    carve(c, p);
+    return c.used + 256;
+}
+
+extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* workspace, size_t workspace_bytes,
+                                    void* stream_ptr) {
+    DecodePlan p;
+    int rc = plan_decode(a, p);
+    if (rc) return rc;
+    if (!a->q || !a->raw_k_rot || !a->raw_v || !a->lat_k || !a->lat_v || !a->raw_len || !a->latent_len ||
+        !a->qpos || !a->uk || !a->uv || !a->cos || !a->sin || !a->out)
+        return fail(SLIMKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if ((a->new_k == nullptr) != (a->new_v == nullptr) || (a->new_lat_k == nullptr) != (a->new_lat_v == nullptr))
+        return fail(SLIMKV_ERR_INVALID_ARGUMENT, "new K/V (and new latent K/V) must be given together");
+    if (a->raw_stride_token % 8 || a->raw_stride_batch % 8 || a->lat_stride_row % 8 || a->lat_stride_batch % 8 ||
+        !aligned16(a->raw_k_rot) || !aligned16(a->raw_v) || !aligned16(a->lat_k) || !aligned16(a->lat_v) ||
+        !aligned16(a->uv))
+        return fail(SLIMKV_ERR_ALIGNMENT, "caches must be 16-byte aligned with strides that are multiples of 8");
+    if (a->raw_stride_token < (int64_t)a->kv_heads * a->head_dim || a->lat_stride_row < std::max(a->rank_k, a->rank_v))
+        return fail(SLIMKV_ERR_INVALID_ARGUMENT, "cache row stride smaller than a row");
+    Carver c(workspace, workspace_bytes);
+    const Buffers w = carve(c, p);
+    if (!workspace || !c.fits())
+        return fail(SLIMKV_ERR_WORKSPACE, "workspace too small (%zu < %zu)", workspace_bytes, c.used);
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    unsigned int* status = status_word();
+
+    // 1. prologue
+    PrologueArgs pa{};
+    pa.q = static_cast<const __nv_bfloat16*>(a->q);
+    pa.q_sb = a->q_stride[0]; pa.q_sl = a->q_stride[1]; pa.q_sh = a->q_stride[2];
+    pa.length = a->length; pa.heads = a->heads; pa.kv_heads = a->kv_heads; pa.dim = a->head_dim;
+    pa.rank_k = a->rank_k; pa.rank_v = a->rank_v; pa.width = p.wl; pa.group = p.group;
+    pa.qpos = a->qpos; pa.qlens = a->query_len; pa.cos = a->cos; pa.sin = a->sin;
+    pa.rope_positions = a->rope_positions;
+    pa.uk = static_cast<const __nv_bfloat16*>(a->uk);
+    pa.q_rot = w.q_rot; pa.q_lat = w.q_lat;
+    pa.new_k = static_cast<const __nv_bfloat16*>(a->new_k);
+    pa.new_v = static_cast<const __nv_bfloat16*>(a->new_v);
+    pa.raw_k_rot = static_cast<__nv_bfloat16*>(a->raw_k_rot);
+    pa.raw_v = static_cast<__nv_bfloat16*>(a->raw_v);
+    pa.raw_k_pre = static_cast<__nv_bfloat16*>(a->raw_k_pre);
+    pa.raw_sb = a->raw_stride_batch; pa.raw_st = a->raw_stride_token;
+    pa.raw_len = a->raw_len; pa.raw_capacity = a->raw_capacity;
+    pa.new_lat_k = static_cast<const __nv_bfloat16*>(a->new_lat_k);
+    pa.new_lat_v = static_cast<const __nv_bfloat16*>(a->new_lat_v);
+    pa.lat_k = static_cast<__nv_bfloat16*>(a->lat_k);
+    pa.lat_v = static_cast<__nv_bfloat16*>(a->lat_v);
+    pa.lat_sb = a->lat_stride_batch; pa.lat_sr = a->lat_stride_row;
+    pa.latent_len = a->latent_len; pa.lat_capacity = a->lat_capacity;
+    pa.status = status;
+    const size_t psmem = size_t(kMaxRows) * a->head_dim * sizeof(float);
+    decode_prologue_kernel<<<dim3(a->kv_heads, a->batch), 256, psmem, stream>>>(pa);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "prologue launch failed: %s", cudaGetErrorString(e));
+
+    // 2. attention over both branches
+    CUtensorMap lk, lv, rk, rv;
+    int bc = 0;
+    const int64_t lat_stride[3] = {a->lat_stride_batch, a->lat_stride_row, a->lat_stride_row};
+    if ((rc = make_bshd_map(&lk, a->lat_k, a->batch, a->lat_capacity, 1, a->rank_k, lat_stride, &bc))) return rc;
+    if ((rc = make_bshd_map(&lv, a->lat_v, a->batch, a->lat_capacity, 1, a->rank_v, lat_stride, &bc))) return rc;
+    const int64_t raw_stride[3] = {a->raw_stride_batch, a->raw_stride_token, a->head_dim};
+    if ((rc = make_bshd_map(&rk, a->raw_k_rot, a->batch, a->raw_capacity, a->kv_heads, a->head_dim, raw_stride, &bc)))
+        return rc;
+    if ((rc = make_bshd_map(&rv, a->raw_v, a->batch, a->raw_capacity, a->kv_heads, a->head_dim, raw_stride, &bc)))
+        return rc;
+    const float scale_log2 = a->scale * 1.4426950408889634f;
+    AttnJob jl{};
+    jl.q = w.q_lat; jl.q_sb = (int64_t)a->length * a->heads * p.wl; jl.q_sl = (int64_t)a->heads * p.wl; jl.q_sh = p.wl;
+    jl.seqlens = a->latent_len; jl.keys = a->lat_capacity; jl.qlens = a->query_len; jl.queries = a->length;
+    jl.group = a->heads; jl.kv_heads = 1; jl.dk = a->rank_k; jl.scale_log2 = scale_log2; jl.causal = 1;
+    jl.splits = p.lat_splits; jl.tiles_per_split = p.lat_tps; jl.rows_alloc = p.lat_rows; jl.out_width = p.wl;
+    jl.part_o = w.lat_o; jl.part_lse = w.lat_lse; jl.status = status;
+    AttnJob jr{};
+    jr.q = w.q_rot; jr.q_sb = (int64_t)a->length * a->heads * a->head_dim; jr.q_sl = (int64_t)a->heads * a->head_dim;
+    jr.q_sh = a->head_dim;
+    jr.seqlens = a->raw_len; jr.keys = a->raw_capacity; jr.qlens = a->query_len; jr.queries = a->length;
+    jr.group = p.group; jr.kv_heads = a->kv_heads; jr.dk = a->head_dim; jr.scale_log2 = scale_log2; jr.causal = 0;
+    jr.splits = p.raw_splits; jr.tiles_per_split = p.raw_tps; jr.rows_alloc = p.raw_rows; jr.out_width = 128;
+    jr.part_o = w.raw_o; jr.part_lse = w.raw_lse; jr.status = status;
+    const int n_latent = a->batch * p.lat_row_blocks * p.lat_splits;
+    const int n_raw = a->batch * a->kv_heads * p.raw_splits;
+    switch (p.wl) {
+        case 128: rc = launch_wl<128>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
+        case 192: rc = launch_wl<192>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
+        case 256: rc = launch_wl<256>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
+        default: rc = launch_wl<320>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
+    }
+    if (rc) return rc;
+
+    // 3. merge
+    MergeArgs ma{};
+    ma.lat_o = w.lat_o; ma.lat_lse = w.lat_lse; ma.lat_splits = p.lat_splits; ma.lat_rows = p.lat_rows;
+    ma.lat_width = p.wl;
+    ma.raw_o = w.raw_o; ma.raw_lse = w.raw_lse; ma.raw_splits = p.raw_splits; ma.raw_rows = p.raw_rows;
+    ma.q_rot = w.q_rot;
+    ma.uv = static_cast<const __nv_bfloat16*>(a->uv);
+    ma.uk_bias = static_cast<const __nv_bfloat16*>(a->uk_bias);
+    ma.uv_bias = static_cast<const __nv_bfloat16*>(a->uv_bias);
+    ma.qlens = a->query_len; ma.length = a->length; ma.heads = a->heads; ma.kv_heads = a->kv_heads;
+    ma.dim = a->head_dim; ma.rank_v = a->rank_v; ma.group = p.group; ma.scale = a->scale;
+    ma.out = static_cast<__nv_bfloat16*>(a->out); ma.o_sb = a->out_stride[0]; ma.o_sl = a->out_stride[1];
+    const size_t msmem = (size_t(kMaxRows) * (p.wl + a->head_dim) + 2 * kMaxRows) * sizeof(float);
+    decode_merge_kernel<<<dim3(a->kv_heads, a->batch), 256, msmem, stream>>>(ma);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "merge launch failed: %s", cudaGetErrorString(e));
+    return SLIMKV_OK;
+}

@@ -1,0 +1,196 @@
+"""Torch-tensor entry points over the C ABI (``include/slimkv_b200.h``).
+
+Each wrapper checks devices, dtypes and shapes, sizes and allocates the
+workspace from PyTorch's caching allocator (so calls can be captured in CUDA
+graphs), and launches on the current CUDA stream.  There is no CPU path:
+CPU tensors or a missing library raise.
+"""
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+
+
+def _ptr(t):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _require(cond, msg):
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _bf16_cuda(*tensors):
+    for t in tensors:
+        _require(t.is_cuda, 'CUDA tensors required')
+        _require(t.dtype == torch.bfloat16, 'BF16 only')
+
+
+def attention_forward(q, k, v, scale, causal=False, num_splits=0, cache_seqlens=None,
+                      lse_masked_positive=True, out=None, lse=None):
+    """Split-KV grouped decode attention over BSHD tensors.
+
+    ``q [B, Q, H, D]``, ``k [B, N, Hkv, D]``, ``v [B, N, Hkv, Dv]`` bf16 with a
+    contiguous last dimension; returns ``(out [B, Q, H, Dv] bf16, lse [B, H,
+    Q] fp32)``.  Rows that see no key get zero output and ``lse = +inf`` when
+    ``lse_masked_positive`` (the reference extension's convention) or
+    ``-inf`` otherwise.
+    """
+    _bf16_cuda(q, k, v)
+    _require(q.dim() == 4 and k.dim() == 4 and v.dim() == 4, 'BSHD tensors required')
+    _require(q.stride(3) == 1 and k.stride(3) == 1 and v.stride(3) == 1, 'Last dimension must be contiguous')
+    _require(q.device == k.device == v.device, 'Same device required')
+    batch, queries, heads, dim = q.shape
+    _require(k.shape[0] == batch and v.shape[:3] == k.shape[:3] and k.shape[3] == dim, 'Invalid K/V shape')
+    if out is None:
+        out = q.new_empty(batch, queries, heads, v.shape[3])
+    if lse is None:
+        lse = torch.empty(batch, heads, queries, device=q.device, dtype=torch.float32)
+    if cache_seqlens is not None:
+        _require(cache_seqlens.is_cuda and cache_seqlens.dtype == torch.int32 and cache_seqlens.is_contiguous()
+                 and cache_seqlens.numel() == batch, 'One CUDA int32 cache length per sequence required')
+    a = _lib.AttentionArgs()
+    a.q, a.q_stride = q.data_ptr(), _lib.I64x3(*q.stride()[:3])
+    a.k, a.k_stride = k.data_ptr(), _lib.I64x3(*k.stride()[:3])
+    a.v, a.v_stride = v.data_ptr(), _lib.I64x3(*v.stride()[:3])
+    a.out, a.out_stride = out.data_ptr(), _lib.I64x3(*out.stride()[:3])
+    a.lse = lse.data_ptr()
+    a.cache_seqlens = 0 if cache_seqlens is None else cache_seqlens.data_ptr()
+    a.batch, a.queries, a.heads, a.kv_heads = batch, queries, heads, k.shape[2]
+    a.keys, a.head_dim, a.value_dim = k.shape[1], dim, v.shape[3]
+    a.scale, a.causal, a.num_splits = float(scale), int(bool(causal)), int(num_splits)
+    a.lse_masked_positive = int(bool(lse_masked_positive))
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        size = lib.slimkv_attention_workspace_size(ctypes.byref(a))
+        if size == 0:   # planning rejected the arguments; surface its error
+            _lib.check(lib.slimkv_attention_forward(ctypes.byref(a), None, 0, _stream()))
+        ws = torch.empty(size, dtype=torch.uint8, device=q.device)
+        _lib.check(lib.slimkv_attention_forward(ctypes.byref(a), _ptr(ws), size, _stream()))
+    return out, lse
+
+
+def rope_decode(q, k, cos, sin, query_positions, raw_indices, sink, history):
+    """BF16-exact decode RoPE (``decode_ops.fused_rope`` contract).
+
+    ``q [B, H, Q, D]`` is rotated at ``query_positions [B, Q]`` (int64); key
+    ``s`` of ``k [B, Hkv, K, D]`` sits at ``s`` when ``s < sink``, at the
+    first query position when it is the last key, and otherwise at
+    ``raw_indices[s - sink] + sink + history``.  Returns contiguous copies.
+    """
+    _bf16_cuda(q, k)
+    _require(cos.dtype == torch.float32 and sin.dtype == torch.float32 and cos.is_cuda, 'fp32 CUDA tables')
+    _require(q.stride(3) == 1 and k.stride(3) == 1, 'Last dimension must be contiguous')
+    _require(q.dim() == 4 and k.dim() == 4 and q.shape[0] == k.shape[0] and q.shape[3] == k.shape[3],
+             'q [B, H, Q, D] and k [B, Hkv, K, D] must share B and D')
+    _require(query_positions.shape == (q.shape[0], q.shape[2]), 'query positions must be [B, Q]')
+    if k.shape[2] - 1 > sink:
+        _require(raw_indices is not None and raw_indices.numel() >= k.shape[2] - 1 - sink,
+                 'raw indices must cover the keys between the sinks and the current token')
+    qpos = query_positions.to(torch.int64)
+    _require(qpos.stride(1) == 1, 'query positions must be row-contiguous')
+    raw = None if raw_indices is None else raw_indices.to(torch.int64).contiguous()
+    oq, ok = torch.empty(q.shape, dtype=q.dtype, device=q.device), torch.empty(k.shape, dtype=k.dtype, device=k.device)
+    st = (ctypes.c_int64 * 3)
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        _lib.check(lib.slimkv_rope_decode(
+            _ptr(q), st(*q.stride()[:3]), _ptr(k), st(*k.stride()[:3]), _ptr(cos), _ptr(sin), cos.shape[0],
+            _ptr(qpos), qpos.stride(0), _ptr(raw), int(sink), int(history), q.shape[0], q.shape[1], k.shape[1],
+            q.shape[2], k.shape[2], q.shape[3], _ptr(oq), _ptr(ok), _stream()))
+    return oq, ok
+
+
+def merge(raw, raw_lse, latent, latent_lse):
+    """LSE merge of BHQD bf16 outputs (``decode_ops.fused_merge`` contract)."""
+    _bf16_cuda(raw, latent)
+    _require(raw.stride(3) == 1 and latent.stride(3) == 1, 'Last dimension must be contiguous')
+    _require(raw_lse.dtype == torch.float32 and latent_lse.dtype == torch.float32, 'fp32 LSE required')
+    out = torch.empty(raw.shape, dtype=raw.dtype, device=raw.device)
+    st = (ctypes.c_int64 * 3)
+    lib = _lib.load()
+    with torch.cuda.device(raw.device):
+        _lib.check(lib.slimkv_merge(_ptr(raw), st(*raw.stride()[:3]), _ptr(raw_lse), st(*raw_lse.stride()[:3]),
+                                    _ptr(latent), st(*latent.stride()[:3]), _ptr(latent_lse),
+                                    st(*latent_lse.stride()[:3]), raw.shape[0], raw.shape[1], raw.shape[2],
+                                    raw.shape[3], _ptr(out), _stream()))
+    return out
+
+
+class LatentDecodeCall:
+    """Prepared arguments of ``slimkv_latent_decode`` for fixed buffers.
+
+    Built once per (layer, batch shape) by the decode runtime; ``__call__``
+    re-launches with the same pointers, which is what a CUDA graph captures.
+    """
+
+    def __init__(self, *, q, raw_k_rot, raw_v, lat_k, lat_v, raw_len, latent_len, qpos, uk, uv, cos, sin,
+                 out, query_len=None, raw_k_pre=None, new_k=None, new_v=None, new_lat_k=None, new_lat_v=None,
+                 uk_bias=None, uv_bias=None, scale=None, latent_len_max=0, raw_len_max=0, latent_splits=0,
+                 raw_splits=0):
+        _bf16_cuda(q, raw_k_rot, raw_v, lat_k, lat_v, uk, uv, out)
+        batch, length, heads, dim = q.shape
+        kv_heads = raw_k_rot.shape[2]
+        _require(raw_k_rot.shape[0] == batch and raw_k_rot.shape[3] == dim, 'raw cache shape')
+        _require(raw_k_rot.stride() == raw_v.stride() and raw_k_rot.stride(3) == 1 and raw_k_rot.stride(2) == dim,
+                 'raw caches must be token-major [B, cap, Hkv, D] with contiguous heads')
+        _require(lat_k.stride() == lat_v.stride() and lat_k.stride(2) == 1 and lat_v.stride(2) == 1,
+                 'latent caches [B, cap, R] need matching strides and contiguous rows')
+        for t in (raw_len, latent_len, qpos) + (() if query_len is None else (query_len,)):
+            _require(t.is_cuda and t.dtype == torch.int32 and t.is_contiguous(), 'int32 CUDA metadata')
+        a = _lib.LatentDecodeArgs()
+        a.batch, a.length, a.heads, a.kv_heads, a.head_dim = batch, length, heads, kv_heads, dim
+        a.rank_k, a.rank_v = lat_k.shape[2], lat_v.shape[2]
+        _require(uk.shape == (kv_heads * dim, a.rank_k) and uv.shape == (kv_heads * dim, a.rank_v),
+                 'up-projection weights must be [Hkv*D, R]')
+        a.scale = float(scale if scale is not None else 1.0 / math.sqrt(dim))
+        a.q, a.q_stride = q.data_ptr(), _lib.I64x3(*q.stride()[:3])
+        a.raw_k_rot, a.raw_v = raw_k_rot.data_ptr(), raw_v.data_ptr()
+        a.raw_k_pre = 0 if raw_k_pre is None else raw_k_pre.data_ptr()
+        a.raw_stride_batch, a.raw_stride_token = raw_k_rot.stride(0), raw_k_rot.stride(1)
+        a.raw_capacity = raw_k_rot.shape[1]
+        a.lat_k, a.lat_v = lat_k.data_ptr(), lat_v.data_ptr()
+        a.lat_stride_batch, a.lat_stride_row = lat_k.stride(0), lat_k.stride(1)
+        a.lat_capacity = lat_k.shape[1]
+        a.raw_len, a.latent_len, a.qpos = raw_len.data_ptr(), latent_len.data_ptr(), qpos.data_ptr()
+        a.query_len = 0 if query_len is None else query_len.data_ptr()
+        for name, t in (('new_k', new_k), ('new_v', new_v), ('new_lat_k', new_lat_k), ('new_lat_v', new_lat_v),
+                        ('uk_bias', uk_bias), ('uv_bias', uv_bias)):
+            if t is not None:
+                _bf16_cuda(t)
+                _require(t.is_contiguous(), f'{name} must be contiguous')
+            setattr(a, name, 0 if t is None else t.data_ptr())
+        a.uk, a.uv = uk.data_ptr(), uv.data_ptr()
+        _require(cos.dtype == torch.float32 and cos.is_contiguous() and sin.is_contiguous(), 'fp32 tables')
+        a.cos, a.sin, a.rope_positions = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
+        _require(out.shape == (batch, length, heads * dim) and out.stride(2) == 1, 'out must be [B, L, H*D]')
+        a.out, a.out_stride = out.data_ptr(), _lib.I64x2(out.stride(0), out.stride(1))
+        a.latent_len_max, a.raw_len_max = int(latent_len_max), int(raw_len_max)
+        a.latent_splits, a.raw_splits = int(latent_splits), int(raw_splits)
+        self.args = a
+        self.device = q.device
+        self._keep = (q, raw_k_rot, raw_v, raw_k_pre, lat_k, lat_v, raw_len, latent_len, query_len, qpos,
+                      new_k, new_v, new_lat_k, new_lat_v, uk, uv, uk_bias, uv_bias, cos, sin, out)
+        lib = _lib.load()
+        size = lib.slimkv_latent_decode_workspace_size(ctypes.byref(a))
+        if size == 0:
+            _lib.check(lib.slimkv_latent_decode(ctypes.byref(a), None, 0, None))
+        self.workspace = torch.empty(size, dtype=torch.uint8, device=q.device)
+
+    def __call__(self):
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.slimkv_latent_decode(ctypes.byref(self.args), _ptr(self.workspace),
+                                                self.workspace.numel(), _stream()))
+        return self._keep[-1]
+
+
+def latent_decode(**kwargs):
+    """One fused decode-attention step (see :class:`LatentDecodeCall`)."""
+    return LatentDecodeCall(**kwargs)()

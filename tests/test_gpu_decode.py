@@ -1,0 +1,196 @@
+"""GPU parity of the fused latent decode step, RoPE and merge.
+
+``slimkv_latent_decode`` (C ABI) is compared with the oracle's restatement
+of ``fa2_decode.decode`` steps 3-8 on identical seeded bf16 inputs at the
+Llama-3.1-8B geometry (H=32, Hkv=8, D=128) with small caches, and its cache
+writes are checked bit-exactly.  Attention outputs use the parity bar of
+norm-wise relative error 2e-3 plus the reference GPU validation's
+element-wise tolerance (0.015); RoPE and cache writes must be bit-exact.
+"""
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from oracle.decode import latent_decode_attention
+from cases import decode_case, LLAMA8B
+from gpu_util import assert_attention_close, assert_bits_equal, to_bf16
+
+pytestmark = pytest.mark.gpu
+
+_TABLES = {}
+
+
+def tables(positions=16384):
+    if positions not in _TABLES:
+        cos, sin = oracle.rope_tables(128, LLAMA8B['theta'], positions, LLAMA8B['scaling'])
+        _TABLES[positions] = (cos, sin, torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda())
+    return _TABLES[positions]
+
+
+def run_fused(c, query_len, extra_cap=3, pre=True):
+    """Stage the caches without this step's entries, run the fused step."""
+    from slimkv_b200 import kernels
+    cos, sin, cos_t, sin_t = tables()
+    B, L, H, D = c['q'].shape
+    Hkv, rk, rv = c['kv_heads'], c['rk'], c['rv']
+    n_raw, n_lat = c['n_raw'], c['n_lat']
+    raw_cap = int(n_raw.max()) + extra_cap
+    lat_cap = int(n_lat.max()) + extra_cap
+    raw_k = np.zeros((B, raw_cap, Hkv, D), np.float32)
+    raw_v = np.zeros_like(raw_k)
+    lat_k = np.zeros((B, lat_cap, rk), np.float32)
+    lat_v = np.zeros((B, lat_cap, rv), np.float32)
+    new_k = np.zeros((B, Hkv * D), np.float32)
+    new_v = np.zeros_like(new_k)
+    new_lk = np.zeros((B, rk), np.float32)
+    new_lv = np.zeros((B, rv), np.float32)
+    for b in range(B):
+        r = int(n_raw[b]) - 1                        # row of the current token
+        raw_k[b, :r] = oracle.rope_bf16(c['raw_k'][b, :r], cos, sin, c['kpos'][b, :r, None])
+        raw_v[b, :r] = c['raw_v'][b, :r]
+        new_k[b] = c['raw_k'][b, r].reshape(-1)
+        new_v[b] = c['raw_v'][b, r].reshape(-1)
+        n = int(n_lat[b]) - (1 if query_len[b] == 2 else 0)
+        lat_k[b, :n] = c['lat_k'][b, :n]
+        lat_v[b, :n] = c['lat_v'][b, :n]
+        if query_len[b] == 2:
+            new_lk[b] = c['lat_k'][b, n]
+            new_lv[b] = c['lat_v'][b, n]
+    t = dict(q=to_bf16(c['q']), raw_k_rot=to_bf16(raw_k), raw_v=to_bf16(raw_v), lat_k=to_bf16(lat_k),
+             lat_v=to_bf16(lat_v), uk=to_bf16(c['uk']), uv=to_bf16(c['uv']), cos=cos_t, sin=sin_t,
+             raw_len=torch.tensor(n_raw, dtype=torch.int32, device='cuda'),
+             latent_len=torch.tensor(n_lat, dtype=torch.int32, device='cuda'),
+             query_len=torch.tensor(query_len, dtype=torch.int32, device='cuda'),
+             qpos=torch.tensor(c['qpos'], dtype=torch.int32, device='cuda'),
+             new_k=to_bf16(new_k), new_v=to_bf16(new_v), new_lat_k=to_bf16(new_lk), new_lat_v=to_bf16(new_lv),
+             out=torch.zeros(B, L, H * D, dtype=torch.bfloat16, device='cuda'))
+    if pre:
+        t['raw_k_pre'] = torch.zeros_like(t['raw_k_rot'])
+    if c['bk'] is not None:
+        t['uk_bias'], t['uv_bias'] = to_bf16(c['bk']), to_bf16(c['bv'])
+    kernels.latent_decode(**t)
+    torch.cuda.synchronize()
+    return t
+
+
+def oracle_rows(c, query_len):
+    """Per-row oracle results (each row with its own query length)."""
+    cos, sin, _, _ = tables()
+    outs = []
+    for b in range(c['q'].shape[0]):
+        L = int(query_len[b])
+        nr, nl = int(c['n_raw'][b]), int(c['n_lat'][b])
+        r = latent_decode_attention(c['q'][b:b + 1, :L], c['raw_k'][b:b + 1, :nr], c['raw_v'][b:b + 1, :nr],
+                                    c['lat_k'][b:b + 1, :nl], c['lat_v'][b:b + 1, :nl], c['uk'], c['uv'], cos, sin,
+                                    c['qpos'][b:b + 1, :L], c['kpos'][b:b + 1, :nr], L - 1,
+                                    uk_bias=c['bk'], uv_bias=c['bv'])
+        outs.append(r)
+    return outs
+
+
+def check(c, query_len, t):
+    refs = oracle_rows(c, query_len)
+    errs = []
+    for b, r in enumerate(refs):
+        L = int(query_len[b])
+        errs.append(assert_attention_close(t['out'][b:b + 1, :L], r['out']))
+        # Cache writes: rotated / pre-RoPE current key, value, new latents.
+        row = int(c['n_raw'][b]) - 1
+        assert_bits_equal(t['raw_k_rot'][b, row], r['k_rot'][0, row])
+        assert_bits_equal(t['raw_v'][b, row], c['raw_v'][b, row])
+        if 'raw_k_pre' in t:
+            assert_bits_equal(t['raw_k_pre'][b, row], c['raw_k'][b, row])
+        if L == 2:
+            n = int(c['n_lat'][b]) - 1
+            assert_bits_equal(t['lat_k'][b, n], c['lat_k'][b, n])
+            assert_bits_equal(t['lat_v'][b, n], c['lat_v'][b, n])
+    return max(errs)
+
+
+@pytest.mark.parametrize('length,history,tail,rank,bias,ragged', [
+    (1, 300, 37, 320, False, False),
+    (2, 300, 39, 320, False, False),
+    (1, 1024, 0, 320, False, False),
+    (2, 200, 3, 320, True, False),
+    (1, 513, 700, 160, False, True),
+    (2, 129, 1023, 320, False, True),
+    (1, 64, 5, 256, True, True),
+    (2, 2048, 511, 320, False, True),
+])
+def test_fused_decode_matches_oracle(length, history, tail, rank, bias, ragged):
+    c = decode_case(100 + history + tail, batch=3, length=length, history=history, tail=tail, rk=rank, rv=rank,
+                    bias=bias, ragged=ragged)
+    query_len = np.full(3, length)
+    check(c, query_len, run_fused(c, query_len))
+
+
+def test_mixed_query_lengths_in_one_batch():
+    """Only some rows insert a Beacon this step (per-row query_len)."""
+    c = decode_case(7, batch=4, length=2, history=400, tail=19)
+    query_len = np.array([2, 1, 2, 1])
+    c['n_lat'] = c['n_lat'] - (query_len == 1)           # rows without a Beacon have one latent fewer
+    check(c, query_len, run_fused(c, query_len))
+
+
+def test_distinct_key_and_value_ranks():
+    c = decode_case(9, batch=2, length=2, history=300, tail=11, rk=160, rv=192)
+    query_len = np.full(2, 2)
+    check(c, query_len, run_fused(c, query_len))
+
+
+def test_no_history_only_window_latents():
+    """First open window: no completed history, a handful of window latents."""
+    c = decode_case(11, batch=2, length=1, history=0, tail=12, sink=1)
+    query_len = np.full(2, 1)
+    check(c, query_len, run_fused(c, query_len))
+
+
+def test_rope_decode_is_bit_exact_against_reference_bits():
+    from slimkv_b200 import kernels
+    golden = np.load(Path(__file__).parent / 'golden' / 'reference_golden.npz')
+    cos, sin = oracle.rope_tables(128, LLAMA8B['theta'], LLAMA8B['max_positions'], LLAMA8B['scaling'])
+    cos_t, sin_t = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    q = torch.from_numpy(golden['rope_q_in']).cuda().view(torch.bfloat16)       # [2, 32, 2, 128]
+    k = torch.from_numpy(golden['rope_k_in']).cuda().view(torch.bfloat16)       # [2, 8, 70, 128]
+    pos = torch.from_numpy(golden['rope_pos']).cuda()                          # [2, 70]
+    # Express the reference's free positions through the decode contract:
+    # no sink, raw indices = positions[:-1] for row 0 (history 0).
+    qo, _ = kernels.rope_decode(q, k, cos_t, sin_t, pos[:, -2:].contiguous(), pos[0, :-1], 0, 0)
+    assert np.array_equal(qo.view(torch.int16).cpu().numpy(), golden['rope_q_out'])
+    _, ko = kernels.rope_decode(q[:1], k[:1], cos_t, sin_t, pos[:1, -1:].expand(1, 2).contiguous(), pos[0, :-1], 0, 0)
+    assert np.array_equal(ko.view(torch.int16).cpu().numpy(), golden['rope_k_out'][:1])
+
+
+def test_rope_decode_with_sinks_and_history_matches_oracle():
+    from slimkv_b200 import kernels
+    cos, sin, cos_t, sin_t = tables()
+    rng = np.random.default_rng(5)
+    B, H, Hkv, Q, K, S, hist = 2, 32, 8, 2, 51, 4, 384
+    q = oracle.round_bf16(rng.standard_normal((B, H, Q, 128), dtype=np.float32) * 2)
+    k = oracle.round_bf16(rng.standard_normal((B, Hkv, K, 128), dtype=np.float32) * 2)
+    raw_idx = np.arange(K - S - 1) * 2
+    first = hist + S + 2 * raw_idx.size
+    qpos = np.tile(np.arange(first, first + Q), (B, 1))
+    qo, ko = kernels.rope_decode(to_bf16(q), to_bf16(k), cos_t, sin_t, torch.from_numpy(qpos).cuda(),
+                                 torch.from_numpy(raw_idx).cuda(), S, hist)
+    kpos = oracle.raw_key_positions(S, raw_idx, hist, first)
+    assert_bits_equal(qo, oracle.rope_bf16(q, cos, sin, qpos[:, None, :]))
+    assert_bits_equal(ko, oracle.rope_bf16(k, cos, sin, np.tile(kpos, (B, 1))[:, None, :]))
+
+
+def test_merge_matches_oracle():
+    from slimkv_b200 import kernels
+    rng = np.random.default_rng(21)
+    raw = oracle.round_bf16(rng.standard_normal((2, 32, 2, 128), dtype=np.float32))
+    lat = oracle.round_bf16(rng.standard_normal((2, 32, 2, 128), dtype=np.float32))
+    rl = rng.standard_normal((2, 32, 2), dtype=np.float32) * 4
+    ll = rng.standard_normal((2, 32, 2), dtype=np.float32) * 4
+    ll[..., 0] = -np.inf
+    out = kernels.merge(to_bf16(raw), torch.from_numpy(rl).cuda(), to_bf16(lat), torch.from_numpy(ll).cuda())
+    ref = oracle.merge_attention(raw, rl, lat, ll)
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=1e-3, rtol=8e-3)
+    assert_bits_equal(out[:, :, 0], raw[:, :, 0])
