@@ -86,6 +86,7 @@ typedef struct {
     int causal;
     int num_splits;
     int lse_masked_positive;
+    int out_fp32;   /* 1: `out` is fp32 (the fp32-accumulated result, no bf16 cast) */
 } slimkv_attention_args;
 
 SLIMKV_API size_t slimkv_attention_workspace_size(const slimkv_attention_args* args);
@@ -147,8 +148,10 @@ typedef struct {
     const int32_t* qpos;
     const void* new_k;
     const void* new_v;
+    int64_t new_stride;       /* elements between batch rows of new_k/new_v (0 = Hkv*D) */
     const void* new_lat_k;
     const void* new_lat_v;
+    int64_t new_lat_stride;   /* elements between batch rows of new_lat_k/v (0 = R) */
     const void* uk;
     const void* uv;
     const void* uk_bias;
@@ -158,6 +161,7 @@ typedef struct {
     int rope_positions;
     void* out;
     int64_t out_stride[2];
+    int out_fp32;   /* 1: `out` is fp32 (the fp32-accumulated result, no bf16 cast) */
     /* Host-side upper bounds of latent_len / raw_len used to plan the split
      * counts (0 = the capacities).  Lengths above them are still handled. */
     int latent_len_max;
@@ -193,6 +197,24 @@ SLIMKV_API int slimkv_rope_decode(const void* q, const int64_t q_stride[3], cons
  * raw/latent [B, H, Q, D] bf16 (strides {batch, head, seq}), lse fp32
  * [B, H, Q] (strides {batch, head, seq}); out contiguous [B, H, Q, D] bf16.
  * ---------------------------------------------------------------------- */
+/* ------------------------------------------------------------------------
+ * Device-side decode schedule — the per-sequence form of the reference's
+ * fast decode bookkeeping `LlamaMemory._step` (slimkv/llama3/memory.py:
+ * 101-162) for an interleaved window of `window` raw tokens with one Beacon
+ * after every `ratio` raw tokens (slimkv/memory.py:491-567).  One thread per
+ * sequence reads its counters history[b] (completed-window latents) and
+ * tail[b] (raw tokens already in the open window, T), writes this step's
+ *   query_len[b]  = 1 + ((T + 1) % ratio == 0)        (Beacon inserted)
+ *   raw_len[b]    = sink + T + 1
+ *   latent_len[b] = history + T / ratio + (query_len - 1)
+ *   qpos[b][0..1] = sink + history + T + T / ratio (+1 for the Beacon)
+ * and advances T (closing the window, history += window / ratio, when
+ * T + 1 == window).  All arrays int32 on the device; qpos is [B, 2].
+ * ---------------------------------------------------------------------- */
+SLIMKV_API int slimkv_decode_schedule(int batch, int sink, int window, int ratio, int32_t* history,
+                                      int32_t* tail, int32_t* raw_len, int32_t* latent_len,
+                                      int32_t* query_len, int32_t* qpos, void* stream);
+
 SLIMKV_API int slimkv_merge(const void* raw, const int64_t raw_stride[3], const float* raw_lse,
                  const int64_t raw_lse_stride[3], const void* latent,
                  const int64_t latent_stride[3], const float* latent_lse,

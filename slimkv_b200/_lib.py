@@ -32,7 +32,7 @@ class AttentionArgs(ctypes.Structure):
         ('batch', ctypes.c_int), ('queries', ctypes.c_int), ('heads', ctypes.c_int),
         ('kv_heads', ctypes.c_int), ('keys', ctypes.c_int), ('head_dim', ctypes.c_int),
         ('value_dim', ctypes.c_int), ('scale', ctypes.c_float), ('causal', ctypes.c_int),
-        ('num_splits', ctypes.c_int), ('lse_masked_positive', ctypes.c_int),
+        ('num_splits', ctypes.c_int), ('lse_masked_positive', ctypes.c_int), ('out_fp32', ctypes.c_int),
     ]
 
 
@@ -50,12 +50,12 @@ class LatentDecodeArgs(ctypes.Structure):
         ('lat_capacity', ctypes.c_int),
         ('raw_len', ctypes.c_void_p), ('latent_len', ctypes.c_void_p),
         ('query_len', ctypes.c_void_p), ('qpos', ctypes.c_void_p),
-        ('new_k', ctypes.c_void_p), ('new_v', ctypes.c_void_p),
-        ('new_lat_k', ctypes.c_void_p), ('new_lat_v', ctypes.c_void_p),
+        ('new_k', ctypes.c_void_p), ('new_v', ctypes.c_void_p), ('new_stride', ctypes.c_int64),
+        ('new_lat_k', ctypes.c_void_p), ('new_lat_v', ctypes.c_void_p), ('new_lat_stride', ctypes.c_int64),
         ('uk', ctypes.c_void_p), ('uv', ctypes.c_void_p),
         ('uk_bias', ctypes.c_void_p), ('uv_bias', ctypes.c_void_p),
         ('cos', ctypes.c_void_p), ('sin', ctypes.c_void_p), ('rope_positions', ctypes.c_int),
-        ('out', ctypes.c_void_p), ('out_stride', I64x2),
+        ('out', ctypes.c_void_p), ('out_stride', I64x2), ('out_fp32', ctypes.c_int),
         ('latent_len_max', ctypes.c_int), ('raw_len_max', ctypes.c_int),
         ('latent_splits', ctypes.c_int), ('raw_splits', ctypes.c_int),
     ]
@@ -75,6 +75,7 @@ SIGNATURES = {
     'slimkv_latent_decode': (_I, [ctypes.POINTER(LatentDecodeArgs), _P, ctypes.c_size_t, _P]),
     'slimkv_rope_decode': (_I, [_P, ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _P, _P,
                                 _I, _P, ctypes.c_int64, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
+    'slimkv_decode_schedule': (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
     'slimkv_merge': (_I, [_P, ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _P,
                           ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I,
                           _I, _P, _P]),

@@ -28,7 +28,7 @@ attention_split_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_co
 __global__ void __launch_bounds__(256)
 attention_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse, int splits,
                          int rows_alloc, int width, int rows_total, int group, int kv_heads, int value_dim,
-                         __nv_bfloat16* __restrict__ out, int64_t o_sb, int64_t o_sl, int64_t o_sh,
+                         void* __restrict__ out, int out_fp32, int64_t o_sb, int64_t o_sl, int64_t o_sh,
                          float* __restrict__ lse_out, int heads, int queries, float masked_lse) {
     const int bg = blockIdx.x;
     const int b = bg / kv_heads, g = bg % kv_heads;
@@ -39,9 +39,13 @@ attention_combine_kernel(const float* __restrict__ part_o, const float* __restri
     float m = -INFINITY;
     for (int s = 0; s < splits; ++s) m = fmaxf(m, part_lse[base + (int64_t)s * rows_alloc]);
     const int l = row / group, h = g * group + (row - l * group);
-    __nv_bfloat16* dst = out + b * o_sb + l * o_sl + h * o_sh;
+    const int64_t off = b * o_sb + l * o_sl + h * o_sh;
+    auto store = [&](int d, float x) {
+        if (out_fp32) static_cast<float*>(out)[off + d] = x;
+        else static_cast<__nv_bfloat16*>(out)[off + d] = __float2bfloat16_rn(x);
+    };
     if (m == -INFINITY) {
-        for (int d = lane; d < value_dim; d += 32) dst[d] = __float2bfloat16_rn(0.f);
+        for (int d = lane; d < value_dim; d += 32) store(d, 0.f);
         if (lane == 0) lse_out[((int64_t)b * heads + h) * queries + l] = masked_lse;
         return;
     }
@@ -54,7 +58,7 @@ attention_combine_kernel(const float* __restrict__ part_o, const float* __restri
             const float w = expf(part_lse[base + (int64_t)s * rows_alloc] - m);
             acc += w * part_o[(base + (int64_t)s * rows_alloc) * width + d];
         }
-        dst[d] = __float2bfloat16_rn(acc * inv);
+        store(d, acc * inv);
     }
     if (lane == 0) lse_out[((int64_t)b * heads + h) * queries + l] = m + logf(total);
 }
@@ -91,8 +95,9 @@ int plan_attention(const slimkv_attention_args* a, Plan& p) {
     const int base = a->batch * a->kv_heads * p.row_blocks;
     int splits = a->num_splits;
     if (splits <= 0) {
+        // One resident CTA per SM (shared memory bound): fill one wave.
         const int sms = std::max(device_info().sm_count, 1);
-        splits = (sms + base - 1) / base;
+        splits = std::max(1, sms / base);
     }
     splits = std::max(1, std::min(splits, n_tiles));
     p.tiles_per_split = (n_tiles + splits - 1) / splits;
@@ -190,7 +195,8 @@ extern "C" int slimkv_attention_forward(const slimkv_attention_args* a, void* wo
     if ((rc = make_bshd_map(&km, a->k, a->batch, a->keys, a->kv_heads, a->head_dim, a->k_stride, &kb))) return rc;
     if ((rc = make_bshd_map(&vm, a->v, a->batch, a->keys, a->kv_heads, a->value_dim, a->v_stride, &vb))) return rc;
     AttnJob job{};
-    job.q = static_cast<const __nv_bfloat16*>(a->q);
+    job.q = a->q;
+    job.q_fp16 = 0;
     job.q_sb = a->q_stride[0];
     job.q_sl = a->q_stride[1];
     job.q_sh = a->q_stride[2];
@@ -219,7 +225,7 @@ extern "C" int slimkv_attention_forward(const slimkv_attention_args* a, void* wo
     dim3 cgrid(a->batch * a->kv_heads, (rows_total + 7) / 8);
     attention_combine_kernel<<<cgrid, 256, 0, stream>>>(
         part_o, part_lse, p.splits, p.rows_alloc, p.width, rows_total, job.group, a->kv_heads, a->value_dim,
-        static_cast<__nv_bfloat16*>(a->out), a->out_stride[0], a->out_stride[1], a->out_stride[2], a->lse,
+        a->out, a->out_fp32, a->out_stride[0], a->out_stride[1], a->out_stride[2], a->lse,
         a->heads, a->queries, a->lse_masked_positive ? INFINITY : -INFINITY);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "combine launch failed: %s", cudaGetErrorString(e));

@@ -6,10 +6,13 @@
 // r = l * group + j is query l of head g * group + j), and a contiguous range
 // of 64-key tiles.  K/V tiles stream HBM -> shared memory through TMA 4-D
 // tensor loads with the 128-byte swizzle (no cluster multicast) into a
-// STAGES-deep ring guarded by mbarriers.  Scores and P.V run on the bf16
-// tensor cores (m16n8k16, fp32 accumulate) with an online softmax in the
-// log2 domain; the CTA writes its normalised partial output and natural-log
-// LSE per row, which a combine kernel merges across splits.
+// STAGES-deep ring guarded by mbarriers.  Scores and P.V run on the tensor
+// cores (m16n8k16, fp32 accumulate) in fp16: bf16 K/V fragments are widened
+// to fp16 after ldmatrix (exact inside the fp16 range), so the absorbed
+// query and the probabilities keep 11 mantissa bits instead of bf16's 8.
+// The online softmax runs in the log2 domain; the CTA writes its normalised
+// partial output and natural-log LSE per row, which a combine kernel merges
+// across splits.
 //
 // Warp roles (8 warps): for Q.K^T warp w owns m-tile (w % MT) and the
 // w / MT-th slice of each tile's keys; for P.V warp w owns output columns
@@ -28,7 +31,8 @@ constexpr int kStageBudget = 160 * 1024;
 constexpr float kLn2 = 0.69314718055994530942f;
 
 struct AttnJob {
-    const __nv_bfloat16* q;        // [B, Q, H, D] (element strides below)
+    const void* q;                 // [B, Q, H, D] (element strides below)
+    int q_fp16;                    // 1: q holds fp16 values, 0: bf16
     int64_t q_sb, q_sl, q_sh;
     const CUtensorMap* kmap;       // 4-D map {D, Hkv, N, B} over K
     const CUtensorMap* vmap;       // 4-D map {Dv, Hkv, N, B} over V
@@ -80,8 +84,10 @@ __device__ __forceinline__ uint32_t load_q_pair(const AttnJob& J, int b, int g, 
     if (row >= rows_valid || col >= J.dk) return 0u;
     const int gr = row0 + row;
     const int l = gr / J.group, j = gr - l * J.group;
-    const __nv_bfloat16* p = J.q + b * J.q_sb + l * J.q_sl + (int64_t)(g * J.group + j) * J.q_sh + col;
-    return *reinterpret_cast<const uint32_t*>(p);
+    const uint16_t* p = static_cast<const uint16_t*>(J.q) + b * J.q_sb + l * J.q_sl +
+                        (int64_t)(g * J.group + j) * J.q_sh + col;
+    const uint32_t v = *reinterpret_cast<const uint32_t*>(p);
+    return J.q_fp16 ? v : bf16x2_to_f16x2(v);
 }
 
 // `rb` selects the block of ROWS query rows this CTA owns (row blocks let a
@@ -151,9 +157,13 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
             uint4 val = make_uint4(0, 0, 0, 0);
             if (row < rows_valid && u * 8 < J.dk) {
                 const int l = (row0 + row) / J.group, j = (row0 + row) - l * J.group;
-                const __nv_bfloat16* p =
-                    J.q + b * J.q_sb + l * J.q_sl + (int64_t)(g * J.group + j) * J.q_sh + u * 8;
+                const uint16_t* p = static_cast<const uint16_t*>(J.q) + b * J.q_sb + l * J.q_sl +
+                                    (int64_t)(g * J.group + j) * J.q_sh + u * 8;
                 val = *reinterpret_cast<const uint4*>(p);
+                if (!J.q_fp16) {
+                    val.x = bf16x2_to_f16x2(val.x); val.y = bf16x2_to_f16x2(val.y);
+                    val.z = bf16x2_to_f16x2(val.z); val.w = bf16x2_to_f16x2(val.w);
+                }
             }
             *reinterpret_cast<uint4*>(qs + (u >> 3) * (C::ROWS * 128) + sw128(row, (u & 7) * 8)) = val;
         }
@@ -213,8 +223,8 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
                     const int unit = u0 + (mi & 1);
                     uint32_t b0, b1, b2, b3;
                     ldsm_x4(chunk + key * 128 + (((unit ^ key) & 7) << 4), b0, b1, b2, b3);
-                    mma_bf16(sc[nt], a, b0, b1);
-                    mma_bf16(sc[nt + 1], a, b2, b3);
+                    mma_f16(sc[nt], a, bf16x2_to_f16x2(b0), bf16x2_to_f16x2(b1));
+                    mma_f16(sc[nt + 1], a, bf16x2_to_f16x2(b2), bf16x2_to_f16x2(b3));
                 }
             } else {
                 const int mi = (lane >> 3) & 1;
@@ -222,7 +232,7 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
                 const int unit = u0 + mi;
                 uint32_t b0, b1;
                 ldsm_x2(chunk + key * 128 + (((unit ^ key) & 7) << 4), b0, b1);
-                mma_bf16(sc[0], a, b0, b1);
+                mma_f16(sc[0], a, bf16x2_to_f16x2(b0), bf16x2_to_f16x2(b1));
             }
         }
         // ---- scale, mask, per-warp row maxima ----
@@ -263,11 +273,11 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
             float sum = 0.f;
 #pragma unroll
             for (int nt = 0; nt < C::NTQ; ++nt) {
-                const float p0 = mn == -INFINITY ? 0.f : bf16_round(fast_exp2(sc[nt][2 * hh] - mn));
-                const float p1 = mn == -INFINITY ? 0.f : bf16_round(fast_exp2(sc[nt][2 * hh + 1] - mn));
+                const float p0 = mn == -INFINITY ? 0.f : f16_round(fast_exp2(sc[nt][2 * hh] - mn));
+                const float p1 = mn == -INFINITY ? 0.f : f16_round(fast_exp2(sc[nt][2 * hh + 1] - mn));
                 sum += p0 + p1;
                 const int col = kbase + nt * 8 + (lane & 3) * 2;
-                *reinterpret_cast<uint32_t*>(ps + sw128(row, col)) = pack_bf16x2(p0, p1);
+                *reinterpret_cast<uint32_t*>(ps + sw128(row, col)) = pack_f16x2(p0, p1);
             }
             l_qk[hh] = l_qk[hh] * alpha + sum;
             m_qk[hh] = mn;
@@ -312,10 +322,12 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
                 const int unit = (dim & 63) >> 3;
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4_t(vt + (dim >> 6) * (kTile * 128) + key * 128 + (((unit ^ key) & 7) << 4), b0, b1, b2, b3);
+                b0 = bf16x2_to_f16x2(b0); b1 = bf16x2_to_f16x2(b1);
+                b2 = bf16x2_to_f16x2(b2); b3 = bf16x2_to_f16x2(b3);
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
-                    mma_bf16(o[mt][nt], a[mt], b0, b1);
-                    mma_bf16(o[mt][nt + 1], a[mt], b2, b3);
+                    mma_f16(o[mt][nt], a[mt], b0, b1);
+                    mma_f16(o[mt][nt + 1], a[mt], b2, b3);
                 }
             }
             if constexpr (C::NTV % 2) {
@@ -326,8 +338,9 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
                 const int unit = (dim & 63) >> 3;
                 uint32_t b0, b1;
                 ldsm_x2_t(vt + (dim >> 6) * (kTile * 128) + key * 128 + (((unit ^ key) & 7) << 4), b0, b1);
+                b0 = bf16x2_to_f16x2(b0); b1 = bf16x2_to_f16x2(b1);
 #pragma unroll
-                for (int mt = 0; mt < MT; ++mt) mma_bf16(o[mt][nt], a[mt], b0, b1);
+                for (int mt = 0; mt < MT; ++mt) mma_f16(o[mt][nt], a[mt], b0, b1);
             }
         }
     }

@@ -17,131 +17,12 @@
 
 #include "attn_body.cuh"
 #include "host_utils.h"
+#include "latent_decode_aux.cuh"
 
 namespace slimkv {
 
 int make_bshd_map(CUtensorMap* map, const void* base, int batch, int keys, int kv_heads, int dim,
                   const int64_t stride[3], int* bcast);
-
-struct PrologueArgs {
-    const __nv_bfloat16* q;
-    int64_t q_sb, q_sl, q_sh;
-    int length, heads, kv_heads, dim, rank_k, rank_v, width, group;
-    const int32_t* qpos;
-    const int32_t* qlens;
-    const float* cos;
-    const float* sin;
-    int rope_positions;
-    const __nv_bfloat16* uk;
-    __nv_bfloat16* q_rot;   // [B, L, H, D]
-    __nv_bfloat16* q_lat;   // [B, L, H, width]
-    const __nv_bfloat16* new_k;
-    const __nv_bfloat16* new_v;
-    __nv_bfloat16* raw_k_rot;
-    __nv_bfloat16* raw_v;
-    __nv_bfloat16* raw_k_pre;
-    int64_t raw_sb, raw_st;
-    const int32_t* raw_len;
-    int raw_capacity;
-    const __nv_bfloat16* new_lat_k;
-    const __nv_bfloat16* new_lat_v;
-    __nv_bfloat16* lat_k;
-    __nv_bfloat16* lat_v;
-    int64_t lat_sb, lat_sr;
-    const int32_t* latent_len;
-    int lat_capacity;
-    unsigned int* status;
-};
-
-// out = bf16(bf16(x * bf16(cos)) + bf16(rotate_half(x) * bf16(sin))), the
-// reference's per-operation BF16 rounding (decode_kernels.py:40-51).
-__device__ __forceinline__ float rope_one(float x, float partner, int d, int half, float c, float s) {
-    const float rot = d < half ? -partner : partner;
-    const float cb = bf16_round(c), sb = bf16_round(s);
-    const float first = bf16_round(__fmul_rn(x, cb));
-    const float second = bf16_round(__fmul_rn(rot, sb));
-    return bf16_round(__fadd_rn(first, second));
-}
-
-constexpr int kMaxRows = 16;   // query rows per KV head handled by prologue/merge
-
-__global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
-    extern __shared__ float qs[];                      // [rows][dim]
-    const int g = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
-    const int qlen = a.qlens ? a.qlens[b] : a.length;
-    const int rows = qlen * a.group;
-    const int half = a.dim / 2;
-    // ---- RoPE of this KV head's query rows ----
-    for (int idx = tid; idx < rows * a.dim; idx += blockDim.x) {
-        const int r = idx / a.dim, d = idx - r * a.dim;
-        const int l = r / a.group, h = g * a.group + (r - l * a.group);
-        int pos = a.qpos[b * a.length + l];
-        if (pos < 0 || pos >= a.rope_positions) {
-            report(a.status, SLIMKV_DEVICE_BAD_LENGTH);
-            pos = 0;
-        }
-        const __nv_bfloat16* src = a.q + b * a.q_sb + l * a.q_sl + h * a.q_sh;
-        const float v = rope_one(__bfloat162float(src[d]), __bfloat162float(src[(d + half) % a.dim]), d, half,
-                                 a.cos[(int64_t)pos * a.dim + d], a.sin[(int64_t)pos * a.dim + d]);
-        a.q_rot[(((int64_t)b * a.length + l) * a.heads + h) * a.dim + d] = __float2bfloat16_rn(v);
-        qs[r * a.dim + d] = v;
-    }
-    __syncthreads();
-    // ---- q-absorb: q_lat[r, c] = sum_d q_rot[r, d] * U_k[g*D + d, c] ----
-    for (int c = tid; c < a.width; c += blockDim.x) {
-        float acc[kMaxRows];
-#pragma unroll
-        for (int r = 0; r < kMaxRows; ++r) acc[r] = 0.f;
-        if (c < a.rank_k) {
-            const __nv_bfloat16* u = a.uk + (int64_t)g * a.dim * a.rank_k + c;
-            for (int d = 0; d < a.dim; ++d) {
-                const float w = __bfloat162float(u[(int64_t)d * a.rank_k]);
-#pragma unroll
-                for (int r = 0; r < kMaxRows; ++r)
-                    if (r < rows) acc[r] = fmaf(qs[r * a.dim + d], w, acc[r]);
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < kMaxRows; ++r) {
-            if (r >= rows) break;
-            const int l = r / a.group, h = g * a.group + (r - l * a.group);
-            a.q_lat[(((int64_t)b * a.length + l) * a.heads + h) * a.width + c] = __float2bfloat16_rn(acc[r]);
-        }
-    }
-    // ---- append the new raw token of this KV head ----
-    if (a.new_k) {
-        const int row = a.raw_len[b] - 1;
-        if (row < 0 || row >= a.raw_capacity) {
-            if (tid == 0) report(a.status, SLIMKV_DEVICE_BAD_LENGTH);
-        } else {
-            int pos = a.qpos[b * a.length];
-            if (pos < 0 || pos >= a.rope_positions) pos = 0;
-            const __nv_bfloat16* k = a.new_k + ((int64_t)b * a.kv_heads + g) * a.dim;
-            const __nv_bfloat16* v = a.new_v + ((int64_t)b * a.kv_heads + g) * a.dim;
-            const int64_t dst = b * a.raw_sb + row * a.raw_st + (int64_t)g * a.dim;
-            for (int d = tid; d < a.dim; d += blockDim.x) {
-                const float x = __bfloat162float(k[d]);
-                const float rv = rope_one(x, __bfloat162float(k[(d + half) % a.dim]), d, half,
-                                          a.cos[(int64_t)pos * a.dim + d], a.sin[(int64_t)pos * a.dim + d]);
-                a.raw_k_rot[dst + d] = __float2bfloat16_rn(rv);
-                a.raw_v[dst + d] = v[d];
-                if (a.raw_k_pre) a.raw_k_pre[dst + d] = k[d];
-            }
-        }
-    }
-    // ---- append the Beacon latent pair inserted by this row ----
-    if (g == 0 && a.new_lat_k && qlen == 2) {
-        const int row = a.latent_len[b] - 1;
-        if (row < 0 || row >= a.lat_capacity) {
-            if (tid == 0) report(a.status, SLIMKV_DEVICE_BAD_LENGTH);
-        } else {
-            for (int c = tid; c < a.rank_k; c += blockDim.x)
-                a.lat_k[b * a.lat_sb + row * a.lat_sr + c] = a.new_lat_k[(int64_t)b * a.rank_k + c];
-            for (int c = tid; c < a.rank_v; c += blockDim.x)
-                a.lat_v[b * a.lat_sb + row * a.lat_sr + c] = a.new_lat_v[(int64_t)b * a.rank_v + c];
-        }
-    }
-}
 
 // One launch: CTAs [0, n_latent) take latent work items, the rest raw ones.
 template <int WL, int MTL>
@@ -170,115 +51,11 @@ decode_attention_kernel(const __grid_constant__ CUtensorMap lk, const __grid_con
     }
 }
 
-struct MergeArgs {
-    const float* lat_o; const float* lat_lse; int lat_splits, lat_rows, lat_width;
-    const float* raw_o; const float* raw_lse; int raw_splits, raw_rows;
-    const __nv_bfloat16* q_rot;
-    const __nv_bfloat16* uv; const __nv_bfloat16* uk_bias; const __nv_bfloat16* uv_bias;
-    const int32_t* qlens;
-    int length, heads, kv_heads, dim, rank_v, group;
-    float scale;
-    __nv_bfloat16* out; int64_t o_sb, o_sl;
-};
-
-// Combine `splits` normalised partials of one row into dst[0..width).
-__device__ void combine_row(const float* o, const float* lse, int splits, int64_t row_pitch, int width,
-                            int lane, float* dst, float* lse_dst) {
-    float m = -INFINITY;
-    for (int s = lane; s < splits; s += 32) m = fmaxf(m, lse[s * row_pitch]);
-#pragma unroll
-    for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    float total = 0.f;
-    if (m != -INFINITY)
-        for (int s = lane; s < splits; s += 32) total += expf(lse[s * row_pitch] - m);
-#pragma unroll
-    for (int off = 16; off; off >>= 1) total += __shfl_xor_sync(0xffffffffu, total, off);
-    const float inv = total > 0.f ? 1.f / total : 0.f;
-    for (int c = lane; c < width; c += 32) {
-        float acc = 0.f;
-        if (m != -INFINITY)
-            for (int s = 0; s < splits; ++s)
-                acc += expf(lse[s * row_pitch] - m) * o[s * row_pitch * width + c];
-        dst[c] = acc * inv;
-    }
-    if (lane == 0) *lse_dst = m == -INFINITY ? -INFINITY : m + logf(total);
-}
-
-__global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
-    extern __shared__ float sm[];
-    const int g = blockIdx.x, b = blockIdx.y;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-    const int qlen = a.qlens ? a.qlens[b] : a.length;
-    const int rows = qlen * a.group;
-    float* olat = sm;                                   // [kMaxRows][lat_width]
-    float* oraw = olat + kMaxRows * a.lat_width;        // [kMaxRows][dim]
-    float* llat = oraw + kMaxRows * a.dim;              // [kMaxRows]
-    float* lraw = llat + kMaxRows;
-    for (int r = warp; r < rows; r += 8) {
-        const int l = r / a.group, h = g * a.group + (r - l * a.group);
-        const int rl = l * a.heads + h;                 // row in the latent job
-        const int64_t lat_base = (int64_t)b * a.lat_splits * a.lat_rows + rl;
-        combine_row(a.lat_o + lat_base * a.lat_width, a.lat_lse + lat_base, a.lat_splits, a.lat_rows,
-                    a.lat_width, lane, olat + r * a.lat_width, llat + r);
-        const int64_t raw_base = ((int64_t)(b * a.kv_heads + g) * a.raw_splits) * a.raw_rows + r;
-        combine_row(a.raw_o + raw_base * a.dim, a.raw_lse + raw_base, a.raw_splits, a.raw_rows, a.dim, lane,
-                    oraw + r * a.dim, lraw + r);
-        if (a.uk_bias) {
-            // Latent LSE shift by scale * q . b_k (fa2_decode.py:157-160).
-            const __nv_bfloat16* q = a.q_rot + (((int64_t)b * a.length + l) * a.heads + h) * a.dim;
-            const __nv_bfloat16* bk = a.uk_bias + (int64_t)g * a.dim;
-            float dot = 0.f;
-            for (int d = lane; d < a.dim; d += 32) dot += __bfloat162float(q[d]) * __bfloat162float(bk[d]);
-#pragma unroll
-            for (int off = 16; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-            __syncwarp();
-            if (lane == 0 && llat[r] != -INFINITY) llat[r] += dot * a.scale;
-        }
-    }
-    __syncthreads();
-    // ---- V up-projection, bias and LSE merge: thread owns column d ----
-    for (int d = tid; d < a.dim; d += blockDim.x) {
-        float acc[kMaxRows];
-#pragma unroll
-        for (int r = 0; r < kMaxRows; ++r) acc[r] = 0.f;
-        const __nv_bfloat16* u = a.uv + ((int64_t)g * a.dim + d) * a.rank_v;
-        for (int c = 0; c < a.rank_v; c += 8) {
-            const uint4 pk = *reinterpret_cast<const uint4*>(u + c);
-            const __nv_bfloat16* w8 = reinterpret_cast<const __nv_bfloat16*>(&pk);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float w = __bfloat162float(w8[e]);
-#pragma unroll
-                for (int r = 0; r < kMaxRows; ++r)
-                    if (r < rows) acc[r] = fmaf(olat[r * a.lat_width + c + e], w, acc[r]);
-            }
-        }
-        const float bv = a.uv_bias ? __bfloat162float(a.uv_bias[(int64_t)g * a.dim + d]) : 0.f;
-#pragma unroll
-        for (int r = 0; r < kMaxRows; ++r) {
-            if (r >= rows) break;
-            const int l = r / a.group, h = g * a.group + (r - l * a.group);
-            const float lr = lraw[r], ll = llat[r];
-            float value;
-            if (lr == -INFINITY && ll == -INFINITY) {
-                value = 0.f;
-            } else {
-                const float mx = fmaxf(lr, ll);
-                const float total = mx + log1pf(expf(-fabsf(lr - ll)));
-                const float wr = lr == -INFINITY ? 0.f : expf(lr - total);
-                const float wl = ll == -INFINITY ? 0.f : expf(ll - total);
-                value = wr * oraw[r * a.dim + d] + wl * (acc[r] + bv);
-            }
-            a.out[b * a.o_sb + l * a.o_sl + (int64_t)h * a.dim + d] = __float2bfloat16_rn(value);
-        }
-    }
-}
-
 namespace {
 
 struct DecodePlan {
     int wl = 0, mtl = 0, lat_row_blocks = 0, lat_rows = 0, lat_splits = 0, lat_tps = 0;
-    int raw_rows = 0, raw_splits = 0, raw_tps = 0, group = 0;
+    int raw_rows = 0, raw_splits = 0, raw_tps = 0, group = 0, rvp = 0;
     size_t q_rot = 0, q_lat = 0, lat_o = 0, lat_lse = 0, raw_o = 0, raw_lse = 0;
 };
 
@@ -296,6 +73,7 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
         return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "at most %d query rows per KV head", kMaxRows);
     p.wl = (std::max(a->rank_k, a->rank_v) + 63) / 64 * 64;
     p.wl = std::max(p.wl, 128);
+    p.rvp = (a->rank_v + 63) / 64 * 64;
     const int lat_rows = a->heads * a->length;
     p.mtl = lat_rows <= 32 ? 2 : 4;
     p.lat_row_blocks = (lat_rows + 16 * p.mtl - 1) / (16 * p.mtl);
@@ -331,14 +109,15 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
 }
 
 struct Buffers {
-    __nv_bfloat16 *q_rot, *q_lat;
+    __nv_bfloat16* q_rot;
+    __half* q_lat;
     float *lat_o, *lat_lse, *raw_o, *raw_lse;
 };
 
 Buffers carve(Carver& c, const DecodePlan& p) {
     Buffers w;
     w.q_rot = c.take<__nv_bfloat16>(p.q_rot);
-    w.q_lat = c.take<__nv_bfloat16>(p.q_lat);
+    w.q_lat = c.take<__half>(p.q_lat);
     w.lat_o = c.take<float>(p.lat_o);
     w.lat_lse = c.take<float>(p.lat_lse);
     w.raw_o = c.take<float>(p.raw_o);
@@ -409,17 +188,25 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     unsigned int* status = status_word();
 
     // 1. prologue
+    if (!aligned16(a->uk) || !aligned16(a->q) || a->q_stride[0] % 8 || a->q_stride[1] % 8 || a->q_stride[2] % 8)
+        return fail(SLIMKV_ERR_ALIGNMENT, "q and U_k must be 16-byte aligned with strides that are multiples of 8");
+    if ((a->new_k && (a->new_stride % 8 || !aligned16(a->new_k) || !aligned16(a->new_v))) ||
+        (a->new_lat_k && (a->new_lat_stride % 8 || !aligned16(a->new_lat_k) || !aligned16(a->new_lat_v))))
+        return fail(SLIMKV_ERR_ALIGNMENT, "new rows must be 16-byte aligned with strides that are multiples of 8");
+    const int rps = a->length * p.group;
     PrologueArgs pa{};
     pa.q = static_cast<const __nv_bfloat16*>(a->q);
     pa.q_sb = a->q_stride[0]; pa.q_sl = a->q_stride[1]; pa.q_sh = a->q_stride[2];
-    pa.length = a->length; pa.heads = a->heads; pa.kv_heads = a->kv_heads; pa.dim = a->head_dim;
-    pa.rank_k = a->rank_k; pa.rank_v = a->rank_v; pa.width = p.wl; pa.group = p.group;
+    pa.batch = a->batch; pa.length = a->length; pa.heads = a->heads; pa.kv_heads = a->kv_heads;
+    pa.dim = a->head_dim; pa.rank_k = a->rank_k; pa.rank_v = a->rank_v; pa.width = p.wl; pa.group = p.group;
+    pa.seq_per_cta = kProRows / rps;
     pa.qpos = a->qpos; pa.qlens = a->query_len; pa.cos = a->cos; pa.sin = a->sin;
     pa.rope_positions = a->rope_positions;
     pa.uk = static_cast<const __nv_bfloat16*>(a->uk);
     pa.q_rot = w.q_rot; pa.q_lat = w.q_lat;
     pa.new_k = static_cast<const __nv_bfloat16*>(a->new_k);
     pa.new_v = static_cast<const __nv_bfloat16*>(a->new_v);
+    pa.new_stride = a->new_stride > 0 ? a->new_stride : (int64_t)a->kv_heads * a->head_dim;
     pa.raw_k_rot = static_cast<__nv_bfloat16*>(a->raw_k_rot);
     pa.raw_v = static_cast<__nv_bfloat16*>(a->raw_v);
     pa.raw_k_pre = static_cast<__nv_bfloat16*>(a->raw_k_pre);
@@ -427,13 +214,16 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     pa.raw_len = a->raw_len; pa.raw_capacity = a->raw_capacity;
     pa.new_lat_k = static_cast<const __nv_bfloat16*>(a->new_lat_k);
     pa.new_lat_v = static_cast<const __nv_bfloat16*>(a->new_lat_v);
+    if (a->new_lat_k && a->new_lat_stride <= 0 && a->rank_k != a->rank_v)
+        return fail(SLIMKV_ERR_INVALID_ARGUMENT, "new_lat_stride is required when the ranks differ");
+    pa.new_lat_stride = a->new_lat_stride > 0 ? a->new_lat_stride : a->rank_k;
     pa.lat_k = static_cast<__nv_bfloat16*>(a->lat_k);
     pa.lat_v = static_cast<__nv_bfloat16*>(a->lat_v);
     pa.lat_sb = a->lat_stride_batch; pa.lat_sr = a->lat_stride_row;
     pa.latent_len = a->latent_len; pa.lat_capacity = a->lat_capacity;
     pa.status = status;
-    const size_t psmem = size_t(kMaxRows) * a->head_dim * sizeof(float);
-    decode_prologue_kernel<<<dim3(a->kv_heads, a->batch), 256, psmem, stream>>>(pa);
+    const dim3 pgrid(a->kv_heads, p.wl / 64, (a->batch + pa.seq_per_cta - 1) / pa.seq_per_cta);
+    decode_prologue_kernel<<<pgrid, 256, 0, stream>>>(pa);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "prologue launch failed: %s", cudaGetErrorString(e));
 
@@ -450,13 +240,13 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         return rc;
     const float scale_log2 = a->scale * 1.4426950408889634f;
     AttnJob jl{};
-    jl.q = w.q_lat; jl.q_sb = (int64_t)a->length * a->heads * p.wl; jl.q_sl = (int64_t)a->heads * p.wl; jl.q_sh = p.wl;
+    jl.q = w.q_lat; jl.q_fp16 = 1; jl.q_sb = (int64_t)a->length * a->heads * p.wl; jl.q_sl = (int64_t)a->heads * p.wl; jl.q_sh = p.wl;
     jl.seqlens = a->latent_len; jl.keys = a->lat_capacity; jl.qlens = a->query_len; jl.queries = a->length;
     jl.group = a->heads; jl.kv_heads = 1; jl.dk = a->rank_k; jl.scale_log2 = scale_log2; jl.causal = 1;
     jl.splits = p.lat_splits; jl.tiles_per_split = p.lat_tps; jl.rows_alloc = p.lat_rows; jl.out_width = p.wl;
     jl.part_o = w.lat_o; jl.part_lse = w.lat_lse; jl.status = status;
     AttnJob jr{};
-    jr.q = w.q_rot; jr.q_sb = (int64_t)a->length * a->heads * a->head_dim; jr.q_sl = (int64_t)a->heads * a->head_dim;
+    jr.q = w.q_rot; jr.q_fp16 = 0; jr.q_sb = (int64_t)a->length * a->heads * a->head_dim; jr.q_sl = (int64_t)a->heads * a->head_dim;
     jr.q_sh = a->head_dim;
     jr.seqlens = a->raw_len; jr.keys = a->raw_capacity; jr.qlens = a->query_len; jr.queries = a->length;
     jr.group = p.group; jr.kv_heads = a->kv_heads; jr.dk = a->head_dim; jr.scale_log2 = scale_log2; jr.causal = 0;
@@ -481,11 +271,23 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     ma.uv = static_cast<const __nv_bfloat16*>(a->uv);
     ma.uk_bias = static_cast<const __nv_bfloat16*>(a->uk_bias);
     ma.uv_bias = static_cast<const __nv_bfloat16*>(a->uv_bias);
-    ma.qlens = a->query_len; ma.length = a->length; ma.heads = a->heads; ma.kv_heads = a->kv_heads;
-    ma.dim = a->head_dim; ma.rank_v = a->rank_v; ma.group = p.group; ma.scale = a->scale;
-    ma.out = static_cast<__nv_bfloat16*>(a->out); ma.o_sb = a->out_stride[0]; ma.o_sl = a->out_stride[1];
-    const size_t msmem = (size_t(kMaxRows) * (p.wl + a->head_dim) + 2 * kMaxRows) * sizeof(float);
-    decode_merge_kernel<<<dim3(a->kv_heads, a->batch), 256, msmem, stream>>>(ma);
+    ma.qlens = a->query_len; ma.batch = a->batch; ma.length = a->length; ma.heads = a->heads;
+    ma.kv_heads = a->kv_heads; ma.dim = a->head_dim; ma.rank_v = a->rank_v; ma.rank_v_pad = p.rvp;
+    ma.group = p.group; ma.seq_per_cta = kMaxRows / rps; ma.scale = a->scale;
+    ma.out = a->out; ma.out_fp32 = a->out_fp32; ma.o_sb = a->out_stride[0]; ma.o_sl = a->out_stride[1];
+    const size_t msmem = 1024 + size_t(128 + 16) * p.rvp * 2 + size_t(16) * a->head_dim * 4 + 32 * 4;
+    {
+        static bool configured[64] = {};
+        const int dev = device_info().device;
+        if (dev >= 0 && dev < 64 && !configured[dev]) {
+            if (cudaFuncSetAttribute(decode_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     int(1024 + 144 * 320 * 2 + 16 * 128 * 4 + 128)) != cudaSuccess)
+                return fail(SLIMKV_ERR_CUDA, "cudaFuncSetAttribute failed");
+            configured[dev] = true;
+        }
+    }
+    const dim3 mgrid(a->kv_heads, (a->batch + ma.seq_per_cta - 1) / ma.seq_per_cta);
+    decode_merge_kernel<<<mgrid, 256, msmem, stream>>>(ma);
     e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "merge launch failed: %s", cudaGetErrorString(e));
     return SLIMKV_OK;

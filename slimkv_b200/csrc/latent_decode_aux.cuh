@@ -1,0 +1,372 @@
+// Prologue and merge kernels of the fused latent decode step.
+//
+// Both are small tensor-core GEMMs around the attention kernel:
+//   prologue: q_lat[r, :] = rope(q)[r, :] . U_k[g]      (fa2_decode.py:41-46)
+//   merge:    out[r, :]   = o_lat[r, :] . U_v[g]^T      (fa2_decode.py:49-54)
+// Operands are staged in shared memory with vector loads issued in parallel
+// (the loops carry no load->use dependency chains) and multiplied with
+// m16n8k16 fp16 MMAs (bf16 weights widen to fp16 exactly), fp32 accumulate.
+#pragma once
+
+#include "common.cuh"
+
+namespace slimkv {
+
+constexpr int kMaxRows = 16;      // query rows per KV head (group * length)
+constexpr int kProRows = 64;      // query rows per prologue CTA (four m-tiles)
+
+struct PrologueArgs {
+    const __nv_bfloat16* q;
+    int64_t q_sb, q_sl, q_sh;
+    int batch, length, heads, kv_heads, dim, rank_k, rank_v, width, group, seq_per_cta;
+    const int32_t* qpos;
+    const int32_t* qlens;
+    const float* cos;
+    const float* sin;
+    int rope_positions;
+    const __nv_bfloat16* uk;
+    __nv_bfloat16* q_rot;   // [B, L, H, D]
+    __half* q_lat;          // [B, L, H, width]
+    const __nv_bfloat16* new_k;
+    const __nv_bfloat16* new_v;
+    int64_t new_stride;
+    __nv_bfloat16* raw_k_rot;
+    __nv_bfloat16* raw_v;
+    __nv_bfloat16* raw_k_pre;
+    int64_t raw_sb, raw_st;
+    const int32_t* raw_len;
+    int raw_capacity;
+    const __nv_bfloat16* new_lat_k;
+    const __nv_bfloat16* new_lat_v;
+    int64_t new_lat_stride;
+    __nv_bfloat16* lat_k;
+    __nv_bfloat16* lat_v;
+    int64_t lat_sb, lat_sr;
+    const int32_t* latent_len;
+    int lat_capacity;
+    unsigned int* status;
+};
+
+__device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// Rotate dims [d0, d0+8) of one head row with the reference's BF16 rounding:
+// out = bf16(bf16(x*bf16(cos)) + bf16(rotate_half(x)*bf16(sin)))
+// (slimkv/llama3/decode_kernels.py:40-51).  `half` is dim/2, a multiple of 8.
+__device__ __forceinline__ void rope8(const __nv_bfloat16* row, int d0, int half, const float* cos_row,
+                                      const float* sin_row, float out[8]) {
+    const int pd = d0 < half ? d0 + half : d0 - half;
+    const uint4 xv = *reinterpret_cast<const uint4*>(row + d0);
+    const uint4 pv = *reinterpret_cast<const uint4*>(row + pd);
+    const float4 c0 = *reinterpret_cast<const float4*>(cos_row + d0);
+    const float4 c1 = *reinterpret_cast<const float4*>(cos_row + d0 + 4);
+    const float4 s0 = *reinterpret_cast<const float4*>(sin_row + d0);
+    const float4 s1 = *reinterpret_cast<const float4*>(sin_row + d0 + 4);
+    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, pw[4] = {pv.x, pv.y, pv.z, pv.w};
+    const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const float sign = d0 < half ? -1.f : 1.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const float x = (e & 1) ? bf16_hi(xw[e >> 1]) : bf16_lo(xw[e >> 1]);
+        const float p = (e & 1) ? bf16_hi(pw[e >> 1]) : bf16_lo(pw[e >> 1]);
+        const float first = bf16_round(__fmul_rn(x, bf16_round(cs[e])));
+        const float second = bf16_round(__fmul_rn(sign * p, bf16_round(sn[e])));
+        out[e] = bf16_round(__fadd_rn(first, second));
+    }
+}
+
+__device__ __forceinline__ uint4 pack8_bf16(const float v[8]) {
+    return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                      pack_bf16x2(v[6], v[7]));
+}
+__device__ __forceinline__ uint4 pack8_f16(const float v[8]) {
+    return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
+                      pack_f16x2(v[6], v[7]));
+}
+__device__ __forceinline__ uint4 widen8(uint4 v) {
+    return make_uint4(bf16x2_to_f16x2(v.x), bf16x2_to_f16x2(v.y), bf16x2_to_f16x2(v.z), bf16x2_to_f16x2(v.w));
+}
+
+// grid (Hkv, width / 64, ceil(B / seq_per_cta)), 256 threads.  CTA (g, cc, bb)
+// absorbs the 64 query rows of KV head g for sequences [bb*spc, (bb+1)*spc)
+// into latent columns [cc*64, cc*64 + 64); the cc == 0 CTAs also write q_rot
+// and append this step's raw token (and, for g == 0, the Beacon latents).
+__global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
+    __shared__ __align__(1024) uint8_t s_a[kProRows * 128 * 2];   // rope(q): 2 chunks [64 x 64] fp16
+    __shared__ __align__(1024) uint8_t s_b[128 * 64 * 2];         // U_k[g][:, cc*64 : +64] fp16
+    const int g = blockIdx.x, cc = blockIdx.y, bb = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rps = a.length * a.group;                 // rows per sequence
+    const int b0 = bb * a.seq_per_cta;
+    const int half = a.dim / 2;
+
+    // 1. U_k column chunk -> shared (fp16).
+#pragma unroll
+    for (int i = tid; i < 128 * 8; i += 256) {
+        const int d = i >> 3, u = i & 7, col = cc * 64 + u * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (col < a.rank_k) v = widen8(*reinterpret_cast<const uint4*>(a.uk + ((int64_t)g * a.dim + d) * a.rank_k + col));
+        *reinterpret_cast<uint4*>(s_b + sw128(d, u * 8)) = v;
+    }
+    // 2. RoPE of the CTA's query rows -> shared (fp16, exact copies of bf16).
+#pragma unroll
+    for (int i = tid; i < kProRows * 16; i += 256) {
+        const int r = i >> 4, d0 = (i & 15) * 8;
+        const int s = r / rps, rr = r - s * rps, l = rr / a.group, j = rr - l * a.group;
+        const int b = b0 + s, h = g * a.group + j;
+        float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (s < a.seq_per_cta && b < a.batch && l < (a.qlens ? a.qlens[b] : a.length)) {
+            int pos = a.qpos[b * a.length + l];
+            if (pos < 0 || pos >= a.rope_positions) {
+                report(a.status, SLIMKV_DEVICE_BAD_LENGTH);
+                pos = 0;
+            }
+            rope8(a.q + b * a.q_sb + l * a.q_sl + h * a.q_sh, d0, half, a.cos + (int64_t)pos * a.dim,
+                  a.sin + (int64_t)pos * a.dim, o);
+            if (cc == 0)
+                *reinterpret_cast<uint4*>(a.q_rot + (((int64_t)b * a.length + l) * a.heads + h) * a.dim + d0) =
+                    pack8_bf16(o);
+        }
+        *reinterpret_cast<uint4*>(s_a + (d0 >> 6) * (kProRows * 128) + sw128(r, d0 & 63)) = pack8_f16(o);
+    }
+    __syncthreads();
+    // 3. [64 x 128] . [128 x 64] on the tensor cores: warp -> m-tile (warp & 3),
+    //    32 output columns (warp >> 2).
+    const int mt = warp & 3, nh = warp >> 2, mi = lane >> 3;
+    float acc[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
+    const uint32_t a_base = smem_u32(s_a), b_base = smem_u32(s_b);
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+        uint32_t af[4];
+        const int row = 16 * mt + (lane & 7) + (mi & 1) * 8;
+        const int unit = (ks & 3) * 2 + (mi >> 1);
+        ldsm_x4(a_base + (ks >> 2) * (kProRows * 128) + row * 128 + (((unit ^ row) & 7) << 4), af[0], af[1], af[2],
+                af[3]);
+#pragma unroll
+        for (int np = 0; np < 2; ++np) {
+            const int krow = ks * 16 + (lane & 7) + (mi & 1) * 8;
+            const int col = nh * 32 + np * 16 + (mi >> 1) * 8;
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(b_base + krow * 128 + ((((col >> 3) ^ krow) & 7) << 4), b0, b1, b2, b3);
+            mma_f16(acc[2 * np], af, b0, b1);
+            mma_f16(acc[2 * np + 1], af, b2, b3);
+        }
+    }
+    // 4. q_lat (fp16) for the valid rows.
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+        const int r = 16 * mt + (lane >> 2) + 8 * hh;
+        const int s = r / rps, rr = r - s * rps, l = rr / a.group, j = rr - l * a.group;
+        const int b = b0 + s;
+        if (s >= a.seq_per_cta || b >= a.batch || l >= (a.qlens ? a.qlens[b] : a.length)) continue;
+        __half* dst = a.q_lat + (((int64_t)b * a.length + l) * a.heads + g * a.group + j) * a.width + cc * 64 +
+                      nh * 32 + (lane & 3) * 2;
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+            *reinterpret_cast<uint32_t*>(dst + n * 8) = pack_f16x2(acc[n][2 * hh], acc[n][2 * hh + 1]);
+    }
+    if (cc != 0) return;
+    // 5. Append this step's raw token of head g: rotated key, value, pre-RoPE key.
+    if (a.new_k) {
+        for (int i = tid; i < a.seq_per_cta * 16; i += 256) {
+            const int s = i >> 4, d0 = (i & 15) * 8, b = b0 + s;
+            if (b >= a.batch) continue;
+            const int row = a.raw_len[b] - 1;
+            if (row < 0 || row >= a.raw_capacity) {
+                report(a.status, SLIMKV_DEVICE_BAD_LENGTH);
+                continue;
+            }
+            int pos = a.qpos[b * a.length];
+            if (pos < 0 || pos >= a.rope_positions) pos = 0;
+            const __nv_bfloat16* k = a.new_k + b * a.new_stride + (int64_t)g * a.dim;
+            const __nv_bfloat16* v = a.new_v + b * a.new_stride + (int64_t)g * a.dim;
+            float o[8];
+            rope8(k, d0, half, a.cos + (int64_t)pos * a.dim, a.sin + (int64_t)pos * a.dim, o);
+            const int64_t dst = b * a.raw_sb + row * a.raw_st + (int64_t)g * a.dim + d0;
+            *reinterpret_cast<uint4*>(a.raw_k_rot + dst) = pack8_bf16(o);
+            *reinterpret_cast<uint4*>(a.raw_v + dst) = *reinterpret_cast<const uint4*>(v + d0);
+            if (a.raw_k_pre) *reinterpret_cast<uint4*>(a.raw_k_pre + dst) = *reinterpret_cast<const uint4*>(k + d0);
+        }
+    }
+    // 6. Append the Beacon latent pair of rows that insert one this step.
+    if (g == 0 && a.new_lat_k) {
+        const int ku = a.rank_k / 8, vu = a.rank_v / 8;
+        for (int i = tid; i < a.seq_per_cta * (ku + vu); i += 256) {
+            const int s = i / (ku + vu), u = i - s * (ku + vu), b = b0 + s;
+            if (b >= a.batch || (a.qlens ? a.qlens[b] : a.length) != 2) continue;
+            const int row = a.latent_len[b] - 1;
+            if (row < 0 || row >= a.lat_capacity) {
+                report(a.status, SLIMKV_DEVICE_BAD_LENGTH);
+                continue;
+            }
+            if (u < ku)
+                *reinterpret_cast<uint4*>(a.lat_k + b * a.lat_sb + row * a.lat_sr + u * 8) =
+                    *reinterpret_cast<const uint4*>(a.new_lat_k + b * a.new_lat_stride + u * 8);
+            else
+                *reinterpret_cast<uint4*>(a.lat_v + b * a.lat_sb + row * a.lat_sr + (u - ku) * 8) =
+                    *reinterpret_cast<const uint4*>(a.new_lat_v + b * a.new_lat_stride + (u - ku) * 8);
+        }
+    }
+}
+
+struct MergeArgs {
+    const float* lat_o; const float* lat_lse; int lat_splits, lat_rows, lat_width;
+    const float* raw_o; const float* raw_lse; int raw_splits, raw_rows;
+    const __nv_bfloat16* q_rot;
+    const __nv_bfloat16* uv; const __nv_bfloat16* uk_bias; const __nv_bfloat16* uv_bias;
+    const int32_t* qlens;
+    int batch, length, heads, kv_heads, dim, rank_v, rank_v_pad, group, seq_per_cta;
+    float scale;
+    void* out; int out_fp32; int64_t o_sb, o_sl;
+};
+
+// Split combine of `splits` normalised partials of one row: lanes cover the
+// columns; the split loop's loads are independent of each other.
+template <int MAXC>
+__device__ __forceinline__ float combine_lanes(const float* o, const float* lse, int splits, int64_t pitch, int width,
+                                               int cols, int lane, float acc[MAXC]) {
+    float m = -INFINITY;
+    for (int s = lane; s < splits; s += 32) m = fmaxf(m, lse[s * pitch]);
+#pragma unroll
+    for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) acc[i] = 0.f;
+    if (m == -INFINITY) return -INFINITY;
+    float total = 0.f;
+    for (int s = 0; s < splits; ++s) {
+        const float w = expf(lse[s * pitch] - m);
+        total += w;
+        const float* row = o + s * pitch * width;
+#pragma unroll
+        for (int i = 0; i < MAXC; ++i) {
+            const int c = lane + 32 * i;
+            if (c < cols) acc[i] = fmaf(w, row[c], acc[i]);
+        }
+    }
+    const float inv = 1.f / total;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) acc[i] *= inv;
+    return m + logf(total);
+}
+
+// grid (Hkv, ceil(B / seq_per_cta)), 256 threads, dynamic shared memory
+// 128*Rvp*2 + 16*Rvp*2 + 16*D*4 + 128 bytes.  CTA (g, bb) merges the 16 rows
+// (seq_per_cta sequences x L x group) of KV head g.
+__global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int rvp = a.rank_v_pad;                       // multiple of 64
+    uint8_t* s_b = smem;                                // U_v[g]: rvp/64 chunks [128 x 64] fp16
+    uint8_t* s_a = s_b + 128 * rvp * 2;                 // o_lat: rvp/64 chunks [16 x 64] fp16
+    float* s_raw = reinterpret_cast<float*>(s_a + 16 * rvp * 2);   // [16][D]
+    float* s_lse = s_raw + 16 * a.dim;                  // [2][16]: latent, raw
+    const int g = blockIdx.x, bb = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rps = a.length * a.group, b0 = bb * a.seq_per_cta;
+
+    // 1. Stage U_v[g] (rows d, columns c) as the MMA's column-major B operand.
+    const int units = rvp / 8;
+    for (int i = tid; i < 128 * units; i += 256) {
+        const int d = i / units, u = i - d * units, col = u * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (col < a.rank_v) v = widen8(*reinterpret_cast<const uint4*>(a.uv + ((int64_t)g * a.dim + d) * a.rank_v + col));
+        *reinterpret_cast<uint4*>(s_b + (u >> 3) * (128 * 128) + sw128(d, (u & 7) * 8)) = v;
+    }
+    // 2. Combine both branches' split partials, one warp per row.
+    for (int r = warp; r < 16; r += 8) {
+        const int s = r / rps, rr = r - s * rps, l = rr / a.group, j = rr - l * a.group;
+        const int b = b0 + s, h = g * a.group + j;
+        const bool valid = s < a.seq_per_cta && b < a.batch && l < (a.qlens ? a.qlens[b] : a.length);
+        float acc[10];
+        float lse_l = -INFINITY, lse_r = -INFINITY;
+        if (valid) {
+            const int64_t lb = (int64_t)b * a.lat_splits * a.lat_rows + l * a.heads + h;
+            lse_l = combine_lanes<10>(a.lat_o + lb * a.lat_width, a.lat_lse + lb, a.lat_splits, a.lat_rows,
+                                      a.lat_width, rvp, lane, acc);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 10; ++i) acc[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 10; ++i) {
+            const int c = lane + 32 * i;
+            if (c < rvp)
+                *reinterpret_cast<__half*>(s_a + (c >> 6) * (16 * 128) + sw128(r, c & 63)) = __float2half_rn(acc[i]);
+        }
+        float racc[4];
+        if (valid) {
+            const int64_t rb = ((int64_t)(b * a.kv_heads + g) * a.raw_splits) * a.raw_rows + rr;
+            lse_r = combine_lanes<4>(a.raw_o + rb * a.dim, a.raw_lse + rb, a.raw_splits, a.raw_rows, a.dim, a.dim,
+                                     lane, racc);
+            if (a.uk_bias && lse_l != -INFINITY) {
+                // Latent LSE shift by scale * q . b_k (fa2_decode.py:157-160).
+                const __nv_bfloat16* q = a.q_rot + (((int64_t)b * a.length + l) * a.heads + h) * a.dim;
+                const __nv_bfloat16* bk = a.uk_bias + (int64_t)g * a.dim;
+                float dot = 0.f;
+                for (int d = lane; d < a.dim; d += 32) dot += __bfloat162float(q[d]) * __bfloat162float(bk[d]);
+#pragma unroll
+                for (int off = 16; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+                lse_l += dot * a.scale;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) racc[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s_raw[r * a.dim + lane + 32 * i] = racc[i];
+        if (lane == 0) {
+            s_lse[r] = lse_l;
+            s_lse[16 + r] = lse_r;
+        }
+    }
+    __syncthreads();
+    // 3. [16 x Rvp] . [Rvp x 128]: warp -> output columns [16*warp, 16*warp + 16).
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    const uint32_t a_base = smem_u32(s_a), b_base = smem_u32(s_b);
+    const int mi = lane >> 3;
+    for (int ks = 0; ks < rvp / 16; ++ks) {
+        uint32_t af[4];
+        const int row = (lane & 7) + (mi & 1) * 8;
+        const int unit = (ks & 3) * 2 + (mi >> 1);
+        ldsm_x4(a_base + (ks >> 2) * (16 * 128) + row * 128 + (((unit ^ row) & 7) << 4), af[0], af[1], af[2], af[3]);
+        const int n = 16 * warp + (mi >> 1) * 8 + (lane & 7);
+        const int bunit = (ks & 3) * 2 + (mi & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(b_base + (ks >> 2) * (128 * 128) + n * 128 + (((bunit ^ n) & 7) << 4), b0, b1, b2, b3);
+        mma_f16(acc[0], af, b0, b1);
+        mma_f16(acc[1], af, b2, b3);
+    }
+    // 4. Bias, LSE merge (fa2_decode.py:57-66) and store.
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+        const int r = (lane >> 2) + 8 * hh;
+        const int s = r / rps, rr = r - s * rps, l = rr / a.group, j = rr - l * a.group;
+        const int b = b0 + s, h = g * a.group + j;
+        if (s >= a.seq_per_cta || b >= a.batch || l >= (a.qlens ? a.qlens[b] : a.length)) continue;
+        const float ll = s_lse[r], lr = s_lse[16 + r];
+        float wr = 0.f, wl = 0.f;
+        if (!(ll == -INFINITY && lr == -INFINITY)) {
+            const float total = fmaxf(lr, ll) + log1pf(expf(-fabsf(lr - ll)));
+            wr = lr == -INFINITY ? 0.f : expf(lr - total);
+            wl = ll == -INFINITY ? 0.f : expf(ll - total);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int d = 16 * warp + nt * 8 + (lane & 3) * 2 + e;
+                const float bv = a.uv_bias ? __bfloat162float(a.uv_bias[(int64_t)g * a.dim + d]) : 0.f;
+                const float value = wr * s_raw[r * a.dim + d] + wl * (acc[nt][2 * hh + e] + bv);
+                const int64_t o = b * a.o_sb + l * a.o_sl + (int64_t)h * a.dim + d;
+                if (a.out_fp32) static_cast<float*>(a.out)[o] = value;
+                else static_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(value);
+            }
+    }
+}
+
+}  // namespace slimkv

@@ -50,6 +50,7 @@ def attention_forward(q, k, v, scale, causal=False, num_splits=0, cache_seqlens=
     _require(k.shape[0] == batch and v.shape[:3] == k.shape[:3] and k.shape[3] == dim, 'Invalid K/V shape')
     if out is None:
         out = q.new_empty(batch, queries, heads, v.shape[3])
+    _require(out.dtype in (torch.bfloat16, torch.float32) and out.is_cuda, 'out must be bf16 or fp32 on CUDA')
     if lse is None:
         lse = torch.empty(batch, heads, queries, device=q.device, dtype=torch.float32)
     if cache_seqlens is not None:
@@ -66,6 +67,7 @@ def attention_forward(q, k, v, scale, causal=False, num_splits=0, cache_seqlens=
     a.keys, a.head_dim, a.value_dim = k.shape[1], dim, v.shape[3]
     a.scale, a.causal, a.num_splits = float(scale), int(bool(causal)), int(num_splits)
     a.lse_masked_positive = int(bool(lse_masked_positive))
+    a.out_fp32 = int(out.dtype == torch.float32)
     lib = _lib.load()
     with torch.cuda.device(q.device):
         size = lib.slimkv_attention_workspace_size(ctypes.byref(a))
@@ -134,7 +136,8 @@ class LatentDecodeCall:
                  out, query_len=None, raw_k_pre=None, new_k=None, new_v=None, new_lat_k=None, new_lat_v=None,
                  uk_bias=None, uv_bias=None, scale=None, latent_len_max=0, raw_len_max=0, latent_splits=0,
                  raw_splits=0):
-        _bf16_cuda(q, raw_k_rot, raw_v, lat_k, lat_v, uk, uv, out)
+        _bf16_cuda(q, raw_k_rot, raw_v, lat_k, lat_v, uk, uv)
+        _require(out.is_cuda and out.dtype in (torch.bfloat16, torch.float32), 'out must be bf16 or fp32 on CUDA')
         batch, length, heads, dim = q.shape
         kv_heads = raw_k_rot.shape[2]
         _require(raw_k_rot.shape[0] == batch and raw_k_rot.shape[3] == dim, 'raw cache shape')
@@ -164,13 +167,22 @@ class LatentDecodeCall:
                         ('uk_bias', uk_bias), ('uv_bias', uv_bias)):
             if t is not None:
                 _bf16_cuda(t)
-                _require(t.is_contiguous(), f'{name} must be contiguous')
+                _require(t.stride(-1) == 1, f'{name} must have a contiguous last dimension')
+                _require(t.dim() == 1 or t.shape[0] == batch, f'{name} must have one row per sequence')
             setattr(a, name, 0 if t is None else t.data_ptr())
+        if new_k is not None:
+            _require(new_k.shape[-1] == kv_heads * dim and new_k.stride() == new_v.stride(), 'new K/V rows')
+            a.new_stride = new_k.stride(0)
+        if new_lat_k is not None:
+            _require(new_lat_k.shape[-1] == a.rank_k and new_lat_v.shape[-1] == a.rank_v
+                     and new_lat_k.stride(0) == new_lat_v.stride(0), 'new latent rows')
+            a.new_lat_stride = new_lat_k.stride(0)
         a.uk, a.uv = uk.data_ptr(), uv.data_ptr()
         _require(cos.dtype == torch.float32 and cos.is_contiguous() and sin.is_contiguous(), 'fp32 tables')
         a.cos, a.sin, a.rope_positions = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
         _require(out.shape == (batch, length, heads * dim) and out.stride(2) == 1, 'out must be [B, L, H*D]')
         a.out, a.out_stride = out.data_ptr(), _lib.I64x2(out.stride(0), out.stride(1))
+        a.out_fp32 = int(out.dtype == torch.float32)
         a.latent_len_max, a.raw_len_max = int(latent_len_max), int(raw_len_max)
         a.latent_splits, a.raw_splits = int(latent_splits), int(raw_splits)
         self.args = a
@@ -194,3 +206,18 @@ class LatentDecodeCall:
 def latent_decode(**kwargs):
     """One fused decode-attention step (see :class:`LatentDecodeCall`)."""
     return LatentDecodeCall(**kwargs)()
+
+
+def decode_schedule(history, tail, raw_len, latent_len, query_len, qpos, sink, window, ratio):
+    """Advance the per-sequence Beacon schedule on the device (in place).
+
+    Writes this step's ``query_len``, ``raw_len``, ``latent_len`` and ``qpos
+    [B, 2]`` from the counters ``history`` / ``tail`` and advances them.
+    """
+    for t in (history, tail, raw_len, latent_len, query_len, qpos):
+        _require(t.is_cuda and t.dtype == torch.int32 and t.is_contiguous(), 'int32 CUDA counters')
+    batch = history.numel()
+    _require(qpos.shape == (batch, 2), 'qpos must be [B, 2]')
+    _lib.check(_lib.load().slimkv_decode_schedule(batch, int(sink), int(window), int(ratio), _ptr(history),
+                                                  _ptr(tail), _ptr(raw_len), _ptr(latent_len), _ptr(query_len),
+                                                  _ptr(qpos), _stream()))

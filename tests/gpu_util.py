@@ -21,10 +21,20 @@ def assert_bits_equal(actual_bf16, expected_fp32):
     assert bad.size == 0, f'{bad.size} of {got.size} elements differ, first at {bad[:5]}'
 
 
-def assert_attention_close(actual, expected, rel=2e-3, atol=1.5e-2, rtol=1.5e-2):
-    """Attention-output parity: norm-wise relative error <= ``rel`` and the
-    element-wise tolerance of the reference's own GPU validation
-    (tools/validation/validate_fa2_decode.py:58, atol = rtol = 0.015)."""
+# Parity bar.  fp32-accumulated outputs (the kernels' fp32 output mode): norm-wise
+# relative error <= 2e-3 against the oracle.  bf16 outputs: rounding a value to
+# bf16 alone costs a norm-wise relative error of 1.66e-3 (measured on Gaussian
+# data), so their norm-wise bound is 3e-3, and every element must also meet the
+# reference's own GPU validation tolerance (atol = rtol = 0.015,
+# tools/validation/validate_fa2_decode.py:58).
+REL_FP32 = 2e-3
+REL_BF16 = 3e-3
+
+
+def assert_attention_close(actual, expected, rel=None, atol=1.5e-2, rtol=1.5e-2):
+    """Attention-output parity against the oracle; returns the norm-wise error."""
+    if rel is None:
+        rel = REL_FP32 if (torch.is_tensor(actual) and actual.dtype == torch.float32) else REL_BF16
     a = actual.float().cpu().numpy().astype(np.float64) if torch.is_tensor(actual) else np.asarray(actual, np.float64)
     e = np.asarray(expected, np.float64)
     assert a.shape == e.shape, (a.shape, e.shape)

@@ -1,10 +1,11 @@
 """GPU parity of the split-KV decode attention (drop-in extension path).
 
 Compares ``slimkv_attention_forward`` (through the C ABI, via the drop-in
-``slimkv_fa2_decode_320`` module) with the CPU oracle's eager attention on
-the same seeded bf16 inputs.  Tolerances: norm-wise relative error 2e-3,
-element-wise atol = rtol = 0.015 and LSE atol 1e-3 (the reference's own
-GPU validation, tools/validation/validate_fa2_decode.py:58-59).
+``slimkv_fa2_decode_320`` module and the fp32-output mode) with the CPU
+oracle's eager attention on the same seeded bf16 inputs.  Tolerances: fp32
+outputs norm-wise relative error 2e-3; bf16 outputs 3e-3 norm-wise (bf16
+rounding alone is 1.66e-3) and element-wise atol = rtol = 0.015; LSE atol 1e-3
+(the reference's own GPU validation, tools/validation/validate_fa2_decode.py:58-59).
 """
 import math
 
@@ -49,10 +50,15 @@ CASES = [
 @pytest.mark.parametrize('spec', CASES, ids=lambda s: f'b{s[1]}q{s[2]}h{s[3]}kv{s[4]}n{s[5]}w{s[6]}')
 @pytest.mark.parametrize('splits', [0, 1, 16])
 def test_attention_matches_oracle(spec, splits):
+    from slimkv_b200 import kernels
     c = attention_case(*spec)
     out, lse, ref, ref_lse = _run(c, splits)
     assert_attention_close(out, ref)
     assert_lse_close(lse, ref_lse)
+    q, k, v = to_bf16(c['q']), to_bf16(c['k']), to_bf16(c['v'])
+    out32 = torch.empty(q.shape[:3] + (v.shape[3],), dtype=torch.float32, device='cuda')
+    kernels.attention_forward(q, k, v, c['scale'], c['causal'], splits, out=out32)
+    assert_attention_close(out32, ref)
 
 
 def test_cache_seqlens_truncate_each_row():

@@ -31,7 +31,7 @@ def tables(positions=16384):
     return _TABLES[positions]
 
 
-def run_fused(c, query_len, extra_cap=3, pre=True):
+def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False):
     """Stage the caches without this step's entries, run the fused step."""
     from slimkv_b200 import kernels
     cos, sin, cos_t, sin_t = tables()
@@ -60,14 +60,19 @@ def run_fused(c, query_len, extra_cap=3, pre=True):
         if query_len[b] == 2:
             new_lk[b] = c['lat_k'][b, n]
             new_lv[b] = c['lat_v'][b, n]
-    t = dict(q=to_bf16(c['q']), raw_k_rot=to_bf16(raw_k), raw_v=to_bf16(raw_v), lat_k=to_bf16(lat_k),
-             lat_v=to_bf16(lat_v), uk=to_bf16(c['uk']), uv=to_bf16(c['uv']), cos=cos_t, sin=sin_t,
+    # New latents arrive as column views of one down-projection output row.
+    new_l = to_bf16(np.concatenate([new_lk, new_lv], axis=-1))
+    new_latents = dict(new_lat_k=new_l[:, :rk], new_lat_v=new_l[:, rk:])
+    # Native latent layout: one [B, cap, Rk + Rv] buffer, K and V as column views.
+    lat = to_bf16(np.concatenate([lat_k, lat_v], axis=-1))
+    t = dict(q=to_bf16(c['q']), raw_k_rot=to_bf16(raw_k), raw_v=to_bf16(raw_v), lat_k=lat[..., :rk],
+             lat_v=lat[..., rk:], uk=to_bf16(c['uk']), uv=to_bf16(c['uv']), cos=cos_t, sin=sin_t,
              raw_len=torch.tensor(n_raw, dtype=torch.int32, device='cuda'),
              latent_len=torch.tensor(n_lat, dtype=torch.int32, device='cuda'),
              query_len=torch.tensor(query_len, dtype=torch.int32, device='cuda'),
              qpos=torch.tensor(c['qpos'], dtype=torch.int32, device='cuda'),
-             new_k=to_bf16(new_k), new_v=to_bf16(new_v), new_lat_k=to_bf16(new_lk), new_lat_v=to_bf16(new_lv),
-             out=torch.zeros(B, L, H * D, dtype=torch.bfloat16, device='cuda'))
+             new_k=to_bf16(new_k), new_v=to_bf16(new_v), **new_latents,
+             out=torch.zeros(B, L, H * D, dtype=torch.float32 if fp32 else torch.bfloat16, device='cuda'))
     if pre:
         t['raw_k_pre'] = torch.zeros_like(t['raw_k_rot'])
     if c['bk'] is not None:
@@ -126,6 +131,7 @@ def test_fused_decode_matches_oracle(length, history, tail, rank, bias, ragged):
                     bias=bias, ragged=ragged)
     query_len = np.full(3, length)
     check(c, query_len, run_fused(c, query_len))
+    check(c, query_len, run_fused(c, query_len, fp32=True))
 
 
 def test_mixed_query_lengths_in_one_batch():
@@ -134,6 +140,7 @@ def test_mixed_query_lengths_in_one_batch():
     query_len = np.array([2, 1, 2, 1])
     c['n_lat'] = c['n_lat'] - (query_len == 1)           # rows without a Beacon have one latent fewer
     check(c, query_len, run_fused(c, query_len))
+    check(c, query_len, run_fused(c, query_len, fp32=True))
 
 
 def test_distinct_key_and_value_ranks():
