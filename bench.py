@@ -1,0 +1,266 @@
+#!/usr/bin/env python
+"""Decode benchmark: Llama-3.1-8B-r4 t4f4, 32k context, batch 16 per GPU.
+
+a full 32-layer decode step of a Llama-3.1-8B-geometry
+SlimKV model (random N(0, 0.02) bf16 weights, latent ranks 320/320, Beacon
+ratio 4, 4 sinks) over batch 16, every sequence with 32 completed 1024-token
+windows (8192 Beacon latents) and a raw tail of U{0..1023} tokens.  One
+"step" decodes one raw token per sequence (plus a Beacon row where the
+schedule inserts one) through all 32 layers, CUDA-graph captured.
+
+Prints one JSON line: ``value`` = decode tokens/s over all ranks (device
+time, inputs resident), ``e2e`` = the same through the public runtime API
+with per-step host->device token upload and device->host read of the
+sampled tokens, ``roofline`` for the fused latent attention step (HBM bytes
+per launch / CUDA-event time), ``cpu_baseline`` = the CPU restatement of the
+same decode step on this host's cores.
+
+``--impl reference`` times the CPU restatement of the reference's eager
+decode (the only reference implementation of this path that runs here) on
+the same workload and metric.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = 'decode tokens/s and latent-attn HBM GB/s (% of peak), Llama-3.1-8B-r4 t4f4 32k ctx'
+UNIT = 'tokens/s'
+BATCH = 16
+HISTORY = 8192          # 32 completed windows x 256 Beacon latents
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__.split('\n')[0])
+    p.add_argument('--gpus', type=int, default=1)
+    p.add_argument('--steps', type=int, default=20)
+    p.add_argument('--warmup', type=int, default=5)
+    p.add_argument('--impl', default='slimkv_b200', choices=['slimkv_b200', 'reference'])
+    p.add_argument('--no-cpu-baseline', action='store_true')
+    return p.parse_args()
+
+
+def config(n):
+    return {'workload': 'Llama-3.1-8B-r4 t4f4 decode step (BASELINE config 2), latent path',
+            'global_batch': BATCH * n, 'batch_per_gpu': BATCH, 'context': '32768 + raw tail U{0..1023}',
+            'beacon_latents': HISTORY, 'latent_rank': '320/320', 'sinks': 4, 'layers': 32,
+            'parallelism': f'dp{n} (independent replicas, no data-path collective)',
+            'l2': 'each step reads ~23 GB (weights + caches) >> 126 MB L2; no flush needed'}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+    QUERY = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+             'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+             'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile('w+', suffix='.csv', delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.QUERY}',
+                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.file.flush()
+        self.file.seek(0)
+        sm, mx, reasons = [], 0.0, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for line in self.file.read().strip().splitlines():
+            f = [x.strip() for x in line.split(',')]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, f[5:9]):
+                if flag.lower() == 'active':
+                    reasons.add(name)
+        os.unlink(self.file.name)
+        if not sm:
+            return None
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': mx, 'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+def peaks():
+    path = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d['hbm_gbs']), 'measured'
+    return FALLBACK_HBM_GBS, 'fallback'
+
+
+def traffic_per_launch():
+    """ncu DRAM bytes of one fused latent attention launch at this workload."""
+    path = os.path.join(ROOT, 'profiles', 'latent_decode_c2_traffic.json')
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        return json.load(f).get('bytes_per_launch')
+
+
+def cpu_baseline(batch, steps_hint=None):
+    from oracle.cpu_decode import time_decode_step
+    seconds, threads, sample = time_decode_step(batch=batch, history=HISTORY)
+    return {'value': batch / seconds, 'unit': UNIT, 'cores': threads, 'kind': 'port', 'sample': sample}
+
+
+def run_reference(args):
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return
+    values = []
+    sample = threads = None
+    for _ in range(max(1, min(args.steps, 3))):
+        from oracle.cpu_decode import time_decode_step
+        seconds, threads, sample = time_decode_step(batch=BATCH, history=HISTORY, repeats=1)
+        values.append(BATCH / seconds)
+    value = statistics.median(values)
+    print(json.dumps({
+        'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus,
+        'steps': len(values), 'warmup': 1, 'ms_per_step': 1000.0 * BATCH / value, 'higher_is_better': True,
+        'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic', 'config': config(1),
+        'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': threads, 'kind': 'port', 'sample': sample},
+        'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+        'note': "CPU restatement of the reference's eager fp32 decode (fa2_decode.decode with eager_forward) "
+                'on all host threads; the reference GPU kernel builds only for sm_90/sm_120'}), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == 'reference':
+        return run_reference(args)
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from slimkv_b200 import _lib
+    from slimkv_b200.runtime import LatentDecodeRuntime, LatentLlamaConfig, RandomWeights
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group('nccl', timeout=timedelta(seconds=300))
+    torch.cuda.set_device(local)
+    device = torch.device('cuda', local)
+    cfg = LatentLlamaConfig()
+    weights = RandomWeights(cfg, device, seed=0)
+    rng = np.random.default_rng(1234 + rank)
+    tails = rng.integers(0, cfg.window, size=BATCH)
+    rt = LatentDecodeRuntime(cfg, weights, [HISTORY] * BATCH, tails, device, extra_windows=1)
+    rt.tokens.copy_(torch.from_numpy(rng.integers(0, cfg.vocab, size=BATCH)).to(device))
+    rt.capture(warmup=2)
+    for _ in range(max(args.warmup, 3)):
+        rt.step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    # ---- device-resident timed region -------------------------------------
+    clocks = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    attn_bytes = 0
+    start.record()
+    for _ in range(args.steps):
+        rt.step()
+    end.record()
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    barrier()
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    value = world * BATCH / (ms / 1000.0)
+
+    # ---- end to end through the runtime API: host tokens in, host tokens out -
+    host_in = torch.from_numpy(rng.integers(0, cfg.vocab, size=BATCH)).pin_memory()
+    host_out = torch.empty(BATCH, dtype=torch.int64).pin_memory()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        rt.tokens.copy_(host_in, non_blocking=True)
+        rt.step()
+        host_out.copy_(rt.next_tokens(), non_blocking=True)
+        torch.cuda.current_stream().synchronize()      # the next step needs these tokens
+        host_in.copy_(host_out)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+
+    # ---- roofline of the fused latent attention step ------------------------
+    per_layer_bytes = rt.attention_bytes() / cfg.layers
+    reps = max(args.steps, 8) * 4
+    torch.cuda.synchronize()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    for i in range(reps):
+        rt.calls[i % cfg.layers]()
+    a1.record()
+    torch.cuda.synchronize()
+    launch_ms = a0.elapsed_time(a1) / reps
+    achieved = per_layer_bytes / (launch_ms / 1000.0) / 1e9
+    peak, peak_kind = peaks()
+    status = _lib.device_status(clear=True)
+
+    result = {
+        'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
+        'warmup': max(args.warmup, 3), 'ms_per_step': ms, 'higher_is_better': True, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (random N(0,0.02) weights, synthetic cache)',
+        'config': config(world),
+        'e2e': {'value': world * BATCH / (e2e_ms / 1000.0), 'unit': UNIT, 'h2d_bytes_per_step': BATCH * 8,
+                'd2h_bytes_per_step': BATCH * 8, 'ms_per_step': e2e_ms},
+        'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
+                     'peak_source': f'{peak_kind} (MEASURED_PEAKS.json hbm_gbs)' if peak_kind == 'measured'
+                     else 'fallback 6650 GB/s',
+                     'traffic': traffic_per_launch(), 'kernel': 'fused latent decode step (prologue + '
+                     'attention + merge) per layer', 'bytes_per_launch': per_layer_bytes,
+                     'us_per_launch': launch_ms * 1000.0},
+        'gpu_launches': args.steps * (1 + 3 * cfg.layers),
+        'clocks': clock_info, 'device_status': status,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result['cpu_baseline'] = cpu_baseline(BATCH)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    rt.graph = None
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

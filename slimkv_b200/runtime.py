@@ -1,0 +1,220 @@
+"""Whole-model decode runtime over the native latent cache (B > 1, graphs).
+
+A batched, CUDA-graph-captured decode step of a Llama-3.1-style SlimKV model
+whose attention is the fused latent decode of ``libslimkv_b200.so``:
+
+* per-sequence Beacon schedule advanced on the device every step
+  (``slimkv_decode_schedule``, the per-sequence form of
+  ``LlamaMemory._step``, slimkv/llama3/memory.py:101-162), so a replay
+  needs no host work and sequences may sit at different window offsets;
+* projections and the MLP are cuBLAS GEMMs issued by torch; the raw row uses
+  ``q/k/v_proj`` and the Beacon row ``beacon_q_proj`` plus the K/V
+  down-projections (slimkv/llama3/fa2_decode.py:89-99);
+* every step carries two rows per sequence — the raw token and a Beacon slot
+  that only sequences inserting a Beacon this step use (``query_len``), so
+  the graph shape never changes.
+
+Weights are random N(0, std) (no checkpoint is available offline); the cache
+is filled with synthetic latents/keys of the magnitude that projections of
+unit-variance hidden states produce.  This is the reference's static decode
+(slimkv/llama3/static_decode.py:43-287) generalised to B > 1 and ragged
+lengths.
+"""
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from . import kernels
+from .rope import LLAMA3_SCALING, rope_tables
+
+
+@dataclass
+class LatentLlamaConfig:
+    """Llama-3.1-8B geometry with SlimKV r4 ranks and t4 Beacons."""
+    vocab: int = 128256
+    hidden: int = 4096
+    intermediate: int = 14336
+    layers: int = 32
+    heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 128
+    rank_k: int = 320
+    rank_v: int = 320
+    window: int = 1024
+    ratio: int = 4
+    sink: int = 4
+    rope_theta: float = 500000.0
+    rope_scaling: dict = field(default_factory=lambda: dict(LLAMA3_SCALING))
+    rope_positions: int = 131072
+    rms_eps: float = 1e-5
+
+
+class RandomWeights:
+    """bf16 weights drawn from N(0, std) on the device (norm weights = 1)."""
+
+    def __init__(self, cfg, device, seed=0, std=0.02):
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+        H, I, kvd = cfg.hidden, cfg.intermediate, cfg.kv_heads * cfg.head_dim
+        qd = cfg.heads * cfg.head_dim
+
+        def w(*shape):
+            return torch.randn(*shape, generator=gen, device=device, dtype=torch.bfloat16).mul_(std)
+
+        self.embed = w(cfg.vocab, H)
+        self.beacon_embed = w(1, H)
+        self.final_norm = torch.ones(H, device=device, dtype=torch.bfloat16)
+        self.lm_head = w(cfg.vocab, H)
+        self.layers = []
+        for _ in range(cfg.layers):
+            self.layers.append(dict(
+                norm1=torch.ones(H, device=device, dtype=torch.bfloat16),
+                norm2=torch.ones(H, device=device, dtype=torch.bfloat16),
+                w_raw=w(qd + 2 * kvd, H),                        # q_proj | k_proj | v_proj
+                w_beacon=w(qd + cfg.rank_k + cfg.rank_v, H),     # beacon_q_proj | k_down | v_down
+                w_o=w(H, qd),
+                uk=w(kvd, cfg.rank_k),                           # beacon_k_up_proj.weight
+                uv=w(kvd, cfg.rank_v),                           # beacon_v_up_proj.weight
+                w_gate_up=w(2 * I, H),
+                w_down=w(H, I)))
+
+    def nbytes(self):
+        total = sum(t.numel() * 2 for t in (self.embed, self.beacon_embed, self.lm_head))
+        return total + sum(t.numel() * 2 for layer in self.layers for t in layer.values())
+
+
+class LatentDecodeRuntime:
+    """Batched decode over per-sequence compressed caches.
+
+    ``history[b]`` completed-window latents and ``tails[b]`` raw tokens of the
+    open window per sequence (0 <= tail < window).  Caches are allocated for
+    ``extra_windows`` more windows of growth.
+    """
+
+    def __init__(self, cfg, weights, history, tails, device, extra_windows=1, seed=1, fill_std=1.3):
+        self.cfg, self.w, self.device = cfg, weights, device
+        B = len(history)
+        self.batch = B
+        hist = torch.as_tensor(history, dtype=torch.int32)
+        tail = torch.as_tensor(tails, dtype=torch.int32)
+        if (tail < 0).any() or (tail >= cfg.window).any():
+            raise ValueError('tails must lie in [0, window)')
+        if cfg.sink > 1 and (hist == 0).any():
+            raise ValueError('decode with more than one sink needs a completed first window')
+        per_window = cfg.window // cfg.ratio
+        self.raw_capacity = (cfg.sink + cfg.window + 1 + 63) // 64 * 64
+        self.lat_capacity = (int(hist.max()) + (1 + extra_windows) * per_window + 63) // 64 * 64
+        kvd = cfg.kv_heads * cfg.head_dim
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+
+        def fill(*shape):
+            return torch.randn(*shape, generator=gen, device=device, dtype=torch.bfloat16).mul_(fill_std)
+
+        self.caches = []
+        for _ in range(cfg.layers):
+            raw_k = fill(B, self.raw_capacity, cfg.kv_heads, cfg.head_dim)
+            lat = fill(B, self.lat_capacity, cfg.rank_k + cfg.rank_v)
+            self.caches.append(dict(raw_k_rot=raw_k, raw_k_pre=raw_k.clone(),
+                                    raw_v=fill(B, self.raw_capacity, cfg.kv_heads, cfg.head_dim),
+                                    lat=lat, lat_k=lat[..., :cfg.rank_k], lat_v=lat[..., cfg.rank_k:]))
+        # Per-sequence schedule counters and per-step metadata (device).
+        i32 = dict(dtype=torch.int32, device=device)
+        self.history = hist.to(device)
+        self.tail = tail.to(device)
+        self.raw_len = torch.zeros(B, **i32)
+        self.latent_len = torch.zeros(B, **i32)
+        self.query_len = torch.zeros(B, **i32)
+        self.qpos = torch.zeros(B, 2, **i32)
+        self.cos, self.sin = rope_tables(cfg.head_dim, cfg.rope_theta, cfg.rope_positions, cfg.rope_scaling, device)
+        # Step buffers: two rows per sequence (raw token, Beacon slot).
+        bf = dict(dtype=torch.bfloat16, device=device)
+        H, qd = cfg.hidden, cfg.heads * cfg.head_dim
+        self.width = qd + 2 * kvd
+        self.tokens = torch.zeros(B, dtype=torch.int64, device=device)
+        self.x = torch.zeros(B, 2, H, **bf)
+        self.z = torch.zeros(B, 2, self.width, **bf)            # projection outputs per row
+        self.attn = torch.zeros(B, 2, qd, **bf)
+        self.logits = torch.zeros(B, cfg.vocab, dtype=torch.float32, device=device)
+        self.logits_bf16 = torch.zeros(B, cfg.vocab, **bf)
+        z = self.z
+        q = z[:, :, :qd].unflatten(-1, (cfg.heads, cfg.head_dim))          # [B, 2, H, D]
+        lat_max = int(hist.max()) + per_window + 64
+        self.calls = []
+        for c, layer in zip(self.caches, weights.layers):
+            self.calls.append(kernels.LatentDecodeCall(
+                q=q, raw_k_rot=c['raw_k_rot'], raw_v=c['raw_v'], raw_k_pre=c['raw_k_pre'],
+                lat_k=c['lat_k'], lat_v=c['lat_v'], raw_len=self.raw_len, latent_len=self.latent_len,
+                query_len=self.query_len, qpos=self.qpos, uk=layer['uk'], uv=layer['uv'],
+                cos=self.cos, sin=self.sin, out=self.attn,
+                new_k=z[:, 0, qd:qd + kvd], new_v=z[:, 0, qd + kvd:qd + 2 * kvd],
+                new_lat_k=z[:, 1, qd:qd + cfg.rank_k], new_lat_v=z[:, 1, qd + cfg.rank_k:qd + cfg.rank_k + cfg.rank_v],
+                latent_len_max=min(lat_max, self.lat_capacity), raw_len_max=self.raw_capacity))
+        self.graph = None
+
+    # ------------------------------------------------------------------
+    def step_eager(self):
+        """One decode step on the current stream (what the graph captures)."""
+        cfg, w = self.cfg, self.w
+        B, H, I = self.batch, cfg.hidden, cfg.intermediate
+        qd = cfg.heads * cfg.head_dim
+        nb = qd + cfg.rank_k + cfg.rank_v
+        kernels.decode_schedule(self.history, self.tail, self.raw_len, self.latent_len, self.query_len,
+                                self.qpos, cfg.sink, cfg.window, cfg.ratio)
+        x = self.x
+        x[:, 0].copy_(w.embed.index_select(0, self.tokens))
+        x[:, 1].copy_(w.beacon_embed.expand(B, -1))
+        for layer, call in zip(w.layers, self.calls):
+            h = F.rms_norm(x, (H,), layer['norm1'], cfg.rms_eps)
+            torch.mm(h[:, 0], layer['w_raw'].t(), out=self.z[:, 0])
+            torch.mm(h[:, 1], layer['w_beacon'].t(), out=self.z[:, 1, :nb])
+            call()
+            x.add_((self.attn.view(2 * B, qd) @ layer['w_o'].t()).view(B, 2, H))
+            h2 = F.rms_norm(x, (H,), layer['norm2'], cfg.rms_eps)
+            gu = h2.view(2 * B, H) @ layer['w_gate_up'].t()
+            act = F.silu(gu[:, :I]) * gu[:, I:]
+            x.add_((act @ layer['w_down'].t()).view(B, 2, H))
+        final = F.rms_norm(x[:, 0], (H,), w.final_norm, cfg.rms_eps)
+        torch.mm(final, w.lm_head.t(), out=self.logits_bf16)
+        self.logits.copy_(self.logits_bf16)
+        return self.logits
+
+    def capture(self, warmup=2):
+        """Capture one decode step in a CUDA graph (warm-up steps advance the cache)."""
+        stream = torch.cuda.Stream(self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                self.step_eager()
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            self.step_eager()
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        return self.graph
+
+    def step(self):
+        if self.graph is None:
+            return self.step_eager()
+        self.graph.replay()
+        return self.logits
+
+    def next_tokens(self):
+        return self.logits.argmax(-1)
+
+    # ------------------------------------------------------------------
+    def attention_bytes(self):
+        """Algorithmic HBM bytes of this step's attention, summed over layers.
+
+        Per layer and sequence: the latent K/V rows read (``N (Rk + Rv) 2``),
+        the raw keys/values read (``S + T + 1`` tokens of ``Hkv D`` bf16 K and
+        V), the query and output rows, plus the up-projection weights once.
+        """
+        cfg = self.cfg
+        lat = self.latent_len.long().sum().item() * (cfg.rank_k + cfg.rank_v) * 2
+        raw = self.raw_len.long().sum().item() * cfg.kv_heads * cfg.head_dim * 2 * 2
+        rows = self.query_len.long().sum().item() * cfg.heads * cfg.head_dim * 2 * 2
+        weights = cfg.kv_heads * cfg.head_dim * (cfg.rank_k + cfg.rank_v) * 2
+        return cfg.layers * (lat + raw + rows + weights)
