@@ -94,6 +94,25 @@ SLIMKV_API int slimkv_attention_forward(const slimkv_attention_args* args, void*
                              size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Allocation-free variant of slimkv_attention_forward.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory — for
+ * example a host runtime that reaches this library only through an FFI that
+ * hands over existing device buffers and has no CUDA allocator of its own, or
+ * an engine that reserves all device memory up front and forbids later
+ * allocations.  Same arguments, checks and results as
+ * slimkv_attention_forward, but the split scratch comes from a fixed
+ * 16 MiB array compiled into the library (every GPU that loads the library
+ * holds one until the process exits); calls needing more scratch fail with
+ * SLIMKV_ERR_WORKSPACE and an explanatory message.  Nothing here allocates.
+ * The first call on a device looks up that device's copy of the array, so
+ * make it before capturing a stream into a CUDA graph.  All calls on a device
+ * share the one array and it keeps the previous call's contents (no call
+ * depends on them): calls that can overlap on the GPU — concurrent streams
+ * or threads — race on it, so issue them in order on one stream.
+ * ---------------------------------------------------------------------- */
+SLIMKV_API int slimkv_attention_forward_noalloc(const slimkv_attention_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
  * Fused latent decode step — replaces steps 3-8 of the reference decode
  * `slimkv.llama3.fa2_decode.decode` (slimkv/llama3/fa2_decode.py:77-166):
  * BF16-exact RoPE of q and of the new raw key, cache append of the new raw

@@ -71,6 +71,7 @@ SIGNATURES = {
     'slimkv_device_status': (_I, [ctypes.POINTER(ctypes.c_uint), _I]),
     'slimkv_attention_workspace_size': (ctypes.c_size_t, [ctypes.POINTER(AttentionArgs)]),
     'slimkv_attention_forward': (_I, [ctypes.POINTER(AttentionArgs), _P, ctypes.c_size_t, _P]),
+    'slimkv_attention_forward_noalloc': (_I, [ctypes.POINTER(AttentionArgs), _P]),
     'slimkv_latent_decode_workspace_size': (ctypes.c_size_t, [ctypes.POINTER(LatentDecodeArgs)]),
     'slimkv_latent_decode': (_I, [ctypes.POINTER(LatentDecodeArgs), _P, ctypes.c_size_t, _P]),
     'slimkv_rope_decode': (_I, [_P, ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _P, _P,

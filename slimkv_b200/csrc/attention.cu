@@ -2,6 +2,7 @@
 // replaces the reference's `slimkv_fa2_decode_320.forward`
 // (kernels/fa2_decode/binding.cpp:35-121).
 #include <algorithm>
+#include <mutex>
 
 #include "attn_body.cuh"
 #include "host_utils.h"
@@ -230,4 +231,53 @@ extern "C" int slimkv_attention_forward(const slimkv_attention_args* a, void* wo
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "combine launch failed: %s", cudaGetErrorString(e));
     return SLIMKV_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.  Its split scratch lives in a fixed static device
+// array instead of a caller-provided workspace, for callers that cannot
+// allocate device memory themselves.
+namespace slimkv {
+
+constexpr size_t kStaticScratchBytes = size_t(16) << 20;   // 16 MiB per device
+static __device__ __align__(256) unsigned char g_attention_scratch[kStaticScratchBytes];
+
+// Device address of this device's copy of the scratch array.  The array's name
+// is only a host-side handle, so the address is looked up once per device with
+// that device current and cached.
+static int static_scratch(void** out) {
+    static std::mutex lock;
+    static void* cache[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return fail(SLIMKV_ERR_CUDA, "no current CUDA device");
+    std::lock_guard<std::mutex> guard(lock);
+    if (!cache[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_attention_scratch);
+        if (e != cudaSuccess)
+            return fail(SLIMKV_ERR_CUDA, "cudaGetSymbolAddress of the static scratch failed: %s", cudaGetErrorString(e));
+        cache[dev] = p;
+    }
+    *out = cache[dev];
+    return SLIMKV_OK;
+}
+
+}  // namespace slimkv
+
+extern "C" int slimkv_attention_forward_noalloc(const slimkv_attention_args* a, void* stream) {
+    Plan p;
+    const int rc = plan_attention(a, p);
+    if (rc) return rc;
+    const size_t need = slimkv_attention_workspace_size(a);
+    if (need > kStaticScratchBytes)
+        return fail(SLIMKV_ERR_WORKSPACE,
+                    "this call needs %zu bytes of split scratch; the allocation-free entry point has a fixed "
+                    "%zu-byte buffer (use slimkv_attention_forward with a workspace, or fewer splits)",
+                    need, kStaticScratchBytes);
+    void* scratch = nullptr;
+    if (const int e = static_scratch(&scratch)) return e;
+    // Every element of the partials that the combine reads is written first
+    // by the split kernel, so the shared buffer needs no clearing.
+    return slimkv_attention_forward(a, scratch, kStaticScratchBytes, stream);
 }

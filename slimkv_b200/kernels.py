@@ -78,6 +78,37 @@ def attention_forward(q, k, v, scale, causal=False, num_splits=0, cache_seqlens=
     return out, lse
 
 
+def attention_forward_noalloc(q, k, v, scale, out, lse, causal=False, num_splits=0, cache_seqlens=None,
+                              lse_masked_positive=True):
+    """``attention_forward`` through the allocation-free entry point.
+
+    For callers that cannot allocate device memory: the caller provides
+    ``out`` and ``lse``, and the split scratch comes from the library's fixed
+    16 MiB static buffer.  Calls on one device share that buffer, so they
+    must not overlap on the GPU (keep them on one stream).
+    """
+    _bf16_cuda(q, k, v)
+    _require(q.dim() == 4 and k.dim() == 4 and v.dim() == 4, 'BSHD tensors required')
+    _require(q.stride(3) == 1 and k.stride(3) == 1 and v.stride(3) == 1, 'Last dimension must be contiguous')
+    batch, queries, heads, dim = q.shape
+    _require(out.dtype in (torch.bfloat16, torch.float32) and out.is_cuda, 'out must be bf16 or fp32 on CUDA')
+    a = _lib.AttentionArgs()
+    a.q, a.q_stride = q.data_ptr(), _lib.I64x3(*q.stride()[:3])
+    a.k, a.k_stride = k.data_ptr(), _lib.I64x3(*k.stride()[:3])
+    a.v, a.v_stride = v.data_ptr(), _lib.I64x3(*v.stride()[:3])
+    a.out, a.out_stride = out.data_ptr(), _lib.I64x3(*out.stride()[:3])
+    a.lse = lse.data_ptr()
+    a.cache_seqlens = 0 if cache_seqlens is None else cache_seqlens.data_ptr()
+    a.batch, a.queries, a.heads, a.kv_heads = batch, queries, heads, k.shape[2]
+    a.keys, a.head_dim, a.value_dim = k.shape[1], dim, v.shape[3]
+    a.scale, a.causal, a.num_splits = float(scale), int(bool(causal)), int(num_splits)
+    a.lse_masked_positive = int(bool(lse_masked_positive))
+    a.out_fp32 = int(out.dtype == torch.float32)
+    with torch.cuda.device(q.device):
+        _lib.check(_lib.load().slimkv_attention_forward_noalloc(ctypes.byref(a), _stream()))
+    return out, lse
+
+
 def rope_decode(q, k, cos, sin, query_positions, raw_indices, sink, history):
     """BF16-exact decode RoPE (``decode_ops.fused_rope`` contract).
 
