@@ -54,7 +54,7 @@ struct AttnJob {
     unsigned int* status;          // device status word
 };
 
-template <int W, int MT>
+template <int W, int MT, int BUDGET = kStageBudget>
 struct AttnCfg {
     static constexpr int ROWS = 16 * MT;
     static constexpr int KG = kWarps / MT;      // key groups in Q.K^T
@@ -67,7 +67,7 @@ struct AttnCfg {
     static constexpr bool QREG = MT <= 2;       // Q fragments held in registers
     static constexpr int TILE_BYTES = kTile * W * 2;
     static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-    static constexpr int STAGES = (kStageBudget / STAGE_BYTES) < 4 ? (kStageBudget / STAGE_BYTES) : 4;
+    static constexpr int STAGES = (BUDGET / STAGE_BYTES) < 4 ? (BUDGET / STAGE_BYTES) : 4;
     static constexpr int Q_BYTES = QREG ? 0 : ROWS * W * 2;
     static constexpr int P_BYTES = ROWS * 128;
     static constexpr int RED_FLOATS = 2 * KG * ROWS;
@@ -92,10 +92,10 @@ __device__ __forceinline__ uint32_t load_q_pair(const AttnJob& J, int b, int g, 
 
 // `rb` selects the block of ROWS query rows this CTA owns (row blocks let a
 // GQA group wider than 64 query rows be split across CTAs).
-template <int W, int MT>
+template <int W, int MT, int BUDGET = kStageBudget>
 __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int split, int rb,
                                           uint8_t* smem) {
-    using C = AttnCfg<W, MT>;
+    using C = AttnCfg<W, MT, BUDGET>;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint8_t* stages = smem;
     uint8_t* qs = smem + C::STAGES * C::STAGE_BYTES;

@@ -18,6 +18,7 @@
 #include "attn_body.cuh"
 #include "host_utils.h"
 #include "latent_decode_aux.cuh"
+#include "latent_tc.h"
 
 namespace slimkv {
 
@@ -56,8 +57,25 @@ namespace {
 struct DecodePlan {
     int wl = 0, mtl = 0, lat_row_blocks = 0, lat_rows = 0, lat_splits = 0, lat_tps = 0;
     int raw_rows = 0, raw_splits = 0, raw_tps = 0, group = 0, rvp = 0;
+    bool tc = false;   // latent branch on the tensor-memory kernel (32 query heads)
     size_t q_rot = 0, q_lat = 0, lat_o = 0, lat_lse = 0, raw_o = 0, raw_lse = 0;
 };
+
+// Raw-branch CTAs of the tensor-memory route: shallower pipeline so two CTAs
+// share an SM.
+constexpr int kRawBudget = 64 * 1024;
+
+__global__ void __launch_bounds__(kThreads, 2)
+raw_attention_kernel(const __grid_constant__ CUtensorMap rk, const __grid_constant__ CUtensorMap rv, AttnJob jr) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    if (threadIdx.x == 0) { tma_prefetch_desc(&rk); tma_prefetch_desc(&rv); }
+    jr.kmap = &rk;
+    jr.vmap = &rv;
+    const int split = blockIdx.x % jr.splits;
+    const int bg = blockIdx.x / jr.splits;
+    attn_body<128, 1, kRawBudget>(jr, bg / jr.kv_heads, bg % jr.kv_heads, split, 0, smem);
+}
 
 int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
     if (!a) return fail(SLIMKV_ERR_INVALID_ARGUMENT, "null arguments");
@@ -99,8 +117,23 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
     p.raw_tps = (raw_tiles + rs - 1) / rs;
     p.raw_splits = (raw_tiles + p.raw_tps - 1) / p.raw_tps;
     const size_t B = a->batch, L = a->length, H = a->heads;
+    p.tc = a->heads == 32 && a->latent_splits <= 0;
+    if (p.tc) {
+        // 128-key tiles, one resident CTA per SM over the whole machine; the
+        // raw branch runs as its own launch before it, two CTAs per SM.
+        const int sms = std::max(device_info().sm_count, 1);
+        const int tiles = std::max(1, (lat_len + kTcTileKeys - 1) / kTcTileKeys);
+        int s2 = std::max(1, std::min(tiles, sms / a->batch));
+        p.lat_tps = (tiles + s2 - 1) / s2;
+        p.lat_splits = (tiles + p.lat_tps - 1) / p.lat_tps;
+        p.lat_rows = 64;
+        int r2 = a->raw_splits > 0 ? a->raw_splits : std::max(1, (2 * sms) / (a->batch * a->kv_heads));
+        r2 = std::max(1, std::min(r2, raw_tiles));
+        p.raw_tps = (raw_tiles + r2 - 1) / r2;
+        p.raw_splits = (raw_tiles + p.raw_tps - 1) / p.raw_tps;
+    }
     p.q_rot = B * L * H * a->head_dim;
-    p.q_lat = B * L * H * p.wl;
+    p.q_lat = p.tc ? B * 128 * p.wl : B * L * H * p.wl;
     p.lat_o = B * p.lat_splits * p.lat_rows * p.wl;
     p.lat_lse = B * p.lat_splits * p.lat_rows;
     p.raw_o = B * a->kv_heads * p.raw_splits * p.raw_rows * 128;
@@ -204,6 +237,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     pa.rope_positions = a->rope_positions;
     pa.uk = static_cast<const __nv_bfloat16*>(a->uk);
     pa.q_rot = w.q_rot; pa.q_lat = w.q_lat;
+    pa.q_hilo = reinterpret_cast<__nv_bfloat16*>(w.q_lat); pa.hilo = p.tc ? 1 : 0;
     pa.new_k = static_cast<const __nv_bfloat16*>(a->new_k);
     pa.new_v = static_cast<const __nv_bfloat16*>(a->new_v);
     pa.new_stride = a->new_stride > 0 ? a->new_stride : (int64_t)a->kv_heads * a->head_dim;
@@ -252,8 +286,33 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     jr.group = p.group; jr.kv_heads = a->kv_heads; jr.dk = a->head_dim; jr.scale_log2 = scale_log2; jr.causal = 0;
     jr.splits = p.raw_splits; jr.tiles_per_split = p.raw_tps; jr.rows_alloc = p.raw_rows; jr.out_width = 128;
     jr.part_o = w.raw_o; jr.part_lse = w.raw_lse; jr.status = status;
-    const int n_latent = a->batch * p.lat_row_blocks * p.lat_splits;
     const int n_raw = a->batch * a->kv_heads * p.raw_splits;
+    if (p.tc) {
+        // Raw branch first (its own launch), then the latent branch on the
+        // tensor-memory kernel.
+        constexpr int rsmem = AttnCfg<128, 1, kRawBudget>::SMEM;
+        static bool raw_configured[64] = {};
+        const int dev = device_info().device;
+        if (dev >= 0 && dev < 64 && !raw_configured[dev]) {
+            if (cudaFuncSetAttribute(raw_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rsmem) !=
+                cudaSuccess)
+                return fail(SLIMKV_ERR_CUDA, "cudaFuncSetAttribute (raw) failed");
+            raw_configured[dev] = true;
+        }
+        raw_attention_kernel<<<n_raw, kThreads, rsmem, stream>>>(rk, rv, jr);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "raw attention launch failed: %s", cudaGetErrorString(e));
+        TcLaunch tl{};
+        tl.batch = a->batch; tl.length = a->length; tl.rank_k = a->rank_k; tl.rank_v = a->rank_v;
+        tl.width = p.wl; tl.lat_capacity = a->lat_capacity;
+        tl.lat_k = a->lat_k; tl.lat_v = a->lat_v;
+        tl.lat_stride_batch = a->lat_stride_batch; tl.lat_stride_row = a->lat_stride_row;
+        tl.q_hilo = w.q_lat; tl.latent_len = a->latent_len; tl.query_len = a->query_len; tl.scale = a->scale;
+        tl.splits = p.lat_splits; tl.tiles_per_split = p.lat_tps; tl.rows_alloc = p.lat_rows;
+        tl.part_o = w.lat_o; tl.part_lse = w.lat_lse; tl.status = status;
+        if ((rc = launch_latent_tc(tl, stream))) return rc;
+    } else {
+    const int n_latent = a->batch * p.lat_row_blocks * p.lat_splits;
     switch (p.wl) {
         case 128: rc = launch_wl<128>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
         case 192: rc = launch_wl<192>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
@@ -261,6 +320,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         default: rc = launch_wl<320>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
     }
     if (rc) return rc;
+    }
 
     // 3. merge
     MergeArgs ma{};

@@ -26,7 +26,9 @@ struct PrologueArgs {
     int rope_positions;
     const __nv_bfloat16* uk;
     __nv_bfloat16* q_rot;   // [B, L, H, D]
-    __half* q_lat;          // [B, L, H, width]
+    __half* q_lat;          // [B, L, H, width] fp16 (split-KV path), or
+    __nv_bfloat16* q_hilo;  // [B][128][width] bf16 hi/lo rows (tensor-memory path)
+    int hilo;
     const __nv_bfloat16* new_k;
     const __nv_bfloat16* new_v;
     int64_t new_stride;
@@ -157,18 +159,31 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
             mma_f16(acc[2 * np + 1], af, b2, b3);
         }
     }
-    // 4. q_lat (fp16) for the valid rows.
+    // 4. q_lat for the valid rows: fp16, or a bf16 hi/lo pair (q = hi + lo)
+    //    at rows l*64 + h (hi) and l*64 + 32 + h (lo) of the sequence's block.
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
         const int r = 16 * mt + (lane >> 2) + 8 * hh;
         const int s = r / rps, rr = r - s * rps, l = rr / a.group, j = rr - l * a.group;
         const int b = b0 + s;
         if (s >= a.seq_per_cta || b >= a.batch || l >= (a.qlens ? a.qlens[b] : a.length)) continue;
-        __half* dst = a.q_lat + (((int64_t)b * a.length + l) * a.heads + g * a.group + j) * a.width + cc * 64 +
-                      nh * 32 + (lane & 3) * 2;
+        const int col = cc * 64 + nh * 32 + (lane & 3) * 2;
+        if (a.hilo) {
+            __nv_bfloat16* hi = a.q_hilo + ((int64_t)b * 128 + l * 64 + g * a.group + j) * a.width + col;
+            __nv_bfloat16* lo = hi + 32 * a.width;
 #pragma unroll
-        for (int n = 0; n < 4; ++n)
-            *reinterpret_cast<uint32_t*>(dst + n * 8) = pack_f16x2(acc[n][2 * hh], acc[n][2 * hh + 1]);
+            for (int n = 0; n < 4; ++n) {
+                const float x0 = acc[n][2 * hh], x1 = acc[n][2 * hh + 1];
+                const float h0 = bf16_round(x0), h1 = bf16_round(x1);
+                *reinterpret_cast<uint32_t*>(hi + n * 8) = pack_bf16x2(h0, h1);
+                *reinterpret_cast<uint32_t*>(lo + n * 8) = pack_bf16x2(x0 - h0, x1 - h1);
+            }
+        } else {
+            __half* dst = a.q_lat + (((int64_t)b * a.length + l) * a.heads + g * a.group + j) * a.width + col;
+#pragma unroll
+            for (int n = 0; n < 4; ++n)
+                *reinterpret_cast<uint32_t*>(dst + n * 8) = pack_f16x2(acc[n][2 * hh], acc[n][2 * hh + 1]);
+        }
     }
     if (cc != 0) return;
     // 5. Append this step's raw token of head g: rotated key, value, pre-RoPE key.
