@@ -26,6 +26,8 @@ attention_split_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_co
 }
 
 // Merge split partials into the final output and LSE (one warp per row).
+// Lane s holds split s's LSE and weight; each split's columns are then read
+// with independent loads.
 __global__ void __launch_bounds__(256)
 attention_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse, int splits,
                          int rows_alloc, int width, int rows_total, int group, int kv_heads, int value_dim,
@@ -37,29 +39,52 @@ attention_combine_kernel(const float* __restrict__ part_o, const float* __restri
     const int row = blockIdx.y * 8 + warp;
     if (row >= rows_total) return;
     const int64_t base = (int64_t)bg * splits * rows_alloc + row;
-    float m = -INFINITY;
-    for (int s = 0; s < splits; ++s) m = fmaxf(m, part_lse[base + (int64_t)s * rows_alloc]);
     const int l = row / group, h = g * group + (row - l * group);
     const int64_t off = b * o_sb + l * o_sl + h * o_sh;
     auto store = [&](int d, float x) {
         if (out_fp32) static_cast<float*>(out)[off + d] = x;
         else static_cast<__nv_bfloat16*>(out)[off + d] = __float2bfloat16_rn(x);
     };
+    // splits <= 128: each lane owns up to four splits
+    float my[4], m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int s = lane + 32 * j;
+        my[j] = s < splits ? part_lse[base + (int64_t)s * rows_alloc] : -INFINITY;
+        m = fmaxf(m, my[j]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (m == -INFINITY) {
         for (int d = lane; d < value_dim; d += 32) store(d, 0.f);
         if (lane == 0) lse_out[((int64_t)b * heads + h) * queries + l] = masked_lse;
         return;
     }
-    float total = 0.f;
-    for (int s = 0; s < splits; ++s) total += expf(part_lse[base + (int64_t)s * rows_alloc] - m);
+    float w[4], total = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        w[j] = my[j] == -INFINITY ? 0.f : expf(my[j] - m);
+        total += w[j];
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
     const float inv = 1.f / total;
-    for (int d = lane; d < value_dim; d += 32) {
-        float acc = 0.f;
+    for (int d0 = 0; d0 < value_dim; d0 += 32 * 4) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int s = 0; s < splits; ++s) {
-            const float w = expf(part_lse[base + (int64_t)s * rows_alloc] - m);
-            acc += w * part_o[(base + (int64_t)s * rows_alloc) * width + d];
+            const float ws = __shfl_sync(0xffffffffu, w[s >> 5], s & 31);
+            const float* src = part_o + (base + (int64_t)s * rows_alloc) * width;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int d = d0 + lane + 32 * i;
+                if (d < value_dim) acc[i] = fmaf(ws, src[d], acc[i]);
+            }
         }
-        store(d, acc * inv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int d = d0 + lane + 32 * i;
+            if (d < value_dim) store(d, acc[i] * inv);
+        }
     }
     if (lane == 0) lse_out[((int64_t)b * heads + h) * queries + l] = m + logf(total);
 }
@@ -100,7 +125,7 @@ int plan_attention(const slimkv_attention_args* a, Plan& p) {
         const int sms = std::max(device_info().sm_count, 1);
         splits = std::max(1, sms / base);
     }
-    splits = std::max(1, std::min(splits, n_tiles));
+    splits = std::max(1, std::min({splits, n_tiles, 128}));   // the combine handles <= 128 splits
     p.tiles_per_split = (n_tiles + splits - 1) / splits;
     p.splits = (n_tiles + p.tiles_per_split - 1) / p.tiles_per_split;
     p.part_o = (size_t)a->batch * a->kv_heads * p.splits * p.rows_alloc * p.width;

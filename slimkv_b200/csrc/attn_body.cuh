@@ -303,9 +303,16 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
         if (!mbar_wait(&bars[C::STAGES + s], par)) wait_failed = true;
 
         // ---- O += P V for this warp's columns ----
+        // V rows past the sequence length hold whatever the cache has there;
+        // their P is zero, and zeroing the operand as well keeps a non-finite
+        // stale value from turning 0 * x into NaN.
         const int d0 = warp * C::DPW;
+        const int vlim = n_keys - t * kTile;
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk) {
+            const int kq = kk * 16 + (lane & 3) * 2;
+            const uint32_t m_lo = (kq < vlim ? 0xffffu : 0u) | (kq + 1 < vlim ? 0xffff0000u : 0u);
+            const uint32_t m_hi = (kq + 8 < vlim ? 0xffffu : 0u) | (kq + 9 < vlim ? 0xffff0000u : 0u);
             uint32_t a[MT][4];
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
@@ -322,8 +329,8 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
                 const int unit = (dim & 63) >> 3;
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4_t(vt + (dim >> 6) * (kTile * 128) + key * 128 + (((unit ^ key) & 7) << 4), b0, b1, b2, b3);
-                b0 = bf16x2_to_f16x2(b0); b1 = bf16x2_to_f16x2(b1);
-                b2 = bf16x2_to_f16x2(b2); b3 = bf16x2_to_f16x2(b3);
+                b0 = bf16x2_to_f16x2(b0) & m_lo; b1 = bf16x2_to_f16x2(b1) & m_hi;
+                b2 = bf16x2_to_f16x2(b2) & m_lo; b3 = bf16x2_to_f16x2(b3) & m_hi;
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
                     mma_f16(o[mt][nt], a[mt], b0, b1);
@@ -338,7 +345,7 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
                 const int unit = (dim & 63) >> 3;
                 uint32_t b0, b1;
                 ldsm_x2_t(vt + (dim >> 6) * (kTile * 128) + key * 128 + (((unit ^ key) & 7) << 4), b0, b1);
-                b0 = bf16x2_to_f16x2(b0); b1 = bf16x2_to_f16x2(b1);
+                b0 = bf16x2_to_f16x2(b0) & m_lo; b1 = bf16x2_to_f16x2(b1) & m_hi;
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) mma_f16(o[mt][nt], a[mt], b0, b1);
             }

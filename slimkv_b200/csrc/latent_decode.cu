@@ -110,8 +110,9 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
     int ls = a->latent_splits > 0 ? a->latent_splits
                                   : int(std::ceil(lat_tiles * lat_tile_bytes / std::max(per_cta, 1.0)));
     int rs = a->raw_splits > 0 ? a->raw_splits : int(std::ceil(raw_tiles * raw_tile_bytes / std::max(per_cta, 1.0)));
-    ls = std::max(1, std::min(ls, lat_tiles));
-    rs = std::max(1, std::min(rs, raw_tiles));
+    // The merge kernel combines at most 32 splits per branch.
+    ls = std::max(1, std::min({ls, lat_tiles, 32}));
+    rs = std::max(1, std::min({rs, raw_tiles, 32}));
     p.lat_tps = (lat_tiles + ls - 1) / ls;
     p.lat_splits = (lat_tiles + p.lat_tps - 1) / p.lat_tps;
     p.raw_tps = (raw_tiles + rs - 1) / rs;
@@ -123,12 +124,12 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
         // raw branch runs as its own launch before it, two CTAs per SM.
         const int sms = std::max(device_info().sm_count, 1);
         const int tiles = std::max(1, (lat_len + kTcTileKeys - 1) / kTcTileKeys);
-        int s2 = std::max(1, std::min(tiles, sms / a->batch));
+        int s2 = std::max(1, std::min({tiles, sms / a->batch, 32}));
         p.lat_tps = (tiles + s2 - 1) / s2;
         p.lat_splits = (tiles + p.lat_tps - 1) / p.lat_tps;
         p.lat_rows = 64;
         int r2 = a->raw_splits > 0 ? a->raw_splits : std::max(1, (2 * sms) / (a->batch * a->kv_heads));
-        r2 = std::max(1, std::min(r2, raw_tiles));
+        r2 = std::max(1, std::min({r2, raw_tiles, 32}));
         p.raw_tps = (raw_tiles + r2 - 1) / r2;
         p.raw_splits = (raw_tiles + p.raw_tps - 1) / p.raw_tps;
     }
@@ -232,7 +233,9 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     pa.q_sb = a->q_stride[0]; pa.q_sl = a->q_stride[1]; pa.q_sh = a->q_stride[2];
     pa.batch = a->batch; pa.length = a->length; pa.heads = a->heads; pa.kv_heads = a->kv_heads;
     pa.dim = a->head_dim; pa.rank_k = a->rank_k; pa.rank_v = a->rank_v; pa.width = p.wl; pa.group = p.group;
-    pa.seq_per_cta = kProRows / rps;
+    // About 16 query rows per CTA: enough CTAs to spread the staging loads
+    // over the machine (the MMA tile still has 64 rows; unused rows are zero).
+    pa.seq_per_cta = std::max(1, std::min(kProRows / rps, 16 / rps));
     pa.qpos = a->qpos; pa.qlens = a->query_len; pa.cos = a->cos; pa.sin = a->sin;
     pa.rope_positions = a->rope_positions;
     pa.uk = static_cast<const __nv_bfloat16*>(a->uk);
@@ -333,15 +336,15 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     ma.uv_bias = static_cast<const __nv_bfloat16*>(a->uv_bias);
     ma.qlens = a->query_len; ma.batch = a->batch; ma.length = a->length; ma.heads = a->heads;
     ma.kv_heads = a->kv_heads; ma.dim = a->head_dim; ma.rank_v = a->rank_v; ma.rank_v_pad = p.rvp;
-    ma.group = p.group; ma.seq_per_cta = kMaxRows / rps; ma.scale = a->scale;
+    ma.group = p.group; ma.seq_per_cta = 1; ma.scale = a->scale;
     ma.out = a->out; ma.out_fp32 = a->out_fp32; ma.o_sb = a->out_stride[0]; ma.o_sl = a->out_stride[1];
-    const size_t msmem = 1024 + size_t(128 + 16) * p.rvp * 2 + size_t(16) * a->head_dim * 4 + 32 * 4;
+    const size_t msmem = merge_smem_bytes(p.rvp, a->head_dim);
     {
         static bool configured[64] = {};
         const int dev = device_info().device;
         if (dev >= 0 && dev < 64 && !configured[dev]) {
             if (cudaFuncSetAttribute(decode_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     int(1024 + 144 * 320 * 2 + 16 * 128 * 4 + 128)) != cudaSuccess)
+                                     int(merge_smem_bytes(320, 128))) != cudaSuccess)
                 return fail(SLIMKV_ERR_CUDA, "cudaFuncSetAttribute failed");
             configured[dev] = true;
         }

@@ -58,12 +58,14 @@ __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v 
 __device__ __forceinline__ void rope8(const __nv_bfloat16* row, int d0, int half, const float* cos_row,
                                       const float* sin_row, float out[8]) {
     const int pd = d0 < half ? d0 + half : d0 - half;
-    const uint4 xv = *reinterpret_cast<const uint4*>(row + d0);
-    const uint4 pv = *reinterpret_cast<const uint4*>(row + pd);
-    const float4 c0 = *reinterpret_cast<const float4*>(cos_row + d0);
-    const float4 c1 = *reinterpret_cast<const float4*>(cos_row + d0 + 4);
-    const float4 s0 = *reinterpret_cast<const float4*>(sin_row + d0);
-    const float4 s1 = *reinterpret_cast<const float4*>(sin_row + d0 + 4);
+    // Read-only loads (ld.global.nc): the compiler may issue them ahead of
+    // the caller's stores.
+    const uint4 xv = __ldg(reinterpret_cast<const uint4*>(row + d0));
+    const uint4 pv = __ldg(reinterpret_cast<const uint4*>(row + pd));
+    const float4 c0 = __ldg(reinterpret_cast<const float4*>(cos_row + d0));
+    const float4 c1 = __ldg(reinterpret_cast<const float4*>(cos_row + d0 + 4));
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(sin_row + d0));
+    const float4 s1 = __ldg(reinterpret_cast<const float4*>(sin_row + d0 + 4));
     const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, pw[4] = {pv.x, pv.y, pv.z, pv.w};
     const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
     const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
@@ -108,7 +110,7 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
     for (int i = tid; i < 128 * 8; i += 256) {
         const int d = i >> 3, u = i & 7, col = cc * 64 + u * 8;
         uint4 v = make_uint4(0, 0, 0, 0);
-        if (col < a.rank_k) v = widen8(*reinterpret_cast<const uint4*>(a.uk + ((int64_t)g * a.dim + d) * a.rank_k + col));
+        if (col < a.rank_k) v = widen8(__ldg(reinterpret_cast<const uint4*>(a.uk + ((int64_t)g * a.dim + d) * a.rank_k + col)));
         *reinterpret_cast<uint4*>(s_b + sw128(d, u * 8)) = v;
     }
     // 2. RoPE of the CTA's query rows -> shared (fp16, exact copies of bf16).
@@ -160,17 +162,20 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
         }
     }
     // 4. q_lat for the valid rows: fp16, or a bf16 hi/lo pair (q = hi + lo)
-    //    at rows l*64 + h (hi) and l*64 + 32 + h (lo) of the sequence's block.
+    //    at rows l*32 + h (hi) and 32*nq + l*32 + h (lo) of the sequence's
+    //    block, nq being the sequence's query count.
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
         const int r = 16 * mt + (lane >> 2) + 8 * hh;
         const int s = r / rps, rr = r - s * rps, l = rr / a.group, j = rr - l * a.group;
         const int b = b0 + s;
-        if (s >= a.seq_per_cta || b >= a.batch || l >= (a.qlens ? a.qlens[b] : a.length)) continue;
+        if (s >= a.seq_per_cta || b >= a.batch) continue;
+        const int nq = a.qlens ? a.qlens[b] : a.length;
+        if (l >= nq) continue;
         const int col = cc * 64 + nh * 32 + (lane & 3) * 2;
         if (a.hilo) {
-            __nv_bfloat16* hi = a.q_hilo + ((int64_t)b * 128 + l * 64 + g * a.group + j) * a.width + col;
-            __nv_bfloat16* lo = hi + 32 * a.width;
+            __nv_bfloat16* hi = a.q_hilo + ((int64_t)b * 128 + l * 32 + g * a.group + j) * a.width + col;
+            __nv_bfloat16* lo = hi + 32 * nq * a.width;
 #pragma unroll
             for (int n = 0; n < 4; ++n) {
                 const float x0 = acc[n][2 * hh], x1 = acc[n][2 * hh + 1];
@@ -204,8 +209,8 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
             rope8(k, d0, half, a.cos + (int64_t)pos * a.dim, a.sin + (int64_t)pos * a.dim, o);
             const int64_t dst = b * a.raw_sb + row * a.raw_st + (int64_t)g * a.dim + d0;
             *reinterpret_cast<uint4*>(a.raw_k_rot + dst) = pack8_bf16(o);
-            *reinterpret_cast<uint4*>(a.raw_v + dst) = *reinterpret_cast<const uint4*>(v + d0);
-            if (a.raw_k_pre) *reinterpret_cast<uint4*>(a.raw_k_pre + dst) = *reinterpret_cast<const uint4*>(k + d0);
+            *reinterpret_cast<uint4*>(a.raw_v + dst) = __ldg(reinterpret_cast<const uint4*>(v + d0));
+            if (a.raw_k_pre) *reinterpret_cast<uint4*>(a.raw_k_pre + dst) = __ldg(reinterpret_cast<const uint4*>(k + d0));
         }
     }
     // 6. Append the Beacon latent pair of rows that insert one this step.
@@ -240,38 +245,21 @@ struct MergeArgs {
     void* out; int out_fp32; int64_t o_sb, o_sl;
 };
 
-// Split combine of `splits` normalised partials of one row: lanes cover the
-// columns; the split loop's loads are independent of each other.
-template <int MAXC>
-__device__ __forceinline__ float combine_lanes(const float* o, const float* lse, int splits, int64_t pitch, int width,
-                                               int cols, int lane, float acc[MAXC]) {
-    float m = -INFINITY;
-    for (int s = lane; s < splits; s += 32) m = fmaxf(m, lse[s * pitch]);
-#pragma unroll
-    for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-#pragma unroll
-    for (int i = 0; i < MAXC; ++i) acc[i] = 0.f;
-    if (m == -INFINITY) return -INFINITY;
-    float total = 0.f;
-    for (int s = 0; s < splits; ++s) {
-        const float w = expf(lse[s * pitch] - m);
-        total += w;
-        const float* row = o + s * pitch * width;
-#pragma unroll
-        for (int i = 0; i < MAXC; ++i) {
-            const int c = lane + 32 * i;
-            if (c < cols) acc[i] = fmaf(w, row[c], acc[i]);
-        }
-    }
-    const float inv = 1.f / total;
-#pragma unroll
-    for (int i = 0; i < MAXC; ++i) acc[i] *= inv;
-    return m + logf(total);
+// Dynamic shared memory of decode_merge_kernel for a padded value rank.
+__host__ __device__ constexpr size_t merge_smem_bytes(int rank_v_pad, int dim) {
+    return 1024 + size_t(128 + 16) * rank_v_pad * 2 + size_t(16) * dim * 4 + 32 * 4 + 2 * 16 * 32 * 4;
 }
 
-// grid (Hkv, ceil(B / seq_per_cta)), 256 threads, dynamic shared memory
-// 128*Rvp*2 + 16*Rvp*2 + 16*D*4 + 128 bytes.  CTA (g, bb) merges the 16 rows
+// grid (Hkv, ceil(B / seq_per_cta)), 256 threads, merge_smem_bytes() of
+// dynamic shared memory.  CTA (g, bb) merges the (<= 16) query rows
 // (seq_per_cta sequences x L x group) of KV head g.
+//   1. U_v[g] -> shared (fp16) as the MMA's column-major B operand.
+//   2. One warp per row: lane s holds split s's LSE of each branch and turns
+//      it into a normalised weight (splits <= 32); the row's LSEs (latent one
+//      shifted by scale * q . b_k) go to shared memory.
+//   3. All threads: weighted split sums over (row, 4-column) items, every
+//      split's load independent of the others.
+//   4. Up-projection on the tensor cores, bias, LSE merge, store.
 __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -280,63 +268,137 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
     uint8_t* s_a = s_b + 128 * rvp * 2;                 // o_lat: rvp/64 chunks [16 x 64] fp16
     float* s_raw = reinterpret_cast<float*>(s_a + 16 * rvp * 2);   // [16][D]
     float* s_lse = s_raw + 16 * a.dim;                  // [2][16]: latent, raw
+    float* s_w = s_lse + 32;                            // [2][16][32] split weights: latent, raw
     const int g = blockIdx.x, bb = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rps = a.length * a.group, b0 = bb * a.seq_per_cta;
+    auto row_info = [&](int r, int& b, int& l, int& h, int& rr) -> bool {
+        const int s = r / rps;
+        rr = r - s * rps;
+        l = rr / a.group;
+        b = b0 + s;
+        h = g * a.group + (rr - l * a.group);
+        return s < a.seq_per_cta && b < a.batch && l < (a.qlens ? a.qlens[b] : a.length);
+    };
 
-    // 1. Stage U_v[g] (rows d, columns c) as the MMA's column-major B operand.
+    // 1. Stage U_v[g] (rows d, columns c) as the MMA's column-major B operand:
+    //    batches of ten independent read-only loads, then the stores.
     const int units = rvp / 8;
-    for (int i = tid; i < 128 * units; i += 256) {
-        const int d = i / units, u = i - d * units, col = u * 8;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (col < a.rank_v) v = widen8(*reinterpret_cast<const uint4*>(a.uv + ((int64_t)g * a.dim + d) * a.rank_v + col));
-        *reinterpret_cast<uint4*>(s_b + (u >> 3) * (128 * 128) + sw128(d, (u & 7) * 8)) = v;
+#pragma unroll 1
+    for (int i0 = 0; i0 < 128 * units; i0 += 2560) {
+        uint4 v[10];
+#pragma unroll
+        for (int k = 0; k < 10; ++k) {
+            const int i = i0 + k * 256 + tid, d = i / units, col = (i - d * units) * 8;
+            v[k] = make_uint4(0, 0, 0, 0);
+            if (i < 128 * units && col < a.rank_v)
+                v[k] = __ldg(reinterpret_cast<const uint4*>(a.uv + ((int64_t)g * a.dim + d) * a.rank_v + col));
+        }
+#pragma unroll
+        for (int k = 0; k < 10; ++k) {
+            const int i = i0 + k * 256 + tid, d = i / units, u = i - d * units;
+            if (i < 128 * units)
+                *reinterpret_cast<uint4*>(s_b + (u >> 3) * (128 * 128) + sw128(d, (u & 7) * 8)) = widen8(v[k]);
+        }
     }
-    // 2. Combine both branches' split partials, one warp per row.
+    // 2. Split weights and LSEs per row.
     for (int r = warp; r < 16; r += 8) {
-        const int s = r / rps, rr = r - s * rps, l = rr / a.group, j = rr - l * a.group;
-        const int b = b0 + s, h = g * a.group + j;
-        const bool valid = s < a.seq_per_cta && b < a.batch && l < (a.qlens ? a.qlens[b] : a.length);
-        float acc[10];
-        float lse_l = -INFINITY, lse_r = -INFINITY;
-        if (valid) {
-            const int64_t lb = (int64_t)b * a.lat_splits * a.lat_rows + l * a.heads + h;
-            lse_l = combine_lanes<10>(a.lat_o + lb * a.lat_width, a.lat_lse + lb, a.lat_splits, a.lat_rows,
-                                      a.lat_width, rvp, lane, acc);
-        } else {
+        int b, l, h, rr;
+        const bool valid = row_info(r, b, l, h, rr);
+        float lse_br[2];
 #pragma unroll
-            for (int i = 0; i < 10; ++i) acc[i] = 0.f;
+        for (int br = 0; br < 2; ++br) {
+            float my = -INFINITY;
+            if (valid && lane < (br ? a.raw_splits : a.lat_splits))
+                my = br ? __ldg(a.raw_lse + (((int64_t)b * a.kv_heads + g) * a.raw_splits + lane) * a.raw_rows + rr)
+                        : __ldg(a.lat_lse + ((int64_t)b * a.lat_splits + lane) * a.lat_rows + l * a.heads + h);
+            float m = my;
+#pragma unroll
+            for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+            const float w = (m == -INFINITY || my == -INFINITY) ? 0.f : expf(my - m);
+            float total = w;
+#pragma unroll
+            for (int off = 16; off; off >>= 1) total += __shfl_xor_sync(0xffffffffu, total, off);
+            s_w[(br * 16 + r) * 32 + lane] = total > 0.f ? w / total : 0.f;
+            lse_br[br] = total > 0.f ? m + logf(total) : -INFINITY;
         }
+        if (valid && a.uk_bias && lse_br[0] != -INFINITY) {
+            // Latent LSE shift by scale * q . b_k (fa2_decode.py:157-160).
+            const __nv_bfloat16* q = a.q_rot + (((int64_t)b * a.length + l) * a.heads + h) * a.dim;
+            const __nv_bfloat16* bk = a.uk_bias + (int64_t)g * a.dim;
+            float dot = 0.f;
+            for (int d = lane; d < a.dim; d += 32) dot += __bfloat162float(q[d]) * __bfloat162float(bk[d]);
 #pragma unroll
-        for (int i = 0; i < 10; ++i) {
-            const int c = lane + 32 * i;
-            if (c < rvp)
-                *reinterpret_cast<__half*>(s_a + (c >> 6) * (16 * 128) + sw128(r, c & 63)) = __float2half_rn(acc[i]);
+            for (int off = 16; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+            lse_br[0] += dot * a.scale;
         }
-        float racc[4];
-        if (valid) {
-            const int64_t rb = ((int64_t)(b * a.kv_heads + g) * a.raw_splits) * a.raw_rows + rr;
-            lse_r = combine_lanes<4>(a.raw_o + rb * a.dim, a.raw_lse + rb, a.raw_splits, a.raw_rows, a.dim, a.dim,
-                                     lane, racc);
-            if (a.uk_bias && lse_l != -INFINITY) {
-                // Latent LSE shift by scale * q . b_k (fa2_decode.py:157-160).
-                const __nv_bfloat16* q = a.q_rot + (((int64_t)b * a.length + l) * a.heads + h) * a.dim;
-                const __nv_bfloat16* bk = a.uk_bias + (int64_t)g * a.dim;
-                float dot = 0.f;
-                for (int d = lane; d < a.dim; d += 32) dot += __bfloat162float(q[d]) * __bfloat162float(bk[d]);
-#pragma unroll
-                for (int off = 16; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-                lse_l += dot * a.scale;
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) racc[i] = 0.f;
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) s_raw[r * a.dim + lane + 32 * i] = racc[i];
         if (lane == 0) {
-            s_lse[r] = lse_l;
-            s_lse[16 + r] = lse_r;
+            s_lse[r] = lse_br[0];
+            s_lse[16 + r] = lse_br[1];
+        }
+    }
+    __syncthreads();
+    // 3a. Latent branch: o_lat[r, c:c+4] = sum_s w_s * part_s[r, c:c+4] -> fp16 A operand.
+    {
+        const int c4n = rvp / 4;
+        const int64_t pitch = (int64_t)a.lat_rows * a.lat_width;
+        for (int it = tid; it < 16 * c4n; it += 256) {
+            const int r = it / c4n, c = (it - r * c4n) * 4;
+            int b, l, h, rr;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (row_info(r, b, l, h, rr) && c < a.lat_width) {
+                const float* src = a.lat_o + ((int64_t)b * a.lat_splits * a.lat_rows + l * a.heads + h) * a.lat_width + c;
+                const float* w = s_w + r * 32;
+                int s = 0;
+                for (; s + 8 <= a.lat_splits; s += 8) {
+                    float4 x[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) x[u] = __ldg(reinterpret_cast<const float4*>(src + (s + u) * pitch));
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        acc.x = fmaf(w[s + u], x[u].x, acc.x); acc.y = fmaf(w[s + u], x[u].y, acc.y);
+                        acc.z = fmaf(w[s + u], x[u].z, acc.z); acc.w = fmaf(w[s + u], x[u].w, acc.w);
+                    }
+                }
+                for (; s < a.lat_splits; ++s) {
+                    const float4 x = __ldg(reinterpret_cast<const float4*>(src + s * pitch));
+                    acc.x = fmaf(w[s], x.x, acc.x); acc.y = fmaf(w[s], x.y, acc.y);
+                    acc.z = fmaf(w[s], x.z, acc.z); acc.w = fmaf(w[s], x.w, acc.w);
+                }
+            }
+            *reinterpret_cast<uint2*>(s_a + (c >> 6) * (16 * 128) + sw128(r, c & 63)) =
+                make_uint2(pack_f16x2(acc.x, acc.y), pack_f16x2(acc.z, acc.w));
+        }
+    }
+    // 3b. Raw branch: fp32 combined output rows.
+    {
+        const int c4n = a.dim / 4;
+        const int64_t pitch = (int64_t)a.raw_rows * a.dim;
+        for (int it = tid; it < 16 * c4n; it += 256) {
+            const int r = it / c4n, c = (it - r * c4n) * 4;
+            int b, l, h, rr;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (row_info(r, b, l, h, rr)) {
+                const float* src = a.raw_o + ((((int64_t)b * a.kv_heads + g) * a.raw_splits) * a.raw_rows + rr) * a.dim + c;
+                const float* w = s_w + (16 + r) * 32;
+                int s = 0;
+                for (; s + 8 <= a.raw_splits; s += 8) {
+                    float4 x[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) x[u] = __ldg(reinterpret_cast<const float4*>(src + (s + u) * pitch));
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        acc.x = fmaf(w[s + u], x[u].x, acc.x); acc.y = fmaf(w[s + u], x[u].y, acc.y);
+                        acc.z = fmaf(w[s + u], x[u].z, acc.z); acc.w = fmaf(w[s + u], x[u].w, acc.w);
+                    }
+                }
+                for (; s < a.raw_splits; ++s) {
+                    const float4 x = __ldg(reinterpret_cast<const float4*>(src + s * pitch));
+                    acc.x = fmaf(w[s], x.x, acc.x); acc.y = fmaf(w[s], x.y, acc.y);
+                    acc.z = fmaf(w[s], x.z, acc.z); acc.w = fmaf(w[s], x.w, acc.w);
+                }
+            }
+            *reinterpret_cast<float4*>(s_raw + r * a.dim + c) = acc;
         }
     }
     __syncthreads();

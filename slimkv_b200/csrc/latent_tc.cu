@@ -1,26 +1,38 @@
 // Latent-branch split-KV decode attention on the 5th-generation tensor cores.
 //
 // One CTA owns (sequence b, split): a contiguous range of 128-key tiles of
-// the sequence's latent cache, against all query rows of the step (32 heads x
-// 1 or 2 queries).  Swap-AB so the keys fill the MMA's M = 128:
+// the sequence's latent cache against all query rows of the step (32 heads x
+// nq = 1 or 2 queries).  Swap-AB so the keys fill M:
 //
-//   S^T [128 keys x Np]  = K_tile [128 x Rk] . Q^T           (K-major A and B)
-//   O^T [Rv x Np]       += V_tile^T [Rv x 128] . P^T          (MN-major A and B)
+//   S^T [128 keys x 64]      = K_tile . Q^T                  (M=128, K-major A/B)
+//   O^T [64 dims x 64] (x5) += V_chunk^T . P^T               (M=64, MN-major A/B)
 //
-// Q and P are carried as bf16 hi/lo pairs (q = hi + lo to ~16 mantissa bits)
-// so the bf16 tensor cores keep fp32-level accuracy without converting the
-// bf16 K/V tiles: Np = 64 per query (32 heads hi | 32 heads lo).  Scores and
-// the output accumulate in tensor memory (TMEM); softmax runs with one key per
-// thread reading its TMEM lane, column maxima/sums via warp transpose-reduce,
-// and a lazy rescale (the running max only moves when a column max exceeds it
-// by 2^8), so O^T rarely needs a TMEM read-modify-write.
+// Q and P are split into bf16 hi + lo (x = hi + lo to ~16 mantissa bits), so
+// the bf16 K/V tiles are used as stored and the result keeps fp32-level
+// accuracy.  How the split uses the 64 MMA columns depends on nq:
+//   nq = 1: hi and lo are separate columns (cols 0-31 hi, 32-63 lo, one MMA
+//           per k-step); the softmax and the epilogue add the two halves.
+//   nq = 2: columns are (query, head); hi and lo accumulate into the same
+//           columns (two MMAs per k-step).
+// A single-query CTA therefore needs half the Q and P buffers and gives the
+// space to the K/V ring (10 slots instead of 7): the stream is bound by the
+// bytes in flight against the loaded HBM latency.
 //
-// Warp roles (7 warps): 0 = K TMA producer (ring of 3 [128 x 64] chunks),
-// 1 = Q + V TMA producer (ring of 2 [128 x 128] blocks), 2 = TMEM allocator and
-// single-thread MMA issuer, 3-6 = softmax / epilogue (TMEM lane quarters
-// 3, 0, 1, 2).  TMA loads use the 128-byte swizzle and no cluster multicast.
-// Every wait is bounded: on expiry the CTA reports SLIMKV_DEVICE_TIMEOUT,
-// drains its copies and MMAs (bounded), frees TMEM and returns.
+// K and V stream through one ring of 16 KB [128 keys x 64 columns] chunks in
+// exactly the order the MMAs consume them (S(j+1) is issued before P.V(j) so
+// scores of the next tile overlap the softmax of this one; S is
+// double-buffered in TMEM).  Softmax: one key per thread reading its TMEM
+// lane, column maxima and sums via warp transpose-reduce, and a lazy rescale
+// (the running max moves only when a column max exceeds it by 2^8, so the
+// TMEM read-modify-write of O^T is rare).  The epilogue stages the normalised
+// partial output through shared memory and stores whole rows.
+//
+// Warp roles (7 warps): 0 = TMA producer (Q once, then the K/V ring),
+// 1 = idle helper, 2 = TMEM allocator and single-thread MMA issuer,
+// 3-6 = softmax / epilogue (TMEM lane quarters 3, 0, 1, 2).  TMA loads use the
+// 128-byte swizzle and no cluster multicast.  Every wait is bounded: on expiry
+// the CTA reports SLIMKV_DEVICE_TIMEOUT, drains its copies and MMAs
+// (bounded), frees TMEM and returns.
 #include <algorithm>
 
 #include "common.cuh"
@@ -33,27 +45,27 @@ namespace {
 
 constexpr int kKeys = 128;
 constexpr int kThreads7 = 224;
-constexpr int kKSlots = 3;
-constexpr int kVSlots = 2;
-constexpr uint32_t kChunkBytes = 128 * 128;          // one [128 rows x 64 bf16] swizzled box
-constexpr int kMaxKChunks = 5;                      // rank_k <= 320
+constexpr int kRingMax = 10;
+constexpr uint32_t kChunkBytes = 128 * 128;          // [128 keys x 64 bf16], 128-byte swizzle
+constexpr uint32_t kQChunkBytes = 64 * 128;          // [64 rows x 64 bf16]
+constexpr int kMaxChunks = 5;                        // ranks <= 320
 constexpr float kLazyLog2 = 8.f;
 constexpr uint32_t kTmemCols = 512;
+constexpr int kN = 64;                               // MMA N
 
-constexpr uint32_t kOffK = 0;
-constexpr uint32_t kOffV = kOffK + kKSlots * kChunkBytes;
-constexpr uint32_t kOffQ = kOffV + kVSlots * 2 * kChunkBytes;
-constexpr uint32_t kOffP = kOffQ + kMaxKChunks * kChunkBytes;
-constexpr uint32_t kOffMisc = kOffP + 2 * kChunkBytes;
+// Shared memory: ring (nq = 1: 10 slots, nq = 2: 7) | Q (nq x 40 KB) | P
+// (nq x 16 KB) | ... | Misc at a fixed offset past the larger layout.
+__host__ __device__ constexpr int ring_slots(int nq) { return nq == 1 ? 10 : 7; }
+constexpr uint32_t kOffMisc = 7 * kChunkBytes + 2 * kMaxChunks * kQChunkBytes + 2 * kChunkBytes;
+static_assert(10 * kChunkBytes + kMaxChunks * kQChunkBytes + kChunkBytes <= kOffMisc, "single-query layout");
 
 struct Misc {
-    uint64_t kfull[kKSlots], kempty[kKSlots], vfull[kVSlots], vempty[kVSlots];
-    uint64_t qfull, sfull, sempty, pfull, odone, final_mma;
+    uint64_t full[kRingMax], empty[kRingMax];
+    uint64_t qfull, sfull[2], sempty[2], pfull, odone, final_mma;
     uint32_t tmem_base;
     int abort;
     float m_run[64], l_run[64], alpha[64];
     float red[4][64];
-    int fix;
 };
 constexpr uint32_t kSmemBytes = kOffMisc + sizeof(Misc) + 1024;
 static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -77,8 +89,8 @@ __device__ __forceinline__ bool named_bar_or(int id, int count, bool pred) {
     return r != 0;
 }
 
-// After this, lane `l` holds the reduction over the warp's 32 lanes of the
-// value v[c] with c = l (a transpose-reduce: 31 shuffles for 32 columns).
+// After this, lane `l` holds the reduction of column v[l] over the warp's 32
+// lanes (a transpose-reduce: 31 shuffles for 32 columns).
 template <bool MAX>
 __device__ __forceinline__ float warp_transpose_reduce(float (&v)[32], int lane) {
 #pragma unroll
@@ -95,6 +107,29 @@ __device__ __forceinline__ float warp_transpose_reduce(float (&v)[32], int lane)
     return v[0];
 }
 
+// Chunk n of a CTA's stream, in the order the MMAs consume them:
+// K(0), K(1), V(0), K(2), V(1), ..., K(nt-1), V(nt-2), V(nt-1).
+__device__ __forceinline__ void chunk_at(int n, int nt, int kc, int vc, bool& is_k, int& tile, int& c) {
+    if (n < kc) { is_k = true; tile = 0; c = n; return; }
+    const int m = n - kc, per = kc + vc, j = 1 + m / per, r = m % per;
+    if (j < nt && r < kc) { is_k = true; tile = j; c = r; }
+    else { is_k = false; tile = j - 1; c = j < nt ? r - kc : r; }
+}
+
+// Eight packed bf16 pairs of (hi, lo) for p[8u .. 8u+8).
+__device__ __forceinline__ void split_hilo(const float (&p)[32], int u, uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float a0 = p[8 * u + 2 * e], a1 = p[8 * u + 2 * e + 1];
+        const float h0 = bf16_round(a0), h1 = bf16_round(a1);
+        h[e] = pack_bf16x2(h0, h1);
+        l[e] = pack_bf16x2(a0 - h0, a1 - h1);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads7, 1)
@@ -107,111 +142,123 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
     const int b = blockIdx.x / J.splits, split = blockIdx.x % J.splits;
     const int n_keys = J.seqlens[b];
     const int nq = J.qlens ? J.qlens[b] : J.length;          // 1 or 2 queries
-    const int np = 64 * nq;                                   // MMA N (hi/lo per query)
+    const bool cols = nq == 1;                               // hi / lo as separate columns
     const int rows = 32 * nq;
+    const int ring = ring_slots(nq);
+    const uint32_t off_q = uint32_t(ring) * kChunkBytes;
+    const uint32_t off_p = off_q + uint32_t(nq * kMaxChunks) * kQChunkBytes;
     const int n_tiles = (max(n_keys, 0) + kKeys - 1) / kKeys;
-    const int t0 = split * J.tiles_per_split;
-    const int t1 = split == J.splits - 1 ? n_tiles : min(n_tiles, t0 + J.tiles_per_split);
+    // Tiles spread evenly over the sequence's splits.
+    const int t0 = int((int64_t)split * n_tiles / J.splits);
+    const int t1 = int((int64_t)(split + 1) * n_tiles / J.splits);
     const int nt = max(0, t1 - t0);
+    const int total_chunks = nt * (J.kchunks + J.vchunks);
+    auto issue_chunk = [&](int n) {
+        bool is_k; int tile, c;
+        chunk_at(n, nt, J.kchunks, J.vchunks, is_k, tile, c);
+        const int slot = n % ring;
+        mbar_expect_tx(&ms->full[slot], kChunkBytes);
+        tma_load_4d(smem + slot * kChunkBytes, is_k ? &kmap : &vmap, &ms->full[slot], c * 64, 0,
+                    (t0 + tile) * kKeys, b);
+    };
 
     if (tid == 0) {
-        for (int s = 0; s < kKSlots; ++s) { mbar_init(&ms->kfull[s], 1); mbar_init(&ms->kempty[s], 1); }
-        for (int s = 0; s < kVSlots; ++s) { mbar_init(&ms->vfull[s], 1); mbar_init(&ms->vempty[s], 1); }
+        for (int s = 0; s < kRingMax; ++s) { mbar_init(&ms->full[s], 1); mbar_init(&ms->empty[s], 1); }
         mbar_init(&ms->qfull, 1);
-        mbar_init(&ms->sfull, 1);
-        mbar_init(&ms->sempty, 4);
+        for (int s = 0; s < 2; ++s) { mbar_init(&ms->sfull[s], 1); mbar_init(&ms->sempty[s], 4); }
         mbar_init(&ms->pfull, 4);
         mbar_init(&ms->odone, 1);
         mbar_init(&ms->final_mma, 1);
         ms->abort = 0;
         fence_barrier_init();
-        tma_prefetch_desc(&kmap);
-        tma_prefetch_desc(&vmap);
-        tma_prefetch_desc(&qmap);
+        // The stream starts at once: Q and the first ring's worth of chunks
+        // (first use of each slot needs no wait) overlap the setup below.
+        if (nt > 0) {
+            // Q rows of the sequence: [hi | lo] x 32 * nq (one 64-row box per
+            // chunk for nq = 1, hi and lo boxes for nq = 2).
+            mbar_expect_tx(&ms->qfull, uint32_t(nq * J.kchunks) * kQChunkBytes);
+            for (int c = 0; c < J.kchunks; ++c)
+                for (int hl = 0; hl < nq; ++hl)
+                    tma_load_4d(smem + off_q + (hl * kMaxChunks + c) * kQChunkBytes, &qmap, &ms->qfull, c * 64, 0,
+                                hl * 64, b);
+            for (int n = 0; n < ring && n < total_chunks; ++n) issue_chunk(n);
+        }
     }
     if (warp == 2) {
         tmem_alloc(&ms->tmem_base, kTmemCols);
         tmem_relinquish();
     }
-    if (tid >= 96) {
-        const int r = tid - 96;
-        if (r < 64) { ms->m_run[r] = -INFINITY; ms->l_run[r] = 0.f; }
+    if (tid >= 96 && tid < 160) {
+        ms->m_run[tid - 96] = -INFINITY;
+        ms->l_run[tid - 96] = 0.f;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = ms->tmem_base;
-    const uint32_t o_tmem = tbase;                            // vblocks x np columns
-    const uint32_t s_tmem = tbase + uint32_t(J.vblocks * np); // np columns
+    const uint32_t o_tmem = tbase;                                        // vchunks x 64 columns
+    const uint32_t s_tmem0 = tbase + uint32_t(kMaxChunks * kN);           // two 64-column buffers
     const uint32_t sbase = smem_u32(smem);
 
     if (nt > 0) {
         if (warp == 0 && lane == 0) {
-            // ---- K producer ----
-            int kc = 0;
-            for (int i = 0; i < nt && !ms->abort; ++i) {
-                for (int c = 0; c < J.kchunks; ++c, ++kc) {
-                    const int slot = kc % kKSlots, use = kc / kKSlots;
-                    if (use > 0 && !wait_or_abort(&ms->kempty[slot], (use - 1) & 1, ms, J.status)) break;
-                    mbar_expect_tx(&ms->kfull[slot], kChunkBytes);
-                    tma_load_4d(smem + kOffK + slot * kChunkBytes, &kmap, &ms->kfull[slot], c * 64, 0,
-                                (t0 + i) * kKeys, b);
-                }
-            }
-        } else if (warp == 1 && lane == 0) {
-            // ---- Q + V producer ----
-            mbar_expect_tx(&ms->qfull, J.kchunks * kChunkBytes);
-            for (int c = 0; c < J.kchunks; ++c)
-                tma_load_4d(smem + kOffQ + c * kChunkBytes, &qmap, &ms->qfull, c * 64, 0, 0, b);
-            int vc = 0;
-            for (int i = 0; i < nt && !ms->abort; ++i) {
-                for (int mb = 0; mb < J.vblocks; ++mb, ++vc) {
-                    const int slot = vc % kVSlots, use = vc / kVSlots;
-                    if (use > 0 && !wait_or_abort(&ms->vempty[slot], (use - 1) & 1, ms, J.status)) break;
-                    uint8_t* dst = smem + kOffV + slot * 2 * kChunkBytes;
-                    mbar_expect_tx(&ms->vfull[slot], 2 * kChunkBytes);
-                    tma_load_4d(dst, &vmap, &ms->vfull[slot], mb * 128, 0, (t0 + i) * kKeys, b);
-                    tma_load_4d(dst + kChunkBytes, &vmap, &ms->vfull[slot], mb * 128 + 64, 0, (t0 + i) * kKeys, b);
-                }
+            // ---- TMA producer: the rest of the K/V chunk stream, in MMA order ----
+            for (int n = ring; n < total_chunks; ++n) {
+                if (!wait_or_abort(&ms->empty[n % ring], (n / ring - 1) & 1, ms, J.status)) break;
+                issue_chunk(n);
             }
         } else if (warp == 2 && lane == 0) {
-            // ---- MMA issuer ----
-            const uint32_t idesc_s = umma_idesc_bf16(128, np, 0, 0);
-            const uint32_t idesc_pv = umma_idesc_bf16(128, np, 1, 1);
-            int kc = 0, vc = 0;
-            if (wait_or_abort(&ms->qfull, 0, ms, J.status)) {
-                for (int i = 0; i < nt; ++i) {
-                    if (i > 0 && !wait_or_abort(&ms->sempty, (i - 1) & 1, ms, J.status)) break;
+            // ---- MMA issuer: S(j) then P.V(j-1) ----
+            const uint32_t idesc_s = umma_idesc_bf16(128, kN, 0, 0);
+            const uint32_t idesc_pv = umma_idesc_bf16(64, kN, 1, 1);
+            const uint32_t q0 = sbase + off_q, q1 = q0 + kMaxChunks * kQChunkBytes;
+            const uint32_t p0 = sbase + off_p, p1 = p0 + kChunkBytes;
+            int n = 0;
+            bool ok = wait_or_abort(&ms->qfull, 0, ms, J.status);
+            for (int j = 0; j <= nt && ok; ++j) {
+                if (j < nt) {
+                    const int sb = j & 1;
+                    const uint32_t s_tmem = s_tmem0 + uint32_t(sb * kN);
+                    if (j >= 2 && !(ok = wait_or_abort(&ms->sempty[sb], ((j - 2) >> 1) & 1, ms, J.status))) break;
                     tc_fence_after();
-                    bool ok = true;
-                    for (int c = 0; c < J.kchunks && ok; ++c, ++kc) {
-                        const int slot = kc % kKSlots;
-                        if (!wait_or_abort(&ms->kfull[slot], (kc / kKSlots) & 1, ms, J.status)) { ok = false; break; }
+                    for (int c = 0; c < J.kchunks; ++c, ++n) {
+                        const int slot = n % ring;
+                        if (!(ok = wait_or_abort(&ms->full[slot], (n / ring) & 1, ms, J.status))) break;
                         tc_fence_after();
-                        const uint32_t ka = sbase + kOffK + slot * kChunkBytes;
-                        const uint32_t qa = sbase + kOffQ + c * kChunkBytes;
+                        const uint32_t ka = sbase + slot * kChunkBytes;
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            umma_bf16(s_tmem, umma_desc_sw128(ka + kk * 32, 16, 1024),
-                                      umma_desc_sw128(qa + kk * 32, 16, 1024), idesc_s, (c | kk) != 0);
-                        umma_commit(&ms->kempty[slot]);
+                        for (int kk = 0; kk < 4; ++kk) {
+                            const uint64_t ad = umma_desc_sw128(ka + kk * 32, 16, 1024);
+                            umma_bf16(s_tmem, ad, umma_desc_sw128(q0 + c * kQChunkBytes + kk * 32, 16, 1024),
+                                      idesc_s, (c | kk) != 0);
+                            if (!cols)
+                                umma_bf16(s_tmem, ad, umma_desc_sw128(q1 + c * kQChunkBytes + kk * 32, 16, 1024),
+                                          idesc_s, 1u);
+                        }
+                        umma_commit(&ms->empty[slot]);
                     }
                     if (!ok) break;
-                    umma_commit(&ms->sfull);
-                    if (!wait_or_abort(&ms->pfull, i & 1, ms, J.status)) break;
+                    umma_commit(&ms->sfull[sb]);
+                }
+                if (j >= 1) {
+                    const int i = j - 1;
+                    if (!(ok = wait_or_abort(&ms->pfull, i & 1, ms, J.status))) break;
                     tc_fence_after();
-                    for (int mb = 0; mb < J.vblocks && ok; ++mb, ++vc) {
-                        const int slot = vc % kVSlots;
-                        if (!wait_or_abort(&ms->vfull[slot], (vc / kVSlots) & 1, ms, J.status)) { ok = false; break; }
+                    for (int c = 0; c < J.vchunks; ++c, ++n) {
+                        const int slot = n % ring;
+                        if (!(ok = wait_or_abort(&ms->full[slot], (n / ring) & 1, ms, J.status))) break;
                         tc_fence_after();
-                        const uint32_t va = sbase + kOffV + slot * 2 * kChunkBytes;
-                        const uint32_t pa = sbase + kOffP;
+                        const uint32_t va = sbase + slot * kChunkBytes;
+                        const uint32_t o_c = o_tmem + uint32_t(c * kN);
 #pragma unroll
-                        for (int ks = 0; ks < kKeys / 16; ++ks)
-                            umma_bf16(o_tmem + uint32_t(mb * np), umma_desc_sw128(va + ks * 2048, kChunkBytes, 1024),
-                                      umma_desc_sw128(pa + ks * 2048, kChunkBytes, 1024), idesc_pv,
+                        for (int ks = 0; ks < kKeys / 16; ++ks) {
+                            const uint64_t ad = umma_desc_sw128(va + ks * 2048, kChunkBytes, 1024);
+                            umma_bf16(o_c, ad, umma_desc_sw128(p0 + ks * 2048, kChunkBytes, 1024), idesc_pv,
                                       (i > 0 || ks > 0) ? 1u : 0u);
-                        umma_commit(&ms->vempty[slot]);
+                            if (!cols)
+                                umma_bf16(o_c, ad, umma_desc_sw128(p1 + ks * 2048, kChunkBytes, 1024), idesc_pv, 1u);
+                        }
+                        umma_commit(&ms->empty[slot]);
                     }
                     if (!ok) break;
                     umma_commit(&ms->odone);
@@ -228,33 +275,30 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
             const int st = tid - 96;                      // 0..127
             bool failed = false;
             for (int i = 0; i < nt; ++i) {
+                const int sb = i & 1;
+                const uint32_t s_tmem = s_tmem0 + uint32_t(sb * kN);
                 const int key = (t0 + i) * kKeys + t_local;
-                bool ok = wait_or_abort(&ms->sfull, i & 1, ms, J.status);
+                bool ok = wait_or_abort(&ms->sfull[sb], (i >> 1) & 1, ms, J.status);
                 if (named_bar_or(1, 128, !ok)) { failed = true; break; }
                 tc_fence_after();
                 float v[2][32];
-#pragma unroll
-                for (int l = 0; l < 2; ++l) {
-                    if (l < nq) {
-                        float lo[32];
-                        tmem_ld32(s_tmem + lane_addr + 64 * l, v[l]);
-                        tmem_ld32(s_tmem + lane_addr + 64 * l + 32, lo);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int h = 0; h < 32; ++h) v[l][h] += lo[h];
-                    }
-                }
+                tmem_ld32(s_tmem + lane_addr, v[0]);
+                tmem_ld32(s_tmem + lane_addr + 32, v[1]);
+                tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&ms->sempty);
-                // scale, mask (a Beacon-insertion step's raw query excludes the new Beacon)
+                if (lane == 0) mbar_arrive(&ms->sempty[sb]);
+                if (cols) {
+#pragma unroll
+                    for (int h = 0; h < 32; ++h) v[0][h] += v[1][h];       // hi + lo products
+                }
+                // scale and mask (an insertion step's raw query excludes the new Beacon)
 #pragma unroll
                 for (int l = 0; l < 2; ++l) {
                     const int limit = (nq == 2 && l == 0) ? n_keys - 1 : n_keys;
 #pragma unroll
                     for (int h = 0; h < 32; ++h) v[l][h] = key < limit ? v[l][h] * J.scale_log2 : -INFINITY;
                 }
-                // column maxima of this tile
 #pragma unroll
                 for (int l = 0; l < 2; ++l) {
                     if (l < nq) {
@@ -277,30 +321,52 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
                     ms->m_run[st] = mn;
                     ms->l_run[st] *= alpha;
                 }
-                const bool need_fix = named_bar_or(1, 128, st < rows && ms->alpha[st] != 1.f && i > 0);
-                // P(i) reuses the buffer read by PV(i-1); PV(i-1) precedes S(i)
-                // on the tensor pipe, so it has finished, but wait for it anyway.
+                const bool need_fix = named_bar_or(1, 128, st < rows && i > 0 && ms->alpha[st] != 1.f);
+                // P(i) overwrites the buffer P.V(i-1) reads: wait for it.
                 if (i > 0) {
                     ok = wait_or_abort(&ms->odone, (i - 1) & 1, ms, J.status);
                     if (named_bar_or(1, 128, !ok)) { failed = true; break; }
                     tc_fence_after();
                 }
-                if (need_fix) {
-                    // rescale the O^T columns whose running max moved
-                    for (int mb = 0; mb < J.vblocks; ++mb)
-                        for (int l = 0; l < nq; ++l)
-                            for (int half = 0; half < 2; ++half) {
-                                float o[32];
-                                const uint32_t addr = o_tmem + lane_addr + uint32_t(mb * np + 64 * l + 32 * half);
-                                tmem_ld32(addr, o);
-                                tmem_wait_ld();
+                // The sequence's partial last tile: V rows past the length hold
+                // whatever the cache has there; P is zero for them, and zeroing
+                // the rows too keeps a non-finite stale value from turning 0 * x
+                // into NaN.  Each thread clears its own key row once the chunk
+                // has landed (the slot is not consumed before P is released).
+                if (i == nt - 1 && t0 + i == n_tiles - 1 && (n_keys & (kKeys - 1)) != 0) {
+                    bool okc = true;
+                    if (key >= n_keys) {
+                        const int n0 = J.kchunks * nt + J.vchunks * (nt - 1);
+                        for (int c = 0; c < J.vchunks && okc; ++c) {
+                            const int slot = (n0 + c) % ring;
+                            okc = wait_or_abort(&ms->full[slot], ((n0 + c) / ring) & 1, ms, J.status);
+                            if (okc) {
+                                uint4* row = reinterpret_cast<uint4*>(smem + slot * kChunkBytes + t_local * 128);
 #pragma unroll
-                                for (int h = 0; h < 32; ++h) o[h] *= ms->alpha[32 * l + h];
-                                tmem_st32(addr, o);
+                                for (int u = 0; u < 8; ++u) row[u] = make_uint4(0, 0, 0, 0);
                             }
+                        }
+                    }
+                    if (named_bar_or(1, 128, !okc)) { failed = true; break; }
+                }
+                if (need_fix) {
+                    // O^T column group k (32 columns) belongs to row k*32 + h, or
+                    // to row h for the single-query hi | lo layout.
+                    for (int c = 0; c < J.vchunks; ++c)
+                        for (int k = 0; k < 2; ++k) {
+                            float o[32];
+                            const uint32_t addr = o_tmem + lane_addr + uint32_t(c * kN + 32 * k);
+                            tmem_ld32(addr, o);
+                            tmem_wait_ld();
+                            const float* al = ms->alpha + (cols ? 0 : 32 * k);
+#pragma unroll
+                            for (int h = 0; h < 32; ++h) o[h] *= al[h];
+                            tmem_st32(addr, o);
+                        }
                     tmem_wait_st();
                 }
-                // probabilities -> P^T (hi | lo per query), row sums
+                // probabilities -> P^T rows (hi and lo), row sums
+                uint8_t* prow = smem + off_p + t_local * 128;
 #pragma unroll
                 for (int l = 0; l < 2; ++l) {
                     if (l < nq) {
@@ -310,21 +376,16 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
                             const float m = ms->m_run[32 * l + h];
                             p[h] = (v[l][h] == -INFINITY || m == -INFINITY) ? 0.f : exp2f(v[l][h] - m);
                         }
-                        uint8_t* prow = smem + kOffP + l * kChunkBytes + t_local * 128;
 #pragma unroll
                         for (int u = 0; u < 4; ++u) {
-                            uint32_t hi[4], lo[4];
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const float a0 = p[8 * u + 2 * e], a1 = p[8 * u + 2 * e + 1];
-                                const float h0 = bf16_round(a0), h1 = bf16_round(a1);
-                                hi[e] = pack_bf16x2(h0, h1);
-                                lo[e] = pack_bf16x2(a0 - h0, a1 - h1);
-                            }
-                            *reinterpret_cast<uint4*>(prow + (((u) ^ (t_local & 7)) << 4)) =
-                                make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                            *reinterpret_cast<uint4*>(prow + (((u + 4) ^ (t_local & 7)) << 4)) =
-                                make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                            uint4 hi, lo;
+                            split_hilo(p, u, hi, lo);
+                            // nq = 1: units 0-3 hi, 4-7 lo of one buffer; nq = 2:
+                            // unit 4l + u of the hi and of the lo buffer.
+                            const int uh = cols ? u : 4 * l + u, ul = cols ? 4 + u : 4 * l + u;
+                            uint8_t* lrow = cols ? prow : prow + kChunkBytes;
+                            *reinterpret_cast<uint4*>(prow + ((uh ^ (t_local & 7)) << 4)) = hi;
+                            *reinterpret_cast<uint4*>(lrow + ((ul ^ (t_local & 7)) << 4)) = lo;
                         }
                         ms->red[quarter][32 * l + lane] = warp_transpose_reduce<false>(p, lane);
                     }
@@ -344,23 +405,51 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
             }
             if (!failed) {
                 tc_fence_after();
+                // per-row 1 / l (0 for a row without mass)
+                if (st < 64) ms->alpha[st] = (st < rows && ms->l_run[st] > 0.f) ? 1.f / ms->l_run[st] : 0.f;
+                named_bar(1, 128);
+                // Stage O / l as [chunk][row][64] fp32 in the (drained) ring:
+                // the M=64 accumulator holds dim 16q + L of a chunk in lane
+                // L < 16 of quarter q.
+                // (1 / l is applied when the rows are written out.)
+                float* stage = reinterpret_cast<float*>(smem);
+                for (int c = 0; c < J.vchunks; ++c) {
+                    float o[2][32];
+                    tmem_ld32(o_tmem + lane_addr + uint32_t(c * kN), o[0]);
+                    tmem_ld32(o_tmem + lane_addr + uint32_t(c * kN + 32), o[1]);
+                    tmem_wait_ld();
+                    if (lane < 16) {
+                        float* dst = stage + (c * 64) * 64 + 16 * quarter + lane;
+                        if (cols) {
+#pragma unroll
+                            for (int h = 0; h < 32; ++h) dst[h * 64] = o[0][h] + o[1][h];
+                        } else {
+#pragma unroll
+                            for (int h = 0; h < 64; ++h) dst[h * 64] = o[h >> 5][h & 31];
+                        }
+                    }
+                }
                 named_bar(1, 128);
                 const int64_t base_row = ((int64_t)b * J.splits + split) * J.rows_alloc;
-                for (int mb = 0; mb < J.vblocks; ++mb) {
-                    const int d = mb * 128 + t_local;
-                    for (int l = 0; l < nq; ++l) {
-                        float hi[32], lo[32];
-                        tmem_ld32(o_tmem + lane_addr + uint32_t(mb * np + 64 * l), hi);
-                        tmem_ld32(o_tmem + lane_addr + uint32_t(mb * np + 64 * l + 32), lo);
-                        tmem_wait_ld();
-                        if (d < J.out_width) {
+                const int width = min(J.vchunks * 64, J.out_width);
+                const int f4 = width / 4, items = rows * f4;
+                // Batches of eight row pieces: all shared loads, then all stores.
+#pragma unroll 1
+                for (int it0 = st; it0 < items; it0 += 8 * 128) {
+                    float4 val[8];
 #pragma unroll
-                            for (int h = 0; h < 32; ++h) {
-                                const float lsum = ms->l_run[32 * l + h];
-                                J.part_o[(base_row + 32 * l + h) * J.out_width + d] =
-                                    lsum > 0.f ? (hi[h] + lo[h]) / lsum : 0.f;
-                            }
+                    for (int k = 0; k < 8; ++k) {
+                        const int it = it0 + k * 128, r = it / f4, d = (it - r * f4) * 4;
+                        if (it < items) {
+                            val[k] = *reinterpret_cast<const float4*>(stage + ((d >> 6) * 64 + r) * 64 + (d & 63));
+                            const float inv = ms->alpha[r];
+                            val[k].x *= inv; val[k].y *= inv; val[k].z *= inv; val[k].w *= inv;
                         }
+                    }
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int it = it0 + k * 128, r = it / f4, d = (it - r * f4) * 4;
+                        if (it < items) *reinterpret_cast<float4*>(J.part_o + (base_row + r) * J.out_width + d) = val[k];
                     }
                 }
                 if (st < rows) {
@@ -382,8 +471,10 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
     __syncthreads();
     if (ms->abort && tid == 0) {
         // Drain: wait (bounded) for the last copy issued into every slot.
-        for (int s = 0; s < kKSlots; ++s) { mbar_wait(&ms->kfull[s], 0, 100000000ull); mbar_wait(&ms->kfull[s], 1, 100000000ull); }
-        for (int s = 0; s < kVSlots; ++s) { mbar_wait(&ms->vfull[s], 0, 100000000ull); mbar_wait(&ms->vfull[s], 1, 100000000ull); }
+        for (int s = 0; s < ring; ++s) {
+            mbar_wait(&ms->full[s], 0, 100000000ull);
+            mbar_wait(&ms->full[s], 1, 100000000ull);
+        }
         mbar_wait(&ms->qfull, 0, 100000000ull);
     }
     __syncthreads();
@@ -405,13 +496,13 @@ int launch_latent_tc(const TcLaunch& L, cudaStream_t stream) {
                             L.lat_stride_row * 2, L.lat_stride_batch * 2, kKeys)))
         return rc;
     if ((rc = encode_map_4d(&qm, L.q_hilo, L.width, 1, 128, L.batch, uint64_t(L.width) * 2, uint64_t(L.width) * 2,
-                            uint64_t(L.width) * 2 * 128, 128)))
+                            uint64_t(L.width) * 2 * 128, 64)))
         return rc;
     TcJob J{};
     J.rank_k = L.rank_k;
     J.rank_v = L.rank_v;
     J.kchunks = (L.rank_k + 63) / 64;
-    J.vblocks = (L.rank_v + 127) / 128;
+    J.vchunks = (L.rank_v + 63) / 64;
     J.seqlens = L.latent_len;
     J.qlens = L.query_len;
     J.length = L.length;

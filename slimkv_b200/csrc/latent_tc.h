@@ -7,7 +7,7 @@
 namespace slimkv {
 
 struct TcJob {
-    int rank_k, rank_v, kchunks, vblocks;
+    int rank_k, rank_v, kchunks, vchunks;
     const int32_t* seqlens;   // latents per sequence
     const int32_t* qlens;     // queries per sequence (1 or 2), nullable
     int length;
@@ -24,7 +24,7 @@ struct TcLaunch {
     const void* lat_k;
     const void* lat_v;
     int64_t lat_stride_batch, lat_stride_row;   // elements
-    const void* q_hilo;                          // [B][128][width] bf16: per query l rows l*64 + {0: hi, 32: lo} + head
+    const void* q_hilo;                          // [B][128][width] bf16: row hl*32*nq + l*32 + head, hl 0 = hi, 1 = lo
     const int32_t* latent_len;
     const int32_t* query_len;
     float scale;

@@ -68,6 +68,27 @@ def test_cache_seqlens_truncate_each_row():
     assert_lse_close(lse, ref_lse)
 
 
+@pytest.mark.parametrize('stale', [float('nan'), float('inf')])
+def test_cache_rows_past_cache_seqlens_are_ignored(stale):
+    """Like the reference kernel, rows past a length never reach the output."""
+    from slimkv_b200 import kernels
+    c = attention_case(25, 3, 1, 32, 1, 600, 320, 320, False)
+    lengths = [600, 1, 333]
+    q, k, v = to_bf16(c['q']), to_bf16(c['k']), to_bf16(c['v'])
+    for b, n in enumerate(lengths):
+        k[b, n:] = stale
+        v[b, n:] = stale
+    seq = torch.tensor(lengths, dtype=torch.int32, device='cuda')
+    for splits in (0, 1, 16):
+        out, lse = kernels.attention_forward(q, k, v, c['scale'], False, splits, seq)
+        assert torch.isfinite(out.float()).all()
+        for b, n in enumerate(lengths):
+            ref, ref_lse = oracle.eager_attention(c['q'][b:b + 1], c['k'][b:b + 1, :n], c['v'][b:b + 1, :n],
+                                                  c['scale'], False)
+            assert_attention_close(out[b:b + 1], ref)
+            assert_lse_close(lse[b:b + 1], ref_lse)
+
+
 def test_cache_seqlens_with_causal_pair():
     c = attention_case(22, 2, 2, 32, 1, 300, 320, 320, True)
     out, lse, ref, ref_lse = _run(c, lengths=[1, 257])

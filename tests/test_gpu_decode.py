@@ -31,8 +31,11 @@ def tables(positions=16384):
     return _TABLES[positions]
 
 
-def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False):
-    """Stage the caches without this step's entries, run the fused step."""
+def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False, stale=0.0):
+    """Stage the caches without this step's entries, run the fused step.
+
+    Cache rows past each sequence's staged length hold ``stale``.
+    """
     from slimkv_b200 import kernels
     cos, sin, cos_t, sin_t = tables()
     B, L, H, D = c['q'].shape
@@ -40,10 +43,10 @@ def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False):
     n_raw, n_lat = c['n_raw'], c['n_lat']
     raw_cap = int(n_raw.max()) + extra_cap
     lat_cap = int(n_lat.max()) + extra_cap
-    raw_k = np.zeros((B, raw_cap, Hkv, D), np.float32)
-    raw_v = np.zeros_like(raw_k)
-    lat_k = np.zeros((B, lat_cap, rk), np.float32)
-    lat_v = np.zeros((B, lat_cap, rv), np.float32)
+    raw_k = np.full((B, raw_cap, Hkv, D), stale, np.float32)
+    raw_v = np.full_like(raw_k, stale)
+    lat_k = np.full((B, lat_cap, rk), stale, np.float32)
+    lat_v = np.full((B, lat_cap, rv), stale, np.float32)
     new_k = np.zeros((B, Hkv * D), np.float32)
     new_v = np.zeros_like(new_k)
     new_lk = np.zeros((B, rk), np.float32)
@@ -114,6 +117,17 @@ def check(c, query_len, t):
             assert_bits_equal(t['lat_k'][b, n], c['lat_k'][b, n])
             assert_bits_equal(t['lat_v'][b, n], c['lat_v'][b, n])
     return max(errs)
+
+
+@pytest.mark.parametrize('stale', [float('nan'), float('inf')])
+def test_stale_cache_rows_past_the_length_are_ignored(stale):
+    """Rows past each length may hold anything (NaN, inf) and must not leak."""
+    c = decode_case(71, batch=3, length=2, history=300, tail=39, ragged=True)
+    query_len = np.array([2, 1, 2])
+    for fp32 in (False, True):
+        t = run_fused(c, query_len, extra_cap=200, fp32=fp32, stale=stale)
+        assert torch.isfinite(t['out'].float()).all()
+        check(c, query_len, t)
 
 
 @pytest.mark.parametrize('length,history,tail,rank,bias,ragged', [
