@@ -4,8 +4,10 @@
 // the sequence's latent cache against all query rows of the step (32 heads x
 // nq = 1 or 2 queries).  Swap-AB so the keys fill M:
 //
-//   S^T [128 keys x 64]      = K_tile . Q^T                  (M=128, K-major A/B)
-//   O^T [64 dims x 64] (x5) += V_chunk^T . P^T               (M=64, MN-major A/B)
+//   S^T [128 keys x 64]        = K_tile . Q^T          (M=128, K-major A/B)
+//   O^T [128 dims x 64] (x2,3) += V_pair^T . P^T       (M=128 over two 64-dim
+//                                                       V chunks; M=64 for an
+//                                                       odd last chunk)
 //
 // Q and P are split into bf16 hi + lo (x = hi + lo to ~16 mantissa bits), so
 // the bf16 K/V tiles are used as stored and the result keeps fp32-level
@@ -14,25 +16,26 @@
 //           per k-step); the softmax and the epilogue add the two halves.
 //   nq = 2: columns are (query, head); hi and lo accumulate into the same
 //           columns (two MMAs per k-step).
-// A single-query CTA therefore needs half the Q and P buffers and gives the
-// space to the K/V ring (10 slots instead of 7): the stream is bound by the
-// bytes in flight against the loaded HBM latency.
 //
-// K and V stream through one ring of 16 KB [128 keys x 64 columns] chunks in
-// exactly the order the MMAs consume them (S(j+1) is issued before P.V(j) so
-// scores of the next tile overlap the softmax of this one; S is
-// double-buffered in TMEM).  Softmax: one key per thread reading its TMEM
-// lane, column maxima and sums via warp transpose-reduce, and a lazy rescale
-// (the running max moves only when a column max exceeds it by 2^8, so the
-// TMEM read-modify-write of O^T is rare).  The epilogue stages the normalised
-// partial output through shared memory and stores whole rows.
+// Streams.  K and V chunks (16 KB, [128 keys x 64 columns], 128-byte
+// swizzle) flow through two rings so the V chunks that wait for a tile's
+// probabilities never hold up the K prefetch: a K ring (5 slots, 2 for
+// nq = 2) and a V ring of one tile (chunk c of every tile in slot c, so the
+// chunk pairs of the M=128 products are always adjacent).  Two threads issue
+// MMAs: one computes S(j) as K chunks land, the other P.V(j) once P(j) is
+// written; each commits the ring slots it read.  S is double-buffered in TMEM.
 //
-// Warp roles (7 warps): 0 = TMA producer (Q once, then the K/V ring),
-// 1 = idle helper, 2 = TMEM allocator and single-thread MMA issuer,
-// 3-6 = softmax / epilogue (TMEM lane quarters 3, 0, 1, 2).  TMA loads use the
-// 128-byte swizzle and no cluster multicast.  Every wait is bounded: on expiry
-// the CTA reports SLIMKV_DEVICE_TIMEOUT, drains its copies and MMAs
-// (bounded), frees TMEM and returns.
+// Softmax: one key per thread reading its TMEM lane, column maxima and sums
+// via warp transpose-reduce, and a lazy rescale (the running max moves only
+// when a column max exceeds it by 2^8, so the TMEM read-modify-write of O^T is
+// rare).  The epilogue stages the normalised partial output through shared
+// memory and stores whole rows.
+//
+// Warp roles (7 warps): 0 = TMA producer, 1 = P.V issuer, 2 = TMEM allocator
+// and S issuer, 3-6 = softmax / epilogue (TMEM lane quarters 3, 0, 1, 2).  No
+// cluster multicast.  Every wait is bounded: on expiry the CTA reports
+// SLIMKV_DEVICE_TIMEOUT, drains its copies and MMAs (bounded), frees TMEM and
+// returns.
 #include <algorithm>
 
 #include "common.cuh"
@@ -45,22 +48,24 @@ namespace {
 
 constexpr int kKeys = 128;
 constexpr int kThreads7 = 224;
-constexpr int kRingMax = 10;
+constexpr int kMaxChunks = 5;                        // ranks <= 320
+constexpr int kKRingMax = 5;
 constexpr uint32_t kChunkBytes = 128 * 128;          // [128 keys x 64 bf16], 128-byte swizzle
 constexpr uint32_t kQChunkBytes = 64 * 128;          // [64 rows x 64 bf16]
-constexpr int kMaxChunks = 5;                        // ranks <= 320
 constexpr float kLazyLog2 = 8.f;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kN = 64;                               // MMA N
+constexpr uint64_t kWaitNs = 2000000000ull;
 
-// Shared memory: ring (nq = 1: 10 slots, nq = 2: 7) | Q (nq x 40 KB) | P
-// (nq x 16 KB) | ... | Misc at a fixed offset past the larger layout.
-__host__ __device__ constexpr int ring_slots(int nq) { return nq == 1 ? 10 : 7; }
-constexpr uint32_t kOffMisc = 7 * kChunkBytes + 2 * kMaxChunks * kQChunkBytes + 2 * kChunkBytes;
-static_assert(10 * kChunkBytes + kMaxChunks * kQChunkBytes + kChunkBytes <= kOffMisc, "single-query layout");
+// Shared memory: V ring (5 slots) | K ring (5 slots for nq = 1, 2 for nq = 2)
+// | Q (nq x 40 KB) | P (nq x 16 KB) | ... | Misc at a fixed offset.
+__host__ __device__ constexpr int k_ring_slots(int nq) { return nq == 1 ? 5 : 2; }
+constexpr uint32_t kOffK = kMaxChunks * kChunkBytes;
+constexpr uint32_t kOffMisc = kOffK + 2 * kChunkBytes + 2 * kMaxChunks * kQChunkBytes + 2 * kChunkBytes;
+static_assert(kOffK + 5 * kChunkBytes + kMaxChunks * kQChunkBytes + kChunkBytes <= kOffMisc, "single-query layout");
 
 struct Misc {
-    uint64_t full[kRingMax], empty[kRingMax];
+    uint64_t kfull[kKRingMax], kempty[kKRingMax], vfull[kMaxChunks], vempty[kMaxChunks];
     uint64_t qfull, sfull[2], sempty[2], pfull, odone, final_mma;
     uint32_t tmem_base;
     int abort;
@@ -72,7 +77,7 @@ static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Misc* ms, unsigned* status) {
     if (ms->abort) return false;
-    if (mbar_wait(bar, parity)) return true;
+    if (mbar_wait(bar, parity, kWaitNs)) return true;
     ms->abort = 1;
     report(status, SLIMKV_DEVICE_TIMEOUT);
     return false;
@@ -107,15 +112,6 @@ __device__ __forceinline__ float warp_transpose_reduce(float (&v)[32], int lane)
     return v[0];
 }
 
-// Chunk n of a CTA's stream, in the order the MMAs consume them:
-// K(0), K(1), V(0), K(2), V(1), ..., K(nt-1), V(nt-2), V(nt-1).
-__device__ __forceinline__ void chunk_at(int n, int nt, int kc, int vc, bool& is_k, int& tile, int& c) {
-    if (n < kc) { is_k = true; tile = 0; c = n; return; }
-    const int m = n - kc, per = kc + vc, j = 1 + m / per, r = m % per;
-    if (j < nt && r < kc) { is_k = true; tile = j; c = r; }
-    else { is_k = false; tile = j - 1; c = j < nt ? r - kc : r; }
-}
-
 // Eight packed bf16 pairs of (hi, lo) for p[8u .. 8u+8).
 __device__ __forceinline__ void split_hilo(const float (&p)[32], int u, uint4& hi, uint4& lo) {
     uint32_t h[4], l[4];
@@ -144,44 +140,53 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
     const int nq = J.qlens ? J.qlens[b] : J.length;          // 1 or 2 queries
     const bool cols = nq == 1;                               // hi / lo as separate columns
     const int rows = 32 * nq;
-    const int ring = ring_slots(nq);
-    const uint32_t off_q = uint32_t(ring) * kChunkBytes;
+    const int kring = k_ring_slots(nq);
+    const int kc = J.kchunks, vc = J.vchunks;
+    const uint32_t off_q = kOffK + uint32_t(kring) * kChunkBytes;
     const uint32_t off_p = off_q + uint32_t(nq * kMaxChunks) * kQChunkBytes;
     const int n_tiles = (max(n_keys, 0) + kKeys - 1) / kKeys;
     // Tiles spread evenly over the sequence's splits.
     const int t0 = int((int64_t)split * n_tiles / J.splits);
     const int t1 = int((int64_t)(split + 1) * n_tiles / J.splits);
     const int nt = max(0, t1 - t0);
-    const int total_chunks = nt * (J.kchunks + J.vchunks);
-    auto issue_chunk = [&](int n) {
-        bool is_k; int tile, c;
-        chunk_at(n, nt, J.kchunks, J.vchunks, is_k, tile, c);
-        const int slot = n % ring;
-        mbar_expect_tx(&ms->full[slot], kChunkBytes);
-        tma_load_4d(smem + slot * kChunkBytes, is_k ? &kmap : &vmap, &ms->full[slot], c * 64, 0,
-                    (t0 + tile) * kKeys, b);
+    const int total_k = nt * kc, total_v = nt * vc;
+    // K chunk n -> (tile n / kc, chunk n % kc) in ring slot n % kring;
+    // V chunk n -> (tile n / vc, chunk n % vc) in V slot n % vc.
+    auto issue_k = [&](int n) {
+        const int slot = n % kring;
+        mbar_expect_tx(&ms->kfull[slot], kChunkBytes);
+        tma_load_4d(smem + kOffK + slot * kChunkBytes, &kmap, &ms->kfull[slot], (n % kc) * 64, 0,
+                    (t0 + n / kc) * kKeys, b);
+    };
+    auto issue_v = [&](int n) {
+        const int slot = n % vc;
+        mbar_expect_tx(&ms->vfull[slot], kChunkBytes);
+        tma_load_4d(smem + slot * kChunkBytes, &vmap, &ms->vfull[slot], slot * 64, 0, (t0 + n / vc) * kKeys, b);
     };
 
     if (tid == 0) {
-        for (int s = 0; s < kRingMax; ++s) { mbar_init(&ms->full[s], 1); mbar_init(&ms->empty[s], 1); }
+        for (int s = 0; s < kKRingMax; ++s) { mbar_init(&ms->kfull[s], 1); mbar_init(&ms->kempty[s], 1); }
+        for (int s = 0; s < kMaxChunks; ++s) { mbar_init(&ms->vfull[s], 1); mbar_init(&ms->vempty[s], 1); }
         mbar_init(&ms->qfull, 1);
         for (int s = 0; s < 2; ++s) { mbar_init(&ms->sfull[s], 1); mbar_init(&ms->sempty[s], 4); }
         mbar_init(&ms->pfull, 4);
         mbar_init(&ms->odone, 1);
-        mbar_init(&ms->final_mma, 1);
+        mbar_init(&ms->final_mma, 2);
         ms->abort = 0;
         fence_barrier_init();
-        // The stream starts at once: Q and the first ring's worth of chunks
-        // (first use of each slot needs no wait) overlap the setup below.
+        // The streams start at once: Q, the first ring's worth of K chunks and
+        // the first tile's V chunks (first use of each slot needs no wait)
+        // overlap the setup below.
         if (nt > 0) {
             // Q rows of the sequence: [hi | lo] x 32 * nq (one 64-row box per
             // chunk for nq = 1, hi and lo boxes for nq = 2).
-            mbar_expect_tx(&ms->qfull, uint32_t(nq * J.kchunks) * kQChunkBytes);
-            for (int c = 0; c < J.kchunks; ++c)
+            mbar_expect_tx(&ms->qfull, uint32_t(nq * kc) * kQChunkBytes);
+            for (int c = 0; c < kc; ++c)
                 for (int hl = 0; hl < nq; ++hl)
                     tma_load_4d(smem + off_q + (hl * kMaxChunks + c) * kQChunkBytes, &qmap, &ms->qfull, c * 64, 0,
                                 hl * 64, b);
-            for (int n = 0; n < ring && n < total_chunks; ++n) issue_chunk(n);
+            for (int n = 0; n < kring && n < total_k; ++n) issue_k(n);
+            for (int n = 0; n < vc && n < total_v; ++n) issue_v(n);
         }
     }
     if (warp == 2) {
@@ -196,77 +201,100 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = ms->tmem_base;
-    const uint32_t o_tmem = tbase;                                        // vchunks x 64 columns
-    const uint32_t s_tmem0 = tbase + uint32_t(kMaxChunks * kN);           // two 64-column buffers
+    const uint32_t o_tmem = tbase;                         // up to 3 blocks x 64 columns
+    const uint32_t s_tmem0 = tbase + 3 * kN;               // two 64-column buffers
     const uint32_t sbase = smem_u32(smem);
+    const int vblocks = (vc + 1) / 2;
 
     if (nt > 0) {
         if (warp == 0 && lane == 0) {
-            // ---- TMA producer: the rest of the K/V chunk stream, in MMA order ----
-            for (int n = ring; n < total_chunks; ++n) {
-                if (!wait_or_abort(&ms->empty[n % ring], (n / ring - 1) & 1, ms, J.status)) break;
-                issue_chunk(n);
+            // ---- TMA producer: K chunks first whenever a K slot is free ----
+            int nk = min(kring, total_k), nv = min(vc, total_v);
+            uint64_t idle_since = 0;
+            while ((nk < total_k || nv < total_v) && !ms->abort) {
+                bool progressed = false;
+                if (nk < total_k && mbar_test(&ms->kempty[nk % kring], (nk / kring - 1) & 1)) {
+                    issue_k(nk++);
+                    progressed = true;
+                } else if (nv < total_v && mbar_test(&ms->vempty[nv % vc], (nv / vc - 1) & 1)) {
+                    issue_v(nv++);
+                    progressed = true;
+                }
+                if (progressed) {
+                    idle_since = 0;
+                    continue;
+                }
+                __nanosleep(64);
+                if (idle_since == 0) {
+                    idle_since = global_timer_ns();
+                } else if (global_timer_ns() - idle_since > kWaitNs) {
+                    ms->abort = 1;
+                    report(J.status, SLIMKV_DEVICE_TIMEOUT);
+                }
             }
         } else if (warp == 2 && lane == 0) {
-            // ---- MMA issuer: S(j) then P.V(j-1) ----
+            // ---- S issuer: S(j) = K(j) . Q^T as K chunks land ----
             const uint32_t idesc_s = umma_idesc_bf16(128, kN, 0, 0);
-            const uint32_t idesc_pv = umma_idesc_bf16(64, kN, 1, 1);
             const uint32_t q0 = sbase + off_q, q1 = q0 + kMaxChunks * kQChunkBytes;
-            const uint32_t p0 = sbase + off_p, p1 = p0 + kChunkBytes;
-            int n = 0;
             bool ok = wait_or_abort(&ms->qfull, 0, ms, J.status);
-            for (int j = 0; j <= nt && ok; ++j) {
-                if (j < nt) {
-                    const int sb = j & 1;
-                    const uint32_t s_tmem = s_tmem0 + uint32_t(sb * kN);
-                    if (j >= 2 && !(ok = wait_or_abort(&ms->sempty[sb], ((j - 2) >> 1) & 1, ms, J.status))) break;
+            for (int j = 0; j < nt && ok; ++j) {
+                const int sb = j & 1;
+                const uint32_t s_tmem = s_tmem0 + uint32_t(sb * kN);
+                if (j >= 2 && !(ok = wait_or_abort(&ms->sempty[sb], ((j - 2) >> 1) & 1, ms, J.status))) break;
+                tc_fence_after();
+                for (int c = 0; c < kc; ++c) {
+                    const int n = j * kc + c, slot = n % kring;
+                    if (!(ok = wait_or_abort(&ms->kfull[slot], (n / kring) & 1, ms, J.status))) break;
                     tc_fence_after();
-                    for (int c = 0; c < J.kchunks; ++c, ++n) {
-                        const int slot = n % ring;
-                        if (!(ok = wait_or_abort(&ms->full[slot], (n / ring) & 1, ms, J.status))) break;
-                        tc_fence_after();
-                        const uint32_t ka = sbase + slot * kChunkBytes;
+                    const uint32_t ka = sbase + kOffK + slot * kChunkBytes;
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk) {
-                            const uint64_t ad = umma_desc_sw128(ka + kk * 32, 16, 1024);
-                            umma_bf16(s_tmem, ad, umma_desc_sw128(q0 + c * kQChunkBytes + kk * 32, 16, 1024),
-                                      idesc_s, (c | kk) != 0);
-                            if (!cols)
-                                umma_bf16(s_tmem, ad, umma_desc_sw128(q1 + c * kQChunkBytes + kk * 32, 16, 1024),
-                                          idesc_s, 1u);
-                        }
-                        umma_commit(&ms->empty[slot]);
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t ad = umma_desc_sw128(ka + kk * 32, 16, 1024);
+                        umma_bf16(s_tmem, ad, umma_desc_sw128(q0 + c * kQChunkBytes + kk * 32, 16, 1024), idesc_s,
+                                  (c | kk) != 0);
+                        if (!cols)
+                            umma_bf16(s_tmem, ad, umma_desc_sw128(q1 + c * kQChunkBytes + kk * 32, 16, 1024), idesc_s,
+                                      1u);
                     }
-                    if (!ok) break;
-                    umma_commit(&ms->sfull[sb]);
+                    umma_commit(&ms->kempty[slot]);
                 }
-                if (j >= 1) {
-                    const int i = j - 1;
-                    if (!(ok = wait_or_abort(&ms->pfull, i & 1, ms, J.status))) break;
-                    tc_fence_after();
-                    for (int c = 0; c < J.vchunks; ++c, ++n) {
-                        const int slot = n % ring;
-                        if (!(ok = wait_or_abort(&ms->full[slot], (n / ring) & 1, ms, J.status))) break;
-                        tc_fence_after();
-                        const uint32_t va = sbase + slot * kChunkBytes;
-                        const uint32_t o_c = o_tmem + uint32_t(c * kN);
-#pragma unroll
-                        for (int ks = 0; ks < kKeys / 16; ++ks) {
-                            const uint64_t ad = umma_desc_sw128(va + ks * 2048, kChunkBytes, 1024);
-                            umma_bf16(o_c, ad, umma_desc_sw128(p0 + ks * 2048, kChunkBytes, 1024), idesc_pv,
-                                      (i > 0 || ks > 0) ? 1u : 0u);
-                            if (!cols)
-                                umma_bf16(o_c, ad, umma_desc_sw128(p1 + ks * 2048, kChunkBytes, 1024), idesc_pv, 1u);
-                        }
-                        umma_commit(&ms->empty[slot]);
-                    }
-                    if (!ok) break;
-                    umma_commit(&ms->odone);
-                }
+                if (!ok) break;
+                umma_commit(&ms->sfull[sb]);
             }
-            // All issued MMAs complete before TMEM is read back or freed.
             umma_commit(&ms->final_mma);
-            mbar_wait(&ms->final_mma, 0);
+        } else if (warp == 1 && lane == 0) {
+            // ---- P.V issuer: O^T += V(j)^T . P(j)^T once P(j) is written ----
+            const uint32_t idesc_pair = umma_idesc_bf16(128, kN, 1, 1);
+            const uint32_t idesc_one = umma_idesc_bf16(64, kN, 1, 1);
+            const uint32_t p0 = sbase + off_p, p1 = p0 + kChunkBytes;
+            bool ok = true;
+            for (int j = 0; j < nt && ok; ++j) {
+                if (!(ok = wait_or_abort(&ms->pfull, j & 1, ms, J.status))) break;
+                tc_fence_after();
+                for (int blk = 0; blk < vblocks; ++blk) {
+                    const int c0 = 2 * blk;
+                    const bool pair = c0 + 1 < vc;
+                    for (int c = c0; c <= c0 + (pair ? 1 : 0); ++c)
+                        if (!(ok = wait_or_abort(&ms->vfull[c], j & 1, ms, J.status))) break;
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t va = sbase + c0 * kChunkBytes;
+                    const uint32_t o_b = o_tmem + uint32_t(blk * kN);
+                    const uint32_t idesc = pair ? idesc_pair : idesc_one;
+#pragma unroll
+                    for (int ks = 0; ks < kKeys / 16; ++ks) {
+                        const uint64_t ad = umma_desc_sw128(va + ks * 2048, kChunkBytes, 1024);
+                        umma_bf16(o_b, ad, umma_desc_sw128(p0 + ks * 2048, kChunkBytes, 1024), idesc,
+                                  (j > 0 || ks > 0) ? 1u : 0u);
+                        if (!cols) umma_bf16(o_b, ad, umma_desc_sw128(p1 + ks * 2048, kChunkBytes, 1024), idesc, 1u);
+                    }
+                    umma_commit(&ms->vempty[c0]);
+                    if (pair) umma_commit(&ms->vempty[c0 + 1]);
+                }
+                if (!ok) break;
+                umma_commit(&ms->odone);
+            }
+            umma_commit(&ms->final_mma);
         } else if (warp >= 3) {
             // ---- softmax and epilogue: thread <-> key (TMEM lane) ----
             const int quarter = warp & 3;
@@ -332,16 +360,14 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
                 // whatever the cache has there; P is zero for them, and zeroing
                 // the rows too keeps a non-finite stale value from turning 0 * x
                 // into NaN.  Each thread clears its own key row once the chunk
-                // has landed (the slot is not consumed before P is released).
+                // has landed (P.V(i) does not start before P(i) is released).
                 if (i == nt - 1 && t0 + i == n_tiles - 1 && (n_keys & (kKeys - 1)) != 0) {
                     bool okc = true;
                     if (key >= n_keys) {
-                        const int n0 = J.kchunks * nt + J.vchunks * (nt - 1);
-                        for (int c = 0; c < J.vchunks && okc; ++c) {
-                            const int slot = (n0 + c) % ring;
-                            okc = wait_or_abort(&ms->full[slot], ((n0 + c) / ring) & 1, ms, J.status);
+                        for (int c = 0; c < vc && okc; ++c) {
+                            okc = wait_or_abort(&ms->vfull[c], i & 1, ms, J.status);
                             if (okc) {
-                                uint4* row = reinterpret_cast<uint4*>(smem + slot * kChunkBytes + t_local * 128);
+                                uint4* row = reinterpret_cast<uint4*>(smem + c * kChunkBytes + t_local * 128);
 #pragma unroll
                                 for (int u = 0; u < 8; ++u) row[u] = make_uint4(0, 0, 0, 0);
                             }
@@ -352,10 +378,10 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
                 if (need_fix) {
                     // O^T column group k (32 columns) belongs to row k*32 + h, or
                     // to row h for the single-query hi | lo layout.
-                    for (int c = 0; c < J.vchunks; ++c)
+                    for (int blk = 0; blk < vblocks; ++blk)
                         for (int k = 0; k < 2; ++k) {
                             float o[32];
-                            const uint32_t addr = o_tmem + lane_addr + uint32_t(c * kN + 32 * k);
+                            const uint32_t addr = o_tmem + lane_addr + uint32_t(blk * kN + 32 * k);
                             tmem_ld32(addr, o);
                             tmem_wait_ld();
                             const float* al = ms->alpha + (cols ? 0 : 32 * k);
@@ -408,18 +434,20 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
                 // per-row 1 / l (0 for a row without mass)
                 if (st < 64) ms->alpha[st] = (st < rows && ms->l_run[st] > 0.f) ? 1.f / ms->l_run[st] : 0.f;
                 named_bar(1, 128);
-                // Stage O / l as [chunk][row][64] fp32 in the (drained) ring:
-                // the M=64 accumulator holds dim 16q + L of a chunk in lane
-                // L < 16 of quarter q.
+                // Stage O as [chunk][row][64] fp32 in the drained V ring.  An
+                // M=128 block holds dim 32q + L of its chunk pair in lane L of
+                // quarter q; the M=64 block holds dim 16q + L in lane L < 16.
                 // (1 / l is applied when the rows are written out.)
                 float* stage = reinterpret_cast<float*>(smem);
-                for (int c = 0; c < J.vchunks; ++c) {
+                for (int blk = 0; blk < vblocks; ++blk) {
+                    const bool pair = 2 * blk + 1 < vc;
                     float o[2][32];
-                    tmem_ld32(o_tmem + lane_addr + uint32_t(c * kN), o[0]);
-                    tmem_ld32(o_tmem + lane_addr + uint32_t(c * kN + 32), o[1]);
+                    tmem_ld32(o_tmem + lane_addr + uint32_t(blk * kN), o[0]);
+                    tmem_ld32(o_tmem + lane_addr + uint32_t(blk * kN + 32), o[1]);
                     tmem_wait_ld();
-                    if (lane < 16) {
-                        float* dst = stage + (c * 64) * 64 + 16 * quarter + lane;
+                    if (pair || lane < 16) {
+                        const int dd = pair ? 32 * quarter + lane : 16 * quarter + lane;   // dim in the block
+                        float* dst = stage + ((2 * blk + (dd >> 6)) * 64) * 64 + (dd & 63);
                         if (cols) {
 #pragma unroll
                             for (int h = 0; h < 32; ++h) dst[h * 64] = o[0][h] + o[1][h];
@@ -431,7 +459,7 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
                 }
                 named_bar(1, 128);
                 const int64_t base_row = ((int64_t)b * J.splits + split) * J.rows_alloc;
-                const int width = min(J.vchunks * 64, J.out_width);
+                const int width = min(vc * 64, J.out_width);
                 const int f4 = width / 4, items = rows * f4;
                 // Batches of eight row pieces: all shared loads, then all stores.
 #pragma unroll 1
@@ -469,11 +497,20 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
             J.part_o[(base_row + idx / J.out_width) * J.out_width + idx % J.out_width] = 0.f;
     }
     __syncthreads();
+    if (nt > 0 && tid == 64) {
+        // Both issuers committed final_mma after their last MMA: every MMA has
+        // completed before TMEM is freed (bounded wait).
+        mbar_wait(&ms->final_mma, 0, kWaitNs);
+    }
     if (ms->abort && tid == 0) {
         // Drain: wait (bounded) for the last copy issued into every slot.
-        for (int s = 0; s < ring; ++s) {
-            mbar_wait(&ms->full[s], 0, 100000000ull);
-            mbar_wait(&ms->full[s], 1, 100000000ull);
+        for (int s = 0; s < kring; ++s) {
+            mbar_wait(&ms->kfull[s], 0, 100000000ull);
+            mbar_wait(&ms->kfull[s], 1, 100000000ull);
+        }
+        for (int s = 0; s < vc; ++s) {
+            mbar_wait(&ms->vfull[s], 0, 100000000ull);
+            mbar_wait(&ms->vfull[s], 1, 100000000ull);
         }
         mbar_wait(&ms->qfull, 0, 100000000ull);
     }
