@@ -72,6 +72,23 @@ int encode_map_4d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, 
     return SLIMKV_OK;
 }
 
+int encode_map_f32_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+                      uint64_t s2, uint32_t box0, uint32_t box1) {
+    auto fn = encode_fn();
+    if (!fn) return fail(SLIMKV_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {s1, s2};
+    cuuint32_t box[3] = {box0, box1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(SLIMKV_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled (f32) failed (%d): dims {%llu,%llu,%llu}", int(r),
+                    (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2);
+    return SLIMKV_OK;
+}
+
 }  // namespace slimkv
 
 extern "C" const char* slimkv_last_error(void) { return slimkv::g_last_error.c_str(); }

@@ -61,22 +61,6 @@ struct DecodePlan {
     size_t q_rot = 0, q_lat = 0, lat_o = 0, lat_lse = 0, raw_o = 0, raw_lse = 0;
 };
 
-// Raw-branch CTAs of the tensor-memory route: shallower pipeline so two CTAs
-// share an SM.
-constexpr int kRawBudget = 64 * 1024;
-
-__global__ void __launch_bounds__(kThreads, 2)
-raw_attention_kernel(const __grid_constant__ CUtensorMap rk, const __grid_constant__ CUtensorMap rv, AttnJob jr) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    if (threadIdx.x == 0) { tma_prefetch_desc(&rk); tma_prefetch_desc(&rv); }
-    jr.kmap = &rk;
-    jr.vmap = &rv;
-    const int split = blockIdx.x % jr.splits;
-    const int bg = blockIdx.x / jr.splits;
-    attn_body<128, 1, kRawBudget>(jr, bg / jr.kv_heads, bg % jr.kv_heads, split, 0, smem);
-}
-
 int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
     if (!a) return fail(SLIMKV_ERR_INVALID_ARGUMENT, "null arguments");
     if (a->batch <= 0 || a->heads <= 0 || a->kv_heads <= 0 || a->heads % a->kv_heads)
@@ -118,20 +102,23 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
     p.raw_tps = (raw_tiles + rs - 1) / rs;
     p.raw_splits = (raw_tiles + p.raw_tps - 1) / p.raw_tps;
     const size_t B = a->batch, L = a->length, H = a->heads;
-    p.tc = a->heads == 32 && a->latent_splits <= 0;
+    p.tc = a->heads == 32;
     if (p.tc) {
-        // 128-key tiles, one resident CTA per SM over the whole machine; the
-        // raw branch runs as its own launch before it, two CTAs per SM.
+        // One launch, 128-key tiles, one CTA per SM: the latent CTAs leave
+        // about one SM per sequence free, where the (short) raw CTAs start;
+        // the rest of the raw CTAs follow as latent CTAs finish.
         const int sms = std::max(device_info().sm_count, 1);
         const int tiles = std::max(1, (lat_len + kTcTileKeys - 1) / kTcTileKeys);
-        int s2 = std::max(1, std::min({tiles, sms / a->batch, 32}));
-        p.lat_tps = (tiles + s2 - 1) / s2;
-        p.lat_splits = (tiles + p.lat_tps - 1) / p.lat_tps;
+        const int per_seq = sms / a->batch;
+        int s2 = a->latent_splits > 0 ? a->latent_splits : (per_seq >= 3 ? per_seq - 1 : std::max(per_seq, 1));
+        p.lat_splits = std::max(1, std::min({s2, tiles, 32}));
+        p.lat_tps = (tiles + p.lat_splits - 1) / p.lat_splits;
         p.lat_rows = 64;
-        int r2 = a->raw_splits > 0 ? a->raw_splits : std::max(1, (2 * sms) / (a->batch * a->kv_heads));
-        r2 = std::max(1, std::min({r2, raw_tiles, 32}));
-        p.raw_tps = (raw_tiles + r2 - 1) / r2;
-        p.raw_splits = (raw_tiles + p.raw_tps - 1) / p.raw_tps;
+        const int rtiles = std::max(1, (raw_len + kTcTileKeys - 1) / kTcTileKeys);
+        const int r2 = a->raw_splits > 0 ? a->raw_splits : 2;
+        p.raw_splits = std::max(1, std::min({r2, rtiles, 32}));
+        p.raw_tps = (rtiles + p.raw_splits - 1) / p.raw_splits;
+        p.raw_rows = 64;
     }
     p.q_rot = B * L * H * a->head_dim;
     p.q_lat = p.tc ? B * 128 * p.wl : B * L * H * p.wl;
@@ -291,29 +278,25 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     jr.part_o = w.raw_o; jr.part_lse = w.raw_lse; jr.status = status;
     const int n_raw = a->batch * a->kv_heads * p.raw_splits;
     if (p.tc) {
-        // Raw branch first (its own launch), then the latent branch on the
-        // tensor-memory kernel.
-        constexpr int rsmem = AttnCfg<128, 1, kRawBudget>::SMEM;
-        static bool raw_configured[64] = {};
-        const int dev = device_info().device;
-        if (dev >= 0 && dev < 64 && !raw_configured[dev]) {
-            if (cudaFuncSetAttribute(raw_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rsmem) !=
-                cudaSuccess)
-                return fail(SLIMKV_ERR_CUDA, "cudaFuncSetAttribute (raw) failed");
-            raw_configured[dev] = true;
-        }
-        raw_attention_kernel<<<n_raw, kThreads, rsmem, stream>>>(rk, rv, jr);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "raw attention launch failed: %s", cudaGetErrorString(e));
+        // Both branches in one launch of the tensor-core kernel.
         TcLaunch tl{};
-        tl.batch = a->batch; tl.length = a->length; tl.rank_k = a->rank_k; tl.rank_v = a->rank_v;
-        tl.width = p.wl; tl.lat_capacity = a->lat_capacity;
-        tl.lat_k = a->lat_k; tl.lat_v = a->lat_v;
-        tl.lat_stride_batch = a->lat_stride_batch; tl.lat_stride_row = a->lat_stride_row;
-        tl.q_hilo = w.q_lat; tl.latent_len = a->latent_len; tl.query_len = a->query_len; tl.scale = a->scale;
-        tl.splits = p.lat_splits; tl.tiles_per_split = p.lat_tps; tl.rows_alloc = p.lat_rows;
-        tl.part_o = w.lat_o; tl.part_lse = w.lat_lse; tl.status = status;
-        if ((rc = launch_latent_tc(tl, stream))) return rc;
+        tl.batch = a->batch; tl.length = a->length; tl.scale = a->scale;
+        tl.query_len = a->query_len; tl.status = status; tl.with_raw = 1;
+        TcSide& L = tl.lat;
+        L.k = a->lat_k; L.v = a->lat_v; L.dim_k = a->rank_k; L.dim_v = a->rank_v;
+        L.kv_heads = 1; L.capacity = a->lat_capacity;
+        L.stride_batch = a->lat_stride_batch; L.stride_row = a->lat_stride_row; L.stride_head = 0;
+        L.q = w.q_lat; L.q_rows = 0; L.heads = a->heads; L.group = a->heads; L.causal = 1;
+        L.seqlens = a->latent_len; L.splits = p.lat_splits; L.rows_alloc = p.lat_rows; L.width = p.wl;
+        L.part_o = w.lat_o; L.part_lse = w.lat_lse;
+        TcSide& R = tl.raw;
+        R.k = a->raw_k_rot; R.v = a->raw_v; R.dim_k = a->head_dim; R.dim_v = a->head_dim;
+        R.kv_heads = a->kv_heads; R.capacity = a->raw_capacity;
+        R.stride_batch = a->raw_stride_batch; R.stride_row = a->raw_stride_token; R.stride_head = a->head_dim;
+        R.q = w.q_rot; R.q_rows = 1; R.heads = a->heads; R.group = p.group; R.causal = 0;
+        R.seqlens = a->raw_len; R.splits = p.raw_splits; R.rows_alloc = p.raw_rows; R.width = a->head_dim;
+        R.part_o = w.raw_o; R.part_lse = w.raw_lse;
+        if ((rc = launch_decode_tc(tl, stream))) return rc;
     } else {
     const int n_latent = a->batch * p.lat_row_blocks * p.lat_splits;
     switch (p.wl) {
@@ -330,6 +313,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     ma.lat_o = w.lat_o; ma.lat_lse = w.lat_lse; ma.lat_splits = p.lat_splits; ma.lat_rows = p.lat_rows;
     ma.lat_width = p.wl;
     ma.raw_o = w.raw_o; ma.raw_lse = w.raw_lse; ma.raw_splits = p.raw_splits; ma.raw_rows = p.raw_rows;
+    ma.raw_l_pitch = p.tc ? 32 : p.group;
     ma.q_rot = w.q_rot;
     ma.uv = static_cast<const __nv_bfloat16*>(a->uv);
     ma.uk_bias = static_cast<const __nv_bfloat16*>(a->uk_bias);

@@ -237,6 +237,7 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
 struct MergeArgs {
     const float* lat_o; const float* lat_lse; int lat_splits, lat_rows, lat_width;
     const float* raw_o; const float* raw_lse; int raw_splits, raw_rows;
+    int raw_l_pitch;        // raw partial row of (query l, head j): l * raw_l_pitch + j
     const __nv_bfloat16* q_rot;
     const __nv_bfloat16* uv; const __nv_bfloat16* uk_bias; const __nv_bfloat16* uv_bias;
     const int32_t* qlens;
@@ -245,62 +246,73 @@ struct MergeArgs {
     void* out; int out_fp32; int64_t o_sb, o_sl;
 };
 
-// Dynamic shared memory of decode_merge_kernel for a padded value rank.
+// Dynamic shared memory of decode_merge_kernel for a padded value rank:
+// U_v[g] bf16 [128 x rvp], o_lat hi and lo bf16 [16 x rvp] each, raw rows
+// fp32 [16 x dim], LSEs [2][16], split weights [2][16][32].
 __host__ __device__ constexpr size_t merge_smem_bytes(int rank_v_pad, int dim) {
-    return 1024 + size_t(128 + 16) * rank_v_pad * 2 + size_t(16) * dim * 4 + 32 * 4 + 2 * 16 * 32 * 4;
+    return 1024 + size_t(128 + 32) * rank_v_pad * 2 + size_t(16) * dim * 4 + 32 * 4 + 2 * 16 * 32 * 4;
 }
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_wait_all() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 // grid (Hkv, ceil(B / seq_per_cta)), 256 threads, merge_smem_bytes() of
 // dynamic shared memory.  CTA (g, bb) merges the (<= 16) query rows
 // (seq_per_cta sequences x L x group) of KV head g.
-//   1. U_v[g] -> shared (fp16) as the MMA's column-major B operand.
+//   1. U_v[g] -> shared with asynchronous copies (bf16 as stored, the MMA's
+//      column-major B operand), overlapping steps 2-3.
 //   2. One warp per row: lane s holds split s's LSE of each branch and turns
 //      it into a normalised weight (splits <= 32); the row's LSEs (latent one
 //      shifted by scale * q . b_k) go to shared memory.
-//   3. All threads: weighted split sums over (row, 4-column) items, every
-//      split's load independent of the others.
-//   4. Up-projection on the tensor cores, bias, LSE merge, store.
+//   3. All threads: weighted split sums over (row, 4-column) items of the
+//      valid rows, every split's load independent of the others; the latent
+//      rows are kept as a bf16 pair hi + lo (fp32-level accuracy through the
+//      bf16 tensor cores).
+//   4. Up-projection (two MMAs per k-step: hi and lo rows), bias, LSE merge,
+//      store.
 __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int rvp = a.rank_v_pad;                       // multiple of 64
-    uint8_t* s_b = smem;                                // U_v[g]: rvp/64 chunks [128 x 64] fp16
-    uint8_t* s_a = s_b + 128 * rvp * 2;                 // o_lat: rvp/64 chunks [16 x 64] fp16
-    float* s_raw = reinterpret_cast<float*>(s_a + 16 * rvp * 2);   // [16][D]
+    uint8_t* s_b = smem;                                // U_v[g]: rvp/64 chunks [128 x 64] bf16
+    uint8_t* s_hi = s_b + 128 * rvp * 2;                // o_lat hi: rvp/64 chunks [16 x 64] bf16
+    uint8_t* s_lo = s_hi + 16 * rvp * 2;                // o_lat lo
+    float* s_raw = reinterpret_cast<float*>(s_lo + 16 * rvp * 2);   // [16][D]
     float* s_lse = s_raw + 16 * a.dim;                  // [2][16]: latent, raw
     float* s_w = s_lse + 32;                            // [2][16][32] split weights: latent, raw
     const int g = blockIdx.x, bb = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rps = a.length * a.group, b0 = bb * a.seq_per_cta;
+    const int nrows = min(16, a.seq_per_cta * rps);
+    // rr: the row's index in the raw branch partials.
     auto row_info = [&](int r, int& b, int& l, int& h, int& rr) -> bool {
-        const int s = r / rps;
-        rr = r - s * rps;
-        l = rr / a.group;
+        const int s = r / rps, rs = r - s * rps;
+        l = rs / a.group;
         b = b0 + s;
-        h = g * a.group + (rr - l * a.group);
-        return s < a.seq_per_cta && b < a.batch && l < (a.qlens ? a.qlens[b] : a.length);
+        const int j = rs - l * a.group;
+        h = g * a.group + j;
+        rr = l * a.raw_l_pitch + j;
+        return r < nrows && b < a.batch && l < (a.qlens ? a.qlens[b] : a.length);
     };
 
-    // 1. Stage U_v[g] (rows d, columns c) as the MMA's column-major B operand:
-    //    batches of ten independent read-only loads, then the stores.
+    // 1. U_v[g] (rows d, columns c) -> shared, asynchronously; zero columns
+    //    past the rank.
     const int units = rvp / 8;
-#pragma unroll 1
-    for (int i0 = 0; i0 < 128 * units; i0 += 2560) {
-        uint4 v[10];
-#pragma unroll
-        for (int k = 0; k < 10; ++k) {
-            const int i = i0 + k * 256 + tid, d = i / units, col = (i - d * units) * 8;
-            v[k] = make_uint4(0, 0, 0, 0);
-            if (i < 128 * units && col < a.rank_v)
-                v[k] = __ldg(reinterpret_cast<const uint4*>(a.uv + ((int64_t)g * a.dim + d) * a.rank_v + col));
-        }
-#pragma unroll
-        for (int k = 0; k < 10; ++k) {
-            const int i = i0 + k * 256 + tid, d = i / units, u = i - d * units;
-            if (i < 128 * units)
-                *reinterpret_cast<uint4*>(s_b + (u >> 3) * (128 * 128) + sw128(d, (u & 7) * 8)) = widen8(v[k]);
-        }
+    for (int i = tid; i < 128 * units; i += 256) {
+        const int d = i / units, u = i - d * units, col = u * 8;
+        uint8_t* dst = s_b + (u >> 3) * (128 * 128) + sw128(d, (u & 7) * 8);
+        if (col < a.rank_v) cp_async16(dst, a.uv + ((int64_t)g * a.dim + d) * a.rank_v + col);
+        else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
+    cp_async_commit();
+    // Rows of the A operand that no query fills stay zero.
+    for (int i = tid; i < 2 * 16 * rvp / 8; i += 256) reinterpret_cast<uint4*>(s_hi)[i] = make_uint4(0, 0, 0, 0);
     // 2. Split weights and LSEs per row.
     for (int r = warp; r < 16; r += 8) {
         int b, l, h, rr;
@@ -338,36 +350,38 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
         }
     }
     __syncthreads();
-    // 3a. Latent branch: o_lat[r, c:c+4] = sum_s w_s * part_s[r, c:c+4] -> fp16 A operand.
+    // 3a. Latent branch: o_lat[r, c:c+4] = sum_s w_s * part_s[r, c:c+4] -> bf16 hi / lo.
     {
         const int c4n = rvp / 4;
         const int64_t pitch = (int64_t)a.lat_rows * a.lat_width;
-        for (int it = tid; it < 16 * c4n; it += 256) {
+        for (int it = tid; it < nrows * c4n; it += 256) {
             const int r = it / c4n, c = (it - r * c4n) * 4;
             int b, l, h, rr;
+            if (!row_info(r, b, l, h, rr) || c >= a.lat_width) continue;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (row_info(r, b, l, h, rr) && c < a.lat_width) {
-                const float* src = a.lat_o + ((int64_t)b * a.lat_splits * a.lat_rows + l * a.heads + h) * a.lat_width + c;
-                const float* w = s_w + r * 32;
-                int s = 0;
-                for (; s + 8 <= a.lat_splits; s += 8) {
-                    float4 x[8];
+            const float* src = a.lat_o + ((int64_t)b * a.lat_splits * a.lat_rows + l * a.heads + h) * a.lat_width + c;
+            const float* w = s_w + r * 32;
+            int s = 0;
+            for (; s + 8 <= a.lat_splits; s += 8) {
+                float4 x[8];
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) x[u] = __ldg(reinterpret_cast<const float4*>(src + (s + u) * pitch));
+                for (int u = 0; u < 8; ++u) x[u] = __ldg(reinterpret_cast<const float4*>(src + (s + u) * pitch));
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        acc.x = fmaf(w[s + u], x[u].x, acc.x); acc.y = fmaf(w[s + u], x[u].y, acc.y);
-                        acc.z = fmaf(w[s + u], x[u].z, acc.z); acc.w = fmaf(w[s + u], x[u].w, acc.w);
-                    }
-                }
-                for (; s < a.lat_splits; ++s) {
-                    const float4 x = __ldg(reinterpret_cast<const float4*>(src + s * pitch));
-                    acc.x = fmaf(w[s], x.x, acc.x); acc.y = fmaf(w[s], x.y, acc.y);
-                    acc.z = fmaf(w[s], x.z, acc.z); acc.w = fmaf(w[s], x.w, acc.w);
+                for (int u = 0; u < 8; ++u) {
+                    acc.x = fmaf(w[s + u], x[u].x, acc.x); acc.y = fmaf(w[s + u], x[u].y, acc.y);
+                    acc.z = fmaf(w[s + u], x[u].z, acc.z); acc.w = fmaf(w[s + u], x[u].w, acc.w);
                 }
             }
-            *reinterpret_cast<uint2*>(s_a + (c >> 6) * (16 * 128) + sw128(r, c & 63)) =
-                make_uint2(pack_f16x2(acc.x, acc.y), pack_f16x2(acc.z, acc.w));
+            for (; s < a.lat_splits; ++s) {
+                const float4 x = __ldg(reinterpret_cast<const float4*>(src + s * pitch));
+                acc.x = fmaf(w[s], x.x, acc.x); acc.y = fmaf(w[s], x.y, acc.y);
+                acc.z = fmaf(w[s], x.z, acc.z); acc.w = fmaf(w[s], x.w, acc.w);
+            }
+            const float hx = bf16_round(acc.x), hy = bf16_round(acc.y), hz = bf16_round(acc.z), hw = bf16_round(acc.w);
+            const int off = (c >> 6) * (16 * 128) + sw128(r, c & 63);
+            *reinterpret_cast<uint2*>(s_hi + off) = make_uint2(pack_bf16x2(hx, hy), pack_bf16x2(hz, hw));
+            *reinterpret_cast<uint2*>(s_lo + off) =
+                make_uint2(pack_bf16x2(acc.x - hx, acc.y - hy), pack_bf16x2(acc.z - hz, acc.w - hw));
         }
     }
     // 3b. Raw branch: fp32 combined output rows.
@@ -401,30 +415,35 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
             *reinterpret_cast<float4*>(s_raw + r * a.dim + c) = acc;
         }
     }
+    cp_async_wait_all();
     __syncthreads();
-    // 3. [16 x Rvp] . [Rvp x 128]: warp -> output columns [16*warp, 16*warp + 16).
+    // 4. [16 x Rvp] . [Rvp x 128] with A = hi + lo: warp -> output columns
+    //    [16*warp, 16*warp + 16).
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    const uint32_t a_base = smem_u32(s_a), b_base = smem_u32(s_b);
+    const uint32_t hi_base = smem_u32(s_hi), lo_base = smem_u32(s_lo), b_base = smem_u32(s_b);
     const int mi = lane >> 3;
     for (int ks = 0; ks < rvp / 16; ++ks) {
-        uint32_t af[4];
+        uint32_t ah[4], al[4];
         const int row = (lane & 7) + (mi & 1) * 8;
         const int unit = (ks & 3) * 2 + (mi >> 1);
-        ldsm_x4(a_base + (ks >> 2) * (16 * 128) + row * 128 + (((unit ^ row) & 7) << 4), af[0], af[1], af[2], af[3]);
+        const uint32_t aoff = (ks >> 2) * (16 * 128) + row * 128 + (((unit ^ row) & 7) << 4);
+        ldsm_x4(hi_base + aoff, ah[0], ah[1], ah[2], ah[3]);
+        ldsm_x4(lo_base + aoff, al[0], al[1], al[2], al[3]);
         const int n = 16 * warp + (mi >> 1) * 8 + (lane & 7);
         const int bunit = (ks & 3) * 2 + (mi & 1);
         uint32_t b0, b1, b2, b3;
         ldsm_x4(b_base + (ks >> 2) * (128 * 128) + n * 128 + (((bunit ^ n) & 7) << 4), b0, b1, b2, b3);
-        mma_f16(acc[0], af, b0, b1);
-        mma_f16(acc[1], af, b2, b3);
+        mma_bf16(acc[0], ah, b0, b1);
+        mma_bf16(acc[1], ah, b2, b3);
+        mma_bf16(acc[0], al, b0, b1);
+        mma_bf16(acc[1], al, b2, b3);
     }
-    // 4. Bias, LSE merge (fa2_decode.py:57-66) and store.
+    // 5. Bias, LSE merge (fa2_decode.py:57-66) and store.
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
         const int r = (lane >> 2) + 8 * hh;
-        const int s = r / rps, rr = r - s * rps, l = rr / a.group, j = rr - l * a.group;
-        const int b = b0 + s, h = g * a.group + j;
-        if (s >= a.seq_per_cta || b >= a.batch || l >= (a.qlens ? a.qlens[b] : a.length)) continue;
+        int b, l, h, rr;
+        if (!row_info(r, b, l, h, rr)) continue;
         const float ll = s_lse[r], lr = s_lse[16 + r];
         float wr = 0.f, wl = 0.f;
         if (!(ll == -INFINITY && lr == -INFINITY)) {

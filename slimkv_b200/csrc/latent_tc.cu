@@ -28,8 +28,8 @@
 // Softmax: one key per thread reading its TMEM lane, column maxima and sums
 // via warp transpose-reduce, and a lazy rescale (the running max moves only
 // when a column max exceeds it by 2^8, so the TMEM read-modify-write of O^T is
-// rare).  The epilogue stages the normalised partial output through shared
-// memory and stores whole rows.
+// rare).  The epilogue stages the normalised partial output in shared memory
+// and writes it with bulk tensor stores.
 //
 // Warp roles (7 warps): 0 = TMA producer, 1 = P.V issuer, 2 = TMEM allocator
 // and S issuer, 3-6 = softmax / epilogue (TMEM lane quarters 3, 0, 1, 2).  No
@@ -128,14 +128,29 @@ __device__ __forceinline__ void split_hilo(const float (&p)[32], int u, uint4& h
 
 }  // namespace
 
+// CTAs [0, n_lat) take latent work (b, split); the rest raw work
+// (b, KV head g, split).  Each branch has its own K / V / Q / partial-output
+// maps and job.
 __global__ void __launch_bounds__(kThreads7, 1)
-latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-                 const __grid_constant__ CUtensorMap qmap, TcJob J) {
+decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constant__ CUtensorMap lvmap,
+                 const __grid_constant__ CUtensorMap lqmap, const __grid_constant__ CUtensorMap lomap,
+                 const __grid_constant__ CUtensorMap rkmap, const __grid_constant__ CUtensorMap rvmap,
+                 const __grid_constant__ CUtensorMap rqmap, const __grid_constant__ CUtensorMap romap,
+                 const __grid_constant__ TcJob jl, const __grid_constant__ TcJob jr, int n_lat) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Misc* ms = reinterpret_cast<Misc*>(smem + kOffMisc);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int b = blockIdx.x / J.splits, split = blockIdx.x % J.splits;
+    const bool is_lat = int(blockIdx.x) < n_lat;
+    const TcJob& J = is_lat ? jl : jr;
+    const CUtensorMap* kmap = is_lat ? &lkmap : &rkmap;
+    const CUtensorMap* vmap = is_lat ? &lvmap : &rvmap;
+    const CUtensorMap* qmap = is_lat ? &lqmap : &rqmap;
+    const CUtensorMap* omap = is_lat ? &lomap : &romap;
+    const int idx = is_lat ? int(blockIdx.x) : int(blockIdx.x) - n_lat;
+    const int split = idx % J.splits, bg = idx / J.splits;
+    const int b = bg / J.kv_heads, g = bg - b * J.kv_heads;
+    const int z = bg * J.splits + split;                     // partial-output slot
     const int n_keys = J.seqlens[b];
     const int nq = J.qlens ? J.qlens[b] : J.length;          // 1 or 2 queries
     const bool cols = nq == 1;                               // hi / lo as separate columns
@@ -155,15 +170,22 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
     auto issue_k = [&](int n) {
         const int slot = n % kring;
         mbar_expect_tx(&ms->kfull[slot], kChunkBytes);
-        tma_load_4d(smem + kOffK + slot * kChunkBytes, &kmap, &ms->kfull[slot], (n % kc) * 64, 0,
+        tma_load_4d(smem + kOffK + slot * kChunkBytes, kmap, &ms->kfull[slot], (n % kc) * 64, g,
                     (t0 + n / kc) * kKeys, b);
     };
     auto issue_v = [&](int n) {
         const int slot = n % vc;
         mbar_expect_tx(&ms->vfull[slot], kChunkBytes);
-        tma_load_4d(smem + slot * kChunkBytes, &vmap, &ms->vfull[slot], slot * 64, 0, (t0 + n / vc) * kKeys, b);
+        tma_load_4d(smem + slot * kChunkBytes, vmap, &ms->vfull[slot], slot * 64, g, (t0 + n / vc) * kKeys, b);
     };
 
+    if (warp == 0 && J.q_rows && nt > 0) {
+        // Row-mode Q fills only the valid rows of each chunk: zero the rest.
+        for (int i = lane; i < kc * int(kQChunkBytes / 16); i += 32)
+            reinterpret_cast<uint4*>(smem + off_q)[i] = make_uint4(0, 0, 0, 0);
+        fence_async_shared();
+        __syncwarp();
+    }
     if (tid == 0) {
         for (int s = 0; s < kKRingMax; ++s) { mbar_init(&ms->kfull[s], 1); mbar_init(&ms->kempty[s], 1); }
         for (int s = 0; s < kMaxChunks; ++s) { mbar_init(&ms->vfull[s], 1); mbar_init(&ms->vempty[s], 1); }
@@ -178,13 +200,22 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
         // the first tile's V chunks (first use of each slot needs no wait)
         // overlap the setup below.
         if (nt > 0) {
-            // Q rows of the sequence: [hi | lo] x 32 * nq (one 64-row box per
-            // chunk for nq = 1, hi and lo boxes for nq = 2).
-            mbar_expect_tx(&ms->qfull, uint32_t(nq * kc) * kQChunkBytes);
-            for (int c = 0; c < kc; ++c)
-                for (int hl = 0; hl < nq; ++hl)
-                    tma_load_4d(smem + off_q + (hl * kMaxChunks + c) * kQChunkBytes, &qmap, &ms->qfull, c * 64, 0,
-                                hl * 64, b);
+            if (J.q_rows) {
+                // The group's query heads of query l -> rows 32 l + j.
+                mbar_expect_tx(&ms->qfull, uint32_t(kc * nq * J.group) * 128u);
+                for (int c = 0; c < kc; ++c)
+                    for (int l = 0; l < nq; ++l)
+                        tma_load_4d(smem + off_q + c * kQChunkBytes + l * 32 * 128, qmap, &ms->qfull, c * 64, 0,
+                                    g * J.group, b * J.length + l);
+            } else {
+                // Q rows of the sequence: [hi | lo] x 32 * nq (one 64-row box
+                // per chunk for nq = 1, hi and lo boxes for nq = 2).
+                mbar_expect_tx(&ms->qfull, uint32_t(nq * kc) * kQChunkBytes);
+                for (int c = 0; c < kc; ++c)
+                    for (int hl = 0; hl < nq; ++hl)
+                        tma_load_4d(smem + off_q + (hl * kMaxChunks + c) * kQChunkBytes, qmap, &ms->qfull, c * 64,
+                                    0, hl * 64, b);
+            }
             for (int n = 0; n < kring && n < total_k; ++n) issue_k(n);
             for (int n = 0; n < vc && n < total_v; ++n) issue_v(n);
         }
@@ -252,7 +283,7 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
                         const uint64_t ad = umma_desc_sw128(ka + kk * 32, 16, 1024);
                         umma_bf16(s_tmem, ad, umma_desc_sw128(q0 + c * kQChunkBytes + kk * 32, 16, 1024), idesc_s,
                                   (c | kk) != 0);
-                        if (!cols)
+                        if (!cols && !J.q_rows)
                             umma_bf16(s_tmem, ad, umma_desc_sw128(q1 + c * kQChunkBytes + kk * 32, 16, 1024), idesc_s,
                                       1u);
                     }
@@ -323,7 +354,7 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
                 // scale and mask (an insertion step's raw query excludes the new Beacon)
 #pragma unroll
                 for (int l = 0; l < 2; ++l) {
-                    const int limit = (nq == 2 && l == 0) ? n_keys - 1 : n_keys;
+                    const int limit = (J.causal && nq == 2 && l == 0) ? n_keys - 1 : n_keys;
 #pragma unroll
                     for (int h = 0; h < 32; ++h) v[l][h] = key < limit ? v[l][h] * J.scale_log2 : -INFINITY;
                 }
@@ -434,10 +465,16 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
                 // per-row 1 / l (0 for a row without mass)
                 if (st < 64) ms->alpha[st] = (st < rows && ms->l_run[st] > 0.f) ? 1.f / ms->l_run[st] : 0.f;
                 named_bar(1, 128);
-                // Stage O as [chunk][row][64] fp32 in the drained V ring.  An
+                // Stage O / l as [chunk][row][64] fp32 in the drained V ring.  An
                 // M=128 block holds dim 32q + L of its chunk pair in lane L of
                 // quarter q; the M=64 block holds dim 16q + L in lane L < 16.
-                // (1 / l is applied when the rows are written out.)
+                // Bulk tensor stores then write whole [32 rows x 64] boxes.
+                float inv0[32], inv1[32];
+#pragma unroll
+                for (int h = 0; h < 32; ++h) {
+                    inv0[h] = ms->alpha[h];
+                    inv1[h] = ms->alpha[32 + h];
+                }
                 float* stage = reinterpret_cast<float*>(smem);
                 for (int blk = 0; blk < vblocks; ++blk) {
                     const bool pair = 2 * blk + 1 < vc;
@@ -450,35 +487,25 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
                         float* dst = stage + ((2 * blk + (dd >> 6)) * 64) * 64 + (dd & 63);
                         if (cols) {
 #pragma unroll
-                            for (int h = 0; h < 32; ++h) dst[h * 64] = o[0][h] + o[1][h];
+                            for (int h = 0; h < 32; ++h) dst[h * 64] = (o[0][h] + o[1][h]) * inv0[h];
                         } else {
 #pragma unroll
-                            for (int h = 0; h < 64; ++h) dst[h * 64] = o[h >> 5][h & 31];
+                            for (int h = 0; h < 32; ++h) {
+                                dst[h * 64] = o[0][h] * inv0[h];
+                                dst[(32 + h) * 64] = o[1][h] * inv1[h];
+                            }
                         }
                     }
                 }
+                fence_async_shared();
                 named_bar(1, 128);
-                const int64_t base_row = ((int64_t)b * J.splits + split) * J.rows_alloc;
-                const int width = min(vc * 64, J.out_width);
-                const int f4 = width / 4, items = rows * f4;
-                // Batches of eight row pieces: all shared loads, then all stores.
-#pragma unroll 1
-                for (int it0 = st; it0 < items; it0 += 8 * 128) {
-                    float4 val[8];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const int it = it0 + k * 128, r = it / f4, d = (it - r * f4) * 4;
-                        if (it < items) {
-                            val[k] = *reinterpret_cast<const float4*>(stage + ((d >> 6) * 64 + r) * 64 + (d & 63));
-                            const float inv = ms->alpha[r];
-                            val[k].x *= inv; val[k].y *= inv; val[k].z *= inv; val[k].w *= inv;
-                        }
-                    }
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const int it = it0 + k * 128, r = it / f4, d = (it - r * f4) * 4;
-                        if (it < items) *reinterpret_cast<float4*>(J.part_o + (base_row + r) * J.out_width + d) = val[k];
-                    }
+                const int64_t base_row = (int64_t)z * J.rows_alloc;
+                if (st == 0) {
+                    for (int c = 0; c < vc; ++c)
+                        for (int rb = 0; rb < nq; ++rb)
+                            tma_store_3d(omap, stage + (c * 64 + rb * 32) * 64, c * 64, rb * 32, z);
+                    bulk_commit();
+                    bulk_wait_read_all();
                 }
                 if (st < rows) {
                     const float lsum = ms->l_run[st];
@@ -491,7 +518,7 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
     } else if (tid >= 96) {
         // Empty split: zero mass.
         const int st = tid - 96;
-        const int64_t base_row = ((int64_t)b * J.splits + split) * J.rows_alloc;
+        const int64_t base_row = (int64_t)z * J.rows_alloc;
         if (st < rows) J.part_lse[base_row + st] = -INFINITY;
         for (int idx = st; idx < rows * J.out_width; idx += 128)
             J.part_o[(base_row + idx / J.out_width) * J.out_width + idx % J.out_width] = 0.f;
@@ -521,47 +548,80 @@ latent_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
     }
 }
 
-int launch_latent_tc(const TcLaunch& L, cudaStream_t stream) {
-    if (L.rank_k > 320 || L.rank_v > 320 || L.width < 64 || L.width % 64)
-        return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "latent tensor-core path needs ranks <= 320");
-    CUtensorMap km, vm, qm;
+namespace {
+
+int make_side(const TcSide& S, int batch, int length, float scale, const int32_t* qlens, unsigned* status, TcJob& J,
+              CUtensorMap& km, CUtensorMap& vm, CUtensorMap& qm, CUtensorMap& om) {
+    if (S.dim_k > 320 || S.dim_v > 320 || S.width < 64 || S.width % 64 || S.rows_alloc % 32 ||
+        (reinterpret_cast<uintptr_t>(S.part_o) & 15) || S.group > 32)
+        return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "tensor-core decode attention: unsupported branch shape");
     int rc;
-    if ((rc = encode_map_4d(&km, L.lat_k, L.rank_k, 1, L.lat_capacity, L.batch, L.lat_stride_row * 2,
-                            L.lat_stride_row * 2, L.lat_stride_batch * 2, kKeys)))
+    const uint64_t head_bytes = S.kv_heads > 1 ? uint64_t(S.stride_head) * 2 : uint64_t(S.stride_row) * 2;
+    if ((rc = encode_map_4d(&km, S.k, S.dim_k, S.kv_heads, S.capacity, batch, head_bytes, uint64_t(S.stride_row) * 2,
+                            uint64_t(S.stride_batch) * 2, kKeys)))
         return rc;
-    if ((rc = encode_map_4d(&vm, L.lat_v, L.rank_v, 1, L.lat_capacity, L.batch, L.lat_stride_row * 2,
-                            L.lat_stride_row * 2, L.lat_stride_batch * 2, kKeys)))
+    if ((rc = encode_map_4d(&vm, S.v, S.dim_v, S.kv_heads, S.capacity, batch, head_bytes, uint64_t(S.stride_row) * 2,
+                            uint64_t(S.stride_batch) * 2, kKeys)))
         return rc;
-    if ((rc = encode_map_4d(&qm, L.q_hilo, L.width, 1, 128, L.batch, uint64_t(L.width) * 2, uint64_t(L.width) * 2,
-                            uint64_t(L.width) * 2 * 128, 64)))
+    if (S.q_rows) {
+        // q_rot [B][L][H][dim] as (dim, 1, H, B * L), boxes of `group` rows.
+        const uint64_t row = uint64_t(S.dim_k) * 2;
+        if ((rc = encode_map_4d(&qm, S.q, S.dim_k, 1, S.heads, uint64_t(batch) * length, row, row, row * S.heads,
+                                S.group)))
+            return rc;
+    } else {
+        const uint64_t row = uint64_t(S.width) * 2;
+        if ((rc = encode_map_4d(&qm, S.q, S.width, 1, 128, batch, row, row, row * 128, 64))) return rc;
+    }
+    if ((rc = encode_map_f32_3d(&om, S.part_o, S.width, S.rows_alloc, uint64_t(batch) * S.kv_heads * S.splits,
+                                uint64_t(S.width) * 4, uint64_t(S.width) * 4 * S.rows_alloc, 64, 32)))
         return rc;
-    TcJob J{};
-    J.rank_k = L.rank_k;
-    J.rank_v = L.rank_v;
-    J.kchunks = (L.rank_k + 63) / 64;
-    J.vchunks = (L.rank_v + 63) / 64;
-    J.seqlens = L.latent_len;
-    J.qlens = L.query_len;
-    J.length = L.length;
-    J.scale_log2 = L.scale * 1.4426950408889634f;
-    J.splits = L.splits;
-    J.tiles_per_split = L.tiles_per_split;
-    J.rows_alloc = L.rows_alloc;
-    J.out_width = L.width;
-    J.part_o = L.part_o;
-    J.part_lse = L.part_lse;
-    J.status = L.status;
+    J = TcJob{};
+    J.kchunks = (S.dim_k + 63) / 64;
+    J.vchunks = (S.dim_v + 63) / 64;
+    J.kv_heads = S.kv_heads;
+    J.group = S.group;
+    J.causal = S.causal;
+    J.q_rows = S.q_rows;
+    J.seqlens = S.seqlens;
+    J.qlens = qlens;
+    J.length = length;
+    J.scale_log2 = scale * 1.4426950408889634f;
+    J.splits = S.splits;
+    J.rows_alloc = S.rows_alloc;
+    J.out_width = S.width;
+    J.part_o = S.part_o;
+    J.part_lse = S.part_lse;
+    J.status = status;
+    return SLIMKV_OK;
+}
+
+}  // namespace
+
+int launch_decode_tc(const TcLaunch& L, cudaStream_t stream) {
+    CUtensorMap lk, lv, lq, lo, rk, rv, rq, ro;
+    TcJob jl, jr;
+    int rc;
+    if ((rc = make_side(L.lat, L.batch, L.length, L.scale, L.query_len, L.status, jl, lk, lv, lq, lo))) return rc;
+    if (L.with_raw) {
+        if ((rc = make_side(L.raw, L.batch, L.length, L.scale, L.query_len, L.status, jr, rk, rv, rq, ro))) return rc;
+    } else {
+        jr = jl;
+        rk = lk; rv = lv; rq = lq; ro = lo;
+    }
     static bool configured[64] = {};
     const int dev = device_info().device;
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        if (cudaFuncSetAttribute(latent_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) !=
+        if (cudaFuncSetAttribute(decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) !=
             cudaSuccess)
-            return fail(SLIMKV_ERR_CUDA, "cudaFuncSetAttribute (latent tc) failed");
+            return fail(SLIMKV_ERR_CUDA, "cudaFuncSetAttribute (decode tc) failed");
         configured[dev] = true;
     }
-    latent_tc_kernel<<<L.batch * L.splits, kThreads7, kSmemBytes, stream>>>(km, vm, qm, J);
+    const int n_lat = L.batch * L.lat.splits;
+    const int n_raw = L.with_raw ? L.batch * L.raw.kv_heads * L.raw.splits : 0;
+    decode_tc_kernel<<<n_lat + n_raw, kThreads7, kSmemBytes, stream>>>(lk, lv, lq, lo, rk, rv, rq, ro, jl, jr, n_lat);
     const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "latent tc launch failed: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "decode tc launch failed: %s", cudaGetErrorString(e));
     return SLIMKV_OK;
 }
 

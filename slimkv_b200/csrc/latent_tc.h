@@ -1,4 +1,6 @@
-// Launch interface of the tcgen05 latent-branch attention (latent_tc.cu).
+// Launch interface of the tcgen05 decode attention (latent_tc.cu): one launch
+// streams the latent cache (one shared latent head, all query heads per CTA)
+// and the raw sink + tail (per KV head) with the same tensor-core pipeline.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -6,36 +8,51 @@
 
 namespace slimkv {
 
+// Per-branch job as the kernel sees it.
 struct TcJob {
-    int rank_k, rank_v, kchunks, vchunks;
-    const int32_t* seqlens;   // latents per sequence
+    int kchunks, vchunks;     // 64-column chunks of a K / V row
+    int kv_heads;             // KV heads per sequence in the grid (1 for the latent branch)
+    int group;                // query heads per KV head (rows of a Q box in row mode)
+    int causal;               // two queries: the first excludes the last key (the new Beacon)
+    int q_rows;               // Q read per query from [B*L][H][dim] rows (exact bf16: no lo part)
+    const int32_t* seqlens;   // keys per sequence
     const int32_t* qlens;     // queries per sequence (1 or 2), nullable
     int length;
     float scale_log2;
-    int splits, tiles_per_split;
-    int rows_alloc, out_width;
-    float* part_o;            // [B][splits][rows_alloc][out_width]
-    float* part_lse;          // [B][splits][rows_alloc]
+    int splits, rows_alloc, out_width;
+    float* part_o;            // [B][kv_heads][splits][rows_alloc][out_width]
+    float* part_lse;          // [B][kv_heads][splits][rows_alloc]
     unsigned int* status;
 };
 
-struct TcLaunch {
-    int batch, length, rank_k, rank_v, width, lat_capacity;
-    const void* lat_k;
-    const void* lat_v;
-    int64_t lat_stride_batch, lat_stride_row;   // elements
-    const void* q_hilo;                          // [B][128][width] bf16: row hl*32*nq + l*32 + head, hl 0 = hi, 1 = lo
-    const int32_t* latent_len;
-    const int32_t* query_len;
-    float scale;
-    int splits, tiles_per_split, rows_alloc;
+// One branch as the host describes it.
+struct TcSide {
+    const void* k;
+    const void* v;
+    int dim_k, dim_v;          // latent ranks, or the head dim
+    int kv_heads, capacity;
+    int64_t stride_batch, stride_row, stride_head;   // elements
+    // Latent: q_hilo [B][128][width] bf16 with row hl*32*nq + l*32 + head
+    // (hl 0 = hi, 1 = lo).  Raw: q_rot [B][L][H][dim] bf16.
+    const void* q;
+    int q_rows, heads, group, causal;
+    const int32_t* seqlens;
+    int splits, rows_alloc, width;
     float* part_o;
     float* part_lse;
+};
+
+struct TcLaunch {
+    int batch, length;
+    float scale;
+    const int32_t* query_len;
     unsigned int* status;
+    TcSide lat, raw;
+    int with_raw;
 };
 
 constexpr int kTcTileKeys = 128;
 
-int launch_latent_tc(const TcLaunch& launch, cudaStream_t stream);
+int launch_decode_tc(const TcLaunch& launch, cudaStream_t stream);
 
 }  // namespace slimkv
