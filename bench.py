@@ -45,6 +45,8 @@ def parse():
     p.add_argument('--warmup', type=int, default=5)
     p.add_argument('--impl', default='slimkv_b200', choices=['slimkv_b200', 'reference'])
     p.add_argument('--no-cpu-baseline', action='store_true')
+    p.add_argument('--kernel-only', action='store_true',
+                   help='one layer of the same workload: time the attention kernel alone (profiling runs)')
     return p.parse_args()
 
 
@@ -111,13 +113,17 @@ def peaks():
     return FALLBACK_HBM_GBS, 'fallback'
 
 
-def traffic_per_launch():
-    """ncu DRAM bytes of one fused latent attention launch at this workload."""
-    path = os.path.join(ROOT, 'profiles', 'latent_decode_c2_traffic.json')
+def traffic_per_launch(kernel_bytes):
+    """ncu DRAM bytes (read + write) of one attention launch, from the
+    committed capture of the same kernel on one layer of this workload,
+    scaled to this run's algorithmic bytes per launch (traffic grows with the
+    latent / raw rows streamed)."""
+    path = os.path.join(ROOT, 'profiles', 'decode_tc_kernel_c2_traffic.json')
     if not os.path.exists(path):
         return None
     with open(path) as f:
-        return json.load(f).get('bytes_per_launch')
+        d = json.load(f)
+    return (d['dram_read_bytes'] + d['dram_write_bytes']) * kernel_bytes / d['algorithmic_bytes']
 
 
 def cpu_baseline(batch, steps_hint=None):
@@ -147,10 +153,53 @@ def run_reference(args):
                 'on all host threads; the reference GPU kernel builds only for sm_90/sm_120'}), flush=True)
 
 
+def attention_kernel_time(rt, reps):
+    """Average device time of the attention launch (both branches) alone:
+    CUDA events recorded by the library right around that kernel, on the
+    launching stream, over `reps` launches cycling through the layers."""
+    import torch
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for b, e in events:         # creates the CUDA events (torch makes them lazily); the library re-records them
+        b.record()
+        e.record()
+    torch.cuda.synchronize()
+    for i in range(reps):
+        rt.calls[i % len(rt.calls)](attn_events=events[i])
+    torch.cuda.synchronize()
+    return sum(b.elapsed_time(e) for b, e in events) / reps
+
+
+def kernel_only(args):
+    """One layer of the bench workload (same batch, history, tails): the
+    fused decode call repeated; prints the attention kernel's time.  Small
+    device footprint, for ncu captures of the dominant kernel."""
+    import numpy as np
+    import torch
+    from slimkv_b200 import _lib
+    from slimkv_b200.runtime import LatentDecodeRuntime, LatentLlamaConfig, RandomWeights
+    device = torch.device('cuda', 0)
+    cfg = LatentLlamaConfig(layers=1)
+    weights = RandomWeights(cfg, device, seed=0)
+    rng = np.random.default_rng(1234)
+    tails = rng.integers(0, cfg.window, size=BATCH)
+    rt = LatentDecodeRuntime(cfg, weights, [HISTORY] * BATCH, tails, device, extra_windows=1)
+    rt.tokens.copy_(torch.from_numpy(rng.integers(0, cfg.vocab, size=BATCH)).to(device))
+    rt.step_eager()
+    for _ in range(max(args.warmup, 1)):
+        rt.calls[0]()
+    ms = attention_kernel_time(rt, max(args.steps, 1))
+    nbytes = rt.attention_kernel_bytes()
+    print(json.dumps({'kernel_only': True, 'attention_us': ms * 1e3, 'bytes_per_launch': nbytes,
+                      'achieved_gbs': nbytes / (ms / 1e3) / 1e9, 'device_status': _lib.device_status(clear=True)}),
+          flush=True)
+
+
 def main():
     args = parse()
     if args.impl == 'reference':
         return run_reference(args)
+    if args.kernel_only:
+        return kernel_only(args)
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -222,9 +271,13 @@ def main():
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
 
-    # ---- roofline of the fused latent attention step ------------------------
-    per_layer_bytes = rt.attention_bytes() / cfg.layers
+    # ---- roofline of the dominant kernel: the attention launch (latent + raw
+    # branches) timed alone with CUDA events on its stream; the whole fused
+    # step per layer (prologue + attention + merge) is reported beside it.
     reps = max(args.steps, 8) * 4
+    kernel_bytes = rt.attention_kernel_bytes()
+    attn_ms = attention_kernel_time(rt, reps)
+    achieved = kernel_bytes / (attn_ms / 1000.0) / 1e9
     torch.cuda.synchronize()
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a0.record()
@@ -232,8 +285,8 @@ def main():
         rt.calls[i % cfg.layers]()
     a1.record()
     torch.cuda.synchronize()
-    launch_ms = a0.elapsed_time(a1) / reps
-    achieved = per_layer_bytes / (launch_ms / 1000.0) / 1e9
+    layer_ms = a0.elapsed_time(a1) / reps
+    layer_bytes = rt.attention_bytes() / cfg.layers
     peak, peak_kind = peaks()
     status = _lib.device_status(clear=True)
 
@@ -247,9 +300,10 @@ def main():
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
                      'peak_source': f'{peak_kind} (MEASURED_PEAKS.json hbm_gbs)' if peak_kind == 'measured'
                      else 'fallback 6650 GB/s',
-                     'traffic': traffic_per_launch(), 'kernel': 'fused latent decode step (prologue + '
-                     'attention + merge) per layer', 'bytes_per_launch': per_layer_bytes,
-                     'us_per_launch': launch_ms * 1000.0},
+                     'traffic': traffic_per_launch(kernel_bytes), 'kernel': 'decode_tc_kernel (latent + raw branches, '
+                     'one launch per layer)', 'bytes_per_launch': kernel_bytes, 'us_per_launch': attn_ms * 1000.0,
+                     'fused_step_per_layer': {'us': layer_ms * 1000.0, 'bytes': layer_bytes,
+                                              'gbs': layer_bytes / (layer_ms / 1000.0) / 1e9}},
         'gpu_launches': args.steps * (1 + 3 * cfg.layers),
         'clocks': clock_info, 'device_status': status,
     }

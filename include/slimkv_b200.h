@@ -188,6 +188,11 @@ typedef struct {
     /* Split counts (0 = chosen from the byte volume and the SM count). */
     int latent_splits;
     int raw_splits;
+    /* Optional cudaEvent_t handles (NULL = none) recorded on `stream` right
+     * before and after the attention launch (both branches), so a caller can
+     * time that kernel alone.  Leave NULL inside CUDA graph capture. */
+    void* attn_event_begin;
+    void* attn_event_end;
 } slimkv_latent_decode_args;
 
 SLIMKV_API size_t slimkv_latent_decode_workspace_size(const slimkv_latent_decode_args* args);

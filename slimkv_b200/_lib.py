@@ -58,6 +58,7 @@ class LatentDecodeArgs(ctypes.Structure):
         ('out', ctypes.c_void_p), ('out_stride', I64x2), ('out_fp32', ctypes.c_int),
         ('latent_len_max', ctypes.c_int), ('raw_len_max', ctypes.c_int),
         ('latent_splits', ctypes.c_int), ('raw_splits', ctypes.c_int),
+        ('attn_event_begin', ctypes.c_void_p), ('attn_event_end', ctypes.c_void_p),
     ]
 
 

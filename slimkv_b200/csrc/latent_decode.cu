@@ -296,9 +296,15 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         R.q = w.q_rot; R.q_rows = 1; R.heads = a->heads; R.group = p.group; R.causal = 0;
         R.seqlens = a->raw_len; R.splits = p.raw_splits; R.rows_alloc = p.raw_rows; R.width = a->head_dim;
         R.part_o = w.raw_o; R.part_lse = w.raw_lse;
+        if (a->attn_event_begin && cudaEventRecord(static_cast<cudaEvent_t>(a->attn_event_begin), stream) != cudaSuccess)
+            return fail(SLIMKV_ERR_CUDA, "attn_event_begin record failed");
         if ((rc = launch_decode_tc(tl, stream))) return rc;
+        if (a->attn_event_end && cudaEventRecord(static_cast<cudaEvent_t>(a->attn_event_end), stream) != cudaSuccess)
+            return fail(SLIMKV_ERR_CUDA, "attn_event_end record failed");
     } else {
     const int n_latent = a->batch * p.lat_row_blocks * p.lat_splits;
+    if (a->attn_event_begin && cudaEventRecord(static_cast<cudaEvent_t>(a->attn_event_begin), stream) != cudaSuccess)
+        return fail(SLIMKV_ERR_CUDA, "attn_event_begin record failed");
     switch (p.wl) {
         case 128: rc = launch_wl<128>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
         case 192: rc = launch_wl<192>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
@@ -306,6 +312,8 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         default: rc = launch_wl<320>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
     }
     if (rc) return rc;
+    if (a->attn_event_end && cudaEventRecord(static_cast<cudaEvent_t>(a->attn_event_end), stream) != cudaSuccess)
+        return fail(SLIMKV_ERR_CUDA, "attn_event_end record failed");
     }
 
     // 3. merge

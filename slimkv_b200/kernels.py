@@ -226,11 +226,22 @@ class LatentDecodeCall:
             _lib.check(lib.slimkv_latent_decode(ctypes.byref(a), None, 0, None))
         self.workspace = torch.empty(size, dtype=torch.uint8, device=q.device)
 
-    def __call__(self):
+    def __call__(self, attn_events=None):
+        """Launch; ``attn_events`` = (begin, end) ``torch.cuda.Event`` pair
+        (already recorded once, so that torch has created them) re-recorded
+        around the attention kernel alone (not inside graph capture)."""
         lib = _lib.load()
-        with torch.cuda.device(self.device):
-            _lib.check(lib.slimkv_latent_decode(ctypes.byref(self.args), _ptr(self.workspace),
-                                                self.workspace.numel(), _stream()))
+        a = self.args
+        if attn_events is not None:
+            _require(all(e.cuda_event for e in attn_events), 'record the timing events once before passing them')
+        a.attn_event_begin, a.attn_event_end = ((attn_events[0].cuda_event, attn_events[1].cuda_event)
+                                                if attn_events is not None else (0, 0))
+        try:
+            with torch.cuda.device(self.device):
+                _lib.check(lib.slimkv_latent_decode(ctypes.byref(a), _ptr(self.workspace),
+                                                    self.workspace.numel(), _stream()))
+        finally:
+            a.attn_event_begin, a.attn_event_end = 0, 0
         return self._keep[-1]
 
 

@@ -205,6 +205,15 @@ class LatentDecodeRuntime:
         return self.logits.argmax(-1)
 
     # ------------------------------------------------------------------
+    def attention_kernel_bytes(self):
+        """Algorithmic HBM bytes of one attention launch (one layer, both
+        branches): every latent K/V row (``N (Rk + Rv) 2``) and every raw
+        key/value (``(S + T + 1) Hkv D 2`` each) of every sequence, read once."""
+        cfg = self.cfg
+        lat = self.latent_len.long().sum().item() * (cfg.rank_k + cfg.rank_v) * 2
+        raw = self.raw_len.long().sum().item() * cfg.kv_heads * cfg.head_dim * 2 * 2
+        return lat + raw
+
     def attention_bytes(self):
         """Algorithmic HBM bytes of this step's attention, summed over layers.
 
