@@ -165,8 +165,13 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
     const int t1 = int((int64_t)(split + 1) * n_tiles / J.splits);
     const int nt = max(0, t1 - t0);
     const int total_k = nt * kc, total_v = nt * vc;
-    // K chunk n -> (tile n / kc, chunk n % kc) in ring slot n % kring;
-    // V chunk n -> (tile n / vc, chunk n % vc) in V slot n % vc.
+    // K chunk n -> (tile n / kc, chunk n % kc) in ring slot n % kring.
+    // V chunk n -> (tile T = n / vc, chunk c = n % vc) in V slot c; with <= 2
+    // chunks per tile (the raw branch) tiles alternate between slot pairs
+    // (0,1) and (2,3), so two tiles of V are in flight.
+    const bool dbl = vc <= 2;
+    auto v_slot = [&](int T, int c) -> int { return dbl ? 2 * (T & 1) + c : c; };
+    auto v_use = [&](int T) -> int { return dbl ? T >> 1 : T; };     // earlier uses of the slot
     auto issue_k = [&](int n) {
         const int slot = n % kring;
         mbar_expect_tx(&ms->kfull[slot], kChunkBytes);
@@ -174,9 +179,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     (t0 + n / kc) * kKeys, b);
     };
     auto issue_v = [&](int n) {
-        const int slot = n % vc;
+        const int c = n % vc, slot = v_slot(n / vc, c);
         mbar_expect_tx(&ms->vfull[slot], kChunkBytes);
-        tma_load_4d(smem + slot * kChunkBytes, vmap, &ms->vfull[slot], slot * 64, g, (t0 + n / vc) * kKeys, b);
+        tma_load_4d(smem + slot * kChunkBytes, vmap, &ms->vfull[slot], c * 64, g, (t0 + n / vc) * kKeys, b);
     };
 
     if (warp == 0 && J.q_rows && nt > 0) {
@@ -217,7 +222,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                                     0, hl * 64, b);
             }
             for (int n = 0; n < kring && n < total_k; ++n) issue_k(n);
-            for (int n = 0; n < vc && n < total_v; ++n) issue_v(n);
+            for (int n = 0; n < (dbl ? 2 * vc : vc) && n < total_v; ++n) issue_v(n);
         }
     }
     if (warp == 2) {
@@ -240,14 +245,15 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
     if (nt > 0) {
         if (warp == 0 && lane == 0) {
             // ---- TMA producer: K chunks first whenever a K slot is free ----
-            int nk = min(kring, total_k), nv = min(vc, total_v);
+            int nk = min(kring, total_k), nv = min(dbl ? 2 * vc : vc, total_v);
             uint64_t idle_since = 0;
             while ((nk < total_k || nv < total_v) && !ms->abort) {
                 bool progressed = false;
                 if (nk < total_k && mbar_test(&ms->kempty[nk % kring], (nk / kring - 1) & 1)) {
                     issue_k(nk++);
                     progressed = true;
-                } else if (nv < total_v && mbar_test(&ms->vempty[nv % vc], (nv / vc - 1) & 1)) {
+                } else if (nv < total_v &&
+                           mbar_test(&ms->vempty[v_slot(nv / vc, nv % vc)], (v_use(nv / vc) - 1) & 1)) {
                     issue_v(nv++);
                     progressed = true;
                 }
@@ -303,13 +309,13 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                 if (!(ok = wait_or_abort(&ms->pfull, j & 1, ms, J.status))) break;
                 tc_fence_after();
                 for (int blk = 0; blk < vblocks; ++blk) {
-                    const int c0 = 2 * blk;
+                    const int c0 = 2 * blk, s0 = v_slot(j, c0);
                     const bool pair = c0 + 1 < vc;
                     for (int c = c0; c <= c0 + (pair ? 1 : 0); ++c)
-                        if (!(ok = wait_or_abort(&ms->vfull[c], j & 1, ms, J.status))) break;
+                        if (!(ok = wait_or_abort(&ms->vfull[v_slot(j, c)], v_use(j) & 1, ms, J.status))) break;
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t va = sbase + c0 * kChunkBytes;
+                    const uint32_t va = sbase + s0 * kChunkBytes;
                     const uint32_t o_b = o_tmem + uint32_t(blk * kN);
                     const uint32_t idesc = pair ? idesc_pair : idesc_one;
 #pragma unroll
@@ -319,8 +325,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                                   (j > 0 || ks > 0) ? 1u : 0u);
                         if (!cols) umma_bf16(o_b, ad, umma_desc_sw128(p1 + ks * 2048, kChunkBytes, 1024), idesc, 1u);
                     }
-                    umma_commit(&ms->vempty[c0]);
-                    if (pair) umma_commit(&ms->vempty[c0 + 1]);
+                    umma_commit(&ms->vempty[s0]);
+                    if (pair) umma_commit(&ms->vempty[s0 + 1]);
                 }
                 if (!ok) break;
                 umma_commit(&ms->odone);
@@ -358,29 +364,46 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
 #pragma unroll
                     for (int h = 0; h < 32; ++h) v[l][h] = key < limit ? v[l][h] * J.scale_log2 : -INFINITY;
                 }
+                // Column maxima only when some score exceeds its row's running
+                // max by more than the lazy threshold (always on the first
+                // tile): otherwise the max stays and every p <= 2^8.
+                bool over = i == 0;
+                if (!over) {
 #pragma unroll
-                for (int l = 0; l < 2; ++l) {
-                    if (l < nq) {
-                        float tmp[32];
+                    for (int l = 0; l < 2; ++l)
+                        if (l < nq) {
 #pragma unroll
-                        for (int h = 0; h < 32; ++h) tmp[h] = v[l][h];
-                        ms->red[quarter][32 * l + lane] = warp_transpose_reduce<true>(tmp, lane);
-                    }
+                            for (int h = 0; h < 32; ++h) over |= v[l][h] > ms->m_run[32 * l + h] + kLazyLog2;
+                        }
                 }
-                named_bar(1, 128);
-                if (st < rows) {
-                    const float tm = fmaxf(fmaxf(ms->red[0][st], ms->red[1][st]), fmaxf(ms->red[2][st], ms->red[3][st]));
-                    const float mo = ms->m_run[st];
-                    float mn = mo, alpha = 1.f;
-                    if (tm != -INFINITY && (mo == -INFINITY || tm > mo + kLazyLog2)) {
-                        mn = fmaxf(mo, tm);
-                        alpha = mo == -INFINITY ? 0.f : exp2f(mo - mn);
+                const bool rescan = named_bar_or(1, 128, over);
+                bool need_fix = false;
+                if (rescan) {
+#pragma unroll
+                    for (int l = 0; l < 2; ++l) {
+                        if (l < nq) {
+                            float tmp[32];
+#pragma unroll
+                            for (int h = 0; h < 32; ++h) tmp[h] = v[l][h];
+                            ms->red[quarter][32 * l + lane] = warp_transpose_reduce<true>(tmp, lane);
+                        }
                     }
-                    ms->alpha[st] = alpha;
-                    ms->m_run[st] = mn;
-                    ms->l_run[st] *= alpha;
+                    named_bar(1, 128);
+                    if (st < rows) {
+                        const float tm =
+                            fmaxf(fmaxf(ms->red[0][st], ms->red[1][st]), fmaxf(ms->red[2][st], ms->red[3][st]));
+                        const float mo = ms->m_run[st];
+                        float mn = mo, alpha = 1.f;
+                        if (tm != -INFINITY && (mo == -INFINITY || tm > mo + kLazyLog2)) {
+                            mn = fmaxf(mo, tm);
+                            alpha = mo == -INFINITY ? 0.f : exp2f(mo - mn);
+                        }
+                        ms->alpha[st] = alpha;
+                        ms->m_run[st] = mn;
+                        ms->l_run[st] *= alpha;
+                    }
+                    need_fix = named_bar_or(1, 128, st < rows && i > 0 && ms->alpha[st] != 1.f);
                 }
-                const bool need_fix = named_bar_or(1, 128, st < rows && i > 0 && ms->alpha[st] != 1.f);
                 // P(i) overwrites the buffer P.V(i-1) reads: wait for it.
                 if (i > 0) {
                     ok = wait_or_abort(&ms->odone, (i - 1) & 1, ms, J.status);
@@ -396,9 +419,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     bool okc = true;
                     if (key >= n_keys) {
                         for (int c = 0; c < vc && okc; ++c) {
-                            okc = wait_or_abort(&ms->vfull[c], i & 1, ms, J.status);
+                            const int slot = v_slot(i, c);
+                            okc = wait_or_abort(&ms->vfull[slot], v_use(i) & 1, ms, J.status);
                             if (okc) {
-                                uint4* row = reinterpret_cast<uint4*>(smem + c * kChunkBytes + t_local * 128);
+                                uint4* row = reinterpret_cast<uint4*>(smem + slot * kChunkBytes + t_local * 128);
 #pragma unroll
                                 for (int u = 0; u < 8; ++u) row[u] = make_uint4(0, 0, 0, 0);
                             }
@@ -535,7 +559,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
             mbar_wait(&ms->kfull[s], 0, 100000000ull);
             mbar_wait(&ms->kfull[s], 1, 100000000ull);
         }
-        for (int s = 0; s < vc; ++s) {
+        for (int s = 0; s < (dbl ? 2 * vc : vc); ++s) {
             mbar_wait(&ms->vfull[s], 0, 100000000ull);
             mbar_wait(&ms->vfull[s], 1, 100000000ull);
         }
