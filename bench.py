@@ -229,12 +229,10 @@ def main():
         if world > 1:
             dist.barrier()
 
+    from slimkv_b200.parallel import max_over_ranks as _max_over_ranks
+
     def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return t.item()
+        return _max_over_ranks(x, device=device)
 
     # ---- device-resident timed region -------------------------------------
     clocks = ClockSampler(local)
