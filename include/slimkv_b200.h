@@ -245,6 +245,63 @@ SLIMKV_API int slimkv_merge(const void* raw, const int64_t raw_stride[3], const 
                  const int64_t latent_lse_stride[3], int batch, int heads, int queries,
                  int head_dim, void* out, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Paged cache IO in the vLLM plugin's page layouts, byte for byte
+ * (slimkv/vllm_plugin/paged_cache.py:12-127).  Batched over sequences: row b
+ * of `table` (int32, device, `table_stride` entries) is sequence b's block
+ * table.  Copies are exact (bf16 bits).  A page id or position outside the
+ * allocation sets SLIMKV_DEVICE_BAD_LENGTH and is skipped.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    void* pages;              /* bf16, physical page p at pages + p * page_stride */
+    int64_t page_stride;      /* elements between physical pages */
+    int slots;                /* Beacon rows per page: raw_block_size / token_ratio */
+    int rank_k, rank_v;       /* a row is K (rank_k) then V (rank_v) */
+    int sink_elements;        /* 2 * raw_width: sink K then V at the page start */
+    const int32_t* table;
+    int64_t table_stride;
+    int num_pages;            /* allocation size, for the bounds checks */
+} slimkv_beacon_pages;
+
+/* BeaconPages.append (paged_cache.py:78-87): rows [start[b], start[b]+count)
+ * of sequence b <- key[b][i] (rank_k) ++ value[b][i] (rank_v). */
+SLIMKV_API int slimkv_beacon_pages_append(const slimkv_beacon_pages* pages, int batch, const int32_t* start,
+                                          int count, const void* key, int64_t key_stride_batch,
+                                          int64_t key_stride_row, const void* value, int64_t value_stride_batch,
+                                          int64_t value_stride_row, void* stream);
+/* BeaconPages.read (paged_cache.py:64-76): the first count[b] rows of
+ * sequence b -> dense key[b][i], value[b][i] (rows past count[b] untouched). */
+SLIMKV_API int slimkv_beacon_pages_gather(const slimkv_beacon_pages* pages, int batch, const int32_t* count,
+                                          int max_count, void* key, int64_t key_stride_batch,
+                                          int64_t key_stride_row, void* value, int64_t value_stride_batch,
+                                          int64_t value_stride_row, void* stream);
+/* BeaconPages.write_sink / read_sink (paged_cache.py:89-100): the sink token
+ * (key[b], value[b]: raw_width elements each) of sequence b at the start of
+ * its root page table[b][0]; write = 1 stores, 0 loads. */
+SLIMKV_API int slimkv_beacon_pages_sink(const slimkv_beacon_pages* pages, int batch, void* key, void* value,
+                                        int64_t stride_batch, int write, void* stream);
+
+typedef struct {
+    void* pages;              /* bf16 [blocks][block_size][2 (K, V)][kv_heads][head_dim] */
+    int block_size, kv_heads, head_dim;
+    const int32_t* table;
+    int64_t table_stride;
+    int num_blocks;
+} slimkv_raw_pages;
+
+/* RawPages.write (paged_cache.py:117-127): absolute raw positions
+ * [start[b], start[b]+count) of sequence b <- key/value [B][count][Hkv][D]. */
+SLIMKV_API int slimkv_raw_pages_write(const slimkv_raw_pages* pages, int batch, const int32_t* start, int count,
+                                      const void* key, int64_t key_stride_batch, int64_t key_stride_token,
+                                      const void* value, int64_t value_stride_batch, int64_t value_stride_token,
+                                      void* stream);
+/* RawPages.read (paged_cache.py:108-115): count[b] tokens from start[b] ->
+ * key/value [B][max_count][Hkv][D] (rows past count[b] untouched). */
+SLIMKV_API int slimkv_raw_pages_read(const slimkv_raw_pages* pages, int batch, const int32_t* start,
+                                     const int32_t* count, int max_count, void* key, int64_t key_stride_batch,
+                                     int64_t key_stride_token, void* value, int64_t value_stride_batch,
+                                     int64_t value_stride_token, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -66,6 +66,26 @@ class LatentDecodeArgs(ctypes.Structure):
 # that the built library exports every one of them.
 _P = ctypes.c_void_p
 _I = ctypes.c_int
+class BeaconPagesArgs(ctypes.Structure):
+    """Mirror of ``slimkv_beacon_pages``."""
+    _fields_ = [
+        ('pages', ctypes.c_void_p), ('page_stride', ctypes.c_int64), ('slots', ctypes.c_int),
+        ('rank_k', ctypes.c_int), ('rank_v', ctypes.c_int), ('sink_elements', ctypes.c_int),
+        ('table', ctypes.c_void_p), ('table_stride', ctypes.c_int64), ('num_pages', ctypes.c_int),
+    ]
+
+
+class RawPagesArgs(ctypes.Structure):
+    """Mirror of ``slimkv_raw_pages``."""
+    _fields_ = [
+        ('pages', ctypes.c_void_p), ('block_size', ctypes.c_int), ('kv_heads', ctypes.c_int),
+        ('head_dim', ctypes.c_int), ('table', ctypes.c_void_p), ('table_stride', ctypes.c_int64),
+        ('num_blocks', ctypes.c_int),
+    ]
+
+
+_L = ctypes.c_int64
+
 SIGNATURES = {
     'slimkv_version': (_I, []),
     'slimkv_last_error': (ctypes.c_char_p, []),
@@ -78,6 +98,11 @@ SIGNATURES = {
     'slimkv_rope_decode': (_I, [_P, ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _P, _P,
                                 _I, _P, ctypes.c_int64, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
     'slimkv_decode_schedule': (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
+    'slimkv_beacon_pages_append': (_I, [ctypes.POINTER(BeaconPagesArgs), _I, _P, _I, _P, _L, _L, _P, _L, _L, _P]),
+    'slimkv_beacon_pages_gather': (_I, [ctypes.POINTER(BeaconPagesArgs), _I, _P, _I, _P, _L, _L, _P, _L, _L, _P]),
+    'slimkv_beacon_pages_sink': (_I, [ctypes.POINTER(BeaconPagesArgs), _I, _P, _P, _L, _I, _P]),
+    'slimkv_raw_pages_write': (_I, [ctypes.POINTER(RawPagesArgs), _I, _P, _I, _P, _L, _L, _P, _L, _L, _P]),
+    'slimkv_raw_pages_read': (_I, [ctypes.POINTER(RawPagesArgs), _I, _P, _P, _I, _P, _L, _L, _P, _L, _L, _P]),
     'slimkv_merge': (_I, [_P, ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _P,
                           ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I,
                           _I, _P, _P]),
