@@ -193,6 +193,21 @@ typedef struct {
      * time that kernel alone.  Leave NULL inside CUDA graph capture. */
     void* attn_event_begin;
     void* attn_event_end;
+    /* Paged latent cache (optional; NULL lat_pages = the dense lat_k / lat_v
+     * above).  The vLLM plugin's Beacon pages (paged_cache.py:12-87): page p
+     * at lat_pages + p * lat_page_stride (bf16 elements) holds
+     * [lat_sink_elements][lat_slots x (rank_k + rank_v)]; latent row n of
+     * sequence b is in page lat_table[b * lat_table_stride + n / lat_slots].
+     * The attention reads the pages directly; the prologue appends the new
+     * Beacon row there.  lat_slots must be a multiple of 16 and the
+     * 32-query-head tensor-core route is required. */
+    void* lat_pages;
+    int64_t lat_page_stride;
+    int lat_slots;
+    int lat_sink_elements;
+    const int32_t* lat_table;
+    int64_t lat_table_stride;
+    int lat_num_pages;
 } slimkv_latent_decode_args;
 
 SLIMKV_API size_t slimkv_latent_decode_workspace_size(const slimkv_latent_decode_args* args);

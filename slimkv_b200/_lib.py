@@ -59,6 +59,9 @@ class LatentDecodeArgs(ctypes.Structure):
         ('latent_len_max', ctypes.c_int), ('raw_len_max', ctypes.c_int),
         ('latent_splits', ctypes.c_int), ('raw_splits', ctypes.c_int),
         ('attn_event_begin', ctypes.c_void_p), ('attn_event_end', ctypes.c_void_p),
+        ('lat_pages', ctypes.c_void_p), ('lat_page_stride', ctypes.c_int64), ('lat_slots', ctypes.c_int),
+        ('lat_sink_elements', ctypes.c_int), ('lat_table', ctypes.c_void_p), ('lat_table_stride', ctypes.c_int64),
+        ('lat_num_pages', ctypes.c_int),
     ]
 
 

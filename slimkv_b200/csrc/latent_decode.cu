@@ -190,17 +190,30 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     DecodePlan p;
     int rc = plan_decode(a, p);
     if (rc) return rc;
-    if (!a->q || !a->raw_k_rot || !a->raw_v || !a->lat_k || !a->lat_v || !a->raw_len || !a->latent_len ||
-        !a->qpos || !a->uk || !a->uv || !a->cos || !a->sin || !a->out)
+    const bool paged = a->lat_pages != nullptr;
+    if (!a->q || !a->raw_k_rot || !a->raw_v || (!paged && (!a->lat_k || !a->lat_v)) || !a->raw_len ||
+        !a->latent_len || !a->qpos || !a->uk || !a->uv || !a->cos || !a->sin || !a->out)
         return fail(SLIMKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
     if ((a->new_k == nullptr) != (a->new_v == nullptr) || (a->new_lat_k == nullptr) != (a->new_lat_v == nullptr))
         return fail(SLIMKV_ERR_INVALID_ARGUMENT, "new K/V (and new latent K/V) must be given together");
-    if (a->raw_stride_token % 8 || a->raw_stride_batch % 8 || a->lat_stride_row % 8 || a->lat_stride_batch % 8 ||
-        !aligned16(a->raw_k_rot) || !aligned16(a->raw_v) || !aligned16(a->lat_k) || !aligned16(a->lat_v) ||
-        !aligned16(a->uv))
+    if (a->raw_stride_token % 8 || a->raw_stride_batch % 8 || !aligned16(a->raw_k_rot) || !aligned16(a->raw_v) ||
+        !aligned16(a->uv) ||
+        (!paged && (a->lat_stride_row % 8 || a->lat_stride_batch % 8 || !aligned16(a->lat_k) || !aligned16(a->lat_v))))
         return fail(SLIMKV_ERR_ALIGNMENT, "caches must be 16-byte aligned with strides that are multiples of 8");
-    if (a->raw_stride_token < (int64_t)a->kv_heads * a->head_dim || a->lat_stride_row < std::max(a->rank_k, a->rank_v))
+    if (a->raw_stride_token < (int64_t)a->kv_heads * a->head_dim ||
+        (!paged && a->lat_stride_row < std::max(a->rank_k, a->rank_v)))
         return fail(SLIMKV_ERR_INVALID_ARGUMENT, "cache row stride smaller than a row");
+    if (paged) {
+        if (!p.tc) return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "paged latent caches need 32 query heads");
+        if (!a->lat_table || a->lat_slots <= 0 || a->lat_slots % 16 || a->lat_num_pages <= 0 ||
+            a->lat_table_stride <= 0 || a->lat_sink_elements < 0 || a->lat_sink_elements % 8 ||
+            a->lat_page_stride % 8 || !aligned16(a->lat_pages) ||
+            a->lat_page_stride < a->lat_sink_elements + int64_t(a->lat_slots) * (a->rank_k + a->rank_v))
+            return fail(SLIMKV_ERR_INVALID_ARGUMENT,
+                        "paged latent cache: need a block table, slots a multiple of 16, 16-byte aligned pages");
+        if (int64_t(a->lat_capacity) > a->lat_table_stride * a->lat_slots)
+            return fail(SLIMKV_ERR_INVALID_ARGUMENT, "lat_capacity exceeds the rows the block table can address");
+    }
     Carver c(workspace, workspace_bytes);
     const Buffers w = carve(c, p);
     if (!workspace || !c.fits())
@@ -245,6 +258,10 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     pa.lat_v = static_cast<__nv_bfloat16*>(a->lat_v);
     pa.lat_sb = a->lat_stride_batch; pa.lat_sr = a->lat_stride_row;
     pa.latent_len = a->latent_len; pa.lat_capacity = a->lat_capacity;
+    pa.lat_pages = static_cast<__nv_bfloat16*>(a->lat_pages);
+    pa.lat_page_stride = a->lat_page_stride; pa.lat_table_stride = a->lat_table_stride;
+    pa.lat_slots = a->lat_slots; pa.lat_sink = a->lat_sink_elements; pa.lat_num_pages = a->lat_num_pages;
+    pa.lat_table = a->lat_table;
     pa.status = status;
     const dim3 pgrid(a->kv_heads, p.wl / 64, (a->batch + pa.seq_per_cta - 1) / pa.seq_per_cta);
     decode_prologue_kernel<<<pgrid, 256, 0, stream>>>(pa);
@@ -252,16 +269,20 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "prologue launch failed: %s", cudaGetErrorString(e));
 
     // 2. attention over both branches
-    CUtensorMap lk, lv, rk, rv;
-    int bc = 0;
-    const int64_t lat_stride[3] = {a->lat_stride_batch, a->lat_stride_row, a->lat_stride_row};
-    if ((rc = make_bshd_map(&lk, a->lat_k, a->batch, a->lat_capacity, 1, a->rank_k, lat_stride, &bc))) return rc;
-    if ((rc = make_bshd_map(&lv, a->lat_v, a->batch, a->lat_capacity, 1, a->rank_v, lat_stride, &bc))) return rc;
-    const int64_t raw_stride[3] = {a->raw_stride_batch, a->raw_stride_token, a->head_dim};
-    if ((rc = make_bshd_map(&rk, a->raw_k_rot, a->batch, a->raw_capacity, a->kv_heads, a->head_dim, raw_stride, &bc)))
-        return rc;
-    if ((rc = make_bshd_map(&rv, a->raw_v, a->batch, a->raw_capacity, a->kv_heads, a->head_dim, raw_stride, &bc)))
-        return rc;
+    CUtensorMap lk, lv, rk, rv;     // maps of the split-KV route (the tensor-core route builds its own)
+    if (!p.tc) {
+        int bc = 0;
+        const int64_t lat_stride[3] = {a->lat_stride_batch, a->lat_stride_row, a->lat_stride_row};
+        if ((rc = make_bshd_map(&lk, a->lat_k, a->batch, a->lat_capacity, 1, a->rank_k, lat_stride, &bc))) return rc;
+        if ((rc = make_bshd_map(&lv, a->lat_v, a->batch, a->lat_capacity, 1, a->rank_v, lat_stride, &bc))) return rc;
+        const int64_t raw_stride[3] = {a->raw_stride_batch, a->raw_stride_token, a->head_dim};
+        if ((rc = make_bshd_map(&rk, a->raw_k_rot, a->batch, a->raw_capacity, a->kv_heads, a->head_dim, raw_stride,
+                                &bc)))
+            return rc;
+        if ((rc = make_bshd_map(&rv, a->raw_v, a->batch, a->raw_capacity, a->kv_heads, a->head_dim, raw_stride,
+                                &bc)))
+            return rc;
+    }
     const float scale_log2 = a->scale * 1.4426950408889634f;
     AttnJob jl{};
     jl.q = w.q_lat; jl.q_fp16 = 1; jl.q_sb = (int64_t)a->length * a->heads * p.wl; jl.q_sl = (int64_t)a->heads * p.wl; jl.q_sh = p.wl;
@@ -289,6 +310,9 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         L.q = w.q_lat; L.q_rows = 0; L.heads = a->heads; L.group = a->heads; L.causal = 1;
         L.seqlens = a->latent_len; L.splits = p.lat_splits; L.rows_alloc = p.lat_rows; L.width = p.wl;
         L.part_o = w.lat_o; L.part_lse = w.lat_lse;
+        L.pages = a->lat_pages; L.page_stride = a->lat_page_stride; L.slots = a->lat_slots;
+        L.sink_elements = a->lat_sink_elements; L.num_pages = a->lat_num_pages;
+        L.table = a->lat_table; L.table_stride = a->lat_table_stride;
         TcSide& R = tl.raw;
         R.k = a->raw_k_rot; R.v = a->raw_v; R.dim_k = a->head_dim; R.dim_v = a->head_dim;
         R.kv_heads = a->kv_heads; R.capacity = a->raw_capacity;

@@ -46,6 +46,12 @@ struct PrologueArgs {
     int64_t lat_sb, lat_sr;
     const int32_t* latent_len;
     int lat_capacity;
+    // Paged latent cache (lat_pages != nullptr): row n of sequence b at
+    // lat_pages + table[b][n / slots] * page_stride + sink + (n % slots) * W.
+    __nv_bfloat16* lat_pages;
+    int64_t lat_page_stride, lat_table_stride;
+    int lat_slots, lat_sink, lat_num_pages;
+    const int32_t* lat_table;
     unsigned int* status;
 };
 
@@ -220,16 +226,26 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
             const int s = i / (ku + vu), u = i - s * (ku + vu), b = b0 + s;
             if (b >= a.batch || (a.qlens ? a.qlens[b] : a.length) != 2) continue;
             const int row = a.latent_len[b] - 1;
+            const uint4 val = u < ku ? *reinterpret_cast<const uint4*>(a.new_lat_k + b * a.new_lat_stride + u * 8)
+                                     : *reinterpret_cast<const uint4*>(a.new_lat_v + b * a.new_lat_stride + (u - ku) * 8);
+            if (a.lat_pages) {
+                // BeaconPages.append of one row (paged_cache.py:78-87).
+                const int64_t pi = row / a.lat_slots;
+                const int page = (row < 0 || pi >= a.lat_table_stride) ? -1 : a.lat_table[b * a.lat_table_stride + pi];
+                if (page < 0 || page >= a.lat_num_pages) {
+                    report(a.status, SLIMKV_DEVICE_BAD_LENGTH);
+                    continue;
+                }
+                *reinterpret_cast<uint4*>(a.lat_pages + int64_t(page) * a.lat_page_stride + a.lat_sink +
+                                          int64_t(row % a.lat_slots) * (a.rank_k + a.rank_v) + u * 8) = val;
+                continue;
+            }
             if (row < 0 || row >= a.lat_capacity) {
                 report(a.status, SLIMKV_DEVICE_BAD_LENGTH);
                 continue;
             }
-            if (u < ku)
-                *reinterpret_cast<uint4*>(a.lat_k + b * a.lat_sb + row * a.lat_sr + u * 8) =
-                    *reinterpret_cast<const uint4*>(a.new_lat_k + b * a.new_lat_stride + u * 8);
-            else
-                *reinterpret_cast<uint4*>(a.lat_v + b * a.lat_sb + row * a.lat_sr + (u - ku) * 8) =
-                    *reinterpret_cast<const uint4*>(a.new_lat_v + b * a.new_lat_stride + (u - ku) * 8);
+            if (u < ku) *reinterpret_cast<uint4*>(a.lat_k + b * a.lat_sb + row * a.lat_sr + u * 8) = val;
+            else *reinterpret_cast<uint4*>(a.lat_v + b * a.lat_sb + row * a.lat_sr + (u - ku) * 8) = val;
         }
     }
 }

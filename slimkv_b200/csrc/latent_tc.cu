@@ -172,16 +172,48 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
     const bool dbl = vc <= 2;
     auto v_slot = [&](int T, int c) -> int { return dbl ? 2 * (T & 1) + c : c; };
     auto v_use = [&](int T) -> int { return dbl ? T >> 1 : T; };     // earlier uses of the slot
+    // Paged K/V: the page of each 16-key block of one tile, cached in
+    // registers per stream (K runs ahead of V).  Keys past the length read a
+    // valid page (their scores are masked and their V rows zeroed).
+    // Paged K/V: the page of each 16-key block of one tile, cached in
+    // registers per stream (K runs ahead of V).  Keys past the length read a
+    // valid page (their scores are masked and their V rows zeroed).
+    struct PageCache { int tile = -1; int page[kKeys / 16]; };
+    PageCache kpc, vpc;
+    auto fill_pages = [&](PageCache& pc, int tile) {
+        if (pc.tile == tile) return;
+        pc.tile = tile;
+        const int last = max(n_keys - 1, 0);
+#pragma unroll
+        for (int i = 0; i < kKeys / 16; ++i) {
+            const int key = min(tile * kKeys + 16 * i, last);
+            pc.page[i] = __ldg(J.table + b * J.table_stride + key / J.slots);
+        }
+    };
+    // One 16 KB chunk [128 keys x 64 columns] at column col: one box of the
+    // dense map, or eight 16-row boxes of the page map.
+    auto load_chunk = [&](uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int col, int tile, PageCache& pc) {
+        if (!J.table) {
+            tma_load_4d(dst, map, bar, col, g, tile * kKeys, b);
+            return;
+        }
+        fill_pages(pc, tile);
+        const int last = max(n_keys - 1, 0);
+#pragma unroll
+        for (int i = 0; i < kKeys / 16; ++i) {
+            const int key = min(tile * kKeys + 16 * i, last);
+            tma_load_4d(dst + i * 2048, map, bar, col, 0, (key % J.slots) & ~15, pc.page[i]);
+        }
+    };
     auto issue_k = [&](int n) {
         const int slot = n % kring;
         mbar_expect_tx(&ms->kfull[slot], kChunkBytes);
-        tma_load_4d(smem + kOffK + slot * kChunkBytes, kmap, &ms->kfull[slot], (n % kc) * 64, g,
-                    (t0 + n / kc) * kKeys, b);
+        load_chunk(smem + kOffK + slot * kChunkBytes, kmap, &ms->kfull[slot], (n % kc) * 64, t0 + n / kc, kpc);
     };
     auto issue_v = [&](int n) {
         const int c = n % vc, slot = v_slot(n / vc, c);
         mbar_expect_tx(&ms->vfull[slot], kChunkBytes);
-        tma_load_4d(smem + slot * kChunkBytes, vmap, &ms->vfull[slot], c * 64, g, (t0 + n / vc) * kKeys, b);
+        load_chunk(smem + slot * kChunkBytes, vmap, &ms->vfull[slot], J.v_col + c * 64, t0 + n / vc, vpc);
     };
 
     if (warp == 0 && J.q_rows && nt > 0) {
@@ -580,13 +612,28 @@ int make_side(const TcSide& S, int batch, int length, float scale, const int32_t
         (reinterpret_cast<uintptr_t>(S.part_o) & 15) || S.group > 32)
         return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "tensor-core decode attention: unsupported branch shape");
     int rc;
-    const uint64_t head_bytes = S.kv_heads > 1 ? uint64_t(S.stride_head) * 2 : uint64_t(S.stride_row) * 2;
-    if ((rc = encode_map_4d(&km, S.k, S.dim_k, S.kv_heads, S.capacity, batch, head_bytes, uint64_t(S.stride_row) * 2,
-                            uint64_t(S.stride_batch) * 2, kKeys)))
-        return rc;
-    if ((rc = encode_map_4d(&vm, S.v, S.dim_v, S.kv_heads, S.capacity, batch, head_bytes, uint64_t(S.stride_row) * 2,
-                            uint64_t(S.stride_batch) * 2, kKeys)))
-        return rc;
+    if (S.pages) {
+        // One map over the pages: (W columns, slots rows, pages), 16-row boxes;
+        // K chunks at columns [0, dim_k), V chunks from dim_k.
+        const int W = S.dim_k + S.dim_v;
+        if (S.slots % 16 || S.dim_k % 8 || S.sink_elements % 8 || S.page_stride % 8 || S.num_pages <= 0 || !S.table ||
+            (reinterpret_cast<uintptr_t>(S.pages) & 15))
+            return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE,
+                        "paged latent attention needs 16-row-aligned pages (slots %% 16, ranks %% 8, 16-byte aligned)");
+        const void* base = static_cast<const uint16_t*>(S.pages) + S.sink_elements;
+        const uint64_t row = uint64_t(W) * 2, page = uint64_t(S.page_stride) * 2;
+        // dims (W, 1, slots, pages): the helper's box {64, 1, 16, 1} spans 16 rows.
+        if ((rc = encode_map_4d(&km, base, W, 1, S.slots, S.num_pages, row, row, page, 16))) return rc;
+        vm = km;
+    } else {
+        const uint64_t head_bytes = S.kv_heads > 1 ? uint64_t(S.stride_head) * 2 : uint64_t(S.stride_row) * 2;
+        if ((rc = encode_map_4d(&km, S.k, S.dim_k, S.kv_heads, S.capacity, batch, head_bytes,
+                                uint64_t(S.stride_row) * 2, uint64_t(S.stride_batch) * 2, kKeys)))
+            return rc;
+        if ((rc = encode_map_4d(&vm, S.v, S.dim_v, S.kv_heads, S.capacity, batch, head_bytes,
+                                uint64_t(S.stride_row) * 2, uint64_t(S.stride_batch) * 2, kKeys)))
+            return rc;
+    }
     if (S.q_rows) {
         // q_rot [B][L][H][dim] as (dim, 1, H, B * L), boxes of `group` rows.
         const uint64_t row = uint64_t(S.dim_k) * 2;
@@ -617,6 +664,10 @@ int make_side(const TcSide& S, int batch, int length, float scale, const int32_t
     J.part_o = S.part_o;
     J.part_lse = S.part_lse;
     J.status = status;
+    J.table = S.pages ? S.table : nullptr;
+    J.table_stride = S.table_stride;
+    J.slots = S.slots;
+    J.v_col = S.pages ? S.dim_k : 0;
     return SLIMKV_OK;
 }
 

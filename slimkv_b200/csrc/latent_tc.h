@@ -23,6 +23,12 @@ struct TcJob {
     float* part_o;            // [B][kv_heads][splits][rows_alloc][out_width]
     float* part_lse;          // [B][kv_heads][splits][rows_alloc]
     unsigned int* status;
+    // Paged K/V (nullptr table = dense maps): row n of sequence b is row
+    // n % slots of page table[b * table_stride + n / slots]; the K/V maps are
+    // then one page map [pages][slots][W] and V starts at column v_col.
+    const int32_t* table;
+    int64_t table_stride;
+    int slots, v_col;
 };
 
 // One branch as the host describes it.
@@ -40,6 +46,13 @@ struct TcSide {
     int splits, rows_alloc, width;
     float* part_o;
     float* part_lse;
+    // Paged K/V: pages [num_pages] of page_stride elements holding
+    // [sink][slots x (dim_k + dim_v)] (k / v unused).
+    const void* pages;
+    int64_t page_stride;
+    int slots, sink_elements, num_pages;
+    const int32_t* table;
+    int64_t table_stride;
 };
 
 struct TcLaunch {

@@ -163,24 +163,41 @@ class LatentDecodeCall:
     re-launches with the same pointers, which is what a CUDA graph captures.
     """
 
-    def __init__(self, *, q, raw_k_rot, raw_v, lat_k, lat_v, raw_len, latent_len, qpos, uk, uv, cos, sin,
+    def __init__(self, *, q, raw_k_rot, raw_v, lat_k=None, lat_v=None, raw_len, latent_len, qpos, uk, uv, cos, sin,
                  out, query_len=None, raw_k_pre=None, new_k=None, new_v=None, new_lat_k=None, new_lat_v=None,
                  uk_bias=None, uv_bias=None, scale=None, latent_len_max=0, raw_len_max=0, latent_splits=0,
-                 raw_splits=0):
-        _bf16_cuda(q, raw_k_rot, raw_v, lat_k, lat_v, uk, uv)
+                 raw_splits=0, lat_pages=None):
+        """``lat_pages = (pages, layout, tables)`` replaces ``lat_k / lat_v``
+        with the vLLM plugin's Beacon pages: ``pages [num_pages, >=
+        layout.page_elements]`` bf16 (a ``pages.BeaconPageLayout`` layout) and
+        ``tables [B, pages_per_seq]`` int32 block tables on the device."""
+        paged = lat_pages is not None
+        _require(paged or (lat_k is not None and lat_v is not None), 'lat_k / lat_v or lat_pages required')
+        _bf16_cuda(q, raw_k_rot, raw_v, uk, uv, *(() if paged else (lat_k, lat_v)))
         _require(out.is_cuda and out.dtype in (torch.bfloat16, torch.float32), 'out must be bf16 or fp32 on CUDA')
         batch, length, heads, dim = q.shape
         kv_heads = raw_k_rot.shape[2]
         _require(raw_k_rot.shape[0] == batch and raw_k_rot.shape[3] == dim, 'raw cache shape')
         _require(raw_k_rot.stride() == raw_v.stride() and raw_k_rot.stride(3) == 1 and raw_k_rot.stride(2) == dim,
                  'raw caches must be token-major [B, cap, Hkv, D] with contiguous heads')
-        _require(lat_k.stride() == lat_v.stride() and lat_k.stride(2) == 1 and lat_v.stride(2) == 1,
-                 'latent caches [B, cap, R] need matching strides and contiguous rows')
+        if not paged:
+            _require(lat_k.stride() == lat_v.stride() and lat_k.stride(2) == 1 and lat_v.stride(2) == 1,
+                     'latent caches [B, cap, R] need matching strides and contiguous rows')
         for t in (raw_len, latent_len, qpos) + (() if query_len is None else (query_len,)):
             _require(t.is_cuda and t.dtype == torch.int32 and t.is_contiguous(), 'int32 CUDA metadata')
         a = _lib.LatentDecodeArgs()
         a.batch, a.length, a.heads, a.kv_heads, a.head_dim = batch, length, heads, kv_heads, dim
-        a.rank_k, a.rank_v = lat_k.shape[2], lat_v.shape[2]
+        if paged:
+            pages, layout, tables = lat_pages
+            _bf16_cuda(pages)
+            flat = pages.flatten(1)
+            _require(flat.data_ptr() == pages.data_ptr() and flat.stride(1) == 1 and
+                     flat.shape[1] >= layout.page_elements, 'pages must be [num_pages, >= page_elements] rows')
+            _require(tables.is_cuda and tables.dtype == torch.int32 and tables.dim() == 2 and
+                     tables.shape[0] == batch and tables.stride(1) == 1, 'block tables must be int32 [B, n] on CUDA')
+            a.rank_k, a.rank_v = layout.key_rank, layout.value_rank
+        else:
+            a.rank_k, a.rank_v = lat_k.shape[2], lat_v.shape[2]
         _require(uk.shape == (kv_heads * dim, a.rank_k) and uv.shape == (kv_heads * dim, a.rank_v),
                  'up-projection weights must be [Hkv*D, R]')
         a.scale = float(scale if scale is not None else 1.0 / math.sqrt(dim))
@@ -189,9 +206,17 @@ class LatentDecodeCall:
         a.raw_k_pre = 0 if raw_k_pre is None else raw_k_pre.data_ptr()
         a.raw_stride_batch, a.raw_stride_token = raw_k_rot.stride(0), raw_k_rot.stride(1)
         a.raw_capacity = raw_k_rot.shape[1]
-        a.lat_k, a.lat_v = lat_k.data_ptr(), lat_v.data_ptr()
-        a.lat_stride_batch, a.lat_stride_row = lat_k.stride(0), lat_k.stride(1)
-        a.lat_capacity = lat_k.shape[1]
+        if paged:
+            a.lat_k = a.lat_v = 0
+            a.lat_pages, a.lat_page_stride = flat.data_ptr(), flat.stride(0)
+            a.lat_slots, a.lat_sink_elements = layout.slots, layout.sink_elements
+            a.lat_table, a.lat_table_stride = tables.data_ptr(), tables.stride(0)
+            a.lat_num_pages = flat.shape[0]
+            a.lat_capacity = tables.shape[1] * layout.slots
+        else:
+            a.lat_k, a.lat_v = lat_k.data_ptr(), lat_v.data_ptr()
+            a.lat_stride_batch, a.lat_stride_row = lat_k.stride(0), lat_k.stride(1)
+            a.lat_capacity = lat_k.shape[1]
         a.raw_len, a.latent_len, a.qpos = raw_len.data_ptr(), latent_len.data_ptr(), qpos.data_ptr()
         a.query_len = 0 if query_len is None else query_len.data_ptr()
         for name, t in (('new_k', new_k), ('new_v', new_v), ('new_lat_k', new_lat_k), ('new_lat_v', new_lat_v),
@@ -218,7 +243,7 @@ class LatentDecodeCall:
         a.latent_splits, a.raw_splits = int(latent_splits), int(raw_splits)
         self.args = a
         self.device = q.device
-        self._keep = (q, raw_k_rot, raw_v, raw_k_pre, lat_k, lat_v, raw_len, latent_len, query_len, qpos,
+        self._keep = (q, raw_k_rot, raw_v, raw_k_pre, lat_k, lat_v, lat_pages, raw_len, latent_len, query_len, qpos,
                       new_k, new_v, new_lat_k, new_lat_v, uk, uv, uk_bias, uv_bias, cos, sin, out)
         lib = _lib.load()
         size = lib.slimkv_latent_decode_workspace_size(ctypes.byref(a))

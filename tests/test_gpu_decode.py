@@ -31,10 +31,12 @@ def tables(positions=16384):
     return _TABLES[positions]
 
 
-def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False, stale=0.0):
+def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False, stale=0.0, paged=False):
     """Stage the caches without this step's entries, run the fused step.
 
-    Cache rows past each sequence's staged length hold ``stale``.
+    Cache rows past each sequence's staged length hold ``stale``.  With
+    ``paged`` the latent cache lives in Beacon pages (vLLM plugin layout,
+    48 slots per page, disjoint shuffled block tables) instead.
     """
     from slimkv_b200 import kernels
     cos, sin, cos_t, sin_t = tables()
@@ -80,8 +82,26 @@ def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False, stale=0.0):
         t['raw_k_pre'] = torch.zeros_like(t['raw_k_rot'])
     if c['bk'] is not None:
         t['uk_bias'], t['uv_bias'] = to_bf16(c['bk']), to_bf16(c['bv'])
-    kernels.latent_decode(**t)
+    if paged:
+        from slimkv_b200 import pages as P
+        layout = P.BeaconPageLayout(192, 4, rk, rv, Hkv * D)
+        per_seq = (lat_cap + layout.slots - 1) // layout.slots
+        n_pages = B * per_seq + 3
+        order = np.random.default_rng(B * lat_cap).permutation(n_pages)[:B * per_seq]
+        block_tables = torch.from_numpy(order.reshape(B, per_seq).astype(np.int32)).cuda()
+        backing = torch.full((n_pages, layout.page_elements + 8), stale, dtype=torch.bfloat16, device='cuda')
+        P.beacon_append(backing, layout, block_tables, np.zeros(B, np.int32), t['lat_k'], t['lat_v'])
+        t['lat_pages'] = (backing, layout, block_tables)
+        t['lat_k_dense'], t['lat_v_dense'] = t.pop('lat_k'), t.pop('lat_v')
+    kernels.latent_decode(**{k: v for k, v in t.items() if not k.endswith('_dense')})
     torch.cuda.synchronize()
+    if paged:
+        # The appended Beacon rows, read back from the pages.
+        backing, layout, block_tables = t['lat_pages']
+        gk, gv = torch.zeros_like(t['lat_k_dense']), torch.zeros_like(t['lat_v_dense'])
+        P.beacon_gather(backing, layout, block_tables, np.full(B, lat_cap, np.int32), gk, gv)
+        torch.cuda.synchronize()
+        t['lat_k'], t['lat_v'] = gk, gv
     return t
 
 
@@ -128,6 +148,16 @@ def test_stale_cache_rows_past_the_length_are_ignored(stale):
         t = run_fused(c, query_len, extra_cap=200, fp32=fp32, stale=stale)
         assert torch.isfinite(t['out'].float()).all()
         check(c, query_len, t)
+
+
+@pytest.mark.parametrize('length,history,tail,bias', [(1, 300, 37, False), (2, 500, 39, True), (2, 129, 1023, False)])
+def test_fused_decode_reads_the_latent_cache_from_pages(length, history, tail, bias):
+    """The latent branch streams Beacon pages through block tables; the
+    inserted Beacon row is appended into its page."""
+    c = decode_case(300 + history, batch=3, length=length, history=history, tail=tail, bias=bias, ragged=True)
+    query_len = np.full(3, length)
+    check(c, query_len, run_fused(c, query_len, paged=True))
+    check(c, query_len, run_fused(c, query_len, paged=True, fp32=True, stale=float('nan')))
 
 
 @pytest.mark.parametrize('length,history,tail,rank,bias,ragged', [
