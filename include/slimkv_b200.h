@@ -317,6 +317,120 @@ SLIMKV_API int slimkv_raw_pages_read(const slimkv_raw_pages* pages, int batch, c
                                      int64_t key_stride_token, void* value, int64_t value_stride_batch,
                                      int64_t value_stride_token, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Prefill window projection with Beacon roles and the cache append.
+ *
+ * Replaces, for one interleaved chunk of a prefill window,
+ *   LlamaAttention.qkv_proj_with_beacon(hidden, beacon_size, beacon_indices,
+ *       return_latents=True)            (slimkv/llama3/modeling_llama.py:1291-1345)
+ *   LlamaAttention._incremental_cache   (modeling_llama.py:1347-1367)
+ * under the prefill metadata of prefill_ops.prepare_metadata
+ * (slimkv/llama3/prefill_ops.py:17-36: raw_indices / beacon_indices of the
+ * chunk, no replica rows), and the cache writes that follow them:
+ * Memory.update_memory (slimkv/llama3/memory.py:233-278) for dense caches
+ * and flush_memory (slimkv/vllm_plugin/paged_model.py:55-83) for pages.
+ *
+ * Every row is projected by the ONE weight set its role selects (the
+ * reference projects every row through both and selects with torch.where):
+ *   raw row    i (chunk row raw_rows[i]):    q = h W_q^T (+b_q),
+ *              k = h W_k^T (+b_k),  v = h W_v^T (+b_v)
+ *   Beacon row j (chunk row beacon_rows[j]): q = h W_bq^T (+b_bq),
+ *              lk = h W_kd^T,  lv = h W_vd^T  (latents, no bias),
+ *              k = lk U_k^T (+b_uk),  v = lv U_v^T (+b_uv)
+ * with fp32 accumulation and one rounding to bf16 per output (nn.Linear in
+ * bf16).  k/v of Beacon rows are up-projected from the bf16 latents.
+ * Weights are nn.Linear weights [out][in] (row-major bf16, rows 16-byte
+ * aligned); biases are bf16 vectors or NULL.  W_kd and W_vd may be the same
+ * pointer (shared K/V down-projection).
+ *
+ * Every output is optional (NULL = not computed):
+ *   query/key/value  [B][rows][.] chunk rows (pre-RoPE), row r of sequence b
+ *                    at base + b*stride_batch + r*stride_row;
+ *   key_latent/value_latent  Beacon j at row (latent_start ? latent_start[b] : 0)
+ *                    + j of latent_rows rows per sequence (a per-chunk
+ *                    [B][beacon_count][R] buffer, or the dense latent cache
+ *                    at its append cursor);
+ *   beacon_pages     Beacon j at logical row beacon_start[b] + j (BeaconPages.append);
+ *   raw_key_cache/raw_value_cache  dense [B][raw_cache_rows][kv_heads*head_dim]
+ *                    raw cache: raw row i >= raw_first at row raw_start[b] + i;
+ *   raw_pages        raw row i >= raw_first at absolute position raw_start[b] + i
+ *                    (RawPages.write);
+ *   write_sink != 0  the raw row at position raw_start[b] + i == 0 also goes
+ *                    to the sink of beacon_pages' root page table[b][0]
+ *                    (BeaconPages.write_sink).
+ * key/value of Beacon rows need key_latent/value_latent (they are read back
+ * by the up-projection).  Index lists are int32 device arrays shared by all
+ * sequences; an index outside [0, rows), a cache row outside its buffer or a
+ * page id outside the allocation sets SLIMKV_DEVICE_BAD_LENGTH and the row is
+ * skipped.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    int batch, rows, hidden;
+    const void* hidden_states;                 /* bf16 [B][rows][hidden] */
+    int64_t hidden_stride_batch, hidden_stride_row;
+    const int32_t* raw_rows;                   /* metadata.raw_indices */
+    int raw_count;
+    const int32_t* beacon_rows;                /* metadata.beacon_indices */
+    int beacon_count;
+    int heads, kv_heads, head_dim, rank_k, rank_v;
+    const void *w_q, *b_q, *w_k, *b_k, *w_v, *b_v;
+    const void *w_bq, *b_bq, *w_k_down, *w_v_down, *w_k_up, *b_k_up, *w_v_up, *b_v_up;
+    void* query;
+    int64_t query_stride_batch, query_stride_row;
+    void* key;
+    int64_t key_stride_batch, key_stride_row;
+    void* value;
+    int64_t value_stride_batch, value_stride_row;
+    void* key_latent;
+    int64_t key_latent_stride_batch, key_latent_stride_row;
+    void* value_latent;
+    int64_t value_latent_stride_batch, value_latent_stride_row;
+    int latent_rows;                           /* rows per sequence of key/value_latent (0: beacon_count) */
+    const int32_t* latent_start;               /* [B] row of Beacon 0 in key/value_latent, or NULL */
+    const slimkv_beacon_pages* beacon_pages;
+    const int32_t* beacon_start;               /* [B] logical page row of Beacon 0 */
+    const int32_t* raw_start;                  /* [B] raw position of raw row 0 */
+    int raw_first;
+    void* raw_key_cache;
+    void* raw_value_cache;
+    int64_t raw_cache_stride_batch, raw_cache_stride_row;
+    int raw_cache_rows;                        /* rows per sequence of the dense raw cache */
+    const slimkv_raw_pages* raw_pages;
+    int write_sink;
+    void* workspace;                           /* optional split-K scratch (16-byte aligned) */
+    size_t workspace_bytes;
+} slimkv_window_project_args;
+
+/* Workspace for the split-K path (0 when the call does not split).  A call
+ * whose output tiles do not fill the GPU splits each reduction into slices
+ * that store fp32 partial tiles in the workspace; a second kernel sums them
+ * in slice order (deterministic), adds the bias, rounds and stores.  Without
+ * a large enough workspace the call runs unsplit (fewer CTAs; results may
+ * differ from the split ones in the last bit).  Calls sharing a workspace
+ * must be ordered (one stream). */
+SLIMKV_API size_t slimkv_window_project_workspace_size(const slimkv_window_project_args* args);
+SLIMKV_API int slimkv_window_project(const slimkv_window_project_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Prefill RoPE — drop-in for prefill_ops.fused_prefill_rope
+ * (slimkv/llama3/prefill_ops.py:48-74, kernel prefill_kernels.py:7-53).
+ * q [B][Hq][Q][D] and k [B][Hk][K][D] with element strides {batch, head,
+ * seq} (last dim contiguous); outputs with their own strides.  Query s is
+ * rotated at positions[b][K - Q + s], key s at positions[b][s] (int64, row
+ * stride positions_stride).  Key s is a Beacon key (kept as is) when
+ * s < prefix = K - role_count and s >= sink, or roles[s - prefix] is 1 or 2
+ * (int64 roles).  Rotation is BF16-exact: out = bf16(bf16(x c) + bf16(r s))
+ * with c, s the fp32 cos/sin table entries rounded to bf16 and r =
+ * rotate_half(x).  cos/sin are fp32 [rope_positions][D].
+ * ---------------------------------------------------------------------- */
+SLIMKV_API int slimkv_prefill_rope(const void* q, const int64_t q_stride[3], const void* k,
+                                   const int64_t k_stride[3], const float* cos, const float* sin,
+                                   int rope_positions, const int64_t* positions, int64_t positions_stride,
+                                   const int64_t* roles, int role_count, int sink, int batch, int heads,
+                                   int kv_heads, int queries, int keys, int head_dim, void* q_out,
+                                   const int64_t q_out_stride[3], void* k_out, const int64_t k_out_stride[3],
+                                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

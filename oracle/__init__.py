@@ -4,7 +4,8 @@ TEST INFRASTRUCTURE ONLY.  This package restates, in plain numpy, the
 algorithms of the reference implementation (Strandding/SlimKV) on the hot
 path: eager grouped attention, BF16-exact RoPE, the LSE merge, query
 absorption and value up-projection, the decode-step Beacon schedule, the
-prefill interleave rule and the paged-cache addressing.  Each function cites
+prefill interleave rule, the prefill window projection / RoPE / cache
+append and the paged-cache addressing.  Each function cites
 the reference file and line range it follows.
 
 It is the parity checker for the CUDA path and the timed CPU baseline.  Only
@@ -22,3 +23,4 @@ from .decode import latent_decode_attention
 from .schedule import FastDecodeSchedule, interleave_roles, paged_restore_roles
 from .pages import BeaconPageLayout, beacon_page_slots, raw_page_slots, beacon_block_size
 from .splits import latent_splits, dense_splits, original_splits
+from .prefill import prefill_metadata, project_with_beacon, prefill_rope, flush_chunk

@@ -89,6 +89,33 @@ class RawPagesArgs(ctypes.Structure):
 
 _L = ctypes.c_int64
 
+
+class WindowProjectArgs(ctypes.Structure):
+    """Mirror of ``slimkv_window_project_args``."""
+    _fields_ = [
+        ('batch', _I), ('rows', _I), ('hidden', _I),
+        ('hidden_states', _P), ('hidden_stride_batch', _L), ('hidden_stride_row', _L),
+        ('raw_rows', _P), ('raw_count', _I), ('beacon_rows', _P), ('beacon_count', _I),
+        ('heads', _I), ('kv_heads', _I), ('head_dim', _I), ('rank_k', _I), ('rank_v', _I),
+        ('w_q', _P), ('b_q', _P), ('w_k', _P), ('b_k', _P), ('w_v', _P), ('b_v', _P),
+        ('w_bq', _P), ('b_bq', _P), ('w_k_down', _P), ('w_v_down', _P), ('w_k_up', _P), ('b_k_up', _P),
+        ('w_v_up', _P), ('b_v_up', _P),
+        ('query', _P), ('query_stride_batch', _L), ('query_stride_row', _L),
+        ('key', _P), ('key_stride_batch', _L), ('key_stride_row', _L),
+        ('value', _P), ('value_stride_batch', _L), ('value_stride_row', _L),
+        ('key_latent', _P), ('key_latent_stride_batch', _L), ('key_latent_stride_row', _L),
+        ('value_latent', _P), ('value_latent_stride_batch', _L), ('value_latent_stride_row', _L),
+        ('latent_rows', _I), ('latent_start', _P), ('beacon_pages', ctypes.POINTER(BeaconPagesArgs)),
+        ('beacon_start', _P),
+        ('raw_start', _P), ('raw_first', _I), ('raw_key_cache', _P), ('raw_value_cache', _P),
+        ('raw_cache_stride_batch', _L), ('raw_cache_stride_row', _L), ('raw_cache_rows', _I),
+        ('raw_pages', ctypes.POINTER(RawPagesArgs)), ('write_sink', _I),
+        ('workspace', _P), ('workspace_bytes', ctypes.c_size_t),
+    ]
+
+
+_PL = ctypes.POINTER(ctypes.c_int64)
+
 SIGNATURES = {
     'slimkv_version': (_I, []),
     'slimkv_last_error': (ctypes.c_char_p, []),
@@ -106,6 +133,10 @@ SIGNATURES = {
     'slimkv_beacon_pages_sink': (_I, [ctypes.POINTER(BeaconPagesArgs), _I, _P, _P, _L, _I, _P]),
     'slimkv_raw_pages_write': (_I, [ctypes.POINTER(RawPagesArgs), _I, _P, _I, _P, _L, _L, _P, _L, _L, _P]),
     'slimkv_raw_pages_read': (_I, [ctypes.POINTER(RawPagesArgs), _I, _P, _P, _I, _P, _L, _L, _P, _L, _L, _P]),
+    'slimkv_window_project_workspace_size': (ctypes.c_size_t, [ctypes.POINTER(WindowProjectArgs)]),
+    'slimkv_window_project': (_I, [ctypes.POINTER(WindowProjectArgs), _P]),
+    'slimkv_prefill_rope': (_I, [_P, _PL, _P, _PL, _P, _P, _I, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _PL,
+                                 _P, _PL, _P]),
     'slimkv_merge': (_I, [_P, ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _P,
                           ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I,
                           _I, _P, _P]),

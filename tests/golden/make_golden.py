@@ -280,6 +280,101 @@ def gen_pages(out):
     out['raw_pages'] = raw.pages.view(torch.int16).numpy()
 
 
+def _prefill_module(seed):
+    """A small bf16 Llama attention with low-rank Beacon K/V (R_k 16, R_v 32)."""
+    import torch
+    from slimkv.llama3.configuration_llama import LlamaConfig
+    from slimkv.llama3.modeling_llama import LlamaAttention
+    from cases import LLAMA8B
+    config = LlamaConfig(
+        vocab_size=64, hidden_size=128, intermediate_size=64, num_hidden_layers=1,
+        num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=512,
+        rope_theta=LLAMA8B['theta'], rope_scaling=dict(LLAMA8B['scaling'], rope_type='llama3'),
+        attention_bias=True, beacon_param=['q', 'k', 'v'], beacon_window=16, beacon_stride=16,
+        beacon_ratio=[4], beacon_ratio_mix='sequence', beacon_sink_size=1,
+        beacon_skip_rope_for_beacon_k=True, beacon_k_compression='lowrank_svd',
+        beacon_v_compression='lowrank_svd', beacon_k_latent_head_dim_list=[8],
+        beacon_v_latent_head_dim_list=[16], beacon_decode_backend='latent', torch_dtype=torch.float32)
+    config._attn_implementation = 'eager'
+    torch.manual_seed(seed)
+    attn = LlamaAttention(config, layer_idx=0).eval()
+    with torch.no_grad():
+        for p in attn.parameters():
+            p.normal_(0, 0.1)
+    # The fp32 rotary tables as built (the bf16 cast below rounds them).
+    tables = attn.rotary_emb.cos_cached[:512].clone(), attn.rotary_emb.sin_cached[:512].clone()
+    return attn.to(torch.bfloat16), tables
+
+
+def gen_prefill(out):
+    """Role-selected projections, latent packing and prefill RoPE of the reference.
+
+    ``qkv_proj_with_beacon`` + ``_incremental_cache`` run under prefill
+    metadata (``prepare_metadata``'s index lists) on a bf16 module; the
+    prefill RoPE comes from ``_apply_rotary_with_beacon`` (the torch rule the
+    fused Triton kernel reproduces bit for bit).
+    """
+    import torch
+    from slimkv.llama3.prefill_ops import PrefillMetadata
+    sys.path.insert(0, str(ROOT))
+    from oracle.schedule import interleave_roles
+    attn, (cos, sin) = _prefill_module(7)
+    names = {'q': attn.q_proj, 'k': attn.k_proj, 'v': attn.v_proj, 'bq': attn.beacon_q_proj,
+             'k_down': attn.beacon_k_down_proj, 'v_down': attn.beacon_v_down_proj,
+             'k_up': attn.beacon_k_up_proj, 'v_up': attn.beacon_v_up_proj}
+    for name, mod in names.items():
+        out[f'prefill_w_{name}'] = mod.weight.detach().view(torch.int16).numpy()
+        if mod.bias is not None:
+            out[f'prefill_w_{name}_bias'] = mod.bias.detach().view(torch.int16).numpy()
+    rng = np.random.default_rng(51)
+    # (tag, previous chunk (raw count, remainder) or None, this chunk (raw count, remainder))
+    cases = [('first', None, (13, 0)), ('second', (13, 0), (7, 1)), ('nobeacon', None, (2, 0)),
+             ('long', None, (61, 3))]
+    for tag, prev, cur in cases:
+        roles, size, _ = interleave_roles(*cur, 4)
+        window = np.concatenate([interleave_roles(*prev, 4)[0], roles]) if prev else roles
+        n = len(roles)
+        hidden = torch.from_numpy(rng.standard_normal((2, n, 128), dtype=np.float32)).to(torch.bfloat16)
+        indices = torch.from_numpy(window)
+        current = indices[-n:]
+        attn._prefill_metadata = PrefillMetadata((current == 0).nonzero().flatten(),
+                                                 (current != 0).nonzero().flatten(), indices, None, False)
+        with torch.inference_mode():
+            q, k, v, kl, vl = attn.qkv_proj_with_beacon(hidden, size, indices, return_latents=True)
+            kv = k.view(2, n, 2, 32).transpose(1, 2)
+            vv = v.view(2, n, 2, 32).transpose(1, 2)
+            update = attn._incremental_cache(kv, vv, size, indices, (kl, vl))
+        attn._prefill_metadata = None
+        out[f'prefill_{tag}_roles'] = window
+        out[f'prefill_{tag}_hidden'] = hidden.view(torch.int16).numpy()
+        out[f'prefill_{tag}_query'] = q.view(torch.int16).numpy()
+        out[f'prefill_{tag}_key'] = k.view(torch.int16).numpy()
+        out[f'prefill_{tag}_value'] = v.view(torch.int16).numpy()
+        out[f'prefill_{tag}_raw_indices'] = update.raw_indices.numpy()
+        if size:
+            out[f'prefill_{tag}_key_latents'] = update.key_latents.view(torch.int16).numpy()
+            out[f'prefill_{tag}_value_latents'] = update.value_latents.view(torch.int16).numpy()
+    # Prefill RoPE: the shapes of the reference's fused-rotary test.
+    for tag, (batch, qlen, length, sink) in {'a': (1, 3, 3, 0), 'b': (2, 37, 129, 1), 'c': (4, 32, 65, 3)}.items():
+        q = torch.from_numpy(rng.standard_normal((batch, 4, qlen, 32), dtype=np.float32) * 2).to(torch.bfloat16)
+        k = torch.from_numpy(rng.standard_normal((batch, 2, length, 32), dtype=np.float32) * 2).to(torch.bfloat16)
+        roles = (torch.arange(qlen) % 5 == 4).long()
+        roles[::17] = 2
+        positions = (torch.arange(length)[None] + 3 * torch.arange(batch)[:, None])
+        attn.config.beacon_sink_size = sink
+        with torch.inference_mode():
+            qo, ko = attn._apply_rotary_with_beacon(q, k, positions, int((roles != 0).sum()), roles)
+        out[f'prope_{tag}_q'] = q.view(torch.int16).numpy()
+        out[f'prope_{tag}_k'] = k.view(torch.int16).numpy()
+        out[f'prope_{tag}_roles'] = roles.numpy()
+        out[f'prope_{tag}_pos'] = positions.numpy()
+        out[f'prope_{tag}_sink'] = np.array(sink)
+        out[f'prope_{tag}_qo'] = qo.contiguous().view(torch.int16).numpy()
+        out[f'prope_{tag}_ko'] = ko.contiguous().view(torch.int16).numpy()
+    out['prope_cos'] = cos.numpy()
+    out['prope_sin'] = sin.numpy()
+
+
 def gen_splits(out):
     from slimkv.llama3.paired_decode import original_splits
     rows = []
@@ -295,12 +390,22 @@ def main():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument('--reference', required=True, help='path to a SlimKV source checkout')
     p.add_argument('--output', default=str(HERE / 'reference_golden.npz'))
+    p.add_argument('--prefill-output', default=str(HERE / 'prefill_golden.npz'))
+    p.add_argument('--only', choices=['decode', 'prefill'], default=None,
+                   help='write only the decode-side or only the prefill-side fixture file')
     args = p.parse_args()
     ref = Path(args.reference).resolve()
     sys.path[:0] = [str(_stubs()), str(ref), str(HERE), str(ROOT)]
     import torch
     torch.set_num_threads(4)
     from cases import config1_layer
+    if args.only != 'decode':
+        pre = {}
+        gen_prefill(pre)
+        np.savez_compressed(args.prefill_output, **pre)
+        print('wrote', args.prefill_output, sum(v.nbytes for v in pre.values()), 'bytes raw')
+    if args.only == 'prefill':
+        return
     out = {}
     gen_attention(out)
     gen_merge(out)
