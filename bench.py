@@ -15,6 +15,11 @@ sampled tokens, ``roofline`` for the fused latent attention step (HBM bytes
 per launch / CUDA-event time), ``cpu_baseline`` = the CPU restatement of the
 same decode step on this host's cores.
 
+``prefill`` (one window of one layer) times the
+role-selected window projection with the Beacon-page append against the
+reference's own recipe run through torch/cuBLAS on the same GPU; its
+roofline is tensor-bound (useful FLOPs / time vs the measured bf16 peak).
+
 ``--impl reference`` times the CPU restatement of the reference's eager
 decode (the only reference implementation of this path that runs here) on
 the same workload and metric.
@@ -45,6 +50,9 @@ def parse():
     p.add_argument('--warmup', type=int, default=5)
     p.add_argument('--impl', default='slimkv_b200', choices=['slimkv_b200', 'reference'])
     p.add_argument('--no-cpu-baseline', action='store_true')
+    p.add_argument('--no-prefill', action='store_true', help='skip the config-4 prefill window measurement')
+    p.add_argument('--prefill-only', action='store_true',
+                   help='only the config-4 prefill window measurement (profiling runs)')
     p.add_argument('--kernel-only', action='store_true',
                    help='one layer of the same workload: time the attention kernel alone (profiling runs)')
     return p.parse_args()
@@ -113,6 +121,15 @@ def peaks():
     return FALLBACK_HBM_GBS, 'fallback'
 
 
+def tensor_peak():
+    """Dense bf16 TFLOP/s to divide by: the measured cuBLAS burst figure."""
+    path = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    if os.path.exists(path):
+        with open(path) as f:
+            return float(json.load(f)['bf16_tflops']), 'measured (MEASURED_PEAKS.json bf16_tflops, burst)'
+    return 1590.0, 'fallback 1590 TFLOP/s'
+
+
 def traffic_per_launch(kernel_bytes):
     """ncu DRAM bytes (read + write) of one attention launch, from the
     committed capture of the same kernel on one layer of this workload,
@@ -151,6 +168,109 @@ def run_reference(args):
         'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
         'note': "CPU restatement of the reference's eager fp32 decode (fa2_decode.decode with eager_forward) "
                 'on all host threads; the reference GPU kernel builds only for sm_90/sm_120'}), flush=True)
+
+
+PREFILL_BATCH = 4
+PREFILL_WINDOW = 1024
+
+
+def prefill_window_step(device, steps, warmup):
+    """BASELINE config 4, one window of one layer: B=4 sequences x 1280
+    interleaved rows (1024 raw tokens + 256 Beacons), Llama-3.1-8B r4 layer
+    (hidden 4096, 32/8 heads, ranks 320/320), hidden rows N(0, 1), random
+    N(0, 0.02) weights.  Times (CUDA graphs, device time) the role-selected
+    projection with the Beacon-page append (``slimkv_window_project``), the
+    append alone (Beacon latents -> pages) and the reference's recipe on the
+    same GPU through torch/cuBLAS: every row through both weight sets,
+    torch.where, index_select and the page write by advanced indexing
+    (modeling_llama.py:1291-1367, paged_cache.py:78-87)."""
+    import numpy as np
+    import torch
+    import oracle
+    from slimkv_b200 import prefill, _lib
+    from slimkv_b200.pages import BeaconPageLayout, BeaconPages
+    g = torch.Generator(device=device)
+    g.manual_seed(4)
+    H, qd, kvd, R, B = 4096, 4096, 1024, 320, PREFILL_BATCH
+
+    def w(*shape, std=0.02):
+        return (torch.randn(*shape, generator=g, device=device) * std).to(torch.bfloat16)
+
+    W = prefill.BeaconProjectionWeights(q=w(qd, H), k=w(kvd, H), v=w(kvd, H), bq=w(qd, H), k_down=w(R, H),
+                                        v_down=w(R, H), k_up=w(kvd, R), v_up=w(kvd, R))
+    roles, _, _ = oracle.interleave_roles(PREFILL_WINDOW, 0, 4)
+    n = len(roles)
+    hidden = w(B, n, H, std=1.0)
+    meta = prefill.metadata_from_roles(torch.from_numpy(roles).to(device), n)
+    meta.raw_indices, meta.beacon_indices = meta.raw_indices.int(), meta.beacon_indices.int()
+    layout = BeaconPageLayout(192, 4, R, R, kvd)
+    per_seq = 32 * 1024 // 192 + 2                        # a 32k prompt's Beacon pages
+    pages = torch.zeros(B * per_seq, layout.page_elements, dtype=torch.bfloat16, device=device)
+    tables = torch.arange(B * per_seq, dtype=torch.int32, device=device).reshape(B, per_seq)
+    lat_start = torch.full((B,), 7 * 256, dtype=torch.int32, device=device)    # the 8th window of the prompt
+    bp = BeaconPages(pages, layout)
+    nb = meta.beacon_indices.numel()
+
+    def ours():
+        return prefill.project_window(W, hidden, meta, 32, 8, 128, lat_start=lat_start, beacon=(bp, tables))
+
+    def append_only():
+        prefill.project_window(W, hidden, meta, 32, 8, 128, query=False, key=False, value=False, latents=False,
+                               lat_start=lat_start, beacon=(bp, tables))
+
+    role_raw = (meta.roles == 0)[:, None]
+    cols = torch.arange(layout.width, device=device)
+
+    def recipe():
+        q = torch.where(role_raw, hidden @ W.q.t(), hidden @ W.bq.t())
+        lk, lv = hidden @ W.k_down.t(), hidden @ W.v_down.t()
+        k = torch.where(role_raw, hidden @ W.k.t(), lk @ W.k_up.t())
+        v = torch.where(role_raw, hidden @ W.v.t(), lv @ W.v_up.t())
+        sk, sv = lk.index_select(1, meta.beacon_indices), lv.index_select(1, meta.beacon_indices)
+        for b in range(B):
+            logical = torch.arange(7 * 256, 7 * 256 + nb, device=device)
+            page = tables[b].long()[logical // layout.slots]
+            col = layout.sink_elements + (logical % layout.slots)[:, None] * layout.width + cols[None]
+            pages[page[:, None], col] = torch.cat([sk[b], sv[b]], dim=-1)
+        return q, k, v
+
+    def graph_us(fn):
+        fn()
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream(device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        for _ in range(max(warmup, 3)):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps * 1000.0
+
+    _lib.device_status(clear=True)
+    t_ours, t_append, t_ref = graph_us(ours), graph_us(append_only), graph_us(recipe)
+    status = _lib.device_status(clear=True)
+    raw_rows, beacon_rows = B * PREFILL_WINDOW, B * nb
+    flops = 2 * H * (raw_rows * (qd + 2 * kvd) + beacon_rows * (qd + 2 * R)) + 2 * beacon_rows * 2 * R * kvd
+    append_flops = 2 * H * beacon_rows * 2 * R
+    append_bytes = beacon_rows * H * 2 + 2 * R * H * 2 + beacon_rows * 2 * R * 2
+    return {'workload': 'BASELINE config 4 window step, one layer: B=4 x (1024 raw + 256 Beacon) interleaved rows, '
+                        'Llama-3.1-8B r4 (hidden 4096, heads 32/8, ranks 320/320), Beacon pages 192 raw tokens',
+            'us_per_window_layer': t_ours, 'raw_tokens_per_s_per_layer': raw_rows / (t_ours / 1e6),
+            'tflops': flops / (t_ours / 1e6) / 1e12, 'flops_per_window_layer': flops,
+            'append_only_us': t_append, 'append_only_gbs': append_bytes / (t_append / 1e6) / 1e9,
+            'append_only_bytes': append_bytes, 'append_only_tflops': append_flops / (t_append / 1e6) / 1e12,
+            'reference_recipe_gpu_us': t_ref, 'speedup_vs_reference_recipe': t_ref / t_ours,
+            'kernels': 'project_kernel (tcgen05, gathered rows) + finalize_kernel when split', 'device_status': status}
 
 
 def attention_kernel_time(rt, reps):
@@ -200,6 +320,12 @@ def main():
         return run_reference(args)
     if args.kernel_only:
         return kernel_only(args)
+    if args.prefill_only:
+        import torch
+        device = torch.device('cuda', 0)
+        print(json.dumps({'prefill_only': True, **prefill_window_step(device, max(args.steps, 1), args.warmup)}),
+              flush=True)
+        return
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -287,6 +413,14 @@ def main():
     layer_bytes = rt.attention_bytes() / cfg.layers
     peak, peak_kind = peaks()
     status = _lib.device_status(clear=True)
+    rt.graph = None
+    prefill = None
+    if not args.no_prefill:
+        prefill = prefill_window_step(device, max(args.steps, 10), args.warmup)
+        prefill['us_per_window_layer'] = max_over_ranks(prefill['us_per_window_layer'])
+        tf_peak = tensor_peak()
+        prefill['roofline'] = {'bound': 'tensor', 'achieved': prefill['tflops'], 'peak': tf_peak[0],
+                               'unit': 'TFLOP/s', 'frac': prefill['tflops'] / tf_peak[0], 'peak_source': tf_peak[1]}
 
     result = {
         'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
@@ -305,11 +439,12 @@ def main():
         'gpu_launches': args.steps * (1 + 3 * cfg.layers),
         'clocks': clock_info, 'device_status': status,
     }
+    if prefill is not None:
+        result['prefill'] = prefill
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result['cpu_baseline'] = cpu_baseline(BATCH)
     if rank == 0:
         print(json.dumps(result), flush=True)
-    rt.graph = None
     if world > 1:
         dist.destroy_process_group()
 

@@ -148,17 +148,26 @@ __device__ __forceinline__ uint16_t* target_row(const PjTarget& T, int b, int j,
     return T.base + int64_t(page) * T.page_stride + T.sink + (row % T.slots) * T.width + T.col;
 }
 
-__device__ __forceinline__ void store_row(uint16_t* dst, const uint32_t (&packed)[16], int cnt) {
-    if (cnt == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-        uint4* d = reinterpret_cast<uint4*>(dst);
+// Per-warp staging tile of 32 rows x 128 bytes, 16-byte chunks swizzled by
+// row so that both the row-per-lane writes and the row-segment reads are
+// free of bank conflicts.
+__device__ __forceinline__ void stage_row(uint8_t* stg, int lane, const uint32_t* w) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-            d[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+    for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<uint4*>(stg + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+            make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+}
+__device__ __forceinline__ uint4 staged_piece(const uint8_t* stg, int row, int piece) {
+    return *reinterpret_cast<const uint4*>(stg + row * 128 + ((piece ^ (row & 7)) << 4));
+}
+// Store `cnt` (<= 8) bf16 values of a 16-byte piece.
+__device__ __forceinline__ void store_piece(uint16_t* dst, uint4 v, int cnt) {
+    if (cnt == 8 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        *reinterpret_cast<uint4*>(dst) = v;
         return;
     }
-#pragma unroll
-    for (int e = 0; e < 32; ++e)
-        if (e < cnt) dst[e] = static_cast<uint16_t>(packed[e >> 1] >> ((e & 1) * 16));
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    for (int e = 0; e < cnt; ++e) dst[e] = static_cast<uint16_t>(w[e >> 1] >> ((e & 1) * 16));
 }
 
 __global__ void __launch_bounds__(kPjThreads, 1)
@@ -245,21 +254,32 @@ project_kernel(const __grid_constant__ PjMaps maps, const __grid_constant__ PjPa
         const int h = warp >> 2, quarter = warp & 3;
         const uint32_t taddr = tbase + (uint32_t(quarter * 32) << 16) + uint32_t(h * 256);
         const int grow = m0 + h * 128 + quarter * 32 + lane;
+        // Staging: each warp turns its 32 rows x 128 bytes (thread = row, as
+        // TMEM delivers them) around through shared memory (stage 0 is free
+        // once every MMA has retired) so lanes store whole row segments.
+        uint8_t* stg = smem + warp * 4096;
+        const int srow = lane >> 3;     // with piece = lane & 7: 4 rows x 8 pieces per store
         if (G.splits > 1) {
             // Store this slice's fp32 partial tile into its workspace slot.
-            float* acc_row = G.acc + ((int64_t(split) * tiles_mn + tile) * kPjTileM + h * 128 + quarter * 32 + lane) *
-                                         G.bn;
+            float* acc_tile = G.acc + (int64_t(split) * tiles_mn + tile) * kPjTileM * G.bn;
+            const int row0 = h * 128 + quarter * 32;
+            const int valid_rows = min(32, total_rows - (m0 + row0));
             if (ok) {
                 for (int c0 = 0; c0 < G.bn; c0 += 32) {
                     float v[32];
                     tmem_ld32(taddr + c0, v);
                     tmem_wait_ld();
-                    const int cnt = grow < total_rows ? min(32, G.bn - c0) : 0;
+                    stage_row(stg, lane, reinterpret_cast<const uint32_t*>(v));
+                    __syncwarp();
+                    const int cnt = min(32, G.bn - c0);
 #pragma unroll
-                    for (int e = 0; e < 32; e += 4)
-                        if (e < cnt)
-                            __stcg(reinterpret_cast<float4*>(acc_row + c0 + e),
-                                   make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
+                    for (int rr = 0; rr < 8; ++rr) {
+                        const int r = rr * 4 + srow;
+                        if (r < valid_rows && piece * 4 < cnt)
+                            __stcg(reinterpret_cast<uint4*>(acc_tile + int64_t(row0 + r) * G.bn + c0 + piece * 4),
+                                   staged_piece(stg, r, piece));
+                    }
+                    __syncwarp();
                 }
             }
             ok = false;
@@ -274,24 +294,38 @@ project_kernel(const __grid_constant__ PjMaps maps, const __grid_constant__ PjPa
                     for (int t = 0; t < kPjMaxTargets; ++t) dst[t] = target_row(G.t[t], b, j, P.status);
                 }
             }
-            for (int c0 = 0; c0 < G.bn; c0 += 32) {
-                float v[32];
-                tmem_ld32(taddr + c0, v);
-                tmem_wait_ld();
+            for (int c0 = 0; c0 < G.bn; c0 += 64) {
                 const int n = n0 + c0;
-                const int cnt = min(32, min(G.bn - c0, G.n - n));
+                const int cnt = min(64, min(G.bn - c0, G.n - n));
                 if (cnt <= 0) break;
-                if (G.bias) {
+                uint32_t packed[32];
 #pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        if (e < cnt) v[e] += __uint_as_float(uint32_t(__ldg(G.bias + n + e)) << 16);
+                for (int half = 0; half < 2; ++half) {
+                    float v[32];
+                    tmem_ld32(taddr + c0 + half * 32, v);
+                    tmem_wait_ld();
+                    if (G.bias) {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (half * 32 + e < cnt) v[e] += __uint_as_float(uint32_t(__ldg(G.bias + n + half * 32 + e)) << 16);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) packed[half * 16 + e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
                 }
-                uint32_t packed[16];
+                stage_row(stg, lane, packed);
+                __syncwarp();
 #pragma unroll
-                for (int e = 0; e < 16; ++e) packed[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+                for (int t = 0; t < kPjMaxTargets; ++t) {
 #pragma unroll
-                for (int t = 0; t < kPjMaxTargets; ++t)
-                    if (dst[t]) store_row(dst[t] + n, packed, cnt);
+                    for (int rr = 0; rr < 8; ++rr) {
+                        const int r = rr * 4 + srow;
+                        uint16_t* d = reinterpret_cast<uint16_t*>(
+                            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(dst[t]), r));
+                        if (d && piece * 8 < cnt) store_piece(d + n + piece * 8, staged_piece(stg, r, piece),
+                                                              min(8, cnt - piece * 8));
+                    }
+                }
+                __syncwarp();
             }
         }
     } else if (warp == 8) {
