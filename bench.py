@@ -53,9 +53,27 @@ def parse():
     p.add_argument('--no-prefill', action='store_true', help='skip the config-4 prefill window measurement')
     p.add_argument('--prefill-only', action='store_true',
                    help='only the config-4 prefill window measurement (profiling runs)')
+    p.add_argument('--config', type=int, default=2, choices=[2, 3],
+                   help='2 (default): the metric\'s config; 3: batched paged decode, r8, B=256, ragged contexts')
     p.add_argument('--kernel-only', action='store_true',
                    help='one layer of the same workload: time the attention kernel alone (profiling runs)')
     return p.parse_args()
+
+
+C3_BATCH = 256
+C3_METRIC = 'decode tokens/s and latent-attn HBM GB/s, paged vLLM-plugin layout, Llama-3.1-8B-r8 t8f8, ' \
+            'B=256, ctx U[2048,131072]'
+
+
+def config3(n, ctx):
+    return {'workload': 'Llama-3.1-8B-r8 t8f8 batched paged decode step (BASELINE config 3), latent path',
+            'global_batch': C3_BATCH * n, 'batch_per_gpu': C3_BATCH,
+            'context': f'U[2048, 131072] seeded (mean {int(ctx.mean())}, max {int(ctx.max())})',
+            'latent_rank': '160/160', 'ratio': 8, 'sinks': 4, 'layers': 32,
+            'latent_cache': 'Beacon pages of the vLLM plugin (96 slots = 768 raw tokens per 64 KB page), '
+                            'shuffled per-sequence block tables; raw tail in the native rotated layout',
+            'parallelism': f'dp{n} (independent replicas, no data-path collective)',
+            'l2': 'each step reads ~60 GB (weights + caches) >> 126 MB L2; no flush needed'}
 
 
 def config(n):
@@ -340,12 +358,25 @@ def main():
         dist.init_process_group('nccl', timeout=timedelta(seconds=300))
     torch.cuda.set_device(local)
     device = torch.device('cuda', local)
-    cfg = LatentLlamaConfig()
-    weights = RandomWeights(cfg, device, seed=0)
     rng = np.random.default_rng(1234 + rank)
-    tails = rng.integers(0, cfg.window, size=BATCH)
-    rt = LatentDecodeRuntime(cfg, weights, [HISTORY] * BATCH, tails, device, extra_windows=1)
-    rt.tokens.copy_(torch.from_numpy(rng.integers(0, cfg.vocab, size=BATCH)).to(device))
+    if args.config == 3:
+        # Config 3: r8 ranks, one Beacon per 8 raw tokens, contexts U[2048, 131072].
+        cfg = LatentLlamaConfig(rank_k=160, rank_v=160, ratio=8)
+        weights = RandomWeights(cfg, device, seed=0)
+        batch = C3_BATCH
+        ctx = rng.integers(2048, 131072 + 1, size=batch)
+        history = (ctx // cfg.window) * (cfg.window // cfg.ratio)
+        tails = ctx % cfg.window
+        rt = LatentDecodeRuntime(cfg, weights, history, tails, device, extra_windows=1, paged=True, raw_pre=False)
+        metric, workload = C3_METRIC, config3(world, ctx)
+    else:
+        cfg = LatentLlamaConfig()
+        weights = RandomWeights(cfg, device, seed=0)
+        batch = BATCH
+        tails = rng.integers(0, cfg.window, size=BATCH)
+        rt = LatentDecodeRuntime(cfg, weights, [HISTORY] * BATCH, tails, device, extra_windows=1)
+        metric, workload = METRIC, config(world)
+    rt.tokens.copy_(torch.from_numpy(rng.integers(0, cfg.vocab, size=batch)).to(device))
     rt.capture(warmup=2)
     for _ in range(max(args.warmup, 3)):
         rt.step()
@@ -375,11 +406,11 @@ def main():
     clock_info = clocks.stop()
     barrier()
     ms = max_over_ranks(start.elapsed_time(end) / args.steps)
-    value = world * BATCH / (ms / 1000.0)
+    value = world * batch / (ms / 1000.0)
 
     # ---- end to end through the runtime API: host tokens in, host tokens out -
-    host_in = torch.from_numpy(rng.integers(0, cfg.vocab, size=BATCH)).pin_memory()
-    host_out = torch.empty(BATCH, dtype=torch.int64).pin_memory()
+    host_in = torch.from_numpy(rng.integers(0, cfg.vocab, size=batch)).pin_memory()
+    host_out = torch.empty(batch, dtype=torch.int64).pin_memory()
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -415,7 +446,7 @@ def main():
     status = _lib.device_status(clear=True)
     rt.graph = None
     prefill = None
-    if not args.no_prefill:
+    if not args.no_prefill and args.config == 2:
         prefill = prefill_window_step(device, max(args.steps, 10), args.warmup)
         prefill['us_per_window_layer'] = max_over_ranks(prefill['us_per_window_layer'])
         tf_peak = tensor_peak()
@@ -423,16 +454,16 @@ def main():
                                'unit': 'TFLOP/s', 'frac': prefill['tflops'] / tf_peak[0], 'peak_source': tf_peak[1]}
 
     result = {
-        'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
+        'metric': metric, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
         'warmup': max(args.warmup, 3), 'ms_per_step': ms, 'higher_is_better': True, 'scaling': 'weak',
         'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (random N(0,0.02) weights, synthetic cache)',
-        'config': config(world),
-        'e2e': {'value': world * BATCH / (e2e_ms / 1000.0), 'unit': UNIT, 'h2d_bytes_per_step': BATCH * 8,
-                'd2h_bytes_per_step': BATCH * 8, 'ms_per_step': e2e_ms},
+        'config': workload,
+        'e2e': {'value': world * batch / (e2e_ms / 1000.0), 'unit': UNIT, 'h2d_bytes_per_step': batch * 8,
+                'd2h_bytes_per_step': batch * 8, 'ms_per_step': e2e_ms},
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
                      'peak_source': f'{peak_kind} (MEASURED_PEAKS.json hbm_gbs)' if peak_kind == 'measured'
                      else 'fallback 6650 GB/s',
-                     'traffic': traffic_per_launch(kernel_bytes), 'kernel': 'decode_tc_kernel (latent + raw branches, '
+                     'traffic': traffic_per_launch(kernel_bytes) if args.config == 2 else None, 'kernel': 'decode_tc_kernel (latent + raw branches, '
                      'one launch per layer)', 'bytes_per_launch': kernel_bytes, 'us_per_launch': attn_ms * 1000.0,
                      'fused_step_per_layer': {'us': layer_ms * 1000.0, 'bytes': layer_bytes,
                                               'gbs': layer_bytes / (layer_ms / 1000.0) / 1e9}},
@@ -441,7 +472,7 @@ def main():
     }
     if prefill is not None:
         result['prefill'] = prefill
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == 2:
         result['cpu_baseline'] = cpu_baseline(BATCH)
     if rank == 0:
         print(json.dumps(result), flush=True)

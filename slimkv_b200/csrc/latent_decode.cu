@@ -58,7 +58,7 @@ struct DecodePlan {
     int wl = 0, mtl = 0, lat_row_blocks = 0, lat_rows = 0, lat_splits = 0, lat_tps = 0;
     int raw_rows = 0, raw_splits = 0, raw_tps = 0, group = 0, rvp = 0;
     bool tc = false;   // latent branch on the tensor-memory kernel (32 query heads)
-    size_t q_rot = 0, q_lat = 0, lat_o = 0, lat_lse = 0, raw_o = 0, raw_lse = 0;
+    size_t q_rot = 0, q_lat = 0, lat_o = 0, lat_lse = 0, raw_o = 0, raw_lse = 0, lat_work = 0;
 };
 
 int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
@@ -107,21 +107,40 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
         // One launch, 128-key tiles, one CTA per SM: the latent CTAs leave
         // about one SM per sequence free, where the (short) raw CTAs start;
         // the rest of the raw CTAs follow as latent CTAs finish.
+        //
+        // Sequences may have different latent lengths: every sequence gets
+        // ceil(tiles_b / tps) splits of at most tps tiles (at least one), and
+        // the prologue writes the list of (sequence, split) work items the
+        // latent CTAs take in order.  Small batches: tps spreads the longest
+        // sequence over about one SM per sequence less one.  Large batches
+        // (fewer than 3 SMs per sequence): splits of at most 16 tiles, so no
+        // single long sequence sets the kernel time.
         const int sms = std::max(device_info().sm_count, 1);
         const int tiles = std::max(1, (lat_len + kTcTileKeys - 1) / kTcTileKeys);
         const int per_seq = sms / a->batch;
-        int s2 = a->latent_splits > 0 ? a->latent_splits : (per_seq >= 3 ? per_seq - 1 : std::max(per_seq, 1));
-        p.lat_splits = std::max(1, std::min({s2, tiles, 32}));
-        p.lat_tps = (tiles + p.lat_splits - 1) / p.lat_splits;
+        int tps;
+        if (a->latent_splits > 0)
+            tps = (tiles + a->latent_splits - 1) / a->latent_splits;
+        else if (per_seq >= 3)
+            tps = (tiles + per_seq - 2) / (per_seq - 1);
+        else
+            tps = std::min(16, std::max(4, (tiles + 7) / 8));
+        tps = std::max(tps, (tiles + 31) / 32);               // the merge combines at most 32 splits
+        p.lat_tps = std::max(1, tps);
+        p.lat_splits = (tiles + p.lat_tps - 1) / p.lat_tps;
         p.lat_rows = 64;
         const int rtiles = std::max(1, (raw_len + kTcTileKeys - 1) / kTcTileKeys);
-        const int r2 = a->raw_splits > 0 ? a->raw_splits : 2;
+        // Raw CTAs are short (a tail of at most 1023 keys per KV head): two
+        // splits help a small batch fill the machine; a large batch has CTAs
+        // to spare and pays each CTA's fixed cost, so one.
+        const int r2 = a->raw_splits > 0 ? a->raw_splits : (per_seq >= 3 ? 2 : 1);
         p.raw_splits = std::max(1, std::min({r2, rtiles, 32}));
         p.raw_tps = (rtiles + p.raw_splits - 1) / p.raw_splits;
         p.raw_rows = 64;
     }
     p.q_rot = B * L * H * a->head_dim;
     p.q_lat = p.tc ? B * 128 * p.wl : B * L * H * p.wl;
+    p.lat_work = p.tc ? B * p.lat_splits : 0;
     p.lat_o = B * p.lat_splits * p.lat_rows * p.wl;
     p.lat_lse = B * p.lat_splits * p.lat_rows;
     p.raw_o = B * a->kv_heads * p.raw_splits * p.raw_rows * 128;
@@ -133,6 +152,7 @@ struct Buffers {
     __nv_bfloat16* q_rot;
     __half* q_lat;
     float *lat_o, *lat_lse, *raw_o, *raw_lse;
+    int32_t* lat_work;      // [B * lat_splits]: latent CTA -> (sequence, split count, split)
 };
 
 Buffers carve(Carver& c, const DecodePlan& p) {
@@ -143,6 +163,7 @@ Buffers carve(Carver& c, const DecodePlan& p) {
     w.lat_lse = c.take<float>(p.lat_lse);
     w.raw_o = c.take<float>(p.raw_o);
     w.raw_lse = c.take<float>(p.raw_lse);
+    w.lat_work = c.take<int32_t>(p.lat_work);
     return w;
 }
 
@@ -262,6 +283,8 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     pa.lat_page_stride = a->lat_page_stride; pa.lat_table_stride = a->lat_table_stride;
     pa.lat_slots = a->lat_slots; pa.lat_sink = a->lat_sink_elements; pa.lat_num_pages = a->lat_num_pages;
     pa.lat_table = a->lat_table;
+    pa.lat_work = p.tc ? w.lat_work : nullptr;
+    pa.lat_tps = p.lat_tps; pa.lat_splits_max = p.lat_splits;
     pa.status = status;
     const dim3 pgrid(a->kv_heads, p.wl / 64, (a->batch + pa.seq_per_cta - 1) / pa.seq_per_cta);
     decode_prologue_kernel<<<pgrid, 256, 0, stream>>>(pa);
@@ -313,6 +336,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         L.pages = a->lat_pages; L.page_stride = a->lat_page_stride; L.slots = a->lat_slots;
         L.sink_elements = a->lat_sink_elements; L.num_pages = a->lat_num_pages;
         L.table = a->lat_table; L.table_stride = a->lat_table_stride;
+        L.work = w.lat_work; L.tiles_per_split = p.lat_tps;
         TcSide& R = tl.raw;
         R.k = a->raw_k_rot; R.v = a->raw_v; R.dim_k = a->head_dim; R.dim_v = a->head_dim;
         R.kv_heads = a->kv_heads; R.capacity = a->raw_capacity;
@@ -344,6 +368,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     MergeArgs ma{};
     ma.lat_o = w.lat_o; ma.lat_lse = w.lat_lse; ma.lat_splits = p.lat_splits; ma.lat_rows = p.lat_rows;
     ma.lat_width = p.wl;
+    ma.lat_tps = p.tc ? p.lat_tps : 0; ma.latent_len = a->latent_len;
     ma.raw_o = w.raw_o; ma.raw_lse = w.raw_lse; ma.raw_splits = p.raw_splits; ma.raw_rows = p.raw_rows;
     ma.raw_l_pitch = p.tc ? 32 : p.group;
     ma.q_rot = w.q_rot;

@@ -9,6 +9,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "latent_tc.h"
 
 namespace slimkv {
 
@@ -52,8 +53,32 @@ struct PrologueArgs {
     int64_t lat_page_stride, lat_table_stride;
     int lat_slots, lat_sink, lat_num_pages;
     const int32_t* lat_table;
+    // Latent work list of the tensor-memory attention (nullable): written by
+    // block (0, 0, 0), one entry per latent CTA (batch * lat_splits_max):
+    // sequence << 11 | splits << 5 | split, then -1 for unused CTAs.
+    int32_t* lat_work;
+    int lat_tps, lat_splits_max;
     unsigned int* status;
 };
+
+// One warp writes the (sequence, split) items of all sequences in order.
+__device__ __forceinline__ void build_latent_work(const PrologueArgs& a, int lane) {
+    int base = 0;
+    for (int b0 = 0; b0 < a.batch; b0 += 32) {
+        const int b = b0 + lane;
+        const int n = b < a.batch ? latent_splits_of(a.latent_len[b], a.lat_tps, a.lat_splits_max) : 0;
+        int x = n;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, off);
+            if (lane >= off) x += y;
+        }
+        const int start = base + x - n;
+        for (int s = 0; s < n; ++s) a.lat_work[start + s] = (b << 11) | (n << 5) | s;
+        base += __shfl_sync(0xffffffffu, x, 31);
+    }
+    for (int i = base + lane; i < a.batch * a.lat_splits_max; i += 32) a.lat_work[i] = -1;
+}
 
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
@@ -107,6 +132,7 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
     __shared__ __align__(1024) uint8_t s_b[128 * 64 * 2];         // U_k[g][:, cc*64 : +64] fp16
     const int g = blockIdx.x, cc = blockIdx.y, bb = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (a.lat_work && g == 0 && cc == 0 && bb == 0 && warp == 0) build_latent_work(a, lane);
     const int rps = a.length * a.group;                 // rows per sequence
     const int b0 = bb * a.seq_per_cta;
     const int half = a.dim / 2;
@@ -252,6 +278,8 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
 
 struct MergeArgs {
     const float* lat_o; const float* lat_lse; int lat_splits, lat_rows, lat_width;
+    int lat_tps;                   // > 0: sequence b has latent_splits_of(latent_len[b]) splits
+    const int32_t* latent_len;
     const float* raw_o; const float* raw_lse; int raw_splits, raw_rows;
     int raw_l_pitch;        // raw partial row of (query l, head j): l * raw_l_pitch + j
     const __nv_bfloat16* q_rot;
@@ -277,6 +305,10 @@ __device__ __forceinline__ void cp_async_commit_wait_all() {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ int lat_splits_row(const MergeArgs& a, int b) {
+    return a.lat_tps > 0 ? latent_splits_of(a.latent_len[b], a.lat_tps, a.lat_splits) : a.lat_splits;
+}
 
 // grid (Hkv, ceil(B / seq_per_cta)), 256 threads, merge_smem_bytes() of
 // dynamic shared memory.  CTA (g, bb) merges the (<= 16) query rows
@@ -337,7 +369,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
 #pragma unroll
         for (int br = 0; br < 2; ++br) {
             float my = -INFINITY;
-            if (valid && lane < (br ? a.raw_splits : a.lat_splits))
+            if (valid && lane < (br ? a.raw_splits : lat_splits_row(a, b)))
                 my = br ? __ldg(a.raw_lse + (((int64_t)b * a.kv_heads + g) * a.raw_splits + lane) * a.raw_rows + rr)
                         : __ldg(a.lat_lse + ((int64_t)b * a.lat_splits + lane) * a.lat_rows + l * a.heads + h);
             float m = my;
@@ -377,8 +409,9 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             const float* src = a.lat_o + ((int64_t)b * a.lat_splits * a.lat_rows + l * a.heads + h) * a.lat_width + c;
             const float* w = s_w + r * 32;
+            const int nsp = lat_splits_row(a, b);
             int s = 0;
-            for (; s + 8 <= a.lat_splits; s += 8) {
+            for (; s + 8 <= nsp; s += 8) {
                 float4 x[8];
 #pragma unroll
                 for (int u = 0; u < 8; ++u) x[u] = __ldg(reinterpret_cast<const float4*>(src + (s + u) * pitch));
@@ -388,7 +421,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
                     acc.z = fmaf(w[s + u], x[u].z, acc.z); acc.w = fmaf(w[s + u], x[u].w, acc.w);
                 }
             }
-            for (; s < a.lat_splits; ++s) {
+            for (; s < nsp; ++s) {
                 const float4 x = __ldg(reinterpret_cast<const float4*>(src + s * pitch));
                 acc.x = fmaf(w[s], x.x, acc.x); acc.y = fmaf(w[s], x.y, acc.y);
                 acc.z = fmaf(w[s], x.z, acc.z); acc.w = fmaf(w[s], x.w, acc.w);

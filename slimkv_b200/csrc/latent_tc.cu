@@ -148,7 +148,15 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
     const CUtensorMap* qmap = is_lat ? &lqmap : &rqmap;
     const CUtensorMap* omap = is_lat ? &lomap : &romap;
     const int idx = is_lat ? int(blockIdx.x) : int(blockIdx.x) - n_lat;
-    const int split = idx % J.splits, bg = idx / J.splits;
+    int split = idx % J.splits, bg = idx / J.splits, nsplits = J.splits;
+    if (J.work) {
+        // Work-list item; the whole CTA leaves on an unused entry.
+        const int item = __ldg(J.work + idx);
+        if (item < 0) return;
+        split = item & 31;
+        nsplits = (item >> 5) & 63;
+        bg = (item >> 11) * J.kv_heads;
+    }
     const int b = bg / J.kv_heads, g = bg - b * J.kv_heads;
     const int z = bg * J.splits + split;                     // partial-output slot
     const int n_keys = J.seqlens[b];
@@ -161,8 +169,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
     const uint32_t off_p = off_q + uint32_t(nq * kMaxChunks) * kQChunkBytes;
     const int n_tiles = (max(n_keys, 0) + kKeys - 1) / kKeys;
     // Tiles spread evenly over the sequence's splits.
-    const int t0 = int((int64_t)split * n_tiles / J.splits);
-    const int t1 = int((int64_t)(split + 1) * n_tiles / J.splits);
+    const int t0 = int((int64_t)split * n_tiles / nsplits);
+    const int t1 = int((int64_t)(split + 1) * n_tiles / nsplits);
     const int nt = max(0, t1 - t0);
     const int total_k = nt * kc, total_v = nt * vc;
     // K chunk n -> (tile n / kc, chunk n % kc) in ring slot n % kring.
@@ -178,20 +186,24 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
     // Paged K/V: the page of each 16-key block of one tile, cached in
     // registers per stream (K runs ahead of V).  Keys past the length read a
     // valid page (their scores are masked and their V rows zeroed).
+    // A tile is J.box_rows-row boxes (box_rows = gcd(slots, 128) >= 16, so
+    // no box crosses a page).
     struct PageCache { int tile = -1; int page[kKeys / 16]; };
     PageCache kpc, vpc;
+    const int boxes = J.table ? kKeys / J.box_rows : 1;
     auto fill_pages = [&](PageCache& pc, int tile) {
         if (pc.tile == tile) return;
         pc.tile = tile;
         const int last = max(n_keys - 1, 0);
 #pragma unroll
         for (int i = 0; i < kKeys / 16; ++i) {
-            const int key = min(tile * kKeys + 16 * i, last);
+            if (i >= boxes) break;
+            const int key = min(tile * kKeys + J.box_rows * i, last);
             pc.page[i] = __ldg(J.table + b * J.table_stride + key / J.slots);
         }
     };
     // One 16 KB chunk [128 keys x 64 columns] at column col: one box of the
-    // dense map, or eight 16-row boxes of the page map.
+    // dense map, or 128 / box_rows boxes of the page map.
     auto load_chunk = [&](uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int col, int tile, PageCache& pc) {
         if (!J.table) {
             tma_load_4d(dst, map, bar, col, g, tile * kKeys, b);
@@ -201,8 +213,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
         const int last = max(n_keys - 1, 0);
 #pragma unroll
         for (int i = 0; i < kKeys / 16; ++i) {
-            const int key = min(tile * kKeys + 16 * i, last);
-            tma_load_4d(dst + i * 2048, map, bar, col, 0, (key % J.slots) & ~15, pc.page[i]);
+            if (i >= boxes) break;
+            const int key = min(tile * kKeys + J.box_rows * i, last);
+            tma_load_4d(dst + i * J.box_rows * 128, map, bar, col, 0, (key % J.slots) & ~(J.box_rows - 1),
+                        pc.page[i]);
         }
     };
     auto issue_k = [&](int n) {
@@ -611,9 +625,9 @@ int make_side(const TcSide& S, int batch, int length, float scale, const int32_t
     if (S.dim_k > 320 || S.dim_v > 320 || S.width < 64 || S.width % 64 || S.rows_alloc % 32 ||
         (reinterpret_cast<uintptr_t>(S.part_o) & 15) || S.group > 32)
         return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "tensor-core decode attention: unsupported branch shape");
-    int rc;
+    int rc, box_rows = 128;
     if (S.pages) {
-        // One map over the pages: (W columns, slots rows, pages), 16-row boxes;
+        // One map over the pages: (W columns, slots rows, pages);
         // K chunks at columns [0, dim_k), V chunks from dim_k.
         const int W = S.dim_k + S.dim_v;
         if (S.slots % 16 || S.dim_k % 8 || S.sink_elements % 8 || S.page_stride % 8 || S.num_pages <= 0 || !S.table ||
@@ -622,8 +636,10 @@ int make_side(const TcSide& S, int batch, int length, float scale, const int32_t
                         "paged latent attention needs 16-row-aligned pages (slots %% 16, ranks %% 8, 16-byte aligned)");
         const void* base = static_cast<const uint16_t*>(S.pages) + S.sink_elements;
         const uint64_t row = uint64_t(W) * 2, page = uint64_t(S.page_stride) * 2;
-        // dims (W, 1, slots, pages): the helper's box {64, 1, 16, 1} spans 16 rows.
-        if ((rc = encode_map_4d(&km, base, W, 1, S.slots, S.num_pages, row, row, page, 16))) return rc;
+        // dims (W, 1, slots, pages), box {64, 1, box_rows, 1}: the largest
+        // power of two <= 128 dividing slots, so boxes never cross pages.
+        while (S.slots % box_rows) box_rows /= 2;
+        if ((rc = encode_map_4d(&km, base, W, 1, S.slots, S.num_pages, row, row, page, box_rows))) return rc;
         vm = km;
     } else {
         const uint64_t head_bytes = S.kv_heads > 1 ? uint64_t(S.stride_head) * 2 : uint64_t(S.stride_row) * 2;
@@ -668,6 +684,9 @@ int make_side(const TcSide& S, int batch, int length, float scale, const int32_t
     J.table_stride = S.table_stride;
     J.slots = S.slots;
     J.v_col = S.pages ? S.dim_k : 0;
+    J.box_rows = box_rows;
+    J.work = S.work;
+    J.tps = S.tiles_per_split > 0 ? S.tiles_per_split : 1;
     return SLIMKV_OK;
 }
 

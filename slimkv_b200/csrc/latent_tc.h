@@ -28,7 +28,13 @@ struct TcJob {
     // then one page map [pages][slots][W] and V starts at column v_col.
     const int32_t* table;
     int64_t table_stride;
-    int slots, v_col;
+    int slots, v_col, box_rows;   // box_rows: rows per page-map box (divides slots and 128)
+    // Work list (nullable): work[i] = sequence << 11 | its split count << 5 |
+    // split for CTA i of the branch, -1 for an unused CTA; a sequence has
+    // latent_splits_of(seqlens[b], tps, splits) splits.  Without it CTA i is
+    // (i / splits, i % splits).
+    const int32_t* work;
+    int tps;
 };
 
 // One branch as the host describes it.
@@ -53,6 +59,8 @@ struct TcSide {
     int slots, sink_elements, num_pages;
     const int32_t* table;
     int64_t table_stride;
+    const int32_t* work;       // see TcJob::work
+    int tiles_per_split;
 };
 
 struct TcLaunch {
@@ -65,6 +73,15 @@ struct TcLaunch {
 };
 
 constexpr int kTcTileKeys = 128;
+
+// Latent splits of a sequence with `len` latent rows when every split holds
+// at most `tps` 128-key tiles (at least one split, at most `smax`).  The
+// prologue's work list, the attention kernel and the merge agree on it.
+__host__ __device__ inline int latent_splits_of(int len, int tps, int smax) {
+    const int tiles = len > 0 ? (len + kTcTileKeys - 1) / kTcTileKeys : 0;
+    const int n = (tiles + tps - 1) / tps;
+    return n < 1 ? 1 : (n > smax ? smax : n);
+}
 
 int launch_decode_tc(const TcLaunch& launch, cudaStream_t stream);
 

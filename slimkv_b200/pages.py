@@ -53,6 +53,19 @@ class BeaconPageLayout:
         return (self.page_elements + self.width - 1) // self.width
 
 
+def beacon_block_size(ratio, raw_width, max_width, raw_block=16):
+    """Raw tokens one Beacon page covers in the vLLM backend
+    (``create_page_layers``, slimkv/vllm_plugin/backend.py:108-118): the page
+    has the bytes of a ``raw_block``-token raw page; after the sink it holds
+    ``(elements - 2 * raw_width) // max_width`` slots of ``ratio`` raw tokens,
+    rounded down to a multiple of ``raw_block``."""
+    page_bytes = raw_block * 2 * raw_width * 2
+    block = (((page_bytes // 2 - 2 * raw_width) // max_width) * ratio // raw_block) * raw_block
+    if block < raw_block or block % ratio:
+        raise ValueError('Cannot represent the selected token ratio in compact pages.')
+    return block
+
+
 def _stream():
     return torch.cuda.current_stream().cuda_stream
 

@@ -93,7 +93,15 @@ class LatentDecodeRuntime:
     ``extra_windows`` more windows of growth.
     """
 
-    def __init__(self, cfg, weights, history, tails, device, extra_windows=1, seed=1, fill_std=1.3):
+    def __init__(self, cfg, weights, history, tails, device, extra_windows=1, seed=1, fill_std=1.3, paged=False,
+                 raw_pre=True, latent_splits=0, raw_splits=0):
+        """``paged`` keeps each layer's latent cache in the vLLM plugin's Beacon
+        pages (page size of a 16-token raw page, ``create_page_layers``,
+        slimkv/vllm_plugin/backend.py:108-131), each sequence owning the pages
+        its own length needs, in shuffled order; ``raw_pre=False`` drops the
+        pre-RoPE copy of the raw keys (only the append writes it);
+        ``latent_splits`` / ``raw_splits`` override the attention split plan
+        (0: the library's choice)."""
         self.cfg, self.w, self.device = cfg, weights, device
         B = len(history)
         self.batch = B
@@ -110,16 +118,46 @@ class LatentDecodeRuntime:
         gen = torch.Generator(device=device)
         gen.manual_seed(seed)
 
-        def fill(*shape):
-            return torch.randn(*shape, generator=gen, device=device, dtype=torch.bfloat16).mul_(fill_std)
+        # Cache contents: N(0, fill_std^2) bf16.  Large caches repeat one
+        # random block (cheap to fill; the values only set magnitudes).
+        block = torch.randn(1 << 24, generator=gen, device=device, dtype=torch.bfloat16).mul_(fill_std)
 
+        def fill(*shape):
+            t = torch.empty(*shape, device=device, dtype=torch.bfloat16)
+            flat = t.view(-1)
+            for i in range(0, flat.numel(), block.numel()):
+                n = min(block.numel(), flat.numel() - i)
+                flat[i:i + n].copy_(block[:n])
+            return t
+
+        self.layout = None
+        if paged:
+            from .pages import BeaconPageLayout, beacon_block_size
+            width = cfg.rank_k + cfg.rank_v
+            self.layout = BeaconPageLayout(beacon_block_size(cfg.ratio, kvd, width), cfg.ratio, cfg.rank_k,
+                                           cfg.rank_v, kvd)
+            slots = self.layout.slots
+            need = [(int(h) + (1 + extra_windows) * per_window + slots - 1) // slots for h in hist.tolist()]
+            order = torch.randperm(sum(need), generator=torch.Generator().manual_seed(seed))
+            tables = torch.zeros(B, max(need), dtype=torch.int32)
+            at = 0
+            for b, n in enumerate(need):
+                tables[b, :n] = order[at:at + n].int()
+                at += n
+            self.tables = tables.to(device)
+            self.num_pages = sum(need)
+            self.lat_capacity = max(need) * slots
         self.caches = []
         for _ in range(cfg.layers):
             raw_k = fill(B, self.raw_capacity, cfg.kv_heads, cfg.head_dim)
-            lat = fill(B, self.lat_capacity, cfg.rank_k + cfg.rank_v)
-            self.caches.append(dict(raw_k_rot=raw_k, raw_k_pre=raw_k.clone(),
-                                    raw_v=fill(B, self.raw_capacity, cfg.kv_heads, cfg.head_dim),
-                                    lat=lat, lat_k=lat[..., :cfg.rank_k], lat_v=lat[..., cfg.rank_k:]))
+            c = dict(raw_k_rot=raw_k, raw_k_pre=raw_k.clone() if raw_pre else None,
+                     raw_v=fill(B, self.raw_capacity, cfg.kv_heads, cfg.head_dim))
+            if paged:
+                c['pages'] = fill(self.num_pages, self.layout.page_elements)
+            else:
+                lat = fill(B, self.lat_capacity, cfg.rank_k + cfg.rank_v)
+                c.update(lat=lat, lat_k=lat[..., :cfg.rank_k], lat_v=lat[..., cfg.rank_k:])
+            self.caches.append(c)
         # Per-sequence schedule counters and per-step metadata (device).
         i32 = dict(dtype=torch.int32, device=device)
         self.history = hist.to(device)
@@ -144,14 +182,17 @@ class LatentDecodeRuntime:
         lat_max = int(hist.max()) + per_window + 64
         self.calls = []
         for c, layer in zip(self.caches, weights.layers):
+            pages = (c['pages'], self.layout, self.tables) if paged else None
             self.calls.append(kernels.LatentDecodeCall(
                 q=q, raw_k_rot=c['raw_k_rot'], raw_v=c['raw_v'], raw_k_pre=c['raw_k_pre'],
-                lat_k=c['lat_k'], lat_v=c['lat_v'], raw_len=self.raw_len, latent_len=self.latent_len,
+                lat_k=c.get('lat_k'), lat_v=c.get('lat_v'), lat_pages=pages, raw_len=self.raw_len,
+                latent_len=self.latent_len,
                 query_len=self.query_len, qpos=self.qpos, uk=layer['uk'], uv=layer['uv'],
                 cos=self.cos, sin=self.sin, out=self.attn,
                 new_k=z[:, 0, qd:qd + kvd], new_v=z[:, 0, qd + kvd:qd + 2 * kvd],
                 new_lat_k=z[:, 1, qd:qd + cfg.rank_k], new_lat_v=z[:, 1, qd + cfg.rank_k:qd + cfg.rank_k + cfg.rank_v],
-                latent_len_max=min(lat_max, self.lat_capacity), raw_len_max=self.raw_capacity))
+                latent_len_max=min(lat_max, self.lat_capacity), raw_len_max=self.raw_capacity,
+                latent_splits=latent_splits, raw_splits=raw_splits))
         self.graph = None
 
     # ------------------------------------------------------------------

@@ -178,6 +178,30 @@ def test_fused_decode_matches_oracle(length, history, tail, rank, bias, ragged):
     check(c, query_len, run_fused(c, query_len, fp32=True))
 
 
+@pytest.mark.parametrize('paged', [False, True])
+def test_large_ragged_batch_splits_every_sequence_by_its_length(paged):
+    """More sequences than SMs / 3 with latent lengths from 1 to ~4.6k rows:
+    each sequence gets its own number of bounded splits (the work list the
+    prologue writes), and the merge combines exactly those."""
+    c = decode_case(77, batch=60, length=2, history=4096, tail=900, rk=160, rv=160, ragged=True)
+    query_len = np.array([1 + (b % 3 == 0) for b in range(60)])
+    c['n_lat'] = c['n_lat'] - (query_len == 1)
+    c['n_lat'][3] = 1                                  # only this step's Beacon
+    c['n_lat'][4] = 0 if query_len[4] == 1 else 1      # no latent at all when no Beacon is inserted
+    c['n_lat'][5] = 129                                # one row past a tile
+    check(c, query_len, run_fused(c, query_len, paged=paged))
+
+
+@pytest.mark.parametrize('length', [1, 2])
+def test_paged_decode_is_bit_identical_to_dense(length):
+    """Same inputs, latent cache in Beacon pages or dense: the same bits."""
+    c = decode_case(5, batch=3, length=length, history=2176, tail=1000, rk=160, rv=160, ratio=8)
+    query_len = np.full(3, length)
+    dense = run_fused(c, query_len, fp32=True)
+    paged = run_fused(c, query_len, fp32=True, paged=True)
+    assert torch.equal(dense['out'], paged['out'])
+
+
 def test_mixed_query_lengths_in_one_batch():
     """Only some rows insert a Beacon this step (per-row query_len)."""
     c = decode_case(7, batch=4, length=2, history=400, tail=19)

@@ -1,0 +1,44 @@
+"""Whole-step decode runtime: the latent cache in the vLLM plugin's Beacon pages.
+
+The paged runtime (per-sequence shuffled block tables, the backend's page
+size rule) must follow the dense runtime given the same cache contents,
+through steps that insert a Beacon row (appended into a page) and steps that
+do not.  The attention step itself is bit-identical between the layouts
+(``test_gpu_decode.py``); the logits also pass through cuBLAS GEMMs, so they
+are held to the bf16-logit bar (2e-2 absolute).
+"""
+import pytest
+import torch
+
+
+@pytest.mark.gpu
+def test_paged_runtime_matches_dense_runtime():
+    from slimkv_b200 import pages as P
+    from slimkv_b200.runtime import LatentDecodeRuntime, LatentLlamaConfig, RandomWeights
+    dev = torch.device('cuda', 0)
+    cfg = LatentLlamaConfig(layers=2, vocab=512, hidden=1024, intermediate=2048, rank_k=160, rank_v=160, ratio=8)
+    w = RandomWeights(cfg, dev, seed=3)
+    per_window = cfg.window // cfg.ratio
+    history, tails = [per_window * 3, per_window * 17, per_window], [5, 1000, 7]
+    dense = LatentDecodeRuntime(cfg, w, history, tails, dev)
+    paged = LatentDecodeRuntime(cfg, w, history, tails, dev, paged=True)
+    assert paged.layout.slots == 96                     # 768 raw tokens per 64 KB page at r8 / t8
+    for cd, cp in zip(dense.caches, paged.caches):
+        for name in ('raw_k_rot', 'raw_k_pre', 'raw_v'):
+            cp[name].copy_(cd[name])
+        for b, h in enumerate(history):
+            n = h + per_window                           # history + the open window's rows
+            P.beacon_append(cp['pages'], paged.layout, paged.tables[b:b + 1], [0], cd['lat_k'][b:b + 1, :n],
+                            cd['lat_v'][b:b + 1, :n])
+    tokens = torch.tensor([3, 77, 500], device=dev)
+    inserted = 0
+    for _ in range(3):
+        dense.tokens.copy_(tokens)
+        paged.tokens.copy_(tokens)
+        ld, lp = dense.step_eager().clone(), paged.step_eager().clone()
+        torch.cuda.synchronize()
+        assert torch.isfinite(ld).all()
+        assert (ld - lp).abs().max().item() <= 2e-2
+        inserted += int((paged.query_len == 2).sum())
+        tokens = ld.argmax(-1)
+    assert inserted >= 2                                # Beacon rows went into pages on some steps
