@@ -53,8 +53,9 @@ def parse():
     p.add_argument('--no-prefill', action='store_true', help='skip the config-4 prefill window measurement')
     p.add_argument('--prefill-only', action='store_true',
                    help='only the config-4 prefill window measurement (profiling runs)')
-    p.add_argument('--config', type=int, default=2, choices=[2, 3],
-                   help='2 (default): the metric\'s config; 3: batched paged decode, r8, B=256, ragged contexts')
+    p.add_argument('--config', type=int, default=2, choices=[2, 3, 5],
+                   help='2 (default): the metric\'s config; 3: batched paged decode, r8, B=256, ragged contexts; '
+                        '5: Qwen2.5-14B geometry, r2, 131072-token contexts, 32 sequences per GPU')
     p.add_argument('--kernel-only', action='store_true',
                    help='one layer of the same workload: time the attention kernel alone (profiling runs)')
     return p.parse_args()
@@ -74,6 +75,19 @@ def config3(n, ctx):
                             'shuffled per-sequence block tables; raw tail in the native rotated layout',
             'parallelism': f'dp{n} (independent replicas, no data-path collective)',
             'l2': 'each step reads ~60 GB (weights + caches) >> 126 MB L2; no flush needed'}
+
+
+C5_BATCH = 32
+C5_METRIC = 'decode tokens/s and latent-attn HBM GB/s, Qwen2.5-14B-r2 t4 latent path, 131072-token contexts'
+
+
+def config5(n):
+    return {'workload': 'Qwen2.5-14B geometry r2 t4 decode step (BASELINE config 5, batch-64 run as 32 sequences '
+                        'per GPU), latent path',
+            'global_batch': C5_BATCH * n, 'batch_per_gpu': C5_BATCH, 'context': '131072 + raw tail U{0..1023}',
+            'beacon_latents': 32768, 'latent_rank': '512/512', 'heads': '40 / 8 KV', 'sinks': 4, 'layers': 48,
+            'parallelism': f'dp{n} (independent replicas; 64 sequences = 2 GPUs)',
+            'l2': 'each step reads ~140 GB (weights + caches) >> 126 MB L2; no flush needed'}
 
 
 def config(n):
@@ -369,6 +383,15 @@ def main():
         tails = ctx % cfg.window
         rt = LatentDecodeRuntime(cfg, weights, history, tails, device, extra_windows=1, paged=True, raw_pre=False)
         metric, workload = C3_METRIC, config3(world, ctx)
+    elif args.config == 5:
+        from slimkv_b200.runtime import qwen25_14b_r2
+        cfg = qwen25_14b_r2()
+        weights = RandomWeights(cfg, device, seed=0)
+        batch = C5_BATCH
+        tails = rng.integers(0, cfg.window, size=batch)
+        history = [131072 // cfg.window * (cfg.window // cfg.ratio)] * batch
+        rt = LatentDecodeRuntime(cfg, weights, history, tails, device, extra_windows=1, raw_pre=False)
+        metric, workload = C5_METRIC, config5(world)
     else:
         cfg = LatentLlamaConfig()
         weights = RandomWeights(cfg, device, seed=0)
@@ -463,8 +486,8 @@ def main():
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
                      'peak_source': f'{peak_kind} (MEASURED_PEAKS.json hbm_gbs)' if peak_kind == 'measured'
                      else 'fallback 6650 GB/s',
-                     'traffic': traffic_per_launch(kernel_bytes) if args.config == 2 else None, 'kernel': 'decode_tc_kernel (latent + raw branches, '
-                     'one launch per layer)', 'bytes_per_launch': kernel_bytes, 'us_per_launch': attn_ms * 1000.0,
+                     'traffic': traffic_per_launch(kernel_bytes) if args.config == 2 else None, 'kernel': ('decode_tc_kernel' if args.config != 5 else 'decode_attention_kernel<512>') +
+                     ' (latent + raw branches, one launch per layer)', 'bytes_per_launch': kernel_bytes, 'us_per_launch': attn_ms * 1000.0,
                      'fused_step_per_layer': {'us': layer_ms * 1000.0, 'bytes': layer_bytes,
                                               'gbs': layer_bytes / (layer_ms / 1000.0) / 1e9}},
         'gpu_launches': args.steps * (1 + 3 * cfg.layers),

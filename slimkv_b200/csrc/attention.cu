@@ -178,7 +178,7 @@ int launch_attention_job(int width, int mt, const CUtensorMap& km, const CUtenso
 // Tensor map over a BSHD cache view [B, N, Hkv, D] with element strides
 // {sb, sn, sh}; a zero batch stride maps one shared batch.
 int make_bshd_map(CUtensorMap* map, const void* base, int batch, int keys, int kv_heads, int dim,
-                  const int64_t stride[3], int* bcast) {
+                  const int64_t stride[3], int* bcast, int box_rows) {
     if (!aligned16(base)) return fail(SLIMKV_ERR_ALIGNMENT, "K/V base pointer must be 16-byte aligned");
     const int64_t sb = stride[0], sn = stride[1], sh = kv_heads > 1 ? stride[2] : stride[1];
     if (sn % 8 || sh % 8 || sb % 8 || sn <= 0 || sh <= 0 || sb < 0)
@@ -186,7 +186,7 @@ int make_bshd_map(CUtensorMap* map, const void* base, int batch, int keys, int k
     *bcast = sb == 0 ? 1 : 0;
     const int b_dim = sb == 0 ? 1 : batch;
     const int64_t sb_eff = sb == 0 ? sn * keys : sb;
-    return encode_map_4d(map, base, dim, kv_heads, keys, b_dim, sh * 2, sn * 2, sb_eff * 2, kTile);
+    return encode_map_4d(map, base, dim, kv_heads, keys, b_dim, sh * 2, sn * 2, sb_eff * 2, box_rows);
 }
 
 }  // namespace slimkv
@@ -218,8 +218,8 @@ extern "C" int slimkv_attention_forward(const slimkv_attention_args* a, void* wo
                                              workspace_bytes, c.used);
     CUtensorMap km, vm;
     int kb = 0, vb = 0;
-    if ((rc = make_bshd_map(&km, a->k, a->batch, a->keys, a->kv_heads, a->head_dim, a->k_stride, &kb))) return rc;
-    if ((rc = make_bshd_map(&vm, a->v, a->batch, a->keys, a->kv_heads, a->value_dim, a->v_stride, &vb))) return rc;
+    if ((rc = make_bshd_map(&km, a->k, a->batch, a->keys, a->kv_heads, a->head_dim, a->k_stride, &kb, kTile))) return rc;
+    if ((rc = make_bshd_map(&vm, a->v, a->batch, a->keys, a->kv_heads, a->value_dim, a->v_stride, &vb, kTile))) return rc;
     AttnJob job{};
     job.q = a->q;
     job.q_fp16 = 0;

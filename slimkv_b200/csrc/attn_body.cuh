@@ -54,18 +54,20 @@ struct AttnJob {
     unsigned int* status;          // device status word
 };
 
-template <int W, int MT, int BUDGET = kStageBudget>
+// TILE keys per pipeline stage: 64, or 32 for the widest latents (W = 512)
+// so that two stages of K and V still fit beside Q.
+template <int W, int MT, int BUDGET = kStageBudget, int TILE = kTile>
 struct AttnCfg {
     static constexpr int ROWS = 16 * MT;
     static constexpr int KG = kWarps / MT;      // key groups in Q.K^T
-    static constexpr int KPW = kTile / KG;      // keys per warp in Q.K^T
+    static constexpr int KPW = TILE / KG;       // keys per warp in Q.K^T
     static constexpr int NTQ = KPW / 8;
     static constexpr int KS = W / 16;
     static constexpr int CH = W / 64;
     static constexpr int DPW = W / kWarps;      // output columns per warp in P.V
     static constexpr int NTV = DPW / 8;
-    static constexpr bool QREG = MT <= 2;       // Q fragments held in registers
-    static constexpr int TILE_BYTES = kTile * W * 2;
+    static constexpr bool QREG = MT <= 2 && W <= 320;   // Q fragments held in registers
+    static constexpr int TILE_BYTES = TILE * W * 2;
     static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
     static constexpr int STAGES = (BUDGET / STAGE_BYTES) < 4 ? (BUDGET / STAGE_BYTES) : 4;
     static constexpr int Q_BYTES = QREG ? 0 : ROWS * W * 2;
@@ -73,7 +75,8 @@ struct AttnCfg {
     static constexpr int RED_FLOATS = 2 * KG * ROWS;
     static constexpr int SMEM = STAGES * STAGE_BYTES + Q_BYTES + P_BYTES + RED_FLOATS * 4 +
                                 2 * STAGES * 8 + 1024;
-    static_assert(W % 64 == 0 && W <= 320, "width");
+    static_assert(W % 64 == 0 && (W <= 320 || (W == 512 && TILE == 32)), "width");
+    static_assert(KPW % 8 == 0, "keys per warp");
     static_assert(DPW % 8 == 0, "P.V column split");
     static_assert(STAGES >= 2, "pipeline depth");
     static_assert(SMEM <= 232448, "shared memory");
@@ -92,10 +95,10 @@ __device__ __forceinline__ uint32_t load_q_pair(const AttnJob& J, int b, int g, 
 
 // `rb` selects the block of ROWS query rows this CTA owns (row blocks let a
 // GQA group wider than 64 query rows be split across CTAs).
-template <int W, int MT, int BUDGET = kStageBudget>
+template <int W, int MT, int BUDGET = kStageBudget, int TILE = kTile>
 __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int split, int rb,
                                           uint8_t* smem) {
-    using C = AttnCfg<W, MT, BUDGET>;
+    using C = AttnCfg<W, MT, BUDGET, TILE>;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint8_t* stages = smem;
     uint8_t* qs = smem + C::STAGES * C::STAGE_BYTES;
@@ -108,7 +111,7 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
     const int qlen = J.qlens ? J.qlens[b] : J.queries;
     const int row0 = rb * C::ROWS;                       // first global row of this CTA
     const int rows_valid = min(qlen * J.group - row0, C::ROWS);
-    const int n_tiles = (max(n_keys, 0) + kTile - 1) / kTile;
+    const int n_tiles = (max(n_keys, 0) + TILE - 1) / TILE;
     // The last split runs to the end, so lengths beyond the planning bound
     // are still covered (only slower).
     const int t0 = split * J.tiles_per_split;
@@ -126,11 +129,11 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
         uint8_t* vd = kd + C::TILE_BYTES;
         mbar_expect_tx(&bars[s], C::TILE_BYTES);
 #pragma unroll
-        for (int c = 0; c < C::CH; ++c) tma_load_4d(kd + c * kTile * 128, J.kmap, &bars[s], c * 64, g, t * kTile, bk);
+        for (int c = 0; c < C::CH; ++c) tma_load_4d(kd + c * TILE * 128, J.kmap, &bars[s], c * 64, g, t * TILE, bk);
         mbar_expect_tx(&bars[C::STAGES + s], C::TILE_BYTES);
 #pragma unroll
         for (int c = 0; c < C::CH; ++c)
-            tma_load_4d(vd + c * kTile * 128, J.vmap, &bars[C::STAGES + s], c * 64, g, t * kTile, bv);
+            tma_load_4d(vd + c * TILE * 128, J.vmap, &bars[C::STAGES + s], c * 64, g, t * TILE, bv);
     };
     if (tid == 0) {
         for (int s = 0; s < C::STAGES && t0 + s < t1; ++s) issue(t0 + s, s);
@@ -213,7 +216,7 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
                 ldsm_x4(qs_addr + (ks >> 2) * (C::ROWS * 128) + row * 128 + (((unit ^ row) & 7) << 4),
                         a[0], a[1], a[2], a[3]);
             }
-            const uint32_t chunk = kt + (ks >> 2) * (kTile * 128);
+            const uint32_t chunk = kt + (ks >> 2) * (TILE * 128);
             const int u0 = (ks & 3) * 2;
             if constexpr (C::NTQ >= 2) {
 #pragma unroll
@@ -236,7 +239,7 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
             }
         }
         // ---- scale, mask, per-warp row maxima ----
-        const int key0 = t * kTile + kbase + (lane & 3) * 2;
+        const int key0 = t * TILE + kbase + (lane & 3) * 2;
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
             const int row = rq0 + 8 * hh;
@@ -307,9 +310,9 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
         // their P is zero, and zeroing the operand as well keeps a non-finite
         // stale value from turning 0 * x into NaN.
         const int d0 = warp * C::DPW;
-        const int vlim = n_keys - t * kTile;
+        const int vlim = n_keys - t * TILE;
 #pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
+        for (int kk = 0; kk < TILE / 16; ++kk) {
             const int kq = kk * 16 + (lane & 3) * 2;
             const uint32_t m_lo = (kq < vlim ? 0xffffu : 0u) | (kq + 1 < vlim ? 0xffff0000u : 0u);
             const uint32_t m_hi = (kq + 8 < vlim ? 0xffffu : 0u) | (kq + 9 < vlim ? 0xffff0000u : 0u);
@@ -328,7 +331,7 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
                 const int dim = d0 + nt * 8 + (mi >> 1) * 8;
                 const int unit = (dim & 63) >> 3;
                 uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(vt + (dim >> 6) * (kTile * 128) + key * 128 + (((unit ^ key) & 7) << 4), b0, b1, b2, b3);
+                ldsm_x4_t(vt + (dim >> 6) * (TILE * 128) + key * 128 + (((unit ^ key) & 7) << 4), b0, b1, b2, b3);
                 b0 = bf16x2_to_f16x2(b0) & m_lo; b1 = bf16x2_to_f16x2(b1) & m_hi;
                 b2 = bf16x2_to_f16x2(b2) & m_lo; b3 = bf16x2_to_f16x2(b3) & m_hi;
 #pragma unroll
@@ -344,7 +347,7 @@ __device__ __forceinline__ void attn_body(const AttnJob& J, int b, int g, int sp
                 const int dim = d0 + nt * 8;
                 const int unit = (dim & 63) >> 3;
                 uint32_t b0, b1;
-                ldsm_x2_t(vt + (dim >> 6) * (kTile * 128) + key * 128 + (((unit ^ key) & 7) << 4), b0, b1);
+                ldsm_x2_t(vt + (dim >> 6) * (TILE * 128) + key * 128 + (((unit ^ key) & 7) << 4), b0, b1);
                 b0 = bf16x2_to_f16x2(b0) & m_lo; b1 = bf16x2_to_f16x2(b1) & m_hi;
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) mma_f16(o[mt][nt], a[mt], b0, b1);

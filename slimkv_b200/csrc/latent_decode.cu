@@ -23,7 +23,10 @@
 namespace slimkv {
 
 int make_bshd_map(CUtensorMap* map, const void* base, int batch, int keys, int kv_heads, int dim,
-                  const int64_t stride[3], int* bcast);
+                  const int64_t stride[3], int* bcast, int box_rows);
+
+// Latent key tile of the split-KV route: 64 keys, 32 for ranks above 320.
+constexpr int lat_tile_keys(int width) { return width > 320 ? 32 : kTile; }
 
 // One launch: CTAs [0, n_latent) take latent work items, the rest raw ones.
 template <int WL, int MTL>
@@ -40,7 +43,8 @@ decode_attention_kernel(const __grid_constant__ CUtensorMap lk, const __grid_con
         jl.vmap = &lv;
         const int split = idx % jl.splits;
         const int rest = idx / jl.splits;
-        attn_body<WL, MTL>(jl, rest / latent_row_blocks, 0, split, rest % latent_row_blocks, smem);
+        attn_body<WL, MTL, kStageBudget, lat_tile_keys(WL)>(jl, rest / latent_row_blocks, 0, split,
+                                                            rest % latent_row_blocks, smem);
     } else {
         idx -= n_latent;
         if (threadIdx.x == 0) { tma_prefetch_desc(&rk); tma_prefetch_desc(&rv); }
@@ -67,14 +71,15 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
         return fail(SLIMKV_ERR_INVALID_ARGUMENT, "invalid head counts");
     if (a->length != 1 && a->length != 2) return fail(SLIMKV_ERR_INVALID_ARGUMENT, "length must be 1 or 2");
     if (a->head_dim != 128) return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "fused decode needs head_dim 128");
-    if (a->rank_k <= 0 || a->rank_k > 320 || a->rank_k % 8 || a->rank_v <= 0 || a->rank_v > 320 || a->rank_v % 8)
-        return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "latent ranks must be multiples of 8 in [8, 320]");
+    if (a->rank_k <= 0 || a->rank_k > 512 || a->rank_k % 8 || a->rank_v <= 0 || a->rank_v > 512 || a->rank_v % 8)
+        return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "latent ranks must be multiples of 8 in [8, 512]");
     if (a->raw_capacity <= 0 || a->lat_capacity <= 0) return fail(SLIMKV_ERR_INVALID_ARGUMENT, "empty cache");
     p.group = a->heads / a->kv_heads;
     if (p.group * a->length > kMaxRows)
         return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "at most %d query rows per KV head", kMaxRows);
     p.wl = (std::max(a->rank_k, a->rank_v) + 63) / 64 * 64;
     p.wl = std::max(p.wl, 128);
+    if (p.wl > 320) p.wl = 512;                  // one wide instantiation (32-key tiles)
     p.rvp = (a->rank_v + 63) / 64 * 64;
     const int lat_rows = a->heads * a->length;
     p.mtl = lat_rows <= 32 ? 2 : 4;
@@ -83,10 +88,11 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
     p.raw_rows = 16;
     const int lat_len = a->latent_len_max > 0 ? std::min(a->latent_len_max, a->lat_capacity) : a->lat_capacity;
     const int raw_len = a->raw_len_max > 0 ? std::min(a->raw_len_max, a->raw_capacity) : a->raw_capacity;
-    const int lat_tiles = std::max(1, (lat_len + kTile - 1) / kTile);
+    const int lt = lat_tile_keys(p.wl);
+    const int lat_tiles = std::max(1, (lat_len + lt - 1) / lt);
     const int raw_tiles = std::max(1, (raw_len + kTile - 1) / kTile);
     // Balance bytes: one CTA per SM, each streaming about the same volume.
-    const double lat_tile_bytes = double(kTile) * (a->rank_k + a->rank_v) * 2;
+    const double lat_tile_bytes = double(lt) * (a->rank_k + a->rank_v) * 2;
     const double raw_tile_bytes = double(kTile) * a->head_dim * 2 * 2;
     const double total = a->batch * (p.lat_row_blocks * lat_tiles * lat_tile_bytes +
                                      a->kv_heads * raw_tiles * raw_tile_bytes);
@@ -102,7 +108,7 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
     p.raw_tps = (raw_tiles + rs - 1) / rs;
     p.raw_splits = (raw_tiles + p.raw_tps - 1) / p.raw_tps;
     const size_t B = a->batch, L = a->length, H = a->heads;
-    p.tc = a->heads == 32;
+    p.tc = a->heads == 32 && p.wl <= 320;
     if (p.tc) {
         // One launch, 128-key tiles, one CTA per SM: the latent CTAs leave
         // about one SM per sequence free, where the (short) raw CTAs start;
@@ -171,7 +177,7 @@ template <int WL, int MTL>
 int launch_decode_attention(const CUtensorMap& lk, const CUtensorMap& lv, const CUtensorMap& rk,
                             const CUtensorMap& rv, const AttnJob& jl, const AttnJob& jr, int row_blocks,
                             int n_latent, int n_raw, cudaStream_t stream) {
-    constexpr int smem = std::max(AttnCfg<WL, MTL>::SMEM, AttnCfg<128, 1>::SMEM);
+    constexpr int smem = std::max(AttnCfg<WL, MTL, kStageBudget, lat_tile_keys(WL)>::SMEM, AttnCfg<128, 1>::SMEM);
     auto kernel = decode_attention_kernel<WL, MTL>;
     static bool configured[64] = {};
     const int dev = device_info().device;
@@ -296,14 +302,17 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     if (!p.tc) {
         int bc = 0;
         const int64_t lat_stride[3] = {a->lat_stride_batch, a->lat_stride_row, a->lat_stride_row};
-        if ((rc = make_bshd_map(&lk, a->lat_k, a->batch, a->lat_capacity, 1, a->rank_k, lat_stride, &bc))) return rc;
-        if ((rc = make_bshd_map(&lv, a->lat_v, a->batch, a->lat_capacity, 1, a->rank_v, lat_stride, &bc))) return rc;
+        const int lt = lat_tile_keys(p.wl);
+        if ((rc = make_bshd_map(&lk, a->lat_k, a->batch, a->lat_capacity, 1, a->rank_k, lat_stride, &bc, lt)))
+            return rc;
+        if ((rc = make_bshd_map(&lv, a->lat_v, a->batch, a->lat_capacity, 1, a->rank_v, lat_stride, &bc, lt)))
+            return rc;
         const int64_t raw_stride[3] = {a->raw_stride_batch, a->raw_stride_token, a->head_dim};
         if ((rc = make_bshd_map(&rk, a->raw_k_rot, a->batch, a->raw_capacity, a->kv_heads, a->head_dim, raw_stride,
-                                &bc)))
+                                &bc, kTile)))
             return rc;
         if ((rc = make_bshd_map(&rv, a->raw_v, a->batch, a->raw_capacity, a->kv_heads, a->head_dim, raw_stride,
-                                &bc)))
+                                &bc, kTile)))
             return rc;
     }
     const float scale_log2 = a->scale * 1.4426950408889634f;
@@ -357,7 +366,8 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         case 128: rc = launch_wl<128>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
         case 192: rc = launch_wl<192>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
         case 256: rc = launch_wl<256>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
-        default: rc = launch_wl<320>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
+        case 320: rc = launch_wl<320>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
+        default: rc = launch_wl<512>(p.mtl, lk, lv, rk, rv, jl, jr, p.lat_row_blocks, n_latent, n_raw, stream); break;
     }
     if (rc) return rc;
     if (a->attn_event_end && cudaEventRecord(static_cast<cudaEvent_t>(a->attn_event_end), stream) != cudaSuccess)
@@ -385,7 +395,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         const int dev = device_info().device;
         if (dev >= 0 && dev < 64 && !configured[dev]) {
             if (cudaFuncSetAttribute(decode_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     int(merge_smem_bytes(320, 128))) != cudaSuccess)
+                                     int(merge_smem_bytes(512, 128))) != cudaSuccess)
                 return fail(SLIMKV_ERR_CUDA, "cudaFuncSetAttribute failed");
             configured[dev] = true;
         }

@@ -49,6 +49,16 @@ class LatentLlamaConfig:
     rope_scaling: dict = field(default_factory=lambda: dict(LLAMA3_SCALING))
     rope_positions: int = 131072
     rms_eps: float = 1e-5
+    qkv_bias: bool = False        # q/k/v (and Beacon q / up-projection) biases, as in Qwen2
+
+
+def qwen25_14b_r2():
+    """Qwen2.5-14B geometry (48 layers, hidden 5120, 40 / 8 heads, q/k/v bias,
+    RoPE theta 1e6 without scaling) with SlimKV r2 ranks (512 / 512) and t4
+    Beacons."""
+    return LatentLlamaConfig(vocab=152064, hidden=5120, intermediate=13824, layers=48, heads=40, kv_heads=8,
+                             head_dim=128, rank_k=512, rank_v=512, ratio=4, rope_theta=1e6, rope_scaling=None,
+                             rope_positions=262144, rms_eps=1e-6, qkv_bias=True)
 
 
 class RandomWeights:
@@ -60,8 +70,8 @@ class RandomWeights:
         H, I, kvd = cfg.hidden, cfg.intermediate, cfg.kv_heads * cfg.head_dim
         qd = cfg.heads * cfg.head_dim
 
-        def w(*shape):
-            return torch.randn(*shape, generator=gen, device=device, dtype=torch.bfloat16).mul_(std)
+        def w(*shape, scale=std):
+            return torch.randn(*shape, generator=gen, device=device, dtype=torch.bfloat16).mul_(scale)
 
         self.embed = w(cfg.vocab, H)
         self.beacon_embed = w(1, H)
@@ -79,6 +89,13 @@ class RandomWeights:
                 uv=w(kvd, cfg.rank_v),                           # beacon_v_up_proj.weight
                 w_gate_up=w(2 * I, H),
                 w_down=w(H, I)))
+            if cfg.qkv_bias:
+                # Biases of q/k/v_proj and beacon_q_proj (the K/V down-projections
+                # have none) and of the up-projections (present with k/v bias).
+                zeros = torch.zeros(cfg.rank_k + cfg.rank_v, device=device, dtype=torch.bfloat16)
+                self.layers[-1].update(b_raw=w(qd + 2 * kvd, scale=0.1),
+                                       b_beacon=torch.cat([w(qd, scale=0.1), zeros]),
+                                       uk_bias=w(kvd, scale=0.1), uv_bias=w(kvd, scale=0.1))
 
     def nbytes(self):
         total = sum(t.numel() * 2 for t in (self.embed, self.beacon_embed, self.lm_head))
@@ -188,6 +205,7 @@ class LatentDecodeRuntime:
                 lat_k=c.get('lat_k'), lat_v=c.get('lat_v'), lat_pages=pages, raw_len=self.raw_len,
                 latent_len=self.latent_len,
                 query_len=self.query_len, qpos=self.qpos, uk=layer['uk'], uv=layer['uv'],
+                uk_bias=layer.get('uk_bias'), uv_bias=layer.get('uv_bias'),
                 cos=self.cos, sin=self.sin, out=self.attn,
                 new_k=z[:, 0, qd:qd + kvd], new_v=z[:, 0, qd + kvd:qd + 2 * kvd],
                 new_lat_k=z[:, 1, qd:qd + cfg.rank_k], new_lat_v=z[:, 1, qd + cfg.rank_k:qd + cfg.rank_k + cfg.rank_v],
@@ -209,8 +227,12 @@ class LatentDecodeRuntime:
         x[:, 1].copy_(w.beacon_embed.expand(B, -1))
         for layer, call in zip(w.layers, self.calls):
             h = F.rms_norm(x, (H,), layer['norm1'], cfg.rms_eps)
-            torch.mm(h[:, 0], layer['w_raw'].t(), out=self.z[:, 0])
-            torch.mm(h[:, 1], layer['w_beacon'].t(), out=self.z[:, 1, :nb])
+            if cfg.qkv_bias:
+                torch.addmm(layer['b_raw'], h[:, 0], layer['w_raw'].t(), out=self.z[:, 0])
+                torch.addmm(layer['b_beacon'], h[:, 1], layer['w_beacon'].t(), out=self.z[:, 1, :nb])
+            else:
+                torch.mm(h[:, 0], layer['w_raw'].t(), out=self.z[:, 0])
+                torch.mm(h[:, 1], layer['w_beacon'].t(), out=self.z[:, 1, :nb])
             call()
             x.add_((self.attn.view(2 * B, qd) @ layer['w_o'].t()).view(B, 2, H))
             h2 = F.rms_norm(x, (H,), layer['norm2'], cfg.rms_eps)

@@ -178,6 +178,19 @@ def test_fused_decode_matches_oracle(length, history, tail, rank, bias, ragged):
     check(c, query_len, run_fused(c, query_len, fp32=True))
 
 
+@pytest.mark.parametrize('length,heads,rank,ragged', [
+    (1, 40, 512, True), (2, 40, 512, False), (2, 32, 384, True), (1, 40, 320, False), (2, 40, 160, True)])
+def test_qwen_geometry_and_wide_latents(length, heads, rank, ragged):
+    """40 query heads over 8 KV heads (Qwen2.5-14B) and latent ranks up to 512
+    (r2), with up-projection biases: the split-KV route with 32-key tiles for
+    ranks above 320."""
+    c = decode_case(500 + rank + length, batch=3, length=length, history=700, tail=300, heads=heads, kv_heads=8,
+                    rk=rank, rv=rank, bias=True, ragged=ragged)
+    query_len = np.full(3, length)
+    check(c, query_len, run_fused(c, query_len))
+    check(c, query_len, run_fused(c, query_len, fp32=True))
+
+
 @pytest.mark.parametrize('paged', [False, True])
 def test_large_ragged_batch_splits_every_sequence_by_its_length(paged):
     """More sequences than SMs / 3 with latent lengths from 1 to ~4.6k rows:

@@ -42,3 +42,26 @@ def test_paged_runtime_matches_dense_runtime():
         inserted += int((paged.query_len == 2).sum())
         tokens = ld.argmax(-1)
     assert inserted >= 2                                # Beacon rows went into pages on some steps
+
+
+@pytest.mark.gpu
+def test_qwen_geometry_runtime_steps():
+    """Qwen2.5-14B geometry (40 / 8 heads, q/k/v and up-projection biases,
+    r2 ranks 512) through whole runtime steps on the split-KV route."""
+    from slimkv_b200.runtime import LatentDecodeRuntime, RandomWeights, qwen25_14b_r2
+    from slimkv_b200 import _lib
+    dev = torch.device('cuda', 0)
+    cfg = qwen25_14b_r2()
+    cfg.layers, cfg.vocab, cfg.hidden, cfg.intermediate = 2, 512, 1024, 2048
+    w = RandomWeights(cfg, dev, seed=5)
+    per_window = cfg.window // cfg.ratio
+    rt = LatentDecodeRuntime(cfg, w, [per_window * 5, per_window * 2], [3, 700], dev, raw_pre=False)
+    _lib.device_status(clear=True)
+    tokens = torch.tensor([11, 400], device=dev)
+    for _ in range(5):                                  # the first row inserts a Beacon at step 1
+        rt.tokens.copy_(tokens)
+        logits = rt.step_eager()
+        torch.cuda.synchronize()
+        assert torch.isfinite(logits).all()
+        tokens = logits.argmax(-1)
+    assert _lib.device_status(clear=True) == 0
