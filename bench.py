@@ -56,6 +56,9 @@ def parse():
     p.add_argument('--config', type=int, default=2, choices=[2, 3, 5],
                    help='2 (default): the metric\'s config; 3: batched paged decode, r8, B=256, ragged contexts; '
                         '5: Qwen2.5-14B geometry, r2, 131072-token contexts, 32 sequences per GPU')
+    p.add_argument('--seq-split', action='store_true',
+                   help='with --config 5: the batch-1 524288-token sequence, its latents split over the N ranks '
+                        '(cross-GPU LSE merge over NCCL every layer)')
     p.add_argument('--kernel-only', action='store_true',
                    help='one layer of the same workload: time the attention kernel alone (profiling runs)')
     return p.parse_args()
@@ -88,6 +91,22 @@ def config5(n):
             'beacon_latents': 32768, 'latent_rank': '512/512', 'heads': '40 / 8 KV', 'sinks': 4, 'layers': 48,
             'parallelism': f'dp{n} (independent replicas; 64 sequences = 2 GPUs)',
             'l2': 'each step reads ~140 GB (weights + caches) >> 126 MB L2; no flush needed'}
+
+
+C5S_CONTEXT = 524288
+C5S_METRIC = 'decode tokens/s of one 524288-token sequence split over N GPUs (cross-GPU LSE merge), ' \
+             'Qwen2.5-14B-r2 t4 latent path'
+
+
+def config5s(n, tail):
+    return {'workload': 'Qwen2.5-14B geometry r2 t4 decode step of one 524288-token sequence (BASELINE config 5, '
+                        'batch-1 run), latents sequence-split over the GPUs',
+            'global_batch': 1, 'context': f'{C5S_CONTEXT} + raw tail {tail}', 'beacon_latents': C5S_CONTEXT // 4,
+            'latent_rank': '512/512', 'heads': '40 / 8 KV', 'sinks': 4, 'layers': 48,
+            'parallelism': f'sequence split over {n} GPU(s): contiguous 64-row latent shards, raw tail and new '
+                           'Beacons on the last rank, one NCCL all-gather of fp32 partials + N-part LSE merge per '
+                           'layer; projections / MLP replicated' if n > 1 else 'one GPU, no split',
+            'l2': 'each step reads ~43 GB (weights + latents) >> 126 MB L2; no flush needed'}
 
 
 def config(n):
@@ -372,8 +391,20 @@ def main():
         dist.init_process_group('nccl', timeout=timedelta(seconds=300))
     torch.cuda.set_device(local)
     device = torch.device('cuda', local)
-    rng = np.random.default_rng(1234 + rank)
-    if args.config == 3:
+    # A sequence split decodes one sequence on every rank: same inputs everywhere.
+    split = args.seq_split and args.config == 5
+    rng = np.random.default_rng(1234 if split else 1234 + rank)
+    if split:
+        from slimkv_b200.runtime import qwen25_14b_r2
+        cfg = qwen25_14b_r2()
+        weights = RandomWeights(cfg, device, seed=0)
+        batch = 1
+        tails = rng.integers(0, cfg.window, size=batch)
+        history = [C5S_CONTEXT // cfg.window * (cfg.window // cfg.ratio)]
+        rt = LatentDecodeRuntime(cfg, weights, history, tails, device, extra_windows=1, raw_pre=False,
+                                 seq_split=True if world > 1 else None)
+        metric, workload = C5S_METRIC, config5s(world, int(tails[0]))
+    elif args.config == 3:
         # Config 3: r8 ranks, one Beacon per 8 raw tokens, contexts U[2048, 131072].
         cfg = LatentLlamaConfig(rank_k=160, rank_v=160, ratio=8)
         weights = RandomWeights(cfg, device, seed=0)
@@ -429,7 +460,8 @@ def main():
     clock_info = clocks.stop()
     barrier()
     ms = max_over_ranks(start.elapsed_time(end) / args.steps)
-    value = world * batch / (ms / 1000.0)
+    jobs = 1 if split else world                 # a split decodes the same sequence on every rank
+    value = jobs * batch / (ms / 1000.0)
 
     # ---- end to end through the runtime API: host tokens in, host tokens out -
     host_in = torch.from_numpy(rng.integers(0, cfg.vocab, size=batch)).pin_memory()
@@ -449,12 +481,28 @@ def main():
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
 
+    merge_us = None
+    if rt.merges:
+        # The cross-GPU exchange alone: all-gather of the fp32 partials + the
+        # N-part merge kernel, cycling through the layers' buffers.
+        barrier()
+        torch.cuda.synchronize()
+        m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        m0.record()
+        for i in range(cfg.layers * 4):
+            rt.merges[i % cfg.layers]()
+        m1.record()
+        torch.cuda.synchronize()
+        merge_us = max_over_ranks(m0.elapsed_time(m1) / (cfg.layers * 4)) * 1000.0
+
     # ---- roofline of the dominant kernel: the attention launch (latent + raw
     # branches) timed alone with CUDA events on its stream; the whole fused
     # step per layer (prologue + attention + merge) is reported beside it.
     reps = max(args.steps, 8) * 4
     kernel_bytes = rt.attention_kernel_bytes()
     attn_ms = attention_kernel_time(rt, reps)
+    if split:
+        attn_ms = max_over_ranks(attn_ms)
     achieved = kernel_bytes / (attn_ms / 1000.0) / 1e9
     torch.cuda.synchronize()
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -478,10 +526,11 @@ def main():
 
     result = {
         'metric': metric, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
-        'warmup': max(args.warmup, 3), 'ms_per_step': ms, 'higher_is_better': True, 'scaling': 'weak',
+        'warmup': max(args.warmup, 3), 'ms_per_step': ms, 'higher_is_better': True,
+        'scaling': 'strong' if split else 'weak',
         'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (random N(0,0.02) weights, synthetic cache)',
         'config': workload,
-        'e2e': {'value': world * batch / (e2e_ms / 1000.0), 'unit': UNIT, 'h2d_bytes_per_step': batch * 8,
+        'e2e': {'value': jobs * batch / (e2e_ms / 1000.0), 'unit': UNIT, 'h2d_bytes_per_step': batch * 8,
                 'd2h_bytes_per_step': batch * 8, 'ms_per_step': e2e_ms},
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
                      'peak_source': f'{peak_kind} (MEASURED_PEAKS.json hbm_gbs)' if peak_kind == 'measured'
@@ -490,11 +539,17 @@ def main():
                      ' (latent + raw branches, one launch per layer)', 'bytes_per_launch': kernel_bytes, 'us_per_launch': attn_ms * 1000.0,
                      'fused_step_per_layer': {'us': layer_ms * 1000.0, 'bytes': layer_bytes,
                                               'gbs': layer_bytes / (layer_ms / 1000.0) / 1e9}},
-        'gpu_launches': args.steps * (1 + 3 * cfg.layers),
+        'gpu_launches': args.steps * (1 + (4 if rt.merges else 3) * cfg.layers),
         'clocks': clock_info, 'device_status': status,
     }
     if prefill is not None:
         result['prefill'] = prefill
+    if split:
+        result['sequence_split'] = {
+            'ranks': world, 'latent_rows_this_rank': int(rt.call_latent_len.sum().item()),
+            'attention_us_per_layer_max_over_ranks': attn_ms * 1000.0,
+            'merge_us_per_layer_max_over_ranks': merge_us,
+            'exchange_bytes_per_rank_per_layer': rt.merges[0].send.numel() * 4 if rt.merges else 0}
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == 2:
         result['cpu_baseline'] = cpu_baseline(BATCH)
     if rank == 0:

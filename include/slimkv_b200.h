@@ -208,6 +208,16 @@ typedef struct {
     const int32_t* lat_table;
     int64_t lat_table_stride;
     int lat_num_pages;
+    /* Sequence split (optional): partial results of shards of one sequence's
+     * keys, merged across GPUs afterwards with the LSE merge of
+     * fa2_decode.py:57-66 taken over N parts.  out_lse (NULL = not written):
+     * fp32 [B][L][H], the natural-log sum of exp of each output row's scores
+     * over this call's keys (latent, with the K-bias shift, and raw); -inf for
+     * a row that sees no key.  latent_shard != 0: this call's latent cache is
+     * a shard that does not hold this step's Beacon row, so the latent branch
+     * is not causal (new_lat_k / new_lat_v must be NULL). */
+    float* out_lse;
+    int latent_shard;
 } slimkv_latent_decode_args;
 
 SLIMKV_API size_t slimkv_latent_decode_workspace_size(const slimkv_latent_decode_args* args);
@@ -430,6 +440,33 @@ SLIMKV_API int slimkv_prefill_rope(const void* q, const int64_t q_stride[3], con
                                    int kv_heads, int queries, int keys, int head_dim, void* q_out,
                                    const int64_t q_out_stride[3], void* k_out, const int64_t k_out_stride[3],
                                    void* stream);
+
+/* ------------------------------------------------------------------------
+ * N-part LSE merge of partial attention — the cross-GPU step of a sequence
+ * split: merge_attention (slimkv/llama3/fa2_decode.py:57-66), which merges two
+ * partitions of one row's keys, generalised to N partitions:
+ *   T = log sum_i exp(lse_i),  out = sum_i exp(lse_i - T) part_i.
+ * part_out: fp32, part i of row r at part_out + i*part_stride + r*dim;
+ * part_lse: fp32, lse of part i of row r at part_lse + i*lse_part_stride + r
+ * (natural log, -inf for a part without keys).  The layout matches one
+ * all-gather of per-rank [rows*dim outputs | rows lses] buffers.  out
+ * [rows][dim] bf16, or fp32 when out_fp32; out_lse [rows] fp32 (nullable).
+ * Rows without keys in any part get zero output and lse -inf.  dim a multiple
+ * of 4, part_stride a multiple of 4, 16-byte aligned part_out (and out when
+ * fp32; 8-byte when bf16).
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    int parts, rows, dim;
+    const float* part_out;
+    int64_t part_stride;
+    const float* part_lse;
+    int64_t lse_part_stride;
+    void* out;
+    int out_fp32;
+    float* out_lse;
+} slimkv_merge_partials_args;
+
+SLIMKV_API int slimkv_merge_partials(const slimkv_merge_partials_args* args, void* stream);
 
 #ifdef __cplusplus
 }

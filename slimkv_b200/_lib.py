@@ -62,6 +62,7 @@ class LatentDecodeArgs(ctypes.Structure):
         ('lat_pages', ctypes.c_void_p), ('lat_page_stride', ctypes.c_int64), ('lat_slots', ctypes.c_int),
         ('lat_sink_elements', ctypes.c_int), ('lat_table', ctypes.c_void_p), ('lat_table_stride', ctypes.c_int64),
         ('lat_num_pages', ctypes.c_int),
+        ('out_lse', ctypes.c_void_p), ('latent_shard', ctypes.c_int),
     ]
 
 
@@ -114,6 +115,14 @@ class WindowProjectArgs(ctypes.Structure):
     ]
 
 
+class MergePartialsArgs(ctypes.Structure):
+    """Mirror of ``slimkv_merge_partials_args``."""
+    _fields_ = [
+        ('parts', _I), ('rows', _I), ('dim', _I), ('part_out', _P), ('part_stride', _L),
+        ('part_lse', _P), ('lse_part_stride', _L), ('out', _P), ('out_fp32', _I), ('out_lse', _P),
+    ]
+
+
 _PL = ctypes.POINTER(ctypes.c_int64)
 
 SIGNATURES = {
@@ -140,6 +149,7 @@ SIGNATURES = {
     'slimkv_merge': (_I, [_P, ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _P,
                           ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I,
                           _I, _P, _P]),
+    'slimkv_merge_partials': (_I, [ctypes.POINTER(MergePartialsArgs), _P]),
 }
 
 _lib = None

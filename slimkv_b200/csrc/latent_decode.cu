@@ -100,9 +100,9 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
     int ls = a->latent_splits > 0 ? a->latent_splits
                                   : int(std::ceil(lat_tiles * lat_tile_bytes / std::max(per_cta, 1.0)));
     int rs = a->raw_splits > 0 ? a->raw_splits : int(std::ceil(raw_tiles * raw_tile_bytes / std::max(per_cta, 1.0)));
-    // The merge kernel combines at most 32 splits per branch.
-    ls = std::max(1, std::min({ls, lat_tiles, 32}));
-    rs = std::max(1, std::min({rs, raw_tiles, 32}));
+    // The merge kernel combines at most kMergeMaxSplits splits per branch.
+    ls = std::max(1, std::min({ls, lat_tiles, kMergeMaxSplits}));
+    rs = std::max(1, std::min({rs, raw_tiles, kMergeMaxSplits}));
     p.lat_tps = (lat_tiles + ls - 1) / ls;
     p.lat_splits = (lat_tiles + p.lat_tps - 1) / p.lat_tps;
     p.raw_tps = (raw_tiles + rs - 1) / rs;
@@ -223,6 +223,8 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         return fail(SLIMKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
     if ((a->new_k == nullptr) != (a->new_v == nullptr) || (a->new_lat_k == nullptr) != (a->new_lat_v == nullptr))
         return fail(SLIMKV_ERR_INVALID_ARGUMENT, "new K/V (and new latent K/V) must be given together");
+    if (a->latent_shard && a->new_lat_k)
+        return fail(SLIMKV_ERR_INVALID_ARGUMENT, "a latent shard without this step's Beacon takes no new latents");
     if (a->raw_stride_token % 8 || a->raw_stride_batch % 8 || !aligned16(a->raw_k_rot) || !aligned16(a->raw_v) ||
         !aligned16(a->uv) ||
         (!paged && (a->lat_stride_row % 8 || a->lat_stride_batch % 8 || !aligned16(a->lat_k) || !aligned16(a->lat_v))))
@@ -319,7 +321,8 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     AttnJob jl{};
     jl.q = w.q_lat; jl.q_fp16 = 1; jl.q_sb = (int64_t)a->length * a->heads * p.wl; jl.q_sl = (int64_t)a->heads * p.wl; jl.q_sh = p.wl;
     jl.seqlens = a->latent_len; jl.keys = a->lat_capacity; jl.qlens = a->query_len; jl.queries = a->length;
-    jl.group = a->heads; jl.kv_heads = 1; jl.dk = a->rank_k; jl.scale_log2 = scale_log2; jl.causal = 1;
+    jl.group = a->heads; jl.kv_heads = 1; jl.dk = a->rank_k; jl.scale_log2 = scale_log2;
+    jl.causal = a->latent_shard ? 0 : 1;
     jl.splits = p.lat_splits; jl.tiles_per_split = p.lat_tps; jl.rows_alloc = p.lat_rows; jl.out_width = p.wl;
     jl.part_o = w.lat_o; jl.part_lse = w.lat_lse; jl.status = status;
     AttnJob jr{};
@@ -339,7 +342,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         L.k = a->lat_k; L.v = a->lat_v; L.dim_k = a->rank_k; L.dim_v = a->rank_v;
         L.kv_heads = 1; L.capacity = a->lat_capacity;
         L.stride_batch = a->lat_stride_batch; L.stride_row = a->lat_stride_row; L.stride_head = 0;
-        L.q = w.q_lat; L.q_rows = 0; L.heads = a->heads; L.group = a->heads; L.causal = 1;
+        L.q = w.q_lat; L.q_rows = 0; L.heads = a->heads; L.group = a->heads; L.causal = a->latent_shard ? 0 : 1;
         L.seqlens = a->latent_len; L.splits = p.lat_splits; L.rows_alloc = p.lat_rows; L.width = p.wl;
         L.part_o = w.lat_o; L.part_lse = w.lat_lse;
         L.pages = a->lat_pages; L.page_stride = a->lat_page_stride; L.slots = a->lat_slots;
@@ -389,6 +392,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     ma.kv_heads = a->kv_heads; ma.dim = a->head_dim; ma.rank_v = a->rank_v; ma.rank_v_pad = p.rvp;
     ma.group = p.group; ma.seq_per_cta = 1; ma.scale = a->scale;
     ma.out = a->out; ma.out_fp32 = a->out_fp32; ma.o_sb = a->out_stride[0]; ma.o_sl = a->out_stride[1];
+    ma.out_lse = a->out_lse;
     const size_t msmem = merge_smem_bytes(p.rvp, a->head_dim);
     {
         static bool configured[64] = {};

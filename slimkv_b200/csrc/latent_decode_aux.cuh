@@ -288,13 +288,17 @@ struct MergeArgs {
     int batch, length, heads, kv_heads, dim, rank_v, rank_v_pad, group, seq_per_cta;
     float scale;
     void* out; int out_fp32; int64_t o_sb, o_sl;
+    float* out_lse;                // [B][L][H] merged LSE (nullable)
 };
+
+// Splits per branch that decode_merge_kernel combines (4 per lane).
+constexpr int kMergeMaxSplits = 128;
 
 // Dynamic shared memory of decode_merge_kernel for a padded value rank:
 // U_v[g] bf16 [128 x rvp], o_lat hi and lo bf16 [16 x rvp] each, raw rows
-// fp32 [16 x dim], LSEs [2][16], split weights [2][16][32].
+// fp32 [16 x dim], LSEs [2][16], split weights [2][16][kMergeMaxSplits].
 __host__ __device__ constexpr size_t merge_smem_bytes(int rank_v_pad, int dim) {
-    return 1024 + size_t(128 + 32) * rank_v_pad * 2 + size_t(16) * dim * 4 + 32 * 4 + 2 * 16 * 32 * 4;
+    return 1024 + size_t(128 + 32) * rank_v_pad * 2 + size_t(16) * dim * 4 + 32 * 4 + 2 * 16 * kMergeMaxSplits * 4;
 }
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
@@ -315,9 +319,10 @@ __device__ __forceinline__ int lat_splits_row(const MergeArgs& a, int b) {
 // (seq_per_cta sequences x L x group) of KV head g.
 //   1. U_v[g] -> shared with asynchronous copies (bf16 as stored, the MMA's
 //      column-major B operand), overlapping steps 2-3.
-//   2. One warp per row: lane s holds split s's LSE of each branch and turns
-//      it into a normalised weight (splits <= 32); the row's LSEs (latent one
-//      shifted by scale * q . b_k) go to shared memory.
+//   2. One warp per row: lane s holds the LSEs of splits s, s+32, s+64 and
+//      s+96 of each branch and turns them into normalised weights (splits <=
+//      kMergeMaxSplits); the row's LSEs (latent one shifted by scale * q .
+//      b_k) go to shared memory.
 //   3. All threads: weighted split sums over (row, 4-column) items of the
 //      valid rows, every split's load independent of the others; the latent
 //      rows are kept as a bf16 pair hi + lo (fp32-level accuracy through the
@@ -333,7 +338,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
     uint8_t* s_lo = s_hi + 16 * rvp * 2;                // o_lat lo
     float* s_raw = reinterpret_cast<float*>(s_lo + 16 * rvp * 2);   // [16][D]
     float* s_lse = s_raw + 16 * a.dim;                  // [2][16]: latent, raw
-    float* s_w = s_lse + 32;                            // [2][16][32] split weights: latent, raw
+    float* s_w = s_lse + 32;                            // [2][16][kMergeMaxSplits] split weights: latent, raw
     const int g = blockIdx.x, bb = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rps = a.length * a.group, b0 = bb * a.seq_per_cta;
@@ -368,18 +373,31 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
         float lse_br[2];
 #pragma unroll
         for (int br = 0; br < 2; ++br) {
-            float my = -INFINITY;
-            if (valid && lane < (br ? a.raw_splits : lat_splits_row(a, b)))
-                my = br ? __ldg(a.raw_lse + (((int64_t)b * a.kv_heads + g) * a.raw_splits + lane) * a.raw_rows + rr)
-                        : __ldg(a.lat_lse + ((int64_t)b * a.lat_splits + lane) * a.lat_rows + l * a.heads + h);
-            float m = my;
+            const int nsp = valid ? (br ? a.raw_splits : lat_splits_row(a, b)) : 0;
+            float my[kMergeMaxSplits / 32];
+            float m = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < kMergeMaxSplits / 32; ++k) {
+                const int sp = lane + 32 * k;
+                my[k] = -INFINITY;
+                if (sp < nsp)
+                    my[k] = br ? __ldg(a.raw_lse + (((int64_t)b * a.kv_heads + g) * a.raw_splits + sp) * a.raw_rows + rr)
+                               : __ldg(a.lat_lse + ((int64_t)b * a.lat_splits + sp) * a.lat_rows + l * a.heads + h);
+                m = fmaxf(m, my[k]);
+            }
 #pragma unroll
             for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-            const float w = (m == -INFINITY || my == -INFINITY) ? 0.f : expf(my - m);
-            float total = w;
+            float total = 0.f;
+#pragma unroll
+            for (int k = 0; k < kMergeMaxSplits / 32; ++k) {
+                my[k] = (m == -INFINITY || my[k] == -INFINITY) ? 0.f : expf(my[k] - m);
+                total += my[k];
+            }
 #pragma unroll
             for (int off = 16; off; off >>= 1) total += __shfl_xor_sync(0xffffffffu, total, off);
-            s_w[(br * 16 + r) * 32 + lane] = total > 0.f ? w / total : 0.f;
+#pragma unroll
+            for (int k = 0; k < kMergeMaxSplits / 32; ++k)
+                s_w[(br * 16 + r) * kMergeMaxSplits + lane + 32 * k] = total > 0.f ? my[k] / total : 0.f;
             lse_br[br] = total > 0.f ? m + logf(total) : -INFINITY;
         }
         if (valid && a.uk_bias && lse_br[0] != -INFINITY) {
@@ -408,7 +426,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
             if (!row_info(r, b, l, h, rr) || c >= a.lat_width) continue;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             const float* src = a.lat_o + ((int64_t)b * a.lat_splits * a.lat_rows + l * a.heads + h) * a.lat_width + c;
-            const float* w = s_w + r * 32;
+            const float* w = s_w + r * kMergeMaxSplits;
             const int nsp = lat_splits_row(a, b);
             int s = 0;
             for (; s + 8 <= nsp; s += 8) {
@@ -443,7 +461,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             if (row_info(r, b, l, h, rr)) {
                 const float* src = a.raw_o + ((((int64_t)b * a.kv_heads + g) * a.raw_splits) * a.raw_rows + rr) * a.dim + c;
-                const float* w = s_w + (16 + r) * 32;
+                const float* w = s_w + (16 + r) * kMergeMaxSplits;
                 int s = 0;
                 for (; s + 8 <= a.raw_splits; s += 8) {
                     float4 x[8];
@@ -494,12 +512,13 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
         int b, l, h, rr;
         if (!row_info(r, b, l, h, rr)) continue;
         const float ll = s_lse[r], lr = s_lse[16 + r];
-        float wr = 0.f, wl = 0.f;
+        float wr = 0.f, wl = 0.f, total = -INFINITY;
         if (!(ll == -INFINITY && lr == -INFINITY)) {
-            const float total = fmaxf(lr, ll) + log1pf(expf(-fabsf(lr - ll)));
+            total = fmaxf(lr, ll) + log1pf(expf(-fabsf(lr - ll)));
             wr = lr == -INFINITY ? 0.f : expf(lr - total);
             wl = ll == -INFINITY ? 0.f : expf(ll - total);
         }
+        if (a.out_lse && warp == 0 && (lane & 3) == 0) a.out_lse[((int64_t)b * a.length + l) * a.heads + h] = total;
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll

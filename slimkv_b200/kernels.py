@@ -166,11 +166,17 @@ class LatentDecodeCall:
     def __init__(self, *, q, raw_k_rot, raw_v, lat_k=None, lat_v=None, raw_len, latent_len, qpos, uk, uv, cos, sin,
                  out, query_len=None, raw_k_pre=None, new_k=None, new_v=None, new_lat_k=None, new_lat_v=None,
                  uk_bias=None, uv_bias=None, scale=None, latent_len_max=0, raw_len_max=0, latent_splits=0,
-                 raw_splits=0, lat_pages=None):
+                 raw_splits=0, lat_pages=None, out_lse=None, latent_shard=False):
         """``lat_pages = (pages, layout, tables)`` replaces ``lat_k / lat_v``
         with the vLLM plugin's Beacon pages: ``pages [num_pages, >=
         layout.page_elements]`` bf16 (a ``pages.BeaconPageLayout`` layout) and
-        ``tables [B, pages_per_seq]`` int32 block tables on the device."""
+        ``tables [B, pages_per_seq]`` int32 block tables on the device.
+
+        Sequence split: ``out_lse`` (fp32 ``[B, L, H]``, contiguous) receives
+        each output row's log-sum-exp over this call's keys, so that shards of
+        one sequence can be merged (:func:`merge_partials`);
+        ``latent_shard=True`` marks a latent cache that does not hold this
+        step's Beacon row (no causal latent mask, no ``new_lat_*``)."""
         paged = lat_pages is not None
         _require(paged or (lat_k is not None and lat_v is not None), 'lat_k / lat_v or lat_pages required')
         _bf16_cuda(q, raw_k_rot, raw_v, uk, uv, *(() if paged else (lat_k, lat_v)))
@@ -241,10 +247,15 @@ class LatentDecodeCall:
         a.out_fp32 = int(out.dtype == torch.float32)
         a.latent_len_max, a.raw_len_max = int(latent_len_max), int(raw_len_max)
         a.latent_splits, a.raw_splits = int(latent_splits), int(raw_splits)
+        if out_lse is not None:
+            _require(out_lse.is_cuda and out_lse.dtype == torch.float32 and out_lse.is_contiguous() and
+                     out_lse.shape == (batch, length, heads), 'out_lse must be contiguous fp32 [B, L, H]')
+        a.out_lse = 0 if out_lse is None else out_lse.data_ptr()
+        a.latent_shard = int(bool(latent_shard))
         self.args = a
         self.device = q.device
         self._keep = (q, raw_k_rot, raw_v, raw_k_pre, lat_k, lat_v, lat_pages, raw_len, latent_len, query_len, qpos,
-                      new_k, new_v, new_lat_k, new_lat_v, uk, uv, uk_bias, uv_bias, cos, sin, out)
+                      new_k, new_v, new_lat_k, new_lat_v, uk, uv, uk_bias, uv_bias, cos, sin, out_lse, out)
         lib = _lib.load()
         size = lib.slimkv_latent_decode_workspace_size(ctypes.byref(a))
         if size == 0:
@@ -273,6 +284,29 @@ class LatentDecodeCall:
 def latent_decode(**kwargs):
     """One fused decode-attention step (see :class:`LatentDecodeCall`)."""
     return LatentDecodeCall(**kwargs)()
+
+
+def merge_partials(part_out, part_lse, out, out_lse=None):
+    """N-part LSE merge (``slimkv_merge_partials``): ``part_out [N, rows,
+    dim]`` fp32 and ``part_lse [N, rows]`` fp32 (any part strides; rows and
+    dim contiguous) into ``out [rows, dim]`` (bf16 or fp32, contiguous) and
+    optionally ``out_lse [rows]``."""
+    _require(part_out.is_cuda and part_out.dtype == torch.float32 and part_lse.dtype == torch.float32,
+             'fp32 CUDA partials')
+    parts, rows, dim = part_out.shape
+    _require(part_out.stride(2) == 1 and part_out.stride(1) == dim and part_lse.shape == (parts, rows) and
+             part_lse.stride(1) == 1, 'partials must be [N, rows, dim] / [N, rows] with contiguous rows')
+    _require(out.is_contiguous() and out.numel() == rows * dim and out.dtype in (torch.bfloat16, torch.float32),
+             'out must be contiguous [rows, dim] bf16 or fp32')
+    if out_lse is not None:
+        _require(out_lse.is_contiguous() and out_lse.numel() == rows and out_lse.dtype == torch.float32,
+                 'out_lse must be contiguous fp32 [rows]')
+    a = _lib.MergePartialsArgs(parts, rows, dim, part_out.data_ptr(), part_out.stride(0), part_lse.data_ptr(),
+                               part_lse.stride(0), out.data_ptr(), int(out.dtype == torch.float32),
+                               0 if out_lse is None else out_lse.data_ptr())
+    with torch.cuda.device(out.device):
+        _lib.check(_lib.load().slimkv_merge_partials(ctypes.byref(a), _stream()))
+    return out
 
 
 def decode_schedule(history, tail, raw_len, latent_len, query_len, qpos, sink, window, ratio):

@@ -13,6 +13,14 @@ Two ways the path scales:
   parts: ``T = logsumexp_r(lse_r)``, ``out = sum_r exp(lse_r - T) out_r``.
   The exchange is one all-gather of the LSEs (B*H*L floats) and one all-reduce
   of the weighted outputs, over NCCL (NVLink) on GPUs or gloo on CPU.
+
+On GPUs the decode runtime uses :class:`SequenceSplitMerge`: the fused decode
+of each rank writes its fp32 partial output and LSE straight into one packed
+buffer, a single NCCL all-gather moves those buffers (the partials after the
+V up-projection: ``B*L*H*(D+1)`` floats a rank, 20 KB a layer for one
+Qwen2.5-14B sequence), and ``slimkv_merge_partials`` combines the N parts on
+every rank.  The merge after the up-projection is exact because the
+up-projection and its bias are linear and the merge weights sum to 1.
 """
 import torch
 import torch.distributed as dist
@@ -55,6 +63,41 @@ def merge_sequence_split(out, lse, group=None):
     merged = (out * weight.unsqueeze(-1)).contiguous()
     dist.all_reduce(merged, op=dist.ReduceOp.SUM, group=group)
     return merged, total
+
+
+class SequenceSplitMerge:
+    """One layer's cross-GPU exchange of a sequence split (graph-capturable).
+
+    ``out`` (fp32 ``[B, L, H*D]``) and ``lse`` (fp32 ``[B, L, H]``) are views
+    of this rank's packed send buffer, handed to the fused decode as its
+    ``out`` / ``out_lse``; :meth:`__call__` all-gathers the packed buffers and
+    merges them into ``merged`` (``[B, L, H*D]``, ``out_dtype``) with
+    ``slimkv_merge_partials``.  Rows that no rank writes (unused Beacon
+    slots) keep LSE ``-inf`` and merge to zeros.
+    """
+
+    def __init__(self, batch, length, heads, head_dim, group=None, device=None, out_dtype=torch.bfloat16,
+                 merged=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        rows = batch * length * heads
+        self.rows, self.dim = rows, head_dim
+        self.lse_at = rows * head_dim
+        width = self.lse_at + (rows + 3) // 4 * 4                    # float4-aligned part stride
+        self.send = torch.zeros(width, dtype=torch.float32, device=device)
+        self.send[self.lse_at:].fill_(float('-inf'))
+        self.gather = torch.empty(self.world, width, dtype=torch.float32, device=device)
+        self.out = self.send[:self.lse_at].view(batch, length, heads * head_dim)
+        self.lse = self.send[self.lse_at:self.lse_at + rows].view(batch, length, heads)
+        self.merged = merged if merged is not None else torch.empty(batch, length, heads * head_dim,
+                                                                    dtype=out_dtype, device=device)
+
+    def __call__(self):
+        from . import kernels
+        dist.all_gather_into_tensor(self.gather, self.send, group=self.group)
+        kernels.merge_partials(self.gather[:, :self.lse_at].view(self.world, self.rows, self.dim),
+                               self.gather[:, self.lse_at:self.lse_at + self.rows], self.merged)
+        return self.merged
 
 
 def max_over_ranks(value, device=None, group=None):

@@ -111,14 +111,26 @@ class LatentDecodeRuntime:
     """
 
     def __init__(self, cfg, weights, history, tails, device, extra_windows=1, seed=1, fill_std=1.3, paged=False,
-                 raw_pre=True, latent_splits=0, raw_splits=0):
+                 raw_pre=True, latent_splits=0, raw_splits=0, seq_split=None):
         """``paged`` keeps each layer's latent cache in the vLLM plugin's Beacon
         pages (page size of a 16-token raw page, ``create_page_layers``,
         slimkv/vllm_plugin/backend.py:108-131), each sequence owning the pages
         its own length needs, in shuffled order; ``raw_pre=False`` drops the
         pre-RoPE copy of the raw keys (only the append writes it);
         ``latent_splits`` / ``raw_splits`` override the attention split plan
-        (0: the library's choice)."""
+        (0: the library's choice).
+
+        ``seq_split`` (a ``torch.distributed`` process group, or ``True`` for
+        the default group) splits every sequence's completed-window latents
+        over the group's ranks in contiguous 64-row shards
+        (``parallel.shard_range``): rank ``r`` holds rows ``[start_r,
+        end_r)``; the last rank also holds the open window, the Beacons this
+        decode appends and the raw cache.  Each layer's fused decode then
+        attends over the rank's shard (``latent_shard`` on all but the last
+        rank) and writes fp32 partials that one NCCL all-gather and
+        ``slimkv_merge_partials`` combine (``parallel.SequenceSplitMerge``).
+        Everything else runs replicated, so every rank keeps identical
+        hidden states."""
         self.cfg, self.w, self.device = cfg, weights, device
         B = len(history)
         self.batch = B
@@ -129,8 +141,25 @@ class LatentDecodeRuntime:
         if cfg.sink > 1 and (hist == 0).any():
             raise ValueError('decode with more than one sink needs a completed first window')
         per_window = cfg.window // cfg.ratio
+        self.split = None
+        if seq_split is not None and seq_split is not False:
+            import torch.distributed as dist
+            from .parallel import shard_range
+            group = None if seq_split is True else seq_split
+            world, rank = dist.get_world_size(group), dist.get_rank(group)
+            if paged:
+                raise ValueError('the sequence split uses the native latent layout')
+            bounds = [shard_range(int(h), world, rank, tile=64) for h in hist.tolist()]
+            self.split = dict(group=group, world=world, rank=rank, last=rank == world - 1,
+                              offset=torch.tensor([a for a, _ in bounds], dtype=torch.int32),
+                              rows=torch.tensor([b - a for a, b in bounds], dtype=torch.int32))
         self.raw_capacity = (cfg.sink + cfg.window + 1 + 63) // 64 * 64
-        self.lat_capacity = (int(hist.max()) + (1 + extra_windows) * per_window + 63) // 64 * 64
+        if self.split is not None and not self.split['last']:
+            self.raw_capacity = 64                   # no raw keys on a shard rank (raw_len 0)
+            self.lat_capacity = max(64, (int(self.split['rows'].max()) + 63) // 64 * 64)
+        else:
+            first = 0 if self.split is None else int(self.split['offset'].min())
+            self.lat_capacity = (int(hist.max()) - first + (1 + extra_windows) * per_window + 63) // 64 * 64
         kvd = cfg.kv_heads * cfg.head_dim
         gen = torch.Generator(device=device)
         gen.manual_seed(seed)
@@ -198,19 +227,41 @@ class LatentDecodeRuntime:
         q = z[:, :, :qd].unflatten(-1, (cfg.heads, cfg.head_dim))          # [B, 2, H, D]
         lat_max = int(hist.max()) + per_window + 64
         self.calls = []
+        self.merges = []
+        sp = self.split
+        call_raw_len, call_lat_len = self.raw_len, self.latent_len
+        if sp is not None:
+            from .parallel import SequenceSplitMerge
+            sp['offset'], sp['rows'] = sp['offset'].to(device), sp['rows'].to(device)
+            # Shard-relative latent counts: fixed on shard ranks, the running
+            # count minus the shard's first row on the last rank.
+            sp['latent_len'] = sp['rows'].clone() if not sp['last'] else torch.zeros(B, **i32)
+            call_lat_len = sp['latent_len']
+            if not sp['last']:
+                call_raw_len = torch.zeros(B, **i32)
+            lat_max = lat_max - int(sp['offset'].min()) if sp['last'] else int(sp['rows'].max())
         for c, layer in zip(self.caches, weights.layers):
             pages = (c['pages'], self.layout, self.tables) if paged else None
+            shard = sp is not None and not sp['last']
+            out, lse = self.attn, None
+            if sp is not None:
+                m = SequenceSplitMerge(B, 2, cfg.heads, cfg.head_dim, group=sp['group'], device=device,
+                                       merged=self.attn)
+                self.merges.append(m)
+                out, lse = m.out, m.lse
             self.calls.append(kernels.LatentDecodeCall(
                 q=q, raw_k_rot=c['raw_k_rot'], raw_v=c['raw_v'], raw_k_pre=c['raw_k_pre'],
-                lat_k=c.get('lat_k'), lat_v=c.get('lat_v'), lat_pages=pages, raw_len=self.raw_len,
-                latent_len=self.latent_len,
+                lat_k=c.get('lat_k'), lat_v=c.get('lat_v'), lat_pages=pages, raw_len=call_raw_len,
+                latent_len=call_lat_len,
                 query_len=self.query_len, qpos=self.qpos, uk=layer['uk'], uv=layer['uv'],
                 uk_bias=layer.get('uk_bias'), uv_bias=layer.get('uv_bias'),
-                cos=self.cos, sin=self.sin, out=self.attn,
-                new_k=z[:, 0, qd:qd + kvd], new_v=z[:, 0, qd + kvd:qd + 2 * kvd],
-                new_lat_k=z[:, 1, qd:qd + cfg.rank_k], new_lat_v=z[:, 1, qd + cfg.rank_k:qd + cfg.rank_k + cfg.rank_v],
+                cos=self.cos, sin=self.sin, out=out, out_lse=lse, latent_shard=shard,
+                new_k=None if shard else z[:, 0, qd:qd + kvd], new_v=None if shard else z[:, 0, qd + kvd:qd + 2 * kvd],
+                new_lat_k=None if shard else z[:, 1, qd:qd + cfg.rank_k],
+                new_lat_v=None if shard else z[:, 1, qd + cfg.rank_k:qd + cfg.rank_k + cfg.rank_v],
                 latent_len_max=min(lat_max, self.lat_capacity), raw_len_max=self.raw_capacity,
                 latent_splits=latent_splits, raw_splits=raw_splits))
+        self.call_latent_len, self.call_raw_len = call_lat_len, call_raw_len
         self.graph = None
 
     # ------------------------------------------------------------------
@@ -222,10 +273,13 @@ class LatentDecodeRuntime:
         nb = qd + cfg.rank_k + cfg.rank_v
         kernels.decode_schedule(self.history, self.tail, self.raw_len, self.latent_len, self.query_len,
                                 self.qpos, cfg.sink, cfg.window, cfg.ratio)
+        sp = self.split
+        if sp is not None and sp['last']:
+            torch.sub(self.latent_len, sp['offset'], out=sp['latent_len'])
         x = self.x
         x[:, 0].copy_(w.embed.index_select(0, self.tokens))
         x[:, 1].copy_(w.beacon_embed.expand(B, -1))
-        for layer, call in zip(w.layers, self.calls):
+        for i, (layer, call) in enumerate(zip(w.layers, self.calls)):
             h = F.rms_norm(x, (H,), layer['norm1'], cfg.rms_eps)
             if cfg.qkv_bias:
                 torch.addmm(layer['b_raw'], h[:, 0], layer['w_raw'].t(), out=self.z[:, 0])
@@ -234,6 +288,8 @@ class LatentDecodeRuntime:
                 torch.mm(h[:, 0], layer['w_raw'].t(), out=self.z[:, 0])
                 torch.mm(h[:, 1], layer['w_beacon'].t(), out=self.z[:, 1, :nb])
             call()
+            if self.merges:
+                self.merges[i]()                     # all-gather of the partials + N-part merge -> self.attn
             x.add_((self.attn.view(2 * B, qd) @ layer['w_o'].t()).view(B, 2, H))
             h2 = F.rms_norm(x, (H,), layer['norm2'], cfg.rms_eps)
             gu = h2.view(2 * B, H) @ layer['w_gate_up'].t()
@@ -271,10 +327,11 @@ class LatentDecodeRuntime:
     def attention_kernel_bytes(self):
         """Algorithmic HBM bytes of one attention launch (one layer, both
         branches): every latent K/V row (``N (Rk + Rv) 2``) and every raw
-        key/value (``(S + T + 1) Hkv D 2`` each) of every sequence, read once."""
+        key/value (``(S + T + 1) Hkv D 2`` each) of every sequence, read once
+        (this rank's shard under a sequence split)."""
         cfg = self.cfg
-        lat = self.latent_len.long().sum().item() * (cfg.rank_k + cfg.rank_v) * 2
-        raw = self.raw_len.long().sum().item() * cfg.kv_heads * cfg.head_dim * 2 * 2
+        lat = self.call_latent_len.long().sum().item() * (cfg.rank_k + cfg.rank_v) * 2
+        raw = self.call_raw_len.long().sum().item() * cfg.kv_heads * cfg.head_dim * 2 * 2
         return lat + raw
 
     def attention_bytes(self):
@@ -285,8 +342,8 @@ class LatentDecodeRuntime:
         V), the query and output rows, plus the up-projection weights once.
         """
         cfg = self.cfg
-        lat = self.latent_len.long().sum().item() * (cfg.rank_k + cfg.rank_v) * 2
-        raw = self.raw_len.long().sum().item() * cfg.kv_heads * cfg.head_dim * 2 * 2
+        lat = self.call_latent_len.long().sum().item() * (cfg.rank_k + cfg.rank_v) * 2
+        raw = self.call_raw_len.long().sum().item() * cfg.kv_heads * cfg.head_dim * 2 * 2
         rows = self.query_len.long().sum().item() * cfg.heads * cfg.head_dim * 2 * 2
         weights = cfg.kv_heads * cfg.head_dim * (cfg.rank_k + cfg.rank_v) * 2
         return cfg.layers * (lat + raw + rows + weights)

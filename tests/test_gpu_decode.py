@@ -282,3 +282,117 @@ def test_merge_matches_oracle():
     ref = oracle.merge_attention(raw, rl, lat, ll)
     np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=1e-3, rtol=8e-3)
     assert_bits_equal(out[:, :, 0], raw[:, :, 0])
+
+
+def run_sharded(c, query_len, starts, paged=False):
+    """Sequence split emulated on one GPU.
+
+    The caches are staged and this step's entries appended by one whole
+    fused step (``run_fused``); then shard ``k`` attends over latent rows
+    ``[starts[k], starts[k+1])`` of every sequence (the last shard: to the
+    sequence's end, with the raw branch and the causal Beacon row; the
+    others: ``latent_shard`` and no raw keys), each writing its output and
+    log-sum-exp, and ``merge_partials`` combines the N partials as the
+    all-gather of a real split would hand them over.  Returns the whole
+    step's caches/outputs, the merged output and LSE, and the partials.
+    """
+    from slimkv_b200 import kernels
+    t = run_fused(c, query_len, fp32=True, paged=paged)
+    _, _, cos_t, sin_t = tables()
+    B, L, H, D = c['q'].shape
+    N = len(starts)
+    common = dict(q=t['q'], raw_k_rot=t['raw_k_rot'], raw_v=t['raw_v'], uk=t['uk'], uv=t['uv'], cos=cos_t,
+                  sin=sin_t, qpos=t['qpos'], query_len=t['query_len'], uk_bias=t.get('uk_bias'),
+                  uv_bias=t.get('uv_bias'))
+    outs = torch.zeros(N, B, L, H * D, dtype=torch.float32, device='cuda')
+    lses = torch.full((N, B, L, H), float('-inf'), dtype=torch.float32, device='cuda')
+    for k in range(N):
+        s, last = starts[k], k == N - 1
+        e = None if last else starts[k + 1]
+        lat_len = c['n_lat'] - s if last else np.full(B, e - s)
+        if paged:
+            backing, layout, block_tables = t['lat_pages']
+            assert s % layout.slots == 0 and (last or e % layout.slots == 0)
+            lat = dict(lat_pages=(backing, layout,
+                                  block_tables[:, s // layout.slots:None if last else e // layout.slots]))
+        else:
+            lat = dict(lat_k=t['lat_k'][:, s:e], lat_v=t['lat_v'][:, s:e])
+        kernels.latent_decode(**common, **lat, latent_len=torch.tensor(lat_len, dtype=torch.int32, device='cuda'),
+                              raw_len=t['raw_len'] if last else torch.zeros(B, dtype=torch.int32, device='cuda'),
+                              out=outs[k], out_lse=lses[k], latent_shard=not last)
+    merged = torch.empty(B, L, H * D, dtype=torch.float32, device='cuda')
+    merged_lse = torch.empty(B, L, H, dtype=torch.float32, device='cuda')
+    kernels.merge_partials(outs.view(N, B * L * H, D), lses.view(N, B * L * H), merged, merged_lse)
+    torch.cuda.synchronize()
+    return t, merged, merged_lse, outs, lses
+
+
+def check_sharded(c, query_len, starts, paged=False):
+    t, merged, merged_lse, _, _ = run_sharded(c, query_len, starts, paged)
+    _, whole, whole_lse, _, _ = run_sharded(c, query_len, [0], paged)
+    for b, r in enumerate(oracle_rows(c, query_len)):
+        L = int(query_len[b])
+        assert_attention_close(merged[b:b + 1, :L], r['out'])
+        lse = np.logaddexp(r['raw_lse'], r['latent_lse'])[0].T            # [L, H]
+        for got in (merged_lse, whole_lse):
+            np.testing.assert_allclose(got[b, :L].cpu().numpy(), lse, atol=2e-3, rtol=1e-4)
+        # The merge of shards is the same attention as the unsplit call, up
+        # to the rounding of probabilities against a different running max.
+        a, w = merged[b, :L].double(), whole[b, :L].double()
+        assert ((a - w).norm() / w.norm()).item() < 1e-3
+        assert torch.equal(whole[b, :L], t['out'][b, :L])
+
+
+@pytest.mark.parametrize('paged', [False, True])
+@pytest.mark.parametrize('starts', [[0, 384], [0, 96, 384, 720]])
+def test_sequence_split_shards_merge_to_the_whole_step(starts, paged):
+    """Latent shards of each sequence (the last one with the raw branch and
+    this step's Beacon) merged with the N-part LSE merge equal the unsplit
+    fused step and the oracle; rows that insert a Beacon and rows that do not
+    are mixed, with up-projection biases."""
+    c = decode_case(41, batch=3, length=2, history=1500, tail=300, bias=True, ragged=True)
+    query_len = np.array([2, 1, 2])
+    c['n_lat'] = c['n_lat'] - (query_len == 1)
+    check_sharded(c, query_len, starts, paged)
+
+
+@pytest.mark.parametrize('length', [1, 2])
+def test_sequence_split_qwen_geometry(length):
+    """40 heads, rank 512 (the split-KV route with 32-key tiles): shards of a
+    long latent history merge to the unsplit step."""
+    c = decode_case(43, batch=2, length=length, history=2000, tail=200, heads=40, rk=512, rv=512, bias=True)
+    query_len = np.full(2, length)
+    check_sharded(c, query_len, [0, 640, 1280])
+
+
+@pytest.mark.parametrize('parts,dim,out_fp32', [(1, 128, True), (3, 128, False), (8, 96, True), (40, 320, True),
+                                                (64, 64, False)])
+def test_merge_partials_matches_numpy(parts, dim, out_fp32):
+    """The N-part LSE merge against a float64 numpy restatement, with parts
+    and whole rows that have no keys (-inf)."""
+    from slimkv_b200 import kernels
+    rng = np.random.default_rng(parts * 1000 + dim)
+    rows = 37
+    out = rng.standard_normal((parts, rows, dim)).astype(np.float32)
+    lse = (rng.standard_normal((parts, rows)) * 6).astype(np.float32)
+    lse[rng.random((parts, rows)) < 0.3] = -np.inf
+    lse[:, 5] = -np.inf                                  # a row without keys anywhere
+    m = lse.max(0)
+    finite = np.isfinite(m)
+    total = np.where(finite, np.log(np.exp(lse.astype(np.float64) - np.where(finite, m, 0)).sum(0)) + m, -np.inf)
+    w = np.where(np.isfinite(lse), np.exp(lse - np.where(finite, total, 0)), 0.0)
+    want = (w[..., None] * out).sum(0)
+    # Part strides wider than a part, as in an all-gather of [outputs | lses].
+    packed = np.zeros((parts, rows * dim + (rows + 3) // 4 * 4 + 4), np.float32)
+    packed[:, :rows * dim] = out.reshape(parts, -1)
+    packed[:, rows * dim:rows * dim + rows] = lse
+    dev = torch.from_numpy(packed).cuda()
+    got = torch.empty(rows, dim, dtype=torch.float32 if out_fp32 else torch.bfloat16, device='cuda')
+    got_lse = torch.empty(rows, dtype=torch.float32, device='cuda')
+    kernels.merge_partials(dev[:, :rows * dim].view(parts, rows, dim), dev[:, rows * dim:rows * dim + rows], got,
+                           got_lse)
+    torch.cuda.synchronize()
+    tol = 1e-5 if out_fp32 else 8e-3
+    np.testing.assert_allclose(got.float().cpu().numpy(), want, rtol=tol, atol=tol)
+    np.testing.assert_allclose(got_lse.cpu().numpy(), total, rtol=1e-6, atol=1e-5)
+    assert np.all(got.float().cpu().numpy()[5] == 0)
