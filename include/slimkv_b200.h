@@ -442,6 +442,45 @@ SLIMKV_API int slimkv_prefill_rope(const void* q, const int64_t q_stride[3], con
                                    void* stream);
 
 /* ------------------------------------------------------------------------
+ * Beacon K/V reconstruction for the reconstruct decode backend — replaces
+ * ReconstructionCache.materialize (slimkv/llama3/memory.py:26-48) and the
+ * per-step history up-projection of reconstruction_attention
+ * (tools/benchmark/context_decode_runtime.py:298-344):
+ *   key[b][start_b + r]   = bf16(lat_k[b][r] . w_k_up^T + b_k_up)     (Hkv*D)
+ *   value[b][start_b + r] = bf16(lat_v[b][r] . w_v_up^T + b_v_up)
+ * for r < rows, start_b = out_start[b] (device int32 [B], NULL = 0), on the
+ * tensor cores with fp32 accumulation and one rounding, as a bf16 nn.Linear.
+ * lat_k / lat_v [B][lat_capacity][R] rows (element strides lat_stride_batch,
+ * lat_stride_row; multiples of 8, 16-byte aligned); w_*_up [Hkv*D][R] as
+ * nn.Linear weights; biases [Hkv*D] or NULL; key / value [B][out_rows][Hkv*D]
+ * with element strides out_stride_batch / out_stride_row (multiples of 8).
+ * A destination row past out_rows is skipped and flagged
+ * SLIMKV_DEVICE_BAD_LENGTH.  workspace (optional) enables split-K for small
+ * calls; size it with slimkv_reconstruct_kv_workspace_size.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    int batch, rows, kv_heads, head_dim, rank_k, rank_v;
+    const void* lat_k;
+    const void* lat_v;
+    int64_t lat_stride_batch, lat_stride_row;
+    int lat_capacity;
+    const void* w_k_up;
+    const void* b_k_up;
+    const void* w_v_up;
+    const void* b_v_up;
+    void* key;
+    void* value;
+    int64_t out_stride_batch, out_stride_row;
+    int out_rows;
+    const int32_t* out_start;
+    void* workspace;
+    size_t workspace_bytes;
+} slimkv_reconstruct_args;
+
+SLIMKV_API size_t slimkv_reconstruct_kv_workspace_size(const slimkv_reconstruct_args* args);
+SLIMKV_API int slimkv_reconstruct_kv(const slimkv_reconstruct_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
  * N-part LSE merge of partial attention — the cross-GPU step of a sequence
  * split: merge_attention (slimkv/llama3/fa2_decode.py:57-66), which merges two
  * partitions of one row's keys, generalised to N partitions:

@@ -24,3 +24,4 @@ from .schedule import FastDecodeSchedule, interleave_roles, paged_restore_roles
 from .pages import BeaconPageLayout, beacon_page_slots, raw_page_slots, beacon_block_size
 from .splits import latent_splits, dense_splits, original_splits
 from .prefill import prefill_metadata, project_with_beacon, prefill_rope, flush_chunk
+from .reconstruct import materialize, reconstruct_decode_attention

@@ -115,6 +115,17 @@ class WindowProjectArgs(ctypes.Structure):
     ]
 
 
+class ReconstructArgs(ctypes.Structure):
+    """Mirror of ``slimkv_reconstruct_args``."""
+    _fields_ = [
+        ('batch', _I), ('rows', _I), ('kv_heads', _I), ('head_dim', _I), ('rank_k', _I), ('rank_v', _I),
+        ('lat_k', _P), ('lat_v', _P), ('lat_stride_batch', _L), ('lat_stride_row', _L), ('lat_capacity', _I),
+        ('w_k_up', _P), ('b_k_up', _P), ('w_v_up', _P), ('b_v_up', _P), ('key', _P), ('value', _P),
+        ('out_stride_batch', _L), ('out_stride_row', _L), ('out_rows', _I), ('out_start', _P),
+        ('workspace', _P), ('workspace_bytes', ctypes.c_size_t),
+    ]
+
+
 class MergePartialsArgs(ctypes.Structure):
     """Mirror of ``slimkv_merge_partials_args``."""
     _fields_ = [
@@ -150,6 +161,8 @@ SIGNATURES = {
                           ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I,
                           _I, _P, _P]),
     'slimkv_merge_partials': (_I, [ctypes.POINTER(MergePartialsArgs), _P]),
+    'slimkv_reconstruct_kv_workspace_size': (ctypes.c_size_t, [ctypes.POINTER(ReconstructArgs)]),
+    'slimkv_reconstruct_kv': (_I, [ctypes.POINTER(ReconstructArgs), _P]),
 }
 
 _lib = None

@@ -847,6 +847,57 @@ extern "C" int slimkv_window_project(const slimkv_window_project_args* a, void* 
     return run(L2, a->batch, a->workspace, a->workspace_bytes, st);
 }
 
+namespace slimkv {
+namespace {
+
+// The two up-projection groups of a Beacon K/V reconstruction.
+int build_reconstruct(const slimkv_reconstruct_args* a, Launch& L) {
+    if (!a) return fail(SLIMKV_ERR_INVALID_ARGUMENT, "null arguments");
+    if (a->batch < 0 || a->rows < 0 || a->kv_heads <= 0 || a->head_dim <= 0 || a->rank_k <= 0 || a->rank_v <= 0)
+        return fail(SLIMKV_ERR_INVALID_ARGUMENT, "reconstruct: invalid shape");
+    if (a->batch == 0 || a->rows == 0) return SLIMKV_OK;
+    if (a->rows > a->lat_capacity || a->out_rows <= 0)
+        return fail(SLIMKV_ERR_INVALID_ARGUMENT, "reconstruct: rows exceed the latent capacity or out_rows is empty");
+    if (!a->lat_k || !a->lat_v || !a->w_k_up || !a->w_v_up || !a->key || !a->value)
+        return fail(SLIMKV_ERR_INVALID_ARGUMENT, "reconstruct: null tensor pointer");
+    if (a->rank_k % 8 || a->rank_v % 8 || !rows_ok(a->lat_k, a->lat_stride_batch, a->lat_stride_row) ||
+        !rows_ok(a->lat_v, a->lat_stride_batch, a->lat_stride_row) ||
+        !rows_ok(a->key, a->out_stride_batch, a->out_stride_row) ||
+        !rows_ok(a->value, a->out_stride_batch, a->out_stride_row))
+        return fail(SLIMKV_ERR_ALIGNMENT, "reconstruct: rows must be 16-byte aligned with strides and ranks %% 8 == 0");
+    const int kvd = a->kv_heads * a->head_dim;
+    if (a->out_stride_row < kvd || a->lat_stride_row < std::max(a->rank_k, a->rank_v))
+        return fail(SLIMKV_ERR_INVALID_ARGUMENT, "reconstruct: row stride smaller than a row");
+    int rc;
+    if ((rc = add_group(L, a->lat_k, a->lat_stride_batch, a->lat_stride_row, nullptr, nullptr, a->lat_capacity,
+                        a->rows, a->w_k_up, a->rank_k, kvd, a->b_k_up,
+                        {dense_target(a->key, a->out_stride_batch, a->out_stride_row, a->out_rows, nullptr,
+                                      a->out_start)},
+                        a->batch)))
+        return rc;
+    return add_group(L, a->lat_v, a->lat_stride_batch, a->lat_stride_row, nullptr, nullptr, a->lat_capacity, a->rows,
+                     a->w_v_up, a->rank_v, kvd, a->b_v_up,
+                     {dense_target(a->value, a->out_stride_batch, a->out_stride_row, a->out_rows, nullptr,
+                                   a->out_start)},
+                     a->batch);
+}
+
+}  // namespace
+}  // namespace slimkv
+
+extern "C" size_t slimkv_reconstruct_kv_workspace_size(const slimkv_reconstruct_args* a) {
+    Launch L;
+    if (build_reconstruct(a, L) != SLIMKV_OK) return 0;
+    return plan_splits(L, device_info().sm_count, nullptr);
+}
+
+extern "C" int slimkv_reconstruct_kv(const slimkv_reconstruct_args* a, void* stream) {
+    Launch L;
+    if (int rc = build_reconstruct(a, L)) return rc;
+    if (a->batch == 0 || a->rows == 0) return SLIMKV_OK;
+    return run(L, a->batch, a->workspace, a->workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int slimkv_prefill_rope(const void* q, const int64_t q_stride[3], const void* k, const int64_t k_stride[3],
                                    const float* cos, const float* sin, int rope_positions, const int64_t* positions,
                                    int64_t positions_stride, const int64_t* roles, int role_count, int sink, int batch,

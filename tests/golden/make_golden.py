@@ -386,12 +386,46 @@ def gen_splits(out):
     out['splits'] = np.array(rows)
 
 
+def gen_reconstruct(out):
+    """``ReconstructionCache.materialize`` (slimkv/llama3/memory.py:26-48) with
+    bf16 up-projections: the Beacon keys / values of the reconstruct backend."""
+    import types
+    import torch
+    from slimkv.llama3.memory import ReconstructionCache
+    for name, (seed, batch, n, rank, kv_heads, dim, bias) in {
+            'qwen_r2': (31, 2, 70, 512, 2, 128, True), 'llama_r4': (32, 1, 45, 320, 2, 128, False)}.items():
+        rng = np.random.default_rng(seed)
+        lat_k = rng.standard_normal((batch, n, rank), dtype=np.float32) * 1.3
+        lat_v = rng.standard_normal((batch, n, rank), dtype=np.float32) * 1.3
+        mods = {}
+        for kind, lat in (('k', lat_k), ('v', lat_v)):
+            lin = torch.nn.Linear(rank, kv_heads * dim, bias=bias, dtype=torch.bfloat16)
+            with torch.no_grad():
+                lin.weight.copy_(torch.from_numpy(rng.standard_normal((kv_heads * dim, rank), dtype=np.float32) * 0.05))
+                if bias:
+                    lin.bias.copy_(torch.from_numpy(rng.standard_normal(kv_heads * dim, dtype=np.float32) * 0.1))
+            mods[kind] = lin
+        attn = types.SimpleNamespace(beacon_k_up_proj=mods['k'], beacon_v_up_proj=mods['v'],
+                                     num_key_value_heads=kv_heads, head_dim=dim)
+        for kind, lat in (('k', lat_k), ('v', lat_v)):
+            hist = torch.from_numpy(lat).to(torch.bfloat16).unsqueeze(1)            # [B, 1, N, R]
+            cache = ReconstructionCache(None, hist, None, None, None, kv_heads, dim, kind)
+            with torch.no_grad():
+                full = cache.materialize(attn)                                       # [B, Hkv, N, D] bf16
+            out[f'{name}_lat_{kind}'] = hist.squeeze(1).view(torch.int16).numpy()
+            out[f'{name}_w_{kind}'] = mods[kind].weight.detach().view(torch.int16).numpy()
+            if bias:
+                out[f'{name}_b_{kind}'] = mods[kind].bias.detach().view(torch.int16).numpy()
+            out[f'{name}_full_{kind}'] = full.transpose(1, 2).contiguous().view(torch.int16).numpy()
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument('--reference', required=True, help='path to a SlimKV source checkout')
     p.add_argument('--output', default=str(HERE / 'reference_golden.npz'))
     p.add_argument('--prefill-output', default=str(HERE / 'prefill_golden.npz'))
-    p.add_argument('--only', choices=['decode', 'prefill'], default=None,
+    p.add_argument('--reconstruct-output', default=str(HERE / 'reconstruct_golden.npz'))
+    p.add_argument('--only', choices=['decode', 'prefill', 'reconstruct'], default=None,
                    help='write only the decode-side or only the prefill-side fixture file')
     args = p.parse_args()
     ref = Path(args.reference).resolve()
@@ -399,6 +433,13 @@ def main():
     import torch
     torch.set_num_threads(4)
     from cases import config1_layer
+    if args.only in (None, 'reconstruct'):
+        rec = {}
+        gen_reconstruct(rec)
+        np.savez_compressed(args.reconstruct_output, **rec)
+        print('wrote', args.reconstruct_output, sum(v.nbytes for v in rec.values()), 'bytes raw')
+        if args.only == 'reconstruct':
+            return
     if args.only != 'decode':
         pre = {}
         gen_prefill(pre)
