@@ -59,6 +59,9 @@ def parse():
     p.add_argument('--seq-split', action='store_true',
                    help='with --config 5: the batch-1 524288-token sequence, its latents split over the N ranks '
                         '(cross-GPU LSE merge over NCCL every layer)')
+    p.add_argument('--reconstruct', action='store_true',
+                   help='with --config 5: the reference\'s reconstruct decode backend (Beacon K/V rebuilt from the '
+                        'latents every step, then attention) instead of the latent backend')
     p.add_argument('--kernel-only', action='store_true',
                    help='one layer of the same workload: time the attention kernel alone (profiling runs)')
     return p.parse_args()
@@ -340,6 +343,46 @@ def attention_kernel_time(rt, reps):
     return sum(b.elapsed_time(e) for b, e in events) / reps
 
 
+def reconstruct_roofline(rt, reps):
+    """The reconstruct backend per layer: the whole attention step (RoPE,
+    appends, Beacon K/V rebuild, attention) and the rebuild alone
+    (``slimkv_reconstruct_kv``: 2 x rows x R x Hkv*D x 2 FLOPs for K and V),
+    CUDA events on the launching stream, cycling through the layers."""
+    import torch
+    from slimkv_b200.reconstruct import reconstruct_kv
+    cfg = rt.cfg
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a0, a1 = ev(), ev()
+    a0.record()
+    for i in range(reps * cfg.layers):
+        rt._reconstruct_attention(i % cfg.layers)
+    a1.record()
+    torch.cuda.synchronize()
+    step_us = a0.elapsed_time(a1) / (reps * cfg.layers) * 1000.0
+    r0, r1 = ev(), ev()
+    r0.record()
+    for i in range(reps * cfg.layers):
+        d = rt.recon[i % cfg.layers]
+        w_k, w_v, b_k, b_v = d.w
+        reconstruct_kv(d.lat_k, d.lat_v, w_k, w_v, d.key_full, d.value_full, d.rows, b_k, b_v, out_start=d.raw_len)
+    r1.record()
+    torch.cuda.synchronize()
+    rebuild_us = r0.elapsed_time(r1) / (reps * cfg.layers) * 1000.0
+    d = rt.recon[0]
+    rows = rt.batch * d.rows
+    kvd = cfg.kv_heads * cfg.head_dim
+    flops = 2.0 * rows * kvd * (cfg.rank_k + cfg.rank_v)
+    tflops = flops / (rebuild_us / 1e6) / 1e12
+    peak, source = tensor_peak()
+    return {'step_per_layer_us': step_us, 'rebuild_per_layer_us': rebuild_us, 'rebuilt_rows_per_layer': rows,
+            'rebuild_flops_per_layer': flops, 'launches_per_layer': 5,
+            'roofline': {'bound': 'tensor', 'achieved': tflops, 'peak': peak, 'unit': 'TFLOP/s',
+                         'frac': tflops / peak, 'peak_source': source, 'traffic': None,
+                         'kernel': 'project_kernel (Beacon K/V rebuild, tcgen05)',
+                         'flops_per_launch': flops, 'us_per_launch': rebuild_us}}
+
+
 def kernel_only(args):
     """One layer of the bench workload (same batch, history, tails): the
     fused decode call repeated; prints the attention kernel's time.  Small
@@ -421,8 +464,14 @@ def main():
         batch = C5_BATCH
         tails = rng.integers(0, cfg.window, size=batch)
         history = [131072 // cfg.window * (cfg.window // cfg.ratio)] * batch
-        rt = LatentDecodeRuntime(cfg, weights, history, tails, device, extra_windows=1, raw_pre=False)
+        backend = 'reconstruct' if args.reconstruct else 'latent'
+        rt = LatentDecodeRuntime(cfg, weights, history, tails, device, extra_windows=1, raw_pre=False,
+                                 backend=backend)
         metric, workload = C5_METRIC, config5(world)
+        if args.reconstruct:
+            metric = metric.replace('latent path', 'reconstruct path')
+            workload['workload'] = workload['workload'].replace('latent path', 'reconstruct backend (Beacon K/V '
+                                                                'rebuilt from latents every step, then attention)')
     else:
         cfg = LatentLlamaConfig()
         weights = RandomWeights(cfg, device, seed=0)
@@ -495,6 +544,9 @@ def main():
         torch.cuda.synchronize()
         merge_us = max_over_ranks(m0.elapsed_time(m1) / (cfg.layers * 4)) * 1000.0
 
+    recon = None
+    if rt.recon:
+        recon = reconstruct_roofline(rt, max(args.steps, 4))
     # ---- roofline of the dominant kernel: the attention launch (latent + raw
     # branches) timed alone with CUDA events on its stream; the whole fused
     # step per layer (prologue + attention + merge) is reported beside it.
@@ -544,6 +596,13 @@ def main():
     }
     if prefill is not None:
         result['prefill'] = prefill
+    if recon is not None:
+        # The reconstruct backend's dominant kernel is the Beacon K/V rebuild
+        # (tensor-bound); the latent fused step above is the comparison.
+        result['reconstruct'] = recon
+        result['roofline'] = recon.pop('roofline')
+        result['latent_backend_fused_step_per_layer_us'] = layer_ms * 1000.0
+        result['gpu_launches'] = args.steps * (1 + cfg.layers * (4 + recon['launches_per_layer']))
     if split:
         result['sequence_split'] = {
             'ranks': world, 'latent_rows_this_rank': int(rt.call_latent_len.sum().item()),

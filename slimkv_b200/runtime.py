@@ -111,7 +111,7 @@ class LatentDecodeRuntime:
     """
 
     def __init__(self, cfg, weights, history, tails, device, extra_windows=1, seed=1, fill_std=1.3, paged=False,
-                 raw_pre=True, latent_splits=0, raw_splits=0, seq_split=None):
+                 raw_pre=True, latent_splits=0, raw_splits=0, seq_split=None, backend='latent'):
         """``paged`` keeps each layer's latent cache in the vLLM plugin's Beacon
         pages (page size of a 16-token raw page, ``create_page_layers``,
         slimkv/vllm_plugin/backend.py:108-131), each sequence owning the pages
@@ -130,7 +130,15 @@ class LatentDecodeRuntime:
         rank) and writes fp32 partials that one NCCL all-gather and
         ``slimkv_merge_partials`` combine (``parallel.SequenceSplitMerge``).
         Everything else runs replicated, so every rank keeps identical
-        hidden states."""
+        hidden states.
+
+        ``backend='reconstruct'`` runs the reference's reconstruct decode
+        backend instead of the latent one (:mod:`slimkv_b200.reconstruct`):
+        per layer the queries and the new raw key are rotated
+        (``slimkv_rope_decode``), the new raw K/V and Beacon latents are
+        appended, every Beacon key and value is rebuilt from its latent
+        (``slimkv_reconstruct_kv``) into a full-dimension buffer shared by the
+        layers, and split-KV attention runs over raw + rebuilt keys."""
         self.cfg, self.w, self.device = cfg, weights, device
         B = len(history)
         self.batch = B
@@ -141,7 +149,12 @@ class LatentDecodeRuntime:
         if cfg.sink > 1 and (hist == 0).any():
             raise ValueError('decode with more than one sink needs a completed first window')
         per_window = cfg.window // cfg.ratio
+        if backend not in ('latent', 'reconstruct'):
+            raise ValueError('backend must be latent or reconstruct')
+        self.backend = backend
         self.split = None
+        if backend == 'reconstruct' and (paged or (seq_split is not None and seq_split is not False)):
+            raise ValueError('the reconstruct backend runs on the native layout without a sequence split')
         if seq_split is not None and seq_split is not False:
             import torch.distributed as dist
             from .parallel import shard_range
@@ -262,6 +275,20 @@ class LatentDecodeRuntime:
                 latent_len_max=min(lat_max, self.lat_capacity), raw_len_max=self.raw_capacity,
                 latent_splits=latent_splits, raw_splits=raw_splits))
         self.call_latent_len, self.call_raw_len = call_lat_len, call_raw_len
+        self.recon = []
+        if backend == 'reconstruct':
+            from .reconstruct import ReconstructDecode
+            full = (B, self.raw_capacity + self.lat_capacity, cfg.kv_heads, cfg.head_dim)
+            self.key_full = torch.zeros(full, **bf)
+            self.value_full = torch.zeros(full, **bf)
+            self.batch_index = torch.arange(B, device=device)
+            for c, layer in zip(self.caches, weights.layers):
+                self.recon.append(ReconstructDecode(
+                    raw_k_rot=c['raw_k_rot'], raw_v=c['raw_v'], lat_k=c['lat_k'], lat_v=c['lat_v'],
+                    w_k_up=layer['uk'], w_v_up=layer['uv'], b_k_up=layer.get('uk_bias'), b_v_up=layer.get('uv_bias'),
+                    raw_len=self.raw_len, latent_len=self.latent_len, query_len=self.query_len,
+                    key_full=self.key_full, value_full=self.value_full,
+                    latent_rows=min(lat_max, self.lat_capacity)))
         self.graph = None
 
     # ------------------------------------------------------------------
@@ -287,7 +314,10 @@ class LatentDecodeRuntime:
             else:
                 torch.mm(h[:, 0], layer['w_raw'].t(), out=self.z[:, 0])
                 torch.mm(h[:, 1], layer['w_beacon'].t(), out=self.z[:, 1, :nb])
-            call()
+            if self.recon:
+                self._reconstruct_attention(i)
+            else:
+                call()
             if self.merges:
                 self.merges[i]()                     # all-gather of the partials + N-part merge -> self.attn
             x.add_((self.attn.view(2 * B, qd) @ layer['w_o'].t()).view(B, 2, H))
@@ -299,6 +329,29 @@ class LatentDecodeRuntime:
         torch.mm(final, w.lm_head.t(), out=self.logits_bf16)
         self.logits.copy_(self.logits_bf16)
         return self.logits
+
+    def _reconstruct_attention(self, i):
+        """One layer of the reconstruct backend (reconstruction_attention,
+        tools/benchmark/context_decode_runtime.py:298-344): RoPE of the
+        queries and of the new raw key, cache appends, Beacon K/V rebuilt from
+        the latents, attention over raw + rebuilt keys into ``self.attn``."""
+        cfg, c = self.cfg, self.caches[i]
+        B, qd, kvd = self.batch, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+        z = self.z
+        q = z[:, :, :qd].unflatten(-1, (cfg.heads, cfg.head_dim)).transpose(1, 2)      # [B, H, 2, D]
+        k_new = z[:, 0, qd:qd + kvd].unflatten(-1, (cfg.kv_heads, 1, cfg.head_dim))    # [B, Hkv, 1, D]
+        q_rot, k_rot = kernels.rope_decode(q, k_new, self.cos, self.sin, self.qpos, None, 0, 0)
+        row = (self.raw_len - 1).long()
+        c['raw_k_rot'].index_put_((self.batch_index, row), k_rot[:, :, 0])
+        c['raw_v'].index_put_((self.batch_index, row), z[:, 0, qd + kvd:qd + 2 * kvd].unflatten(-1, (cfg.kv_heads, cfg.head_dim)))
+        if c['raw_k_pre'] is not None:
+            c['raw_k_pre'].index_put_((self.batch_index, row), k_new[:, :, 0])
+        # The Beacon latent pair of rows that insert one (others rewrite their last row unchanged).
+        lrow = (self.latent_len - 1).clamp_min(0).long()
+        width = cfg.rank_k + cfg.rank_v
+        new_lat = torch.where((self.query_len == 2)[:, None], z[:, 1, qd:qd + width], c['lat'][self.batch_index, lrow])
+        c['lat'].index_put_((self.batch_index, lrow), new_lat)
+        self.recon[i](q_rot.transpose(1, 2), self.attn.view(B, 2, cfg.heads, cfg.head_dim))
 
     def capture(self, warmup=2):
         """Capture one decode step in a CUDA graph (warm-up steps advance the cache)."""

@@ -65,3 +65,59 @@ def test_qwen_geometry_runtime_steps():
         assert torch.isfinite(logits).all()
         tokens = logits.argmax(-1)
     assert _lib.device_status(clear=True) == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize('geometry', ['llama', 'qwen'])
+def test_reconstruct_backend_runtime_follows_latent_backend(geometry):
+    """The reconstruct backend (Beacon K/V rebuilt each step, then attention)
+    against the latent backend on the same caches, through steps that insert
+    Beacons and graph replays.  One layer, so both backends see identical
+    attention inputs each step: the attention rows differ only by the bf16
+    rounding of the rebuilt keys and values (norm-wise 1e-2); the caches the
+    backends append must stay bit-identical."""
+    from slimkv_b200.runtime import LatentDecodeRuntime, LatentLlamaConfig, RandomWeights, qwen25_14b_r2
+    dev = torch.device('cuda', 0)
+    if geometry == 'llama':
+        cfg = LatentLlamaConfig(layers=1, vocab=512, hidden=1024, intermediate=2048)
+    else:
+        cfg = qwen25_14b_r2()
+        cfg.layers, cfg.vocab, cfg.hidden, cfg.intermediate = 1, 512, 1024, 2048
+    w = RandomWeights(cfg, dev, seed=9)
+    per_window = cfg.window // cfg.ratio
+    history, tails = [per_window * 4, per_window * 9, per_window], [1013, 300, 7]
+    lat = LatentDecodeRuntime(cfg, w, history, tails, dev)
+    rec = LatentDecodeRuntime(cfg, w, history, tails, dev, backend='reconstruct')
+    for cl, cr in zip(lat.caches, rec.caches):
+        for name in ('raw_k_rot', 'raw_k_pre', 'raw_v', 'lat'):
+            cr[name].copy_(cl[name])
+    tokens = torch.tensor([3, 77, 500], device=dev)
+    inserted = 0
+
+    def compare(a, b):
+        torch.cuda.synchronize()
+        for bb, q in enumerate(lat.query_len.tolist()):
+            for l in range(q):
+                x, y = lat.attn[bb, l].double(), rec.attn[bb, l].double()
+                assert ((x - y).norm() / x.norm()).item() < 1e-2
+        d = (a.float() - b.float()).abs()
+        assert d.mean().item() < 5e-3 and d.max().item() <= 0.125
+        for cl, cr in zip(lat.caches, rec.caches):
+            for name in ('raw_k_rot', 'raw_k_pre', 'raw_v', 'lat'):
+                assert torch.equal(cl[name], cr[name]), name
+
+    for _ in range(6):
+        lat.tokens.copy_(tokens)
+        rec.tokens.copy_(tokens)
+        compare(lat.step_eager().clone(), rec.step_eager().clone())
+        inserted += int((lat.query_len == 2).sum())
+        tokens = lat.next_tokens().clone()
+    for rt in (lat, rec):
+        rt.tokens.copy_(tokens)
+        rt.capture(warmup=1)
+    for _ in range(2):
+        compare(lat.step().clone(), rec.step().clone())
+        tokens = lat.next_tokens().clone()
+        lat.tokens.copy_(tokens)
+        rec.tokens.copy_(tokens)
+    assert inserted >= 2
