@@ -185,7 +185,10 @@ typedef struct {
      * counts (0 = the capacities).  Lengths above them are still handled. */
     int latent_len_max;
     int raw_len_max;
-    /* Split counts (0 = chosen from the byte volume and the SM count). */
+    /* Split counts (0 = chosen from the byte volume and the SM count).  On the
+     * tensor-core route (32 query heads, ranks <= 320) the work is split on
+     * the device instead: latent_splits then sets the number of persistent
+     * CTAs of the launch and raw_splits the CTAs given to the raw branch. */
     int latent_splits;
     int raw_splits;
     /* Optional cudaEvent_t handles (NULL = none) recorded on `stream` right
@@ -218,6 +221,15 @@ typedef struct {
      * is not causal (new_lat_k / new_lat_v must be NULL). */
     float* out_lse;
     int latent_shard;
+    /* Bound of every pipeline wait inside the attention kernel in ns (0 = 2 s).
+     * A wait that runs out sets SLIMKV_DEVICE_TIMEOUT and the kernel returns
+     * early; a short bound lets a caller (or a test) check that path. */
+    uint64_t wait_limit_ns;
+    /* Element stride between the KV heads of one token in raw_k_rot / raw_v /
+     * raw_k_pre (0 = head_dim: the token-major layout above).  A head-major
+     * cache [B, Hkv, raw_capacity, D] passes raw_stride_token = head_dim and
+     * raw_stride_head = raw_capacity * head_dim. */
+    int64_t raw_stride_head;
 } slimkv_latent_decode_args;
 
 SLIMKV_API size_t slimkv_latent_decode_workspace_size(const slimkv_latent_decode_args* args);
@@ -239,6 +251,21 @@ SLIMKV_API int slimkv_rope_decode(const void* q, const int64_t q_stride[3], cons
                        const int64_t* raw_idx, int sink, int history, int batch, int heads,
                        int kv_heads, int queries, int keys, int head_dim, void* q_out,
                        void* k_out, void* stream);
+
+/* ------------------------------------------------------------------------
+ * BF16-exact RoPE of cache rows at per-sequence positions — the key half of
+ * `decode_ops.fused_rope` (decode_kernels.py:8-51) for a batch whose
+ * sequences sit at different positions (the vLLM plugin's requests, whose
+ * raw tails are read from pages every step, paged_model.py:7-52):
+ *   out[b, t, h, :] = rope(x[b, t, h, :]) at positions[b * positions_stride + t]
+ * for t < counts[b] (counts NULL = all `tokens`), rounding to bf16 after each
+ * multiply and after the add.  x / out bf16 with element strides {batch,
+ * token, head} (last dim contiguous), distinct buffers; positions int32.
+ * ---------------------------------------------------------------------- */
+SLIMKV_API int slimkv_rope_rows(const void* x, const int64_t x_stride[3], void* out, const int64_t out_stride[3],
+                                const int32_t* positions, int64_t positions_stride, const int32_t* counts,
+                                int batch, int tokens, int heads, int head_dim, const float* cos, const float* sin,
+                                int rope_positions, void* stream);
 
 /* ------------------------------------------------------------------------
  * LSE merge — drop-in for `decode_ops.fused_merge`

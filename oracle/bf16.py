@@ -11,12 +11,14 @@ import numpy as np
 def bf16_bits(x):
     """fp32 array -> uint16 bf16 bit patterns, round to nearest even."""
     f = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
-    u = f.view(np.uint32).astype(np.uint64)
+    u = f.view(np.uint32)
+    # uint32 arithmetic wraps only for bit patterns >= 0xFFFF8001, which are
+    # NaNs and are replaced below.
+    r = ((u + np.uint32(0x7FFF) + ((u >> 16) & np.uint32(1))) >> 16).astype(np.uint16)
     nan = np.isnan(f)
-    lsb = (u >> 16) & 1
-    r = ((u + 0x7FFF + lsb) >> 16) & 0xFFFF
-    r = np.where(nan, ((u >> 16) | 0x40) & 0xFFFF, r)
-    return r.astype(np.uint16)
+    if nan.any():
+        r[nan] = ((u[nan] >> 16) | np.uint32(0x40)).astype(np.uint16)
+    return r
 
 
 def from_bf16_bits(bits):

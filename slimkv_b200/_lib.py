@@ -62,7 +62,8 @@ class LatentDecodeArgs(ctypes.Structure):
         ('lat_pages', ctypes.c_void_p), ('lat_page_stride', ctypes.c_int64), ('lat_slots', ctypes.c_int),
         ('lat_sink_elements', ctypes.c_int), ('lat_table', ctypes.c_void_p), ('lat_table_stride', ctypes.c_int64),
         ('lat_num_pages', ctypes.c_int),
-        ('out_lse', ctypes.c_void_p), ('latent_shard', ctypes.c_int),
+        ('out_lse', ctypes.c_void_p), ('latent_shard', ctypes.c_int), ('wait_limit_ns', ctypes.c_uint64),
+        ('raw_stride_head', ctypes.c_int64),
     ]
 
 
@@ -157,6 +158,7 @@ SIGNATURES = {
     'slimkv_window_project': (_I, [ctypes.POINTER(WindowProjectArgs), _P]),
     'slimkv_prefill_rope': (_I, [_P, _PL, _P, _PL, _P, _P, _I, _P, _L, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _PL,
                                  _P, _PL, _P]),
+    'slimkv_rope_rows': (_I, [_P, _PL, _P, _PL, _P, _L, _P, _I, _I, _I, _I, _P, _P, _I, _P]),
     'slimkv_merge': (_I, [_P, ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _P,
                           ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _I, _I, _I,
                           _I, _P, _P]),

@@ -60,6 +60,38 @@ __global__ void rope_decode_kernel(RopeArgs a) {
     }
 }
 
+struct RopeRowsArgs {
+    const __nv_bfloat16* x; int64_t xb, xt, xh;
+    __nv_bfloat16* out; int64_t ob, ot, oh;
+    const int32_t* pos; int64_t pos_stride;
+    const int32_t* count;
+    int batch, tokens, heads, dim;
+    const float* cos; const float* sin; int positions;
+    unsigned int* status;
+};
+
+// out[b, t, h, :] = rope(x[b, t, h, :]) at position pos[b][t], for t < count[b].
+__global__ void rope_rows_kernel(RopeRowsArgs a) {
+    const int64_t n = (int64_t)a.batch * a.tokens * a.heads * a.dim;
+    const int half = a.dim / 2;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int d = i % a.dim;
+        const int h = (i / a.dim) % a.heads;
+        const int t = (i / ((int64_t)a.dim * a.heads)) % a.tokens;
+        const int b = i / ((int64_t)a.dim * a.heads * a.tokens);
+        if (t >= (a.count ? a.count[b] : a.tokens)) continue;
+        int pos = a.pos[b * a.pos_stride + t];
+        if (pos < 0 || pos >= a.positions) {
+            report(a.status, SLIMKV_DEVICE_BAD_LENGTH);
+            pos = 0;
+        }
+        const __nv_bfloat16* row = a.x + b * a.xb + t * a.xt + h * a.xh;
+        const float v = rope_value(__bfloat162float(row[d]), __bfloat162float(row[(d + half) % a.dim]), d, half,
+                                   a.cos[(int64_t)pos * a.dim + d], a.sin[(int64_t)pos * a.dim + d]);
+        a.out[b * a.ob + t * a.ot + h * a.oh + d] = __float2bfloat16_rn(v);
+    }
+}
+
 struct MergeOpArgs {
     const __nv_bfloat16* raw; int64_t rb, rh, rs;
     const float* rl; int64_t rlb, rlh, rls;
@@ -145,4 +177,25 @@ extern "C" int slimkv_merge(const void* raw, const int64_t raw_stride[3], const 
     merge_kernel<<<grid_for(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? SLIMKV_OK : fail(SLIMKV_ERR_CUDA, "merge launch failed: %s", cudaGetErrorString(e));
+}
+
+extern "C" int slimkv_rope_rows(const void* x, const int64_t x_stride[3], void* out, const int64_t out_stride[3],
+                                const int32_t* positions, int64_t positions_stride, const int32_t* counts, int batch,
+                                int tokens, int heads, int head_dim, const float* cos, const float* sin,
+                                int rope_positions, void* stream) {
+    if (!x || !out || !x_stride || !out_stride || !positions || !cos || !sin)
+        return fail(SLIMKV_ERR_INVALID_ARGUMENT, "null pointer");
+    if (x == out) return fail(SLIMKV_ERR_INVALID_ARGUMENT, "rope_rows does not rotate in place");
+    if (batch <= 0 || tokens <= 0 || heads <= 0 || head_dim <= 0 || head_dim % 2 || rope_positions <= 0)
+        return fail(SLIMKV_ERR_INVALID_ARGUMENT, "invalid sizes");
+    RopeRowsArgs a{};
+    a.x = static_cast<const __nv_bfloat16*>(x); a.xb = x_stride[0]; a.xt = x_stride[1]; a.xh = x_stride[2];
+    a.out = static_cast<__nv_bfloat16*>(out); a.ob = out_stride[0]; a.ot = out_stride[1]; a.oh = out_stride[2];
+    a.pos = positions; a.pos_stride = positions_stride; a.count = counts;
+    a.batch = batch; a.tokens = tokens; a.heads = heads; a.dim = head_dim;
+    a.cos = cos; a.sin = sin; a.positions = rope_positions; a.status = status_word();
+    const int64_t n = (int64_t)batch * tokens * heads * head_dim;
+    rope_rows_kernel<<<grid_for(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? SLIMKV_OK : fail(SLIMKV_ERR_CUDA, "rope rows launch failed: %s", cudaGetErrorString(e));
 }

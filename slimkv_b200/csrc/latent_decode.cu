@@ -61,8 +61,9 @@ namespace {
 struct DecodePlan {
     int wl = 0, mtl = 0, lat_row_blocks = 0, lat_rows = 0, lat_splits = 0, lat_tps = 0;
     int raw_rows = 0, raw_splits = 0, raw_tps = 0, group = 0, rvp = 0;
-    bool tc = false;   // latent branch on the tensor-memory kernel (32 query heads)
-    size_t q_rot = 0, q_lat = 0, lat_o = 0, lat_lse = 0, raw_o = 0, raw_lse = 0, lat_work = 0;
+    bool tc = false;   // both branches on the persistent tensor-memory kernel (32 query heads)
+    int ctas = 0, raw_ctas = 0, lat_pieces = 0;          // tensor-memory route
+    size_t q_rot = 0, q_lat = 0, lat_o = 0, lat_lse = 0, raw_o = 0, raw_lse = 0, plan = 0;
 };
 
 int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
@@ -110,47 +111,33 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
     const size_t B = a->batch, L = a->length, H = a->heads;
     p.tc = a->heads == 32 && p.wl <= 320;
     if (p.tc) {
-        // One launch, 128-key tiles, one CTA per SM: the latent CTAs leave
-        // about one SM per sequence free, where the (short) raw CTAs start;
-        // the rest of the raw CTAs follow as latent CTAs finish.
-        //
-        // Sequences may have different latent lengths: every sequence gets
-        // ceil(tiles_b / tps) splits of at most tps tiles (at least one), and
-        // the prologue writes the list of (sequence, split) work items the
-        // latent CTAs take in order.  Small batches: tps spreads the longest
-        // sequence over about one SM per sequence less one.  Large batches
-        // (fewer than 3 SMs per sequence): splits of at most 16 tiles, so no
-        // single long sequence sets the kernel time.
+        // One persistent launch: CTAs (at most one per SM) split the latent and
+        // raw work by volume on the device (latent_tc_plan.cuh).  latent_splits
+        // and raw_splits, when given, set the CTA count of the launch and of
+        // the raw class.
         const int sms = std::max(device_info().sm_count, 1);
-        const int tiles = std::max(1, (lat_len + kTcTileKeys - 1) / kTcTileKeys);
-        const int per_seq = sms / a->batch;
-        int tps;
-        if (a->latent_splits > 0)
-            tps = (tiles + a->latent_splits - 1) / a->latent_splits;
-        else if (per_seq >= 3)
-            tps = (tiles + per_seq - 2) / (per_seq - 1);
-        else
-            tps = std::min(16, std::max(4, (tiles + 7) / 8));
-        tps = std::max(tps, (tiles + 31) / 32);               // the merge combines at most 32 splits
-        p.lat_tps = std::max(1, tps);
-        p.lat_splits = (tiles + p.lat_tps - 1) / p.lat_tps;
+        const int cap = std::min(sms, kMergeMaxSplits - 1);
+        p.ctas = std::max(3, std::min(a->latent_splits > 0 ? a->latent_splits : sms, cap));
+        p.raw_ctas = a->raw_splits > 0 ? std::min(a->raw_splits, p.ctas - 2) : 0;
         p.lat_rows = 64;
-        const int rtiles = std::max(1, (raw_len + kTcTileKeys - 1) / kTcTileKeys);
-        // Raw CTAs are short (a tail of at most 1023 keys per KV head): two
-        // splits help a small batch fill the machine; a large batch has CTAs
-        // to spare and pays each CTA's fixed cost, so one.
-        const int r2 = a->raw_splits > 0 ? a->raw_splits : (per_seq >= 3 ? 2 : 1);
-        p.raw_splits = std::max(1, std::min({r2, rtiles, 32}));
-        p.raw_tps = (rtiles + p.raw_splits - 1) / p.raw_splits;
-        p.raw_rows = 64;
+        p.raw_rows = 2 * p.group;
+        p.lat_pieces = tc_max_pieces(a->batch, p.ctas);
     }
     p.q_rot = B * L * H * a->head_dim;
     p.q_lat = p.tc ? B * 128 * p.wl : B * L * H * p.wl;
-    p.lat_work = p.tc ? B * p.lat_splits : 0;
-    p.lat_o = B * p.lat_splits * p.lat_rows * p.wl;
-    p.lat_lse = B * p.lat_splits * p.lat_rows;
-    p.raw_o = B * a->kv_heads * p.raw_splits * p.raw_rows * 128;
-    p.raw_lse = B * a->kv_heads * p.raw_splits * p.raw_rows;
+    if (p.tc) {
+        const size_t raw_pieces = tc_max_pieces(a->batch * a->kv_heads, p.ctas);
+        p.plan = tc_plan_layout(a->batch, a->kv_heads).words;
+        p.lat_o = 2 * size_t(p.lat_pieces) * p.lat_rows * p.wl;
+        p.lat_lse = 2 * size_t(p.lat_pieces) * p.lat_rows;
+        p.raw_o = raw_pieces * p.raw_rows * 128;
+        p.raw_lse = raw_pieces * p.raw_rows;
+    } else {
+        p.lat_o = B * p.lat_splits * p.lat_rows * p.wl;
+        p.lat_lse = B * p.lat_splits * p.lat_rows;
+        p.raw_o = B * a->kv_heads * p.raw_splits * p.raw_rows * 128;
+        p.raw_lse = B * a->kv_heads * p.raw_splits * p.raw_rows;
+    }
     return SLIMKV_OK;
 }
 
@@ -158,7 +145,7 @@ struct Buffers {
     __nv_bfloat16* q_rot;
     __half* q_lat;
     float *lat_o, *lat_lse, *raw_o, *raw_lse;
-    int32_t* lat_work;      // [B * lat_splits]: latent CTA -> (sequence, split count, split)
+    int32_t* plan;          // tensor-memory route: the device plan (latent_tc.h)
 };
 
 Buffers carve(Carver& c, const DecodePlan& p) {
@@ -169,7 +156,7 @@ Buffers carve(Carver& c, const DecodePlan& p) {
     w.lat_lse = c.take<float>(p.lat_lse);
     w.raw_o = c.take<float>(p.raw_o);
     w.raw_lse = c.take<float>(p.raw_lse);
-    w.lat_work = c.take<int32_t>(p.lat_work);
+    w.plan = c.take<int32_t>(p.plan);
     return w;
 }
 
@@ -229,8 +216,16 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         !aligned16(a->uv) ||
         (!paged && (a->lat_stride_row % 8 || a->lat_stride_batch % 8 || !aligned16(a->lat_k) || !aligned16(a->lat_v))))
         return fail(SLIMKV_ERR_ALIGNMENT, "caches must be 16-byte aligned with strides that are multiples of 8");
-    if (a->raw_stride_token < (int64_t)a->kv_heads * a->head_dim ||
-        (!paged && a->lat_stride_row < std::max(a->rank_k, a->rank_v)))
+    const int64_t raw_sh = a->raw_stride_head > 0 ? a->raw_stride_head : a->head_dim;
+    // Token-major [B, cap, Hkv, D] (head stride D) or head-major [B, Hkv, cap, D]
+    // (token stride D): either way the rows of different heads and tokens must
+    // not overlap.
+    const bool token_major = raw_sh == a->head_dim && a->raw_stride_token >= (int64_t)a->kv_heads * a->head_dim;
+    const bool head_major = a->raw_stride_token == a->head_dim && raw_sh >= (int64_t)a->raw_capacity * a->head_dim;
+    if (raw_sh % 8 || !(token_major || head_major))
+        return fail(SLIMKV_ERR_INVALID_ARGUMENT, "raw caches must be token-major [B, cap, Hkv, D] or head-major "
+                                                 "[B, Hkv, cap, D] (strides multiples of 8)");
+    if (!paged && a->lat_stride_row < std::max(a->rank_k, a->rank_v))
         return fail(SLIMKV_ERR_INVALID_ARGUMENT, "cache row stride smaller than a row");
     if (paged) {
         if (!p.tc) return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "paged latent caches need 32 query heads");
@@ -276,7 +271,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     pa.raw_k_rot = static_cast<__nv_bfloat16*>(a->raw_k_rot);
     pa.raw_v = static_cast<__nv_bfloat16*>(a->raw_v);
     pa.raw_k_pre = static_cast<__nv_bfloat16*>(a->raw_k_pre);
-    pa.raw_sb = a->raw_stride_batch; pa.raw_st = a->raw_stride_token;
+    pa.raw_sb = a->raw_stride_batch; pa.raw_st = a->raw_stride_token; pa.raw_sh = raw_sh;
     pa.raw_len = a->raw_len; pa.raw_capacity = a->raw_capacity;
     pa.new_lat_k = static_cast<const __nv_bfloat16*>(a->new_lat_k);
     pa.new_lat_v = static_cast<const __nv_bfloat16*>(a->new_lat_v);
@@ -291,10 +286,16 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     pa.lat_page_stride = a->lat_page_stride; pa.lat_table_stride = a->lat_table_stride;
     pa.lat_slots = a->lat_slots; pa.lat_sink = a->lat_sink_elements; pa.lat_num_pages = a->lat_num_pages;
     pa.lat_table = a->lat_table;
-    pa.lat_work = p.tc ? w.lat_work : nullptr;
-    pa.lat_tps = p.lat_tps; pa.lat_splits_max = p.lat_splits;
+    if (p.tc) {
+        pa.do_plan = 1;
+        TcPlanArgs& pl = pa.plan;
+        pl.batch = a->batch; pl.kv_heads = a->kv_heads; pl.length = a->length;
+        pl.latent_len = a->latent_len; pl.raw_len = a->raw_len; pl.query_len = a->query_len;
+        pl.lat_chunks = (a->rank_k + 63) / 64 + (a->rank_v + 63) / 64;
+        pl.ctas = p.ctas; pl.raw_ctas = p.raw_ctas; pl.with_raw = 1; pl.plan = w.plan;
+    }
     pa.status = status;
-    const dim3 pgrid(a->kv_heads, p.wl / 64, (a->batch + pa.seq_per_cta - 1) / pa.seq_per_cta);
+    const dim3 pgrid(a->kv_heads, p.wl / 64, (a->batch + pa.seq_per_cta - 1) / pa.seq_per_cta + (p.tc ? 1 : 0));
     decode_prologue_kernel<<<pgrid, 256, 0, stream>>>(pa);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "prologue launch failed: %s", cudaGetErrorString(e));
@@ -309,7 +310,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
             return rc;
         if ((rc = make_bshd_map(&lv, a->lat_v, a->batch, a->lat_capacity, 1, a->rank_v, lat_stride, &bc, lt)))
             return rc;
-        const int64_t raw_stride[3] = {a->raw_stride_batch, a->raw_stride_token, a->head_dim};
+        const int64_t raw_stride[3] = {a->raw_stride_batch, a->raw_stride_token, raw_sh};
         if ((rc = make_bshd_map(&rk, a->raw_k_rot, a->batch, a->raw_capacity, a->kv_heads, a->head_dim, raw_stride,
                                 &bc, kTile)))
             return rc;
@@ -338,23 +339,24 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         TcLaunch tl{};
         tl.batch = a->batch; tl.length = a->length; tl.scale = a->scale;
         tl.query_len = a->query_len; tl.status = status; tl.with_raw = 1;
+        tl.kv_heads = a->kv_heads; tl.ctas = p.ctas; tl.plan = w.plan; tl.lat_pieces = p.lat_pieces;
+        tl.wait_ns = a->wait_limit_ns;
         TcSide& L = tl.lat;
         L.k = a->lat_k; L.v = a->lat_v; L.dim_k = a->rank_k; L.dim_v = a->rank_v;
         L.kv_heads = 1; L.capacity = a->lat_capacity;
         L.stride_batch = a->lat_stride_batch; L.stride_row = a->lat_stride_row; L.stride_head = 0;
         L.q = w.q_lat; L.q_rows = 0; L.heads = a->heads; L.group = a->heads; L.causal = a->latent_shard ? 0 : 1;
-        L.seqlens = a->latent_len; L.splits = p.lat_splits; L.rows_alloc = p.lat_rows; L.width = p.wl;
+        L.seqlens = a->latent_len; L.rows_alloc = p.lat_rows; L.width = p.wl;
         L.part_o = w.lat_o; L.part_lse = w.lat_lse;
         L.pages = a->lat_pages; L.page_stride = a->lat_page_stride; L.slots = a->lat_slots;
         L.sink_elements = a->lat_sink_elements; L.num_pages = a->lat_num_pages;
         L.table = a->lat_table; L.table_stride = a->lat_table_stride;
-        L.work = w.lat_work; L.tiles_per_split = p.lat_tps;
         TcSide& R = tl.raw;
         R.k = a->raw_k_rot; R.v = a->raw_v; R.dim_k = a->head_dim; R.dim_v = a->head_dim;
         R.kv_heads = a->kv_heads; R.capacity = a->raw_capacity;
-        R.stride_batch = a->raw_stride_batch; R.stride_row = a->raw_stride_token; R.stride_head = a->head_dim;
+        R.stride_batch = a->raw_stride_batch; R.stride_row = a->raw_stride_token; R.stride_head = raw_sh;
         R.q = w.q_rot; R.q_rows = 1; R.heads = a->heads; R.group = p.group; R.causal = 0;
-        R.seqlens = a->raw_len; R.splits = p.raw_splits; R.rows_alloc = p.raw_rows; R.width = a->head_dim;
+        R.seqlens = a->raw_len; R.rows_alloc = p.raw_rows; R.width = a->head_dim;
         R.part_o = w.raw_o; R.part_lse = w.raw_lse;
         if (a->attn_event_begin && cudaEventRecord(static_cast<cudaEvent_t>(a->attn_event_begin), stream) != cudaSuccess)
             return fail(SLIMKV_ERR_CUDA, "attn_event_begin record failed");
@@ -381,9 +383,13 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     MergeArgs ma{};
     ma.lat_o = w.lat_o; ma.lat_lse = w.lat_lse; ma.lat_splits = p.lat_splits; ma.lat_rows = p.lat_rows;
     ma.lat_width = p.wl;
-    ma.lat_tps = p.tc ? p.lat_tps : 0; ma.latent_len = a->latent_len;
+    if (p.tc) {
+        ma.plan = w.plan;
+        ma.PL = tc_plan_layout(a->batch, a->kv_heads);
+        ma.lat_pieces = p.lat_pieces;
+    }
     ma.raw_o = w.raw_o; ma.raw_lse = w.raw_lse; ma.raw_splits = p.raw_splits; ma.raw_rows = p.raw_rows;
-    ma.raw_l_pitch = p.tc ? 32 : p.group;
+    ma.raw_l_pitch = p.group;
     ma.q_rot = w.q_rot;
     ma.uv = static_cast<const __nv_bfloat16*>(a->uv);
     ma.uk_bias = static_cast<const __nv_bfloat16*>(a->uk_bias);

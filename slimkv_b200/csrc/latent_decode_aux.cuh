@@ -10,6 +10,7 @@
 
 #include "common.cuh"
 #include "latent_tc.h"
+#include "latent_tc_plan.cuh"
 
 namespace slimkv {
 
@@ -36,7 +37,7 @@ struct PrologueArgs {
     __nv_bfloat16* raw_k_rot;
     __nv_bfloat16* raw_v;
     __nv_bfloat16* raw_k_pre;
-    int64_t raw_sb, raw_st;
+    int64_t raw_sb, raw_st, raw_sh;
     const int32_t* raw_len;
     int raw_capacity;
     const __nv_bfloat16* new_lat_k;
@@ -53,32 +54,13 @@ struct PrologueArgs {
     int64_t lat_page_stride, lat_table_stride;
     int lat_slots, lat_sink, lat_num_pages;
     const int32_t* lat_table;
-    // Latent work list of the tensor-memory attention (nullable): written by
-    // block (0, 0, 0), one entry per latent CTA (batch * lat_splits_max):
-    // sequence << 11 | splits << 5 | split, then -1 for unused CTAs.
-    int32_t* lat_work;
-    int lat_tps, lat_splits_max;
+    // Plan of the tensor-memory attention (latent_tc_plan.cuh), written by
+    // block (0, 0, gridDim.z - 1) when do_plan is set (that z-slice does
+    // nothing else).
+    TcPlanArgs plan;
+    int do_plan;
     unsigned int* status;
 };
-
-// One warp writes the (sequence, split) items of all sequences in order.
-__device__ __forceinline__ void build_latent_work(const PrologueArgs& a, int lane) {
-    int base = 0;
-    for (int b0 = 0; b0 < a.batch; b0 += 32) {
-        const int b = b0 + lane;
-        const int n = b < a.batch ? latent_splits_of(a.latent_len[b], a.lat_tps, a.lat_splits_max) : 0;
-        int x = n;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, x, off);
-            if (lane >= off) x += y;
-        }
-        const int start = base + x - n;
-        for (int s = 0; s < n; ++s) a.lat_work[start + s] = (b << 11) | (n << 5) | s;
-        base += __shfl_sync(0xffffffffu, x, 31);
-    }
-    for (int i = base + lane; i < a.batch * a.lat_splits_max; i += 32) a.lat_work[i] = -1;
-}
 
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
@@ -123,7 +105,8 @@ __device__ __forceinline__ uint4 widen8(uint4 v) {
     return make_uint4(bf16x2_to_f16x2(v.x), bf16x2_to_f16x2(v.y), bf16x2_to_f16x2(v.z), bf16x2_to_f16x2(v.w));
 }
 
-// grid (Hkv, width / 64, ceil(B / seq_per_cta)), 256 threads.  CTA (g, cc, bb)
+// grid (Hkv, width / 64, ceil(B / seq_per_cta) [+ 1 planning slice]), 256
+// threads.  CTA (g, cc, bb)
 // absorbs the 64 query rows of KV head g for sequences [bb*spc, (bb+1)*spc)
 // into latent columns [cc*64, cc*64 + 64); the cc == 0 CTAs also write q_rot
 // and append this step's raw token (and, for g == 0, the Beacon latents).
@@ -132,7 +115,12 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
     __shared__ __align__(1024) uint8_t s_b[128 * 64 * 2];         // U_k[g][:, cc*64 : +64] fp16
     const int g = blockIdx.x, cc = blockIdx.y, bb = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if (a.lat_work && g == 0 && cc == 0 && bb == 0 && warp == 0) build_latent_work(a, lane);
+    if (a.do_plan && bb == int(gridDim.z) - 1) {
+        // The last z-slice only plans the attention (one block, in parallel
+        // with the absorb blocks).
+        if (g == 0 && cc == 0) plan_tc_work(a.plan);
+        return;
+    }
     const int rps = a.length * a.group;                 // rows per sequence
     const int b0 = bb * a.seq_per_cta;
     const int half = a.dim / 2;
@@ -239,7 +227,7 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
             const __nv_bfloat16* v = a.new_v + b * a.new_stride + (int64_t)g * a.dim;
             float o[8];
             rope8(k, d0, half, a.cos + (int64_t)pos * a.dim, a.sin + (int64_t)pos * a.dim, o);
-            const int64_t dst = b * a.raw_sb + row * a.raw_st + (int64_t)g * a.dim + d0;
+            const int64_t dst = b * a.raw_sb + row * a.raw_st + g * a.raw_sh + d0;
             *reinterpret_cast<uint4*>(a.raw_k_rot + dst) = pack8_bf16(o);
             *reinterpret_cast<uint4*>(a.raw_v + dst) = __ldg(reinterpret_cast<const uint4*>(v + d0));
             if (a.raw_k_pre) *reinterpret_cast<uint4*>(a.raw_k_pre + dst) = __ldg(reinterpret_cast<const uint4*>(k + d0));
@@ -278,8 +266,13 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
 
 struct MergeArgs {
     const float* lat_o; const float* lat_lse; int lat_splits, lat_rows, lat_width;
-    int lat_tps;                   // > 0: sequence b has latent_splits_of(latent_len[b]) splits
-    const int32_t* latent_len;
+    // Tensor-memory route (plan != nullptr): the partials of a segment are the
+    // pieces [seg_piece[s], seg_piece[s + 1]) of its class; class 1's latent
+    // pieces follow lat_pieces slots after class 0's.  Otherwise sequence b
+    // (and KV head g) has lat_splits (raw_splits) consecutive partials.
+    const int32_t* plan;
+    TcPlanLayout PL;
+    int lat_pieces;
     const float* raw_o; const float* raw_lse; int raw_splits, raw_rows;
     int raw_l_pitch;        // raw partial row of (query l, head j): l * raw_l_pitch + j
     const __nv_bfloat16* q_rot;
@@ -291,8 +284,8 @@ struct MergeArgs {
     float* out_lse;                // [B][L][H] merged LSE (nullable)
 };
 
-// Splits per branch that decode_merge_kernel combines (4 per lane).
-constexpr int kMergeMaxSplits = 128;
+// Partials per row and branch that decode_merge_kernel combines (5 per lane).
+constexpr int kMergeMaxSplits = 160;
 
 // Dynamic shared memory of decode_merge_kernel for a padded value rank:
 // U_v[g] bf16 [128 x rvp], o_lat hi and lo bf16 [16 x rvp] each, raw rows
@@ -310,8 +303,29 @@ __device__ __forceinline__ void cp_async_commit_wait_all() {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-__device__ __forceinline__ int lat_splits_row(const MergeArgs& a, int b) {
-    return a.lat_tps > 0 ? latent_splits_of(a.latent_len[b], a.lat_tps, a.lat_splits) : a.lat_splits;
+// First partial and partial count of sequence b's latent branch.
+__device__ __forceinline__ void lat_parts(const MergeArgs& a, int b, int& p0, int& n) {
+    if (a.plan) {
+        const int ls = a.plan[a.PL.lat_seg + b], cls = ls >> 24, s = ls & 0xffffff;
+        const int32_t* pc = a.plan + a.PL.seg_piece[cls];
+        p0 = pc[s] + (cls ? a.lat_pieces : 0);
+        n = pc[s + 1] - pc[s];
+    } else {
+        p0 = b * a.lat_splits;
+        n = a.lat_splits;
+    }
+}
+// First partial and partial count of the raw branch of (sequence b, KV head g).
+__device__ __forceinline__ void raw_parts(const MergeArgs& a, int b, int g, int& p0, int& n) {
+    const int s = b * a.kv_heads + g;
+    if (a.plan) {
+        const int32_t* pc = a.plan + a.PL.seg_piece[2];
+        p0 = pc[s];
+        n = pc[s + 1] - pc[s];
+    } else {
+        p0 = s * a.raw_splits;
+        n = a.raw_splits;
+    }
 }
 
 // grid (Hkv, ceil(B / seq_per_cta)), 256 threads, merge_smem_bytes() of
@@ -373,7 +387,11 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
         float lse_br[2];
 #pragma unroll
         for (int br = 0; br < 2; ++br) {
-            const int nsp = valid ? (br ? a.raw_splits : lat_splits_row(a, b)) : 0;
+            int p0 = 0, nsp = 0;
+            if (valid) {
+                if (br) raw_parts(a, b, g, p0, nsp);
+                else lat_parts(a, b, p0, nsp);
+            }
             float my[kMergeMaxSplits / 32];
             float m = -INFINITY;
 #pragma unroll
@@ -381,8 +399,8 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
                 const int sp = lane + 32 * k;
                 my[k] = -INFINITY;
                 if (sp < nsp)
-                    my[k] = br ? __ldg(a.raw_lse + (((int64_t)b * a.kv_heads + g) * a.raw_splits + sp) * a.raw_rows + rr)
-                               : __ldg(a.lat_lse + ((int64_t)b * a.lat_splits + sp) * a.lat_rows + l * a.heads + h);
+                    my[k] = br ? __ldg(a.raw_lse + (int64_t)(p0 + sp) * a.raw_rows + rr)
+                               : __ldg(a.lat_lse + (int64_t)(p0 + sp) * a.lat_rows + l * a.heads + h);
                 m = fmaxf(m, my[k]);
             }
 #pragma unroll
@@ -425,9 +443,10 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
             int b, l, h, rr;
             if (!row_info(r, b, l, h, rr) || c >= a.lat_width) continue;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            const float* src = a.lat_o + ((int64_t)b * a.lat_splits * a.lat_rows + l * a.heads + h) * a.lat_width + c;
+            int p0, nsp;
+            lat_parts(a, b, p0, nsp);
+            const float* src = a.lat_o + ((int64_t)p0 * a.lat_rows + l * a.heads + h) * a.lat_width + c;
             const float* w = s_w + r * kMergeMaxSplits;
-            const int nsp = lat_splits_row(a, b);
             int s = 0;
             for (; s + 8 <= nsp; s += 8) {
                 float4 x[8];
@@ -460,10 +479,12 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
             int b, l, h, rr;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             if (row_info(r, b, l, h, rr)) {
-                const float* src = a.raw_o + ((((int64_t)b * a.kv_heads + g) * a.raw_splits) * a.raw_rows + rr) * a.dim + c;
+                int p0, nsp;
+                raw_parts(a, b, g, p0, nsp);
+                const float* src = a.raw_o + ((int64_t)p0 * a.raw_rows + rr) * a.dim + c;
                 const float* w = s_w + (16 + r) * kMergeMaxSplits;
                 int s = 0;
-                for (; s + 8 <= a.raw_splits; s += 8) {
+                for (; s + 8 <= nsp; s += 8) {
                     float4 x[8];
 #pragma unroll
                     for (int u = 0; u < 8; ++u) x[u] = __ldg(reinterpret_cast<const float4*>(src + (s + u) * pitch));
@@ -473,7 +494,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
                         acc.z = fmaf(w[s + u], x[u].z, acc.z); acc.w = fmaf(w[s + u], x[u].w, acc.w);
                     }
                 }
-                for (; s < a.raw_splits; ++s) {
+                for (; s < nsp; ++s) {
                     const float4 x = __ldg(reinterpret_cast<const float4*>(src + s * pitch));
                     acc.x = fmaf(w[s], x.x, acc.x); acc.y = fmaf(w[s], x.y, acc.y);
                     acc.z = fmaf(w[s], x.z, acc.z); acc.w = fmaf(w[s], x.w, acc.w);

@@ -1,6 +1,20 @@
-// Launch interface of the tcgen05 decode attention (latent_tc.cu): one launch
-// streams the latent cache (one shared latent head, all query heads per CTA)
-// and the raw sink + tail (per KV head) with the same tensor-core pipeline.
+// Launch interface of the tcgen05 decode attention (latent_tc.cu).
+//
+// One persistent launch streams both branches of a decode step: the latent
+// cache (one shared latent head, all query heads per CTA) and the raw sink +
+// tail (per KV head).  The work is planned on the device (plan_tc_work() in
+// latent_tc_plan.cuh, run by the prologue's first block) as three classes of
+// CTAs, each class with a fixed shared-memory layout:
+//   class 0: latent segments of sequences with one query this step,
+//   class 1: latent segments of sequences that insert a Beacon (two queries),
+//   class 2: raw segments, one per (sequence, KV head).
+// A segment's 128-key tiles are laid end to end with the other segments of
+// its class; each CTA of the class takes one contiguous, equal range of that
+// tile sequence, so a CTA may finish one segment and start the next (its
+// pipeline keeps streaming across the boundary) and a long segment spreads
+// over several CTAs.  Every (segment, CTA) intersection is a "piece" with its
+// own partial output and LSE; the pieces of a segment are numbered
+// consecutively, so the merge combines a contiguous range.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -8,7 +22,58 @@
 
 namespace slimkv {
 
-// Per-branch job as the kernel sees it.
+constexpr int kTcTileKeys = 128;
+constexpr int kTcClasses = 3;
+
+// Device-written plan (int32 words in the workspace), header then arrays.
+//   hdr[4k + 0..3] = CTAs, first CTA, segments, tiles of class k
+//   seg_start[k] : [segments + 1] tile prefix of the class's segments
+//   seg_piece[k] : [segments + 1] first piece of each segment (prefix)
+//   seg_id[k]    : [segments] sequence b (latent) or b * Hkv + g (raw)
+//   lat_seg[b]   : (class << 24) | segment of sequence b's latent segment
+struct TcPlanLayout {
+    int max_lat_segs;      // batch
+    int max_raw_segs;      // batch * kv_heads
+    // Word offsets inside the plan array.
+    int hdr, seg_start[kTcClasses], seg_piece[kTcClasses], seg_id[kTcClasses], lat_seg;
+    int words;
+};
+
+__host__ __device__ inline TcPlanLayout tc_plan_layout(int batch, int kv_heads) {
+    TcPlanLayout L{};
+    L.max_lat_segs = batch;
+    L.max_raw_segs = batch * kv_heads;
+    int at = 16;
+    L.hdr = 0;
+    for (int k = 0; k < kTcClasses; ++k) {
+        const int n = k < 2 ? L.max_lat_segs : L.max_raw_segs;
+        L.seg_start[k] = at; at += n + 1;
+        L.seg_piece[k] = at; at += n + 1;
+        L.seg_id[k] = at; at += n;
+    }
+    L.lat_seg = at; at += batch;
+    L.words = at;
+    return L;
+}
+
+// Pieces a class can produce: one per segment plus one per CTA boundary
+// that falls inside a segment.
+__host__ __device__ inline int tc_max_pieces(int segments, int ctas) { return segments + ctas; }
+
+// Inputs of the device planner.
+struct TcPlanArgs {
+    int batch, kv_heads, length;
+    const int32_t* latent_len;
+    const int32_t* raw_len;
+    const int32_t* query_len;        // nullable: `length` for every sequence
+    int lat_chunks;                  // 64-column chunks per latent key row (K + V)
+    int ctas;                        // CTAs of the launch
+    int raw_ctas;                    // > 0: CTAs of the raw class (else by volume)
+    int with_raw;
+    int32_t* plan;
+};
+
+// Per-class job as the kernel sees it.
 struct TcJob {
     int kchunks, vchunks;     // 64-column chunks of a K / V row
     int kv_heads;             // KV heads per sequence in the grid (1 for the latent branch)
@@ -19,9 +84,10 @@ struct TcJob {
     const int32_t* qlens;     // queries per sequence (1 or 2), nullable
     int length;
     float scale_log2;
-    int splits, rows_alloc, out_width;
-    float* part_o;            // [B][kv_heads][splits][rows_alloc][out_width]
-    float* part_lse;          // [B][kv_heads][splits][rows_alloc]
+    int rows_alloc, out_width;
+    float* part_o;            // [pieces][rows_alloc][out_width], row l * rows_per_query + head
+    float* part_lse;          // [pieces][rows_alloc]
+    int piece_base;           // first piece of this class in part_o / part_lse
     unsigned int* status;
     // Paged K/V (nullptr table = dense maps): row n of sequence b is row
     // n % slots of page table[b * table_stride + n / slots]; the K/V maps are
@@ -29,12 +95,7 @@ struct TcJob {
     const int32_t* table;
     int64_t table_stride;
     int slots, v_col, box_rows;   // box_rows: rows per page-map box (divides slots and 128)
-    // Work list (nullable): work[i] = sequence << 11 | its split count << 5 |
-    // split for CTA i of the branch, -1 for an unused CTA; a sequence has
-    // latent_splits_of(seqlens[b], tps, splits) splits.  Without it CTA i is
-    // (i / splits, i % splits).
-    const int32_t* work;
-    int tps;
+    uint64_t wait_ns;             // bound of every pipeline wait
 };
 
 // One branch as the host describes it.
@@ -49,7 +110,7 @@ struct TcSide {
     const void* q;
     int q_rows, heads, group, causal;
     const int32_t* seqlens;
-    int splits, rows_alloc, width;
+    int rows_alloc, width;
     float* part_o;
     float* part_lse;
     // Paged K/V: pages [num_pages] of page_stride elements holding
@@ -59,8 +120,6 @@ struct TcSide {
     int slots, sink_elements, num_pages;
     const int32_t* table;
     int64_t table_stride;
-    const int32_t* work;       // see TcJob::work
-    int tiles_per_split;
 };
 
 struct TcLaunch {
@@ -70,18 +129,15 @@ struct TcLaunch {
     unsigned int* status;
     TcSide lat, raw;
     int with_raw;
+    int kv_heads;              // the plan's KV heads (raw segments per sequence)
+    int ctas;                  // grid size (persistent CTAs)
+    const int32_t* plan;       // device plan written by plan_tc_work
+    int lat_pieces;            // pieces reserved per latent class (class 1 starts after class 0's)
+    uint64_t wait_ns;
 };
 
-constexpr int kTcTileKeys = 128;
-
-// Latent splits of a sequence with `len` latent rows when every split holds
-// at most `tps` 128-key tiles (at least one split, at most `smax`).  The
-// prologue's work list, the attention kernel and the merge agree on it.
-__host__ __device__ inline int latent_splits_of(int len, int tps, int smax) {
-    const int tiles = len > 0 ? (len + kTcTileKeys - 1) / kTcTileKeys : 0;
-    const int n = (tiles + tps - 1) / tps;
-    return n < 1 ? 1 : (n > smax ? smax : n);
-}
+// Shared memory of the launch (same for every class).
+size_t tc_smem_bytes();
 
 int launch_decode_tc(const TcLaunch& launch, cudaStream_t stream);
 

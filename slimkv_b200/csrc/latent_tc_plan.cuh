@@ -1,0 +1,178 @@
+// Device planner of the persistent tcgen05 decode attention (latent_tc.h).
+//
+// Run by one thread block (the prologue's first block, so it needs no launch
+// of its own) from this step's device lengths:
+//   1. segments: the latent rows of every sequence (class 0 for one query,
+//      class 1 for two) and the raw rows of every (sequence, KV head)
+//      (class 2), in sequence order, with the tile prefix of each class;
+//   2. CTAs per class in proportion to the bytes the class streams, weighted
+//      by how fast its layout streams them;
+//   3. pieces: one per segment plus one per CTA boundary falling inside a
+//      segment; seg_piece is their prefix, so segment s owns pieces
+//      [seg_piece[s], seg_piece[s + 1]).
+// The attention CTAs recompute their ranges from the header (class tile
+// count x i / CTAs) and find their segments by binary search.
+#pragma once
+
+#include "latent_tc.h"
+
+namespace slimkv {
+
+// Exclusive prefix of v over the block; *total receives the block sum.
+// blockDim.x a multiple of 32 (<= 1024); every thread must call it.
+__device__ inline int block_exclusive_scan(int v, int* total, int* s_warp) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) s_warp[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < nw) s_warp[lane] = w;
+    }
+    __syncthreads();
+    const int before = warp ? s_warp[warp - 1] : 0;
+    *total = s_warp[nw - 1];
+    __syncthreads();
+    return before + x - v;
+}
+
+__device__ inline int tc_tiles_of(int len) { return len > 0 ? (len + kTcTileKeys - 1) / kTcTileKeys : 0; }
+
+// Largest s in [0, n) with start[s] <= r (start[0] = 0 <= r).
+__device__ inline int tc_segment_of(const int32_t* start, int n, long long r) {
+    int lo = 0, hi = n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (start[mid] <= r) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+// First tile of CTA i of a class with `tiles` tiles over `ctas` CTAs.
+__device__ __host__ inline long long tc_cta_start(int tiles, int ctas, int i) {
+    return (long long)tiles * i / ctas;
+}
+
+__device__ inline void plan_tc_work(const TcPlanArgs& a) {
+    __shared__ int s_warp[32];
+    const TcPlanLayout L = tc_plan_layout(a.batch, a.kv_heads);
+    int32_t* P = a.plan;
+    const int tid = threadIdx.x;
+    // 1. Latent segments of both classes, raw tile prefix.
+    int carry[5] = {0, 0, 0, 0, 0};      // segments / tiles of class 0, 1; raw tiles
+    for (int b0 = 0; b0 < a.batch; b0 += blockDim.x) {
+        const int b = b0 + tid;
+        const bool ok = b < a.batch;
+        const int nq = ok ? (a.query_len ? a.query_len[b] : a.length) : 1;
+        const int cls = nq == 2 ? 1 : 0;
+        const int tl = ok ? tc_tiles_of(a.latent_len[b]) : 0;
+        const int tr = ok && a.with_raw ? tc_tiles_of(a.raw_len[b]) : 0;
+        int tot[5];
+        const int seg0 = block_exclusive_scan(ok && cls == 0, &tot[0], s_warp);
+        const int til0 = block_exclusive_scan(ok && cls == 0 ? tl : 0, &tot[1], s_warp);
+        const int seg1 = block_exclusive_scan(ok && cls == 1, &tot[2], s_warp);
+        const int til1 = block_exclusive_scan(ok && cls == 1 ? tl : 0, &tot[3], s_warp);
+        const int rawp = block_exclusive_scan(tr, &tot[4], s_warp);
+        if (ok) {
+            const int seg = cls ? carry[2] + seg1 : carry[0] + seg0;
+            const int til = cls ? carry[3] + til1 : carry[1] + til0;
+            P[L.seg_start[cls] + seg] = til;
+            P[L.seg_id[cls] + seg] = b;
+            P[L.lat_seg + b] = (cls << 24) | seg;
+            // Raw segments (b, g): tile prefix Hkv * (raw tiles before b) + g * tr.
+            const int rbase = a.kv_heads * (carry[4] + rawp);
+            for (int g = 0; g < a.kv_heads; ++g) {
+                P[L.seg_start[2] + b * a.kv_heads + g] = rbase + g * tr;
+                P[L.seg_id[2] + b * a.kv_heads + g] = b * a.kv_heads + g;
+            }
+        }
+        for (int k = 0; k < 5; ++k) carry[k] += tot[k];
+    }
+    const int nseg[3] = {carry[0], carry[2], a.with_raw ? a.batch * a.kv_heads : 0};
+    const int tiles[3] = {carry[1], carry[3], a.with_raw ? a.kv_heads * carry[4] : 0};
+    if (tid < 3) P[L.seg_start[tid] + nseg[tid]] = tiles[tid];
+    // 2. CTAs per class (thread 0).
+    if (tid == 0) {
+        // Relative cost of a tile: its 16 KB chunks, x1.25 for the two-query
+        // layout (a K ring of two chunks) and x2 for raw tiles (the same
+        // per-tile softmax and MMA work as a latent tile for 2/5 of the bytes,
+        // short segments with a Q load and an epilogue every few tiles).
+        const float w[3] = {float(tiles[0]) * a.lat_chunks, 1.25f * tiles[1] * a.lat_chunks, 2.0f * tiles[2] * 4};
+        // A raw CTA count given by the caller is kept; the other classes share
+        // the rest by weight, at least one CTA each and at most one per tile.
+        const bool fixed2 = a.raw_ctas > 0 && tiles[2] > 0;
+        int n[3] = {0, 0, fixed2 ? min(a.raw_ctas, tiles[2]) : 0};
+        const int avail = a.ctas - n[2];
+        const float wl = w[0] + w[1] + (fixed2 ? 0.f : w[2]);
+        for (int k = 0; k < 3; ++k)
+            if (!(fixed2 && k == 2) && tiles[k] > 0) n[k] = min(tiles[k], max(1, int(avail * w[k] / wl + 0.5f)));
+        for (;;) {                       // too many: take from the class with the most CTAs
+            if (n[0] + n[1] + n[2] <= a.ctas) break;
+            int kmax = -1;
+            for (int k = 0; k < 3; ++k)
+                if (!(fixed2 && k == 2) && n[k] > 1 && (kmax < 0 || n[k] > n[kmax])) kmax = k;
+            if (kmax < 0) break;
+            --n[kmax];
+        }
+        for (;;) {                       // too few: give to the class with the most work per CTA
+            if (n[0] + n[1] + n[2] >= a.ctas) break;
+            int kbest = -1;
+            float best = 0.f;
+            for (int k = 0; k < 3; ++k)
+                if (!(fixed2 && k == 2) && n[k] > 0 && n[k] < tiles[k] && w[k] / n[k] > best) {
+                    best = w[k] / n[k];
+                    kbest = k;
+                }
+            if (kbest < 0) break;
+            ++n[kbest];
+        }
+        int base = 0;
+        for (int k = 0; k < 3; ++k) {
+            P[L.hdr + 4 * k + 0] = n[k];
+            P[L.hdr + 4 * k + 1] = base;
+            P[L.hdr + 4 * k + 2] = nseg[k];
+            P[L.hdr + 4 * k + 3] = tiles[k];
+            base += n[k];
+        }
+    }
+    __syncthreads();
+    // 3. Pieces of every segment: zero for an empty one, else one plus the
+    // CTA boundaries strictly inside it.
+    for (int k = 0; k < 3; ++k) {
+        const int n = P[L.hdr + 4 * k], ns = nseg[k];
+        int32_t* start = P + L.seg_start[k];
+        int32_t* piece = P + L.seg_piece[k];
+        for (int s = tid; s < ns; s += blockDim.x) piece[s] = start[s + 1] > start[s] ? 1 : 0;
+        __syncthreads();
+        for (int i = 1 + tid; i < n; i += blockDim.x) {
+            const long long r = tc_cta_start(tiles[k], n, i);
+            const int s = tc_segment_of(start, ns, r);
+            if (r > start[s]) atomicAdd(piece + s, 1);
+        }
+        __syncthreads();
+        int carry_p = 0;
+        for (int s0 = 0; s0 < ns; s0 += blockDim.x) {
+            const int s = s0 + tid;
+            const int v = s < ns ? piece[s] : 0;
+            int total;
+            const int ex = block_exclusive_scan(v, &total, s_warp);
+            if (s < ns) piece[s] = carry_p + ex;
+            carry_p += total;
+        }
+        if (tid == 0) piece[ns] = carry_p;
+        __syncthreads();
+    }
+}
+
+}  // namespace slimkv

@@ -140,6 +140,29 @@ def rope_decode(q, k, cos, sin, query_positions, raw_indices, sink, history):
     return oq, ok
 
 
+def rope_rows(x, positions, cos, sin, counts=None, out=None):
+    """BF16-exact RoPE of ``x [B, T, H, D]`` rows at ``positions [B, T]``
+    (int32, per sequence), for ``t < counts[b]`` (``slimkv_rope_rows``);
+    returns ``out`` (a new ``[B, T, H, D]`` tensor when not given)."""
+    _bf16_cuda(x)
+    _require(x.dim() == 4 and x.stride(3) == 1, 'x must be [B, T, H, D] with a contiguous last dimension')
+    _require(positions.is_cuda and positions.dtype == torch.int32 and positions.stride(1) == 1 and
+             positions.shape[0] == x.shape[0] and positions.shape[1] >= x.shape[1], 'int32 positions [B, >= T]')
+    _require(cos.dtype == torch.float32 and cos.is_contiguous() and sin.is_contiguous(), 'fp32 tables')
+    if counts is not None:
+        _require(counts.is_cuda and counts.dtype == torch.int32 and counts.numel() == x.shape[0], 'int32 counts [B]')
+    if out is None:
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    _require(out.shape == x.shape and out.stride(3) == 1 and out.data_ptr() != x.data_ptr(), 'distinct out')
+    st = ctypes.c_int64 * 3
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.load().slimkv_rope_rows(
+            _ptr(x), st(*x.stride()[:3]), _ptr(out), st(*out.stride()[:3]), _ptr(positions), positions.stride(0),
+            _ptr(counts), x.shape[0], x.shape[1], x.shape[2], x.shape[3], _ptr(cos), _ptr(sin), cos.shape[0],
+            _stream()))
+    return out
+
+
 def merge(raw, raw_lse, latent, latent_lse):
     """LSE merge of BHQD bf16 outputs (``decode_ops.fused_merge`` contract)."""
     _bf16_cuda(raw, latent)
@@ -166,7 +189,7 @@ class LatentDecodeCall:
     def __init__(self, *, q, raw_k_rot, raw_v, lat_k=None, lat_v=None, raw_len, latent_len, qpos, uk, uv, cos, sin,
                  out, query_len=None, raw_k_pre=None, new_k=None, new_v=None, new_lat_k=None, new_lat_v=None,
                  uk_bias=None, uv_bias=None, scale=None, latent_len_max=0, raw_len_max=0, latent_splits=0,
-                 raw_splits=0, lat_pages=None, out_lse=None, latent_shard=False):
+                 raw_splits=0, lat_pages=None, out_lse=None, latent_shard=False, wait_limit_ns=0):
         """``lat_pages = (pages, layout, tables)`` replaces ``lat_k / lat_v``
         with the vLLM plugin's Beacon pages: ``pages [num_pages, >=
         layout.page_elements]`` bf16 (a ``pages.BeaconPageLayout`` layout) and
@@ -176,7 +199,11 @@ class LatentDecodeCall:
         each output row's log-sum-exp over this call's keys, so that shards of
         one sequence can be merged (:func:`merge_partials`);
         ``latent_shard=True`` marks a latent cache that does not hold this
-        step's Beacon row (no causal latent mask, no ``new_lat_*``)."""
+        step's Beacon row (no causal latent mask, no ``new_lat_*``).
+
+        ``wait_limit_ns`` bounds every pipeline wait of the attention kernel
+        (0: 2 s); a wait that runs out sets ``SLIMKV_DEVICE_TIMEOUT`` in the
+        device status word and the kernel returns early."""
         paged = lat_pages is not None
         _require(paged or (lat_k is not None and lat_v is not None), 'lat_k / lat_v or lat_pages required')
         _bf16_cuda(q, raw_k_rot, raw_v, uk, uv, *(() if paged else (lat_k, lat_v)))
@@ -184,8 +211,9 @@ class LatentDecodeCall:
         batch, length, heads, dim = q.shape
         kv_heads = raw_k_rot.shape[2]
         _require(raw_k_rot.shape[0] == batch and raw_k_rot.shape[3] == dim, 'raw cache shape')
-        _require(raw_k_rot.stride() == raw_v.stride() and raw_k_rot.stride(3) == 1 and raw_k_rot.stride(2) == dim,
-                 'raw caches must be token-major [B, cap, Hkv, D] with contiguous heads')
+        _require(raw_k_rot.stride() == raw_v.stride() and raw_k_rot.stride(3) == 1 and
+                 (raw_k_pre is None or raw_k_pre.stride() == raw_k_rot.stride()),
+                 'raw caches [B, cap, Hkv, D] (token-major, or a head-major view) need matching strides')
         if not paged:
             _require(lat_k.stride() == lat_v.stride() and lat_k.stride(2) == 1 and lat_v.stride(2) == 1,
                      'latent caches [B, cap, R] need matching strides and contiguous rows')
@@ -211,6 +239,7 @@ class LatentDecodeCall:
         a.raw_k_rot, a.raw_v = raw_k_rot.data_ptr(), raw_v.data_ptr()
         a.raw_k_pre = 0 if raw_k_pre is None else raw_k_pre.data_ptr()
         a.raw_stride_batch, a.raw_stride_token = raw_k_rot.stride(0), raw_k_rot.stride(1)
+        a.raw_stride_head = raw_k_rot.stride(2)
         a.raw_capacity = raw_k_rot.shape[1]
         if paged:
             a.lat_k = a.lat_v = 0
@@ -252,6 +281,7 @@ class LatentDecodeCall:
                      out_lse.shape == (batch, length, heads), 'out_lse must be contiguous fp32 [B, L, H]')
         a.out_lse = 0 if out_lse is None else out_lse.data_ptr()
         a.latent_shard = int(bool(latent_shard))
+        a.wait_limit_ns = int(wait_limit_ns)
         self.args = a
         self.device = q.device
         self._keep = (q, raw_k_rot, raw_v, raw_k_pre, lat_k, lat_v, lat_pages, raw_len, latent_len, query_len, qpos,

@@ -102,6 +102,58 @@ class RandomWeights:
         return total + sum(t.numel() * 2 for layer in self.layers for t in layer.values())
 
 
+class StateDictWeights:
+    """Runtime weights from a SlimKV Llama state dict.
+
+    Parameter names are the reference model's (``LlamaForCausalLM`` with
+    Beacon projections, slimkv/llama3/modeling_llama.py:181-277 and 351-382):
+    per layer ``self_attn.{q,k,v,o}_proj``, ``self_attn.beacon_q_proj``, the
+    K/V down-projections (``beacon_{k,v}_down_proj`` or a shared
+    ``beacon_kv_down_proj``), the up-projections ``beacon_{k,v}_up_proj``,
+    ``mlp.{gate,up,down}_proj`` and the two RMSNorms, plus the raw and Beacon
+    embeddings, the final norm and ``lm_head``.  The runtime's fused layout is
+    built from them: ``[q | k | v]`` for the raw row, ``[beacon_q | k_down |
+    v_down]`` for the Beacon row and ``[gate | up]``; biases are taken when the
+    state dict has them (``cfg.qkv_bias``).  Values may be numpy arrays or
+    tensors; they are stored as bf16 on ``device``."""
+
+    def __init__(self, cfg, state_dict, device):
+        def t(name):
+            return torch.as_tensor(state_dict[name]).to(device=device, dtype=torch.bfloat16).contiguous()
+
+        def opt(name):
+            return t(name) if name in state_dict else None
+
+        self.embed = t('model.embed_tokens.weight')
+        self.beacon_embed = t('model.beacon_embed_tokens.weight')
+        self.final_norm = t('model.norm.weight')
+        self.lm_head = t('lm_head.weight')
+        self.layers = []
+        for i in range(cfg.layers):
+            p = f'model.layers.{i}.'
+            a = p + 'self_attn.'
+            shared = a + 'beacon_kv_down_proj.weight' in state_dict
+            kd = t(a + ('beacon_kv_down_proj.weight' if shared else 'beacon_k_down_proj.weight'))
+            vd = kd if shared else t(a + 'beacon_v_down_proj.weight')
+            layer = dict(
+                norm1=t(p + 'input_layernorm.weight'), norm2=t(p + 'post_attention_layernorm.weight'),
+                w_raw=torch.cat([t(a + 'q_proj.weight'), t(a + 'k_proj.weight'), t(a + 'v_proj.weight')]),
+                w_beacon=torch.cat([t(a + 'beacon_q_proj.weight'), kd, vd]),
+                w_o=t(a + 'o_proj.weight'), uk=t(a + 'beacon_k_up_proj.weight'), uv=t(a + 'beacon_v_up_proj.weight'),
+                w_gate_up=torch.cat([t(p + 'mlp.gate_proj.weight'), t(p + 'mlp.up_proj.weight')]),
+                w_down=t(p + 'mlp.down_proj.weight'))
+            if cfg.qkv_bias:
+                zeros = torch.zeros(cfg.rank_k + cfg.rank_v, device=device, dtype=torch.bfloat16)
+                layer.update(b_raw=torch.cat([t(a + 'q_proj.bias'), t(a + 'k_proj.bias'), t(a + 'v_proj.bias')]),
+                             b_beacon=torch.cat([t(a + 'beacon_q_proj.bias'), zeros]),
+                             uk_bias=opt(a + 'beacon_k_up_proj.bias'), uv_bias=opt(a + 'beacon_v_up_proj.bias'))
+            self.layers.append(layer)
+
+    def nbytes(self):
+        total = sum(t.numel() * 2 for t in (self.embed, self.beacon_embed, self.lm_head))
+        return total + sum(t.numel() * 2 for layer in self.layers for t in layer.values() if t is not None)
+
+
 class LatentDecodeRuntime:
     """Batched decode over per-sequence compressed caches.
 
@@ -206,16 +258,26 @@ class LatentDecodeRuntime:
             self.tables = tables.to(device)
             self.num_pages = sum(need)
             self.lat_capacity = max(need) * slots
+        # HBM layout (streaming order of the attention kernel): each (sequence,
+        # KV head) holds its raw keys / values as one contiguous run of tokens
+        # (head-major [B, Hkv, cap, D], seen as a [B, cap, Hkv, D] view), and
+        # each sequence its latent K rows and latent V rows as two contiguous
+        # planes ([B, 2, cap, R]: lat_k = plane 0, lat_v = plane 1), so every
+        # 128-key tile the kernel fetches is one contiguous block of HBM.
         self.caches = []
+        rmax = max(cfg.rank_k, cfg.rank_v)
         for _ in range(cfg.layers):
-            raw_k = fill(B, self.raw_capacity, cfg.kv_heads, cfg.head_dim)
-            c = dict(raw_k_rot=raw_k, raw_k_pre=raw_k.clone() if raw_pre else None,
-                     raw_v=fill(B, self.raw_capacity, cfg.kv_heads, cfg.head_dim))
+            def raw():
+                return fill(B, cfg.kv_heads, self.raw_capacity, cfg.head_dim).transpose(1, 2)
+            raw_k = raw()
+            c = dict(raw_k_rot=raw_k, raw_k_pre=raw() if raw_pre else None, raw_v=raw())
+            if raw_pre:
+                c['raw_k_pre'].copy_(raw_k)
             if paged:
                 c['pages'] = fill(self.num_pages, self.layout.page_elements)
             else:
-                lat = fill(B, self.lat_capacity, cfg.rank_k + cfg.rank_v)
-                c.update(lat=lat, lat_k=lat[..., :cfg.rank_k], lat_v=lat[..., cfg.rank_k:])
+                lat = fill(B, 2, self.lat_capacity, rmax)
+                c.update(lat=lat, lat_k=lat[:, 0, :, :cfg.rank_k], lat_v=lat[:, 1, :, :cfg.rank_v])
             self.caches.append(c)
         # Per-sequence schedule counters and per-step metadata (device).
         i32 = dict(dtype=torch.int32, device=device)
@@ -235,7 +297,6 @@ class LatentDecodeRuntime:
         self.z = torch.zeros(B, 2, self.width, **bf)            # projection outputs per row
         self.attn = torch.zeros(B, 2, qd, **bf)
         self.logits = torch.zeros(B, cfg.vocab, dtype=torch.float32, device=device)
-        self.logits_bf16 = torch.zeros(B, cfg.vocab, **bf)
         z = self.z
         q = z[:, :, :qd].unflatten(-1, (cfg.heads, cfg.head_dim))          # [B, 2, H, D]
         lat_max = int(hist.max()) + per_window + 64
@@ -292,6 +353,62 @@ class LatentDecodeRuntime:
         self.graph = None
 
     # ------------------------------------------------------------------
+    def load_memory(self, layers, window_raw_indices=None):
+        """Fill the caches from the reference's latent Memory after a prefill.
+
+        ``layers[i]`` holds layer i's ``LlamaMemory`` activations
+        (slimkv/llama3/memory.py:219-278), batch-major with every sequence at
+        the history and tail this runtime was built with: ``sink_k/sink_v
+        [B, Hkv, S, D]`` and ``raw_k/raw_v [B, Hkv, T, D]`` (pre-RoPE, as the
+        reference stores them), ``hist_k/hist_v [B, N, R]`` (completed
+        windows) and ``win_k/win_v [B, n, R]`` (the open window's Beacons).
+        ``window_raw_indices`` (``[T]``) places the raw tail in the
+        interleaved window; keys are rotated at ``index + S + N``
+        (fa2_decode.py:127-131) with the BF16-exact rule of the fused decode
+        and stored in the native token-major layout."""
+        if self.layout is not None or self.split is not None:
+            raise ValueError('load_memory fills the dense, unsplit latent layout')
+        cfg, dev = self.cfg, self.device
+        hist, tail = self.history.cpu(), self.tail.cpu()
+        if not (hist == hist[0]).all() or not (tail == tail[0]).all():
+            raise ValueError('load_memory needs every sequence at the same history and tail')
+        N, T, S = int(hist[0]), int(tail[0]), cfg.sink
+        n_win = T // cfg.ratio
+        bf = dict(device=dev, dtype=torch.bfloat16)
+        idx = None
+        if T:
+            if window_raw_indices is None or len(window_raw_indices) != T:
+                raise ValueError('window_raw_indices must place every raw token of the open window')
+            idx = torch.as_tensor(window_raw_indices, dtype=torch.int64, device=dev)
+        B = self.batch
+        def rows(st, name, n, width, heads=None):
+            x = torch.as_tensor(st[name]).to(**bf)
+            if x.numel() != B * (heads or 1) * n * width:
+                raise ValueError(f'{name} must hold {B} x {heads or 1} x {n} x {width} values')
+            return x.reshape(B, heads, n, width) if heads else x.reshape(B, n, width)
+
+        for c, st in zip(self.caches, layers):
+            parts = [('sink_k', 'sink_v', S)] + ([('raw_k', 'raw_v', T)] if T else [])
+            keys = torch.cat([rows(st, k, n, cfg.head_dim, cfg.kv_heads) for k, _, n in parts], dim=2)
+            values = torch.cat([rows(st, v, n, cfg.head_dim, cfg.kv_heads) for _, v, n in parts], dim=2)
+            # The decode RoPE rotates key K-1 at the query position: append a
+            # dummy row there and drop it.
+            dummy = torch.zeros(B, cfg.kv_heads, 1, cfg.head_dim, **bf)
+            q = torch.zeros(B, cfg.heads, 1, cfg.head_dim, **bf)
+            qpos = torch.full((B, 1), S + N + T + n_win, dtype=torch.int64, device=dev)
+            _, k_rot = kernels.rope_decode(q, torch.cat([keys, dummy], dim=2), self.cos, self.sin, qpos, idx, S, N)
+            K = S + T
+            c['raw_k_rot'][:, :K].copy_(k_rot[:, :, :K].transpose(1, 2))
+            if c['raw_k_pre'] is not None:
+                c['raw_k_pre'][:, :K].copy_(keys.transpose(1, 2))
+            c['raw_v'][:, :K].copy_(values.transpose(1, 2))
+            lat_k, lat_v = rows(st, 'hist_k', N, cfg.rank_k), rows(st, 'hist_v', N, cfg.rank_v)
+            if n_win:
+                lat_k = torch.cat([lat_k, rows(st, 'win_k', n_win, cfg.rank_k)], 1)
+                lat_v = torch.cat([lat_v, rows(st, 'win_v', n_win, cfg.rank_v)], 1)
+            c['lat_k'][:, :N + n_win].copy_(lat_k)
+            c['lat_v'][:, :N + n_win].copy_(lat_v)
+
     def step_eager(self):
         """One decode step on the current stream (what the graph captures)."""
         cfg, w = self.cfg, self.w
@@ -326,8 +443,9 @@ class LatentDecodeRuntime:
             act = F.silu(gu[:, :I]) * gu[:, I:]
             x.add_((act @ layer['w_down'].t()).view(B, 2, H))
         final = F.rms_norm(x[:, 0], (H,), w.final_norm, cfg.rms_eps)
-        torch.mm(final, w.lm_head.t(), out=self.logits_bf16)
-        self.logits.copy_(self.logits_bf16)
+        # bf16 operands, the fp32 accumulator kept as the logits (no bf16
+        # rounding of the output: same weight traffic, exact to the GEMM).
+        torch.mm(final, w.lm_head.t(), torch.float32, out=self.logits)
         return self.logits
 
     def _reconstruct_attention(self, i):
@@ -348,9 +466,10 @@ class LatentDecodeRuntime:
             c['raw_k_pre'].index_put_((self.batch_index, row), k_new[:, :, 0])
         # The Beacon latent pair of rows that insert one (others rewrite their last row unchanged).
         lrow = (self.latent_len - 1).clamp_min(0).long()
-        width = cfg.rank_k + cfg.rank_v
-        new_lat = torch.where((self.query_len == 2)[:, None], z[:, 1, qd:qd + width], c['lat'][self.batch_index, lrow])
-        c['lat'].index_put_((self.batch_index, lrow), new_lat)
+        insert = (self.query_len == 2)[:, None]
+        for name, lo, hi in (('lat_k', qd, qd + cfg.rank_k), ('lat_v', qd + cfg.rank_k, qd + cfg.rank_k + cfg.rank_v)):
+            new_lat = torch.where(insert, z[:, 1, lo:hi], c[name][self.batch_index, lrow])
+            c[name].index_put_((self.batch_index, lrow), new_lat)
         self.recon[i](q_rot.transpose(1, 2), self.attn.view(B, 2, cfg.heads, cfg.head_dim))
 
     def capture(self, warmup=2):

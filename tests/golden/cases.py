@@ -124,3 +124,54 @@ def config1_layer(batch=1, length=1, history=2048, sink=4, tail=0, rank=320, see
                 hist_v=lat_v[:, :history], win_k=lat_k[:, history:], win_v=lat_v[:, history:],
                 batch=batch, length=length, history=history, sink=sink, tail=tail, rank=rank,
                 hidden_size=hidden, heads=heads, kv_heads=kv_heads, head_dim=head_dim, bias=bias)
+
+
+# A two-layer SlimKV Llama with the Llama-3.1-8B attention geometry (32 / 8
+# heads, head_dim 128, r4 ranks 320 / 320) but a small vocabulary, a narrow
+# MLP and a 64-token Beacon window, so that the reference model runs prefill
+# plus decode across a window rollover on the CPU in seconds.
+TINY_MODEL = dict(vocab=256, hidden=4096, intermediate=512, layers=2, heads=32, kv_heads=8, head_dim=128,
+                  rank=320, window=64, ratio=4, sink=4, theta=500000.0, rms_eps=1e-5,
+                  prefill=212, steps=60, seed=2024)
+
+
+def tiny_model_weights(spec=TINY_MODEL):
+    """bf16-representable weights (as fp32 arrays) of the tiny model, keyed by
+    the reference's parameter names; linear weights ~ N(0, 0.02) (lm_head
+    N(0, 0.008)), embeddings ~ N(0, 1), norm weights ~ 1 + N(0, 0.1)."""
+    import torch                      # exact round-to-nearest-even, faster than numpy for 139M values
+    rng = np.random.default_rng(spec['seed'])
+    H, I, V, R = spec['hidden'], spec['intermediate'], spec['vocab'], spec['rank']
+    qd, kvd = spec['heads'] * spec['head_dim'], spec['kv_heads'] * spec['head_dim']
+
+    def _bf16(x):
+        return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(torch.bfloat16).float().numpy()
+
+    def w(*shape, std=0.02):
+        return _bf16(rng.standard_normal(shape, dtype=np.float32) * np.float32(std))
+
+    out = {'model.embed_tokens.weight': w(V, H, std=1.0), 'model.beacon_embed_tokens.weight': w(1, H, std=1.0)}
+    for i in range(spec['layers']):
+        p = f'model.layers.{i}.'
+        out.update({
+            p + 'self_attn.q_proj.weight': w(qd, H), p + 'self_attn.k_proj.weight': w(kvd, H),
+            p + 'self_attn.v_proj.weight': w(kvd, H), p + 'self_attn.o_proj.weight': w(H, qd),
+            p + 'self_attn.beacon_q_proj.weight': w(qd, H),
+            p + 'self_attn.beacon_k_down_proj.weight': w(R, H), p + 'self_attn.beacon_k_up_proj.weight': w(kvd, R),
+            p + 'self_attn.beacon_v_down_proj.weight': w(R, H), p + 'self_attn.beacon_v_up_proj.weight': w(kvd, R),
+            p + 'mlp.gate_proj.weight': w(I, H), p + 'mlp.up_proj.weight': w(I, H), p + 'mlp.down_proj.weight': w(H, I),
+            p + 'input_layernorm.weight': _bf16(1 + rng.standard_normal(H, dtype=np.float32) * np.float32(0.1)),
+            p + 'post_attention_layernorm.weight': _bf16(1 + rng.standard_normal(H, dtype=np.float32) * np.float32(0.1))})
+    out['model.norm.weight'] = _bf16(1 + rng.standard_normal(H, dtype=np.float32) * np.float32(0.1))
+    # Logits of std ~0.5, the scale of the reference test suite's tiny model
+    # (hidden 32, weights N(0, 0.1)), so that a bf16 model's rounding noise
+    # stays well inside the 2e-2 logits bar.
+    out['lm_head.weight'] = w(V, H, std=0.008)
+    return out
+
+
+def tiny_model_tokens(spec=TINY_MODEL):
+    """Prefill token ids and the tokens fed at each decode step."""
+    rng = np.random.default_rng(spec['seed'] + 1)
+    return (rng.integers(0, spec['vocab'], size=spec['prefill']),
+            rng.integers(0, spec['vocab'], size=spec['steps']))

@@ -223,6 +223,67 @@ def gen_schedule(out, ref_tests):
         out[f'sched_{tag}_rawidx'] = np.array([np.pad(r, (0, 64 - len(r)), constant_values=-9) for r in raw_idx])
 
 
+def gen_model_decode(out, ref_tests):
+    """Prefill + decode of the reference's SlimKV Llama (``TINY_MODEL``).
+
+    The reference model (fast latent decode, ``beacon_decode_backend='fa2'``,
+    with the reference test suite's fp32 ``reference_forward`` standing in for
+    the FA2 kernel as its own tests do) prefills ``prefill`` tokens, and its
+    memory after prefill is recorded per layer (sinks, Beacon latents of the
+    completed windows, raw tail and window latents of the open window); then
+    ``steps`` single-token decode calls record fp32 logits.  The window is 64
+    tokens, so the decode crosses one window rollover and inserts a Beacon
+    every fourth step.
+    """
+    import torch
+    from unittest.mock import patch
+    sys.path.insert(0, str(ref_tests))
+    from test_llama_fa2_decode import reference_forward
+    from slimkv.llama3.configuration_llama import LlamaConfig
+    from slimkv.llama3.memory import LlamaMemory
+    from slimkv.llama3.modeling_llama import LlamaForCausalLM
+    from cases import LLAMA8B, TINY_MODEL, tiny_model_tokens, tiny_model_weights
+    s = TINY_MODEL
+    config = LlamaConfig(
+        vocab_size=s['vocab'], hidden_size=s['hidden'], intermediate_size=s['intermediate'],
+        num_hidden_layers=s['layers'], num_attention_heads=s['heads'], num_key_value_heads=s['kv_heads'],
+        max_position_embeddings=8192, rope_theta=s['theta'], rms_norm_eps=s['rms_eps'],
+        rope_scaling=dict(LLAMA8B['scaling'], rope_type='llama3'), beacon_param=['q', 'k', 'v'],
+        beacon_window=s['window'], beacon_stride=s['window'], beacon_ratio=[s['ratio']],
+        beacon_ratio_mix='sequence', beacon_sink_size=s['sink'], beacon_skip_rope_for_beacon_k=True,
+        beacon_k_compression='lowrank_svd', beacon_v_compression='lowrank_svd',
+        beacon_k_latent_head_dim_list=[s['rank'] // s['kv_heads']] * s['layers'],
+        beacon_v_latent_head_dim_list=[s['rank'] // s['kv_heads']] * s['layers'],
+        beacon_decode_backend='fa2', torch_dtype=torch.float32)
+    config._attn_implementation = 'eager'
+    model = LlamaForCausalLM(config)
+    model.memory = LlamaMemory(config)
+    weights = tiny_model_weights()
+    params = dict(model.named_parameters())
+    assert set(params) == set(weights), sorted(set(params) ^ set(weights))
+    with torch.no_grad():
+        for name, p in params.items():
+            p.copy_(_t(weights[name]))
+    model.eval()
+    prefill, steps = tiny_model_tokens()
+    logits = []
+    with torch.inference_mode(), patch('slimkv.llama3.fa2_decode.flash_forward', side_effect=reference_forward):
+        model(input_ids=_t(prefill)[None])
+        m = model.memory
+        for i in range(s['layers']):
+            (sk, sv), (hk, hv) = m.sink_activations[i], m.beacon_activations[i]
+            (rk, rv), (wk, wv) = m.raw_activations[i], m.window_beacon_activations[i]
+            out[f'model_l{i}_sink_k'], out[f'model_l{i}_sink_v'] = sk[0].numpy(), sv[0].numpy()
+            out[f'model_l{i}_hist_k'], out[f'model_l{i}_hist_v'] = hk[0, 0].numpy(), hv[0, 0].numpy()
+            out[f'model_l{i}_raw_k'], out[f'model_l{i}_raw_v'] = rk[0].numpy(), rv[0].numpy()
+            out[f'model_l{i}_win_k'], out[f'model_l{i}_win_v'] = wk[0, 0].numpy(), wv[0, 0].numpy()
+        out['model_window_raw_indices'] = m._window_raw_indices.numpy()
+        out['model_remainder'] = np.array(m._interleave_remainder)
+        for tok in steps:
+            logits.append(model(input_ids=torch.tensor([[int(tok)]])).logits[0, -1].float().numpy())
+    out['model_logits'] = np.stack(logits)
+
+
 def gen_interleave(out):
     """Prefill interleave roles from the reference ``Memory._step``."""
     import torch
@@ -456,7 +517,12 @@ def main():
     gen_decode(out, 'small_bias', config1_layer(batch=2, length=2, history=40, tail=11, rank=16,
                                                 hidden=256, heads=8, kv_heads=2, head_dim=32,
                                                 bias=True, seed_w=5, seed_h=6))
+    gen_decode(out, 'bias32', config1_layer(batch=2, length=2, history=300, tail=11, bias=True, seed_w=7,
+                                            seed_h=8))
+    gen_decode(out, 'qwen', config1_layer(batch=1, length=2, history=200, tail=5, rank=512, hidden=5120,
+                                          heads=40, kv_heads=8, bias=True, seed_w=9, seed_h=10))
     gen_schedule(out, ref / 'tests')
+    gen_model_decode(out, ref / 'tests')
     gen_interleave(out)
     gen_pages(out)
     gen_splits(out)

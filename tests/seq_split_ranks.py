@@ -43,8 +43,9 @@ def copy_shard(full, split):
     for cf, cs in zip(full.caches, split.caches):
         for b, (off, n) in enumerate(zip(offsets, rows)):
             if sp['last']:
-                n = min(cs['lat'].shape[1], cf['lat'].shape[1] - off)
-            cs['lat'][b, :n].copy_(cf['lat'][b, off:off + n])
+                n = min(cs['lat_k'].shape[1], cf['lat_k'].shape[1] - off)
+            for key in ('lat_k', 'lat_v'):
+                cs[key][b, :n].copy_(cf[key][b, off:off + n])
         if sp['last']:
             for key in ('raw_k_rot', 'raw_v'):
                 cs[key].copy_(cf[key])

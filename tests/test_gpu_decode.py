@@ -31,7 +31,7 @@ def tables(positions=16384):
     return _TABLES[positions]
 
 
-def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False, stale=0.0, paged=False):
+def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False, stale=0.0, paged=False, wait_limit_ns=0):
     """Stage the caches without this step's entries, run the fused step.
 
     Cache rows past each sequence's staged length hold ``stale``.  With
@@ -93,7 +93,7 @@ def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False, stale=0.0, paged=
         P.beacon_append(backing, layout, block_tables, np.zeros(B, np.int32), t['lat_k'], t['lat_v'])
         t['lat_pages'] = (backing, layout, block_tables)
         t['lat_k_dense'], t['lat_v_dense'] = t.pop('lat_k'), t.pop('lat_v')
-    kernels.latent_decode(**{k: v for k, v in t.items() if not k.endswith('_dense')})
+    kernels.latent_decode(**{k: v for k, v in t.items() if not k.endswith('_dense')}, wait_limit_ns=wait_limit_ns)
     torch.cuda.synchronize()
     if paged:
         # The appended Beacon rows, read back from the pages.
@@ -137,6 +137,24 @@ def check(c, query_len, t):
             assert_bits_equal(t['lat_k'][b, n], c['lat_k'][b, n])
             assert_bits_equal(t['lat_v'][b, n], c['lat_v'][b, n])
     return max(errs)
+
+
+def test_a_wait_that_runs_out_reports_timeout_and_the_context_stays_usable():
+    """Every pipeline wait of the attention kernel is bounded.  With a bound
+    of 1 ns the waits run out while copies are still in flight (the producer
+    finds its rings full at once): the kernel must set
+    SLIMKV_DEVICE_TIMEOUT, drain its copies and MMAs, free its tensor memory
+    and return — no fault, no hang — and the next call, with the default
+    bound, must match the oracle on the same context."""
+    from slimkv_b200 import _lib
+    c = decode_case(91, batch=3, length=2, history=2048, tail=300, ragged=True)
+    query_len = np.array([2, 1, 2])
+    _lib.device_status(clear=True)
+    run_fused(c, query_len, wait_limit_ns=1)
+    assert _lib.device_status(clear=True) & _lib.DEVICE_TIMEOUT
+    t = run_fused(c, query_len)
+    assert _lib.device_status(clear=True) == 0
+    check(c, query_len, t)
 
 
 @pytest.mark.parametrize('stale', [float('nan'), float('inf')])
