@@ -368,6 +368,17 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
         return r < nrows && b < a.batch && l < (a.qlens ? a.qlens[b] : a.length);
     };
 
+    // 0. Each row's partial ranges (latent, raw) once, before any other
+    //    load depends on them.
+    __shared__ int s_parts[16][4];
+    if (tid < 16) {
+        int b, l, h, rr, p0 = 0, n = 0, q0 = 0, m = 0;
+        if (row_info(tid, b, l, h, rr)) {
+            lat_parts(a, b, p0, n);
+            raw_parts(a, b, g, q0, m);
+        }
+        s_parts[tid][0] = p0; s_parts[tid][1] = n; s_parts[tid][2] = q0; s_parts[tid][3] = m;
+    }
     // 1. U_v[g] (rows d, columns c) -> shared, asynchronously; zero columns
     //    past the rank.
     const int units = rvp / 8;
@@ -380,6 +391,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
     cp_async_commit();
     // Rows of the A operand that no query fills stay zero.
     for (int i = tid; i < 2 * 16 * rvp / 8; i += 256) reinterpret_cast<uint4*>(s_hi)[i] = make_uint4(0, 0, 0, 0);
+    __syncthreads();
     // 2. Split weights and LSEs per row.
     for (int r = warp; r < 16; r += 8) {
         int b, l, h, rr;
@@ -387,11 +399,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
         float lse_br[2];
 #pragma unroll
         for (int br = 0; br < 2; ++br) {
-            int p0 = 0, nsp = 0;
-            if (valid) {
-                if (br) raw_parts(a, b, g, p0, nsp);
-                else lat_parts(a, b, p0, nsp);
-            }
+            const int p0 = s_parts[r][2 * br], nsp = valid ? s_parts[r][2 * br + 1] : 0;
             float my[kMergeMaxSplits / 32];
             float m = -INFINITY;
 #pragma unroll
@@ -443,8 +451,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
             int b, l, h, rr;
             if (!row_info(r, b, l, h, rr) || c >= a.lat_width) continue;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            int p0, nsp;
-            lat_parts(a, b, p0, nsp);
+            const int p0 = s_parts[r][0], nsp = s_parts[r][1];
             const float* src = a.lat_o + ((int64_t)p0 * a.lat_rows + l * a.heads + h) * a.lat_width + c;
             const float* w = s_w + r * kMergeMaxSplits;
             int s = 0;
@@ -479,8 +486,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
             int b, l, h, rr;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             if (row_info(r, b, l, h, rr)) {
-                int p0, nsp;
-                raw_parts(a, b, g, p0, nsp);
+                const int p0 = s_parts[r][2], nsp = s_parts[r][3];
                 const float* src = a.raw_o + ((int64_t)p0 * a.raw_rows + rr) * a.dim + c;
                 const float* w = s_w + (16 + r) * kMergeMaxSplits;
                 int s = 0;

@@ -52,7 +52,7 @@ def test_config2_shape_full_plan():
 def test_config5_shape_qwen_rank512():
     c = decode_case(2005, batch=2, length=2, history=32768, tail=700, heads=40, kv_heads=8, rk=512, rv=512, bias=True)
     query_len = np.array([2, 1])
-    check(c, query_len, run_fused(c, query_len, fp32=True))
+    check(c, query_len, run_fused(c, query_len, fp32=True, positions=65536), positions=65536)
 
 
 def test_config3_shape_paged_r8_large_batch():

@@ -31,7 +31,8 @@ def tables(positions=16384):
     return _TABLES[positions]
 
 
-def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False, stale=0.0, paged=False, wait_limit_ns=0):
+def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False, stale=0.0, paged=False, wait_limit_ns=0,
+              positions=16384):
     """Stage the caches without this step's entries, run the fused step.
 
     Cache rows past each sequence's staged length hold ``stale``.  With
@@ -39,7 +40,7 @@ def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False, stale=0.0, paged=
     48 slots per page, disjoint shuffled block tables) instead.
     """
     from slimkv_b200 import kernels
-    cos, sin, cos_t, sin_t = tables()
+    cos, sin, cos_t, sin_t = tables(positions)
     B, L, H, D = c['q'].shape
     Hkv, rk, rv = c['kv_heads'], c['rk'], c['rv']
     n_raw, n_lat = c['n_raw'], c['n_lat']
@@ -105,9 +106,9 @@ def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False, stale=0.0, paged=
     return t
 
 
-def oracle_rows(c, query_len):
+def oracle_rows(c, query_len, positions=16384):
     """Per-row oracle results (each row with its own query length)."""
-    cos, sin, _, _ = tables()
+    cos, sin, _, _ = tables(positions)
     outs = []
     for b in range(c['q'].shape[0]):
         L = int(query_len[b])
@@ -120,8 +121,8 @@ def oracle_rows(c, query_len):
     return outs
 
 
-def check(c, query_len, t):
-    refs = oracle_rows(c, query_len)
+def check(c, query_len, t, positions=16384):
+    refs = oracle_rows(c, query_len, positions)
     errs = []
     for b, r in enumerate(refs):
         L = int(query_len[b])
