@@ -69,22 +69,26 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 // Wait for the given phase parity; gives up after `limit_ns` and returns
-// false (the caller reports SLIMKV_DEVICE_TIMEOUT and winds down).
+// false (the caller reports SLIMKV_DEVICE_TIMEOUT and winds down).  Each
+// try_wait may suspend the thread until the phase completes, for at most a
+// hint no longer than the bound (1 ms at most), so the bound is checked at
+// least that often and a short bound runs out on time.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           uint64_t limit_ns = 2000000000ull) {
     const uint32_t addr = smem_u32(bar);
+    const uint32_t hint = limit_ns < 1000000ull ? uint32_t(limit_ns) : 1000000u;
     uint32_t ok = 0;
     uint64_t start = 0;
     for (int i = 0;; ++i) {
         asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
             " selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(ok)
-            : "r"(addr), "r"(parity)
+            : "r"(addr), "r"(parity), "r"(hint)
             : "memory");
         if (ok) return true;
         if (i == 0) start = global_timer_ns();
-        else if ((i & 63) == 0 && global_timer_ns() - start > limit_ns) return false;
+        else if (global_timer_ns() - start > limit_ns) return false;
     }
 }
 

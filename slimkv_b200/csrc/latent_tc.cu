@@ -38,9 +38,9 @@
 // stores the normalised rows directly (a warp writes 32 consecutive floats of
 // a row).
 //
-// Warp roles (7 warps): 0 = TMA producer, 1 = P.V issuer, 2 = TMEM allocator
-// and S issuer, 3-6 = softmax / epilogue (TMEM lane quarters 3, 0, 1, 2).  No
-// cluster multicast.  Every wait is bounded: on expiry the CTA reports
+// Warp roles (8 warps): 0 = TMA producer of Q and K, 1 = P.V issuer, 2 = TMEM
+// allocator and S issuer, 3-6 = softmax / epilogue (TMEM lane quarters 3, 0,
+// 1, 2), 7 = TMA producer of V.  No cluster multicast.  Every wait is bounded: on expiry the CTA reports
 // SLIMKV_DEVICE_TIMEOUT, drains its copies and MMAs (bounded), frees TMEM and
 // returns.
 #include <algorithm>
@@ -55,7 +55,8 @@ namespace slimkv {
 namespace {
 
 constexpr int kKeys = 128;
-constexpr int kThreads7 = 224;
+constexpr int kThreads8 = 256;
+constexpr int kProducerV = 7;                        // warp of the V producer
 constexpr int kMaxChunks = 5;                        // ranks <= 320
 constexpr int kKRingMax = 5;
 constexpr uint32_t kChunkBytes = 128 * 128;          // [128 keys x 64 bf16], 128-byte swizzle
@@ -186,7 +187,7 @@ __device__ __forceinline__ void next_piece(const Range& R, int k, int& s, long l
 
 // Kernel parameters: the K / V / Q maps of both branches (latent, raw), both
 // jobs, the plan and its layout.
-__global__ void __launch_bounds__(kThreads7, 1)
+__global__ void __launch_bounds__(kThreads8, 1)
 decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constant__ CUtensorMap lvmap,
                  const __grid_constant__ CUtensorMap lqmap, const __grid_constant__ CUtensorMap rkmap,
                  const __grid_constant__ CUtensorMap rvmap, const __grid_constant__ CUtensorMap rqmap,
@@ -249,7 +250,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
     if (J.q_rows) {
         // Row-mode Q fills only the query rows of each chunk; the rest must
         // read as zero in every piece.
-        for (int i = tid; i < LY.qbufs * int(LY.qbytes / 16); i += kThreads7)
+        for (int i = tid; i < LY.qbufs * int(LY.qbytes / 16); i += kThreads8)
             reinterpret_cast<uint4*>(smem + LY.off_q)[i] = make_uint4(0, 0, 0, 0);
         fence_async_shared();
     }
@@ -280,14 +281,17 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
     const uint32_t sbase = smem_u32(smem);
     const int vblocks = (vc + 1) / 2;
 
-    if (warp == 0 && lane == 0) {
-        // ---- TMA producer: Q of the next piece, then K, then V ----
-        // Paged K/V: the page of each box of one tile, cached per stream.
+    if ((warp == 0 || warp == kProducerV) && lane == 0) {
+        // ---- TMA producers: warp 0 streams each piece's Q then its K chunks,
+        // warp 7 its V chunks.  Each waits (blocking, bounded) for the slot
+        // its next copy needs, so the V stream never queues behind K
+        // prefetches and neither thread polls.
+        const bool kq = warp == 0;
+        // Paged K/V: the page of each box of one tile, cached.
         struct PageCache { int b = -1, tile = -1; int page[kKeys / 16]; };
-        PageCache kpc, vpc;
+        PageCache pc;
         const int boxes = J.table ? kKeys / J.box_rows : 1;
-        auto load_chunk = [&](uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int col, const Piece& p, int tile,
-                              PageCache& pc) {
+        auto load_chunk = [&](uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int col, const Piece& p, int tile) {
             if (!J.table) {
                 tma_load_4d(dst, map, bar, col, p.g, tile * kKeys, p.b);
                 return;
@@ -311,22 +315,21 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                             pc.page[i]);
             }
         };
-        // Three cursors walk the same pieces: Q (one load per piece), K and V
-        // (chunk counters; the walk advances when a piece's tiles run out).
-        int qs = R.s0, ks = R.s0, vs = R.s0;
-        long long qpos = R.r0, kpos = R.r0, vpos = R.r0;
-        int qk = 0, kk = 0, vk = 0;                          // pieces entered by each cursor
-        Piece qp{}, kp{}, vp{};
-        int k_end = 0, v_end = 0;                            // CTA tile where the current piece ends
-        int nk = 0, nv = 0;
-        uint64_t idle_since = 0;
-        while ((qpos < R.r1 || nk < total_k || nv < total_v) && !ms->abort) {
-            bool progressed = false;
-            if (qpos < R.r1 && (qk < LY.qbufs || mbar_test(&ms->qempty[qk % LY.qbufs], ((qk / LY.qbufs) - 1) & 1))) {
-                next_piece(R, qk, qs, qpos, J.kv_heads, qp);
-                const int qb = qk % LY.qbufs;
+        int s = R.s0;
+        long long pos = R.r0;
+        bool ok = true;
+        int j = 0;                                           // CTA tile
+        for (int k = 0; pos < R.r1 && ok; ++k) {
+            Piece p;
+            next_piece(R, k, s, pos, J.kv_heads, p);
+            if (kq) {
+                // Q of the piece, into a buffer S has finished with.
+                const int qb = k % LY.qbufs;
+                if (k >= LY.qbufs &&
+                    !(ok = wait_or_abort(&ms->qempty[qb], ((k / LY.qbufs) - 1) & 1, ms, J.status, wait_ns)))
+                    break;
                 uint8_t* qdst = smem + LY.off_q + qb * LY.qbytes;
-                const int nq = J.qlens ? J.qlens[qp.b] : J.length;
+                const int nq = J.qlens ? J.qlens[p.b] : J.length;
                 if (J.q_rows) {
                     // The group's query heads of query l -> rows 32 l + j (the
                     // other rows of the chunk stay zero from the start).
@@ -334,7 +337,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     for (int c = 0; c < kc; ++c)
                         for (int l = 0; l < nq; ++l)
                             tma_load_4d(qdst + c * kQChunkBytes + l * 32 * 128, qmap, &ms->qfull[qb], c * 64, 0,
-                                        qp.g * J.group, qp.b * J.length + l);
+                                        p.g * J.group, p.b * J.length + l);
                 } else {
                     // [hi | lo] x 32 * nq rows: one 64-row box per chunk for
                     // nq = 1, hi and lo boxes for nq = 2.
@@ -342,45 +345,28 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     for (int c = 0; c < kc; ++c)
                         for (int hl = 0; hl < nq; ++hl)
                             tma_load_4d(qdst + (hl * kMaxChunks + c) * kQChunkBytes, qmap, &ms->qfull[qb], c * 64, 0,
-                                        hl * 64, qp.b);
+                                        hl * 64, p.b);
                 }
-                ++qk;
-                progressed = true;
-            } else if (nk < total_k && (nk < kring || mbar_test(&ms->kempty[nk % kring], ((nk / kring) - 1) & 1))) {
-                const int T = nk / kc, c = nk - T * kc;
-                if (T >= k_end) {
-                    next_piece(R, kk++, ks, kpos, J.kv_heads, kp);
-                    k_end = T + (kp.t1 - kp.t0);
-                }
-                const int tile = kp.t1 - (k_end - T);
-                const int slot = nk % kring;
-                mbar_expect_tx(&ms->kfull[slot], kChunkBytes);
-                load_chunk(smem + LY.off_k + slot * kChunkBytes, kmap, &ms->kfull[slot], c * 64, kp, tile, kpc);
-                ++nk;
-                progressed = true;
-            } else if (nv < total_v && mbar_test(&ms->vempty[v_slot(nv / vc, nv % vc)], (v_use(nv / vc) - 1) & 1)) {
-                const int T = nv / vc, c = nv - T * vc;
-                if (T >= v_end) {
-                    next_piece(R, vk++, vs, vpos, J.kv_heads, vp);
-                    v_end = T + (vp.t1 - vp.t0);
-                }
-                const int tile = vp.t1 - (v_end - T);
-                const int slot = v_slot(T, c);
-                mbar_expect_tx(&ms->vfull[slot], kChunkBytes);
-                load_chunk(smem + slot * kChunkBytes, vmap, &ms->vfull[slot], J.v_col + c * 64, vp, tile, vpc);
-                ++nv;
-                progressed = true;
             }
-            if (progressed) {
-                idle_since = 0;
-                continue;
-            }
-            __nanosleep(32);
-            if (idle_since == 0) {
-                idle_since = global_timer_ns();
-            } else if (global_timer_ns() - idle_since > wait_ns) {
-                ms->abort = 1;
-                report(J.status, SLIMKV_DEVICE_TIMEOUT);
+            for (int t = p.t0; t < p.t1 && ok; ++t, ++j) {
+                if (kq) {
+                    for (int c = 0; c < kc; ++c) {
+                        const int n = j * kc + c, slot = n % kring;
+                        if (n >= kring &&
+                            !(ok = wait_or_abort(&ms->kempty[slot], ((n / kring) - 1) & 1, ms, J.status, wait_ns)))
+                            break;
+                        mbar_expect_tx(&ms->kfull[slot], kChunkBytes);
+                        load_chunk(smem + LY.off_k + slot * kChunkBytes, kmap, &ms->kfull[slot], c * 64, p, t);
+                    }
+                } else {
+                    for (int c = 0; c < vc; ++c) {
+                        const int slot = v_slot(j, c), use = v_use(j);
+                        if (use > 0 && !(ok = wait_or_abort(&ms->vempty[slot], (use - 1) & 1, ms, J.status, wait_ns)))
+                            break;
+                        mbar_expect_tx(&ms->vfull[slot], kChunkBytes);
+                        load_chunk(smem + slot * kChunkBytes, vmap, &ms->vfull[slot], J.v_col + c * 64, p, t);
+                    }
+                }
             }
         }
     } else if (warp == 2 && lane == 0) {
@@ -476,7 +462,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
             }
         }
         umma_commit(&ms->final_mma);
-    } else if (warp >= 3) {
+    } else if (warp >= 3 && warp <= 6) {
         // ---- softmax and epilogue: thread <-> key (TMEM lane) ----
         const int quarter = warp & 3;
         const int t_local = 32 * quarter + lane;
@@ -818,7 +804,7 @@ int launch_decode_tc(const TcLaunch& L, cudaStream_t stream) {
         configured[dev] = true;
     }
     const TcPlanLayout PL = tc_plan_layout(L.batch, L.kv_heads);
-    decode_tc_kernel<<<L.ctas, kThreads7, kSmemBytes, stream>>>(lk, lv, lq, rk, rv, rq, jl, jr, L.plan, PL,
+    decode_tc_kernel<<<L.ctas, kThreads8, kSmemBytes, stream>>>(lk, lv, lq, rk, rv, rq, jl, jr, L.plan, PL,
                                                                  L.lat_pieces);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "decode tc launch failed: %s", cudaGetErrorString(e));
