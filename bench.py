@@ -12,17 +12,19 @@ Prints one JSON line: ``value`` = decode tokens/s over all ranks (device
 time, inputs resident), ``e2e`` = the same through the public runtime API
 with per-step host->device token upload and device->host read of the
 sampled tokens, ``roofline`` for the fused latent attention step (HBM bytes
-per launch / CUDA-event time), ``cpu_baseline`` = the CPU restatement of the
-same decode step on this host's cores.
+per launch / CUDA-event time), ``cpu_baseline`` = one whole decode step of
+the reference's own CPU path on this host's cores.
 
 ``prefill`` (one window of one layer) times the
 role-selected window projection with the Beacon-page append against the
 reference's own recipe run through torch/cuBLAS on the same GPU; its
 roofline is tensor-bound (useful FLOPs / time vs the measured bf16 peak).
 
-``--impl reference`` times the CPU restatement of the reference's eager
-decode (the only reference implementation of this path that runs here) on
-the same workload and metric.
+``--impl reference`` times the reference's own eager decode
+(``fa2_decode.decode`` with ``eager_forward``, imported from the package
+installed under ``baseline/_ref``) with its Llama modules, whole 32-layer
+steps on the host's cores, on the same workload and metric; without that
+install it times the numpy restatement in ``oracle/cpu_decode.py``.
 """
 import argparse
 import json
@@ -197,31 +199,198 @@ def traffic_per_launch(kernel_bytes):
     return (d['dram_read_bytes'] + d['dram_write_bytes']) * kernel_bytes / d['algorithmic_bytes']
 
 
-def cpu_baseline(batch, steps_hint=None):
-    from oracle.cpu_decode import time_decode_step
-    seconds, threads, sample = time_decode_step(batch=batch, history=HISTORY)
-    return {'value': batch / seconds, 'unit': UNIT, 'cores': threads, 'kind': 'port', 'sample': sample}
+REF_DIR = os.path.join(ROOT, 'baseline', '_ref')
+
+
+def _cpu_model():
+    try:
+        with open('/proc/cpuinfo') as f:
+            for line in f:
+                if line.startswith('model name'):
+                    return line.split(':', 1)[1].strip()
+    except OSError:
+        pass
+    return 'unknown'
+
+
+def _reference_package():
+    """Import the reference package installed under ``baseline/_ref`` (``pip
+    install --no-deps --target``).  It imports two packages at load time that
+    this path never uses (``pytz`` for a version check, ``accelerate`` for a
+    type); minimal stand-ins are written to a temporary directory when they
+    are absent.  Returns the modules, or raises ImportError."""
+    import importlib.util
+    if not os.path.isdir(os.path.join(REF_DIR, 'slimkv')):
+        raise ImportError('baseline/_ref holds no installed slimkv package')
+    stubs = tempfile.mkdtemp(prefix='slimkv_stubs_')
+    if importlib.util.find_spec('pytz') is None:
+        os.makedirs(os.path.join(stubs, 'pytz'))
+        with open(os.path.join(stubs, 'pytz', '__init__.py'), 'w') as f:
+            f.write('__version__ = "2024.1"\n')
+    if importlib.util.find_spec('accelerate') is None:
+        os.makedirs(os.path.join(stubs, 'accelerate'))
+        with open(os.path.join(stubs, 'accelerate', '__init__.py'), 'w') as f:
+            f.write('__version__ = "1.0.0"\nclass Accelerator:\n    pass\n')
+    sys.path[:0] = [stubs, REF_DIR]
+    from slimkv.llama3 import fa2_decode
+    from slimkv.llama3.configuration_llama import LlamaConfig
+    from slimkv.llama3.latent_decode import eager_forward
+    from slimkv.llama3.memory import ReconstructionCache
+    from slimkv.llama3.modeling_llama import LlamaAttention, LlamaMLP, LlamaRMSNorm
+    return dict(fa2_decode=fa2_decode, LlamaConfig=LlamaConfig, eager_forward=eager_forward,
+                ReconstructionCache=ReconstructionCache, LlamaAttention=LlamaAttention, LlamaMLP=LlamaMLP,
+                LlamaRMSNorm=LlamaRMSNorm)
+
+
+class ReferenceDecodeStep:
+    """One decode step of the workload through the reference's own modules
+    on the CPU: per layer ``LlamaRMSNorm``, ``fa2_decode.decode(...,
+    forward=eager_forward)`` (the reference's eager latent decode with its
+    ``o_proj``), the residual, ``LlamaRMSNorm`` and ``LlamaMLP``; then the
+    final norm and the vocabulary projection of the raw rows.  fp32, the
+    reference's CPU dtype.  The reference batches only equal-length caches,
+    so each sequence (its own raw tail) is its own ``decode`` call; norms and
+    MLP run on the whole batch.  One layer's weights serve all 32 layers
+    (32 distinct fp32 layers do not fit host memory); every layer's
+    arithmetic runs.  Caches: N(0, 1.3^2), weights the modules' own init."""
+
+    LAYERS, VOCAB, HIDDEN, SINK, RANK, KV_HEADS, HEAD_DIM = 32, 128256, 4096, 4, 320, 8, 128
+
+    def __init__(self, m, batch, history, seed=1234):
+        import numpy as np
+        import torch
+        self.m, self.torch = m, torch
+        R, Hkv, D, S = self.RANK, self.KV_HEADS, self.HEAD_DIM, self.SINK
+        cfg = m['LlamaConfig'](
+            vocab_size=self.VOCAB, hidden_size=self.HIDDEN, intermediate_size=14336, num_hidden_layers=self.LAYERS,
+            num_attention_heads=32, num_key_value_heads=Hkv, max_position_embeddings=131072, rope_theta=500000.0,
+            rope_scaling=dict(factor=8.0, low_freq_factor=1.0, high_freq_factor=4.0,
+                              original_max_position_embeddings=8192, rope_type='llama3'),
+            beacon_param=['q', 'k', 'v'], beacon_window=1024, beacon_stride=1024, beacon_ratio=[4],
+            beacon_ratio_mix='sequence', beacon_sink_size=S, beacon_skip_rope_for_beacon_k=True,
+            beacon_k_compression='lowrank_svd', beacon_v_compression='lowrank_svd',
+            beacon_k_latent_head_dim_list=[R // Hkv] * self.LAYERS,
+            beacon_v_latent_head_dim_list=[R // Hkv] * self.LAYERS, beacon_decode_backend='latent',
+            torch_dtype=torch.float32)
+        cfg._attn_implementation = 'eager'
+        with torch.no_grad():
+            self.attn = m['LlamaAttention'](cfg, layer_idx=0).eval()
+            self.mlp = m['LlamaMLP'](cfg).eval()
+            self.norm1, self.norm2, self.norm_f = (m['LlamaRMSNorm'](self.HIDDEN) for _ in range(3))
+            self.lm_head = torch.empty(self.VOCAB, self.HIDDEN).normal_(0, 0.02)
+        gen = torch.Generator().manual_seed(seed)
+        tails = np.random.default_rng(seed).integers(0, 1024, size=batch)     # the GPU arm's tails
+        self.seqs = []
+        for t in map(int, tails):
+            nw = t // 4
+            rnd = lambda *shape: torch.randn(*shape, generator=gen) * 1.3
+            raw_idx = torch.arange(t) + torch.arange(t) // 4 if t else None
+            win_roles = torch.zeros(t + nw, dtype=torch.bool)
+            win_roles[4::5] = True
+            size = int((t + 1) % 4 == 0)
+            roles = torch.zeros(t + nw + 1 + size, dtype=torch.long)
+            roles[:t + nw] = win_roles.long()
+            roles[-1] = size
+
+            def cache(kind):
+                return m['ReconstructionCache'](rnd(1, Hkv, S, D), rnd(1, 1, history, R),
+                                                rnd(1, Hkv, t, D) if t else None, rnd(1, 1, nw, R) if nw else None,
+                                                win_roles if t else None, Hkv, D, kind, raw_idx)
+            positions = torch.arange(S + history + t + nw + 1 + size)[None]
+            self.seqs.append((cache('k'), cache('v'), size, roles, positions))
+        self.x = torch.randn(batch, 2, self.HIDDEN, generator=gen)
+
+    def layer(self, x):
+        fa2 = self.m['fa2_decode']
+        y = x.clone()
+        for b, (pk, pv, size, roles, positions) in enumerate(self.seqs):
+            h = self.norm1(x[b:b + 1, :size + 1])
+            out, _, _ = fa2.decode(self.attn, h, positions, (pk, pv, size, roles), forward=self.m['eager_forward'])
+            y[b:b + 1, :size + 1] += out
+        return y + self.mlp(self.norm2(y))
+
+    def step(self, layers=None):
+        with self.torch.inference_mode():
+            x = self.x
+            for _ in range(layers or self.LAYERS):
+                x = self.layer(x)
+            return self.norm_f(x[:, 0]) @ self.lm_head.T
+
+
+def _reference_or_port(batch):
+    """(runner, kind, description): the reference's own decode step when its
+    package is installed under baseline/_ref, else the numpy restatement
+    (pinned to the reference's decode goldens)."""
+    try:
+        ref = ReferenceDecodeStep(_reference_package(), batch, HISTORY)
+        return ref, 'reference', ('reference SlimKV (baseline/_ref) fa2_decode.decode(forward=eager_forward) + '
+                                  'LlamaRMSNorm/LlamaMLP modules, fp32 torch on CPU')
+    except ImportError as e:
+        return None, 'port', f'numpy restatement of the reference decode ({e})'
+
+
+def cpu_baseline(batch):
+    import torch
+    ref, kind, what = _reference_or_port(batch)
+    if ref is None:
+        from oracle.cpu_decode import time_decode_step
+        seconds, threads, sample = time_decode_step(batch=batch, history=HISTORY)
+        return {'value': batch / seconds, 'unit': UNIT, 'cores': threads, 'kind': 'port', 'sample': sample,
+                'cpu': _cpu_model()}
+    ref.step(layers=1)                                    # warm-up
+    t0 = time.perf_counter()
+    ref.step()
+    seconds = time.perf_counter() - t0
+    return {'value': batch / seconds, 'unit': UNIT, 'cores': torch.get_num_threads(), 'kind': kind,
+            'sample': f'one whole decode step (32 layers + vocab projection), batch {batch}; {what}',
+            'cpu': _cpu_model()}
 
 
 def run_reference(args):
+    """The reference arm: the reference's own CPU decode on this host, the
+    same workload and metric, whole steps (W warm-up, K timed)."""
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
         return
-    values = []
-    sample = threads = None
-    for _ in range(max(1, min(args.steps, 3))):
-        from oracle.cpu_decode import time_decode_step
-        seconds, threads, sample = time_decode_step(batch=BATCH, history=HISTORY, repeats=1)
-        values.append(BATCH / seconds)
-    value = statistics.median(values)
+    import torch
+    ref, kind, what = _reference_or_port(BATCH)
+    if ref is None:
+        from oracle.cpu_decode import CpuDecodeLayer, _rms
+        import numpy as np
+        rng = np.random.default_rng(1234)
+        layer, lengths = CpuDecodeLayer.synthetic(HISTORY, rng.integers(0, 1024, size=BATCH))
+        x0 = rng.standard_normal((BATCH, 2, 4096), dtype=np.float32)
+        head = rng.standard_normal((128256, 4096), dtype=np.float32) * np.float32(0.02)
+
+        def step():
+            x = x0
+            for _ in range(32):
+                x = layer.forward(x, lengths)
+            return _rms(x[:, 0]) @ head.T
+        threads = len(os.sched_getaffinity(0))
+    else:
+        step = ref.step
+        threads = torch.get_num_threads()
+    for _ in range(args.warmup):
+        step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = BATCH * args.steps / total
+    sample = f'{args.steps} whole decode steps (32 layers + vocab projection) of batch {BATCH}; {what}'
     print(json.dumps({
         'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus,
-        'steps': len(values), 'warmup': 1, 'ms_per_step': 1000.0 * BATCH / value, 'higher_is_better': True,
-        'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic', 'config': config(1),
-        'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': threads, 'kind': 'port', 'sample': sample},
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': 1000.0 * total / args.steps,
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+        'config': config(1),
+        'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': threads, 'kind': kind, 'sample': sample,
+                         'cpu': _cpu_model()},
         'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
-        'note': "CPU restatement of the reference's eager fp32 decode (fa2_decode.decode with eager_forward) "
-                'on all host threads; the reference GPU kernel builds only for sm_90/sm_120'}), flush=True)
+        'note': 'CPU: the reference GPU decode kernel builds only for sm_90/sm_120; rank 0 alone runs under '
+                'torchrun'}), flush=True)
 
 
 PREFILL_BATCH = 4
@@ -365,22 +534,36 @@ def reconstruct_roofline(rt, reps):
     for i in range(reps * cfg.layers):
         d = rt.recon[i % cfg.layers]
         w_k, w_v, b_k, b_v = d.w
-        reconstruct_kv(d.lat_k, d.lat_v, w_k, w_v, d.key_full, d.value_full, d.rows, b_k, b_v, out_start=d.raw_len)
+        reconstruct_kv(d.lat_k, d.lat_v, w_k, w_v, d.key_full, d.value_full, d.rows, b_k, b_v, out_start=d.raw_len,
+                       row_count=d.latent_len)
     r1.record()
     torch.cuda.synchronize()
     rebuild_us = r0.elapsed_time(r1) / (reps * cfg.layers) * 1000.0
-    d = rt.recon[0]
-    rows = rt.batch * d.rows
+    rows = int(rt.latent_len.sum().item())
     kvd = cfg.kv_heads * cfg.head_dim
     flops = 2.0 * rows * kvd * (cfg.rank_k + cfg.rank_v)
     tflops = flops / (rebuild_us / 1e6) / 1e12
     peak, source = tensor_peak()
     return {'step_per_layer_us': step_us, 'rebuild_per_layer_us': rebuild_us, 'rebuilt_rows_per_layer': rows,
-            'rebuild_flops_per_layer': flops, 'launches_per_layer': 5,
+            'rebuild_flops_per_layer': flops,
             'roofline': {'bound': 'tensor', 'achieved': tflops, 'peak': peak, 'unit': 'TFLOP/s',
                          'frac': tflops / peak, 'peak_source': source, 'traffic': None,
                          'kernel': 'project_kernel (Beacon K/V rebuild, tcgen05)',
                          'flops_per_launch': flops, 'us_per_launch': rebuild_us}}
+
+
+def own_launches_per_step(rt):
+    """Kernels of this repository's library (names in the ``slimkv``
+    namespace) that one eager decode step launches, counted by the CUDA
+    profiler (torch/cuBLAS kernels excluded).  Run after the timed region;
+    the step advances the cache like any other."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        rt.step_eager()
+        torch.cuda.synchronize()
+    return sum(1 for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA and 'slimkv' in e.name)
 
 
 def kernel_only(args):
@@ -591,7 +774,7 @@ def main():
                      ' (latent + raw branches, one launch per layer)', 'bytes_per_launch': kernel_bytes, 'us_per_launch': attn_ms * 1000.0,
                      'fused_step_per_layer': {'us': layer_ms * 1000.0, 'bytes': layer_bytes,
                                               'gbs': layer_bytes / (layer_ms / 1000.0) / 1e9}},
-        'gpu_launches': args.steps * (1 + (4 if rt.merges else 3) * cfg.layers),
+        'gpu_launches': args.steps * own_launches_per_step(rt),
         'clocks': clock_info, 'device_status': status,
     }
     if prefill is not None:
@@ -602,7 +785,6 @@ def main():
         result['reconstruct'] = recon
         result['roofline'] = recon.pop('roofline')
         result['latent_backend_fused_step_per_layer_us'] = layer_ms * 1000.0
-        result['gpu_launches'] = args.steps * (1 + cfg.layers * (4 + recon['launches_per_layer']))
     if split:
         result['sequence_split'] = {
             'ranks': world, 'latent_rows_this_rank': int(rt.call_latent_len.sum().item()),

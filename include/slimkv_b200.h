@@ -40,6 +40,9 @@ extern "C" {
 /* Device status bits written by kernels (slimkv_device_status). */
 #define SLIMKV_DEVICE_TIMEOUT 0x1u
 #define SLIMKV_DEVICE_BAD_LENGTH 0x2u
+/* A kernel found its dynamic shared memory less aligned than it needs and
+ * returned without work. */
+#define SLIMKV_DEVICE_MISALIGNED 0x4u
 
 /* Library version as 10000*major + 100*minor + patch. */
 SLIMKV_API int slimkv_version(void);
@@ -182,7 +185,10 @@ typedef struct {
     int64_t out_stride[2];
     int out_fp32;   /* 1: `out` is fp32 (the fp32-accumulated result, no bf16 cast) */
     /* Host-side upper bounds of latent_len / raw_len used to plan the split
-     * counts (0 = the capacities).  Lengths above them are still handled. */
+     * counts (0 = the capacities).  On the split-KV route a sequence longer
+     * than the rows the plan covers is flagged SLIMKV_DEVICE_BAD_LENGTH (its
+     * extra rows are not attended); the tensor-core route plans on the
+     * device from the lengths themselves, up to the capacities. */
     int latent_len_max;
     int raw_len_max;
     /* Split counts (0 = chosen from the byte volume and the SM count).  On the
@@ -475,7 +481,9 @@ SLIMKV_API int slimkv_prefill_rope(const void* q, const int64_t q_stride[3], con
  * (tools/benchmark/context_decode_runtime.py:298-344):
  *   key[b][start_b + r]   = bf16(lat_k[b][r] . w_k_up^T + b_k_up)     (Hkv*D)
  *   value[b][start_b + r] = bf16(lat_v[b][r] . w_v_up^T + b_v_up)
- * for r < rows, start_b = out_start[b] (device int32 [B], NULL = 0), on the
+ * for r < rows (and r < row_count[b] when row_count, device int32 [B], is
+ * given: the rows of a sequence past its latent count are neither read nor
+ * written), start_b = out_start[b] (device int32 [B], NULL = 0), on the
  * tensor cores with fp32 accumulation and one rounding, as a bf16 nn.Linear.
  * lat_k / lat_v [B][lat_capacity][R] rows (element strides lat_stride_batch,
  * lat_stride_row; multiples of 8, 16-byte aligned); w_*_up [Hkv*D][R] as
@@ -502,6 +510,7 @@ typedef struct {
     const int32_t* out_start;
     void* workspace;
     size_t workspace_bytes;
+    const int32_t* row_count;
 } slimkv_reconstruct_args;
 
 SLIMKV_API size_t slimkv_reconstruct_kv_workspace_size(const slimkv_reconstruct_args* args);

@@ -17,6 +17,7 @@ ERRORS = {1: 'invalid argument', 2: 'unsupported shape', 3: 'alignment', 4: 'wor
           5: 'CUDA error', 6: 'tensor map'}
 DEVICE_TIMEOUT = 0x1
 DEVICE_BAD_LENGTH = 0x2
+DEVICE_MISALIGNED = 0x4
 
 I64x3 = ctypes.c_int64 * 3
 I64x2 = ctypes.c_int64 * 2
@@ -124,6 +125,7 @@ class ReconstructArgs(ctypes.Structure):
         ('w_k_up', _P), ('b_k_up', _P), ('w_v_up', _P), ('b_v_up', _P), ('key', _P), ('value', _P),
         ('out_stride_batch', _L), ('out_stride_row', _L), ('out_rows', _I), ('out_start', _P),
         ('workspace', _P), ('workspace_bytes', ctypes.c_size_t),
+        ('row_count', _P),
     ]
 
 

@@ -63,6 +63,7 @@ struct DecodePlan {
     int raw_rows = 0, raw_splits = 0, raw_tps = 0, group = 0, rvp = 0;
     bool tc = false;   // both branches on the persistent tensor-memory kernel (32 query heads)
     int ctas = 0, raw_ctas = 0, lat_pieces = 0;          // tensor-memory route
+    int lat_cover = 0, raw_cover = 0;                    // rows per sequence the launch attends to
     size_t q_rot = 0, q_lat = 0, lat_o = 0, lat_lse = 0, raw_o = 0, raw_lse = 0, plan = 0;
 };
 
@@ -108,8 +109,10 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
     p.lat_splits = (lat_tiles + p.lat_tps - 1) / p.lat_tps;
     p.raw_tps = (raw_tiles + rs - 1) / rs;
     p.raw_splits = (raw_tiles + p.raw_tps - 1) / p.raw_tps;
+    p.lat_cover = std::min(a->lat_capacity, p.lat_splits * p.lat_tps * lt);
+    p.raw_cover = std::min(a->raw_capacity, p.raw_splits * p.raw_tps * kTile);
     const size_t B = a->batch, L = a->length, H = a->heads;
-    p.tc = a->heads == 32 && p.wl <= 320;
+    p.tc = a->heads == 32 && p.wl <= 320 && p.group <= 8;   // 8: the raw score columns per query
     if (p.tc) {
         // One persistent launch: CTAs (at most one per SM) split the latent and
         // raw work by volume on the device (latent_tc_plan.cuh).  latent_splits
@@ -122,6 +125,9 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
         p.lat_rows = 64;
         p.raw_rows = 2 * p.group;
         p.lat_pieces = tc_max_pieces(a->batch, p.ctas);
+        // The device plan tiles every sequence to its own length.
+        p.lat_cover = a->lat_capacity;
+        p.raw_cover = a->raw_capacity;
     }
     p.q_rot = B * L * H * a->head_dim;
     p.q_lat = p.tc ? B * 128 * p.wl : B * L * H * p.wl;
@@ -282,6 +288,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     pa.lat_v = static_cast<__nv_bfloat16*>(a->lat_v);
     pa.lat_sb = a->lat_stride_batch; pa.lat_sr = a->lat_stride_row;
     pa.latent_len = a->latent_len; pa.lat_capacity = a->lat_capacity;
+    pa.lat_cover = p.lat_cover; pa.raw_cover = p.raw_cover;
     pa.lat_pages = static_cast<__nv_bfloat16*>(a->lat_pages);
     pa.lat_page_stride = a->lat_page_stride; pa.lat_table_stride = a->lat_table_stride;
     pa.lat_slots = a->lat_slots; pa.lat_sink = a->lat_sink_elements; pa.lat_num_pages = a->lat_num_pages;

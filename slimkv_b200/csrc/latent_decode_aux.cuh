@@ -48,6 +48,10 @@ struct PrologueArgs {
     int64_t lat_sb, lat_sr;
     const int32_t* latent_len;
     int lat_capacity;
+    // Latent and raw rows per sequence the attention launch covers: a longer
+    // sequence is flagged SLIMKV_DEVICE_BAD_LENGTH (its extra rows would be
+    // outside every split).
+    int lat_cover, raw_cover;
     // Paged latent cache (lat_pages != nullptr): row n of sequence b at
     // lat_pages + table[b][n / slots] * page_stride + sink + (n % slots) * W.
     __nv_bfloat16* lat_pages;
@@ -124,6 +128,13 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
     const int rps = a.length * a.group;                 // rows per sequence
     const int b0 = bb * a.seq_per_cta;
     const int half = a.dim / 2;
+    if (g == 0 && cc == 0) {
+        for (int s = tid; s < a.seq_per_cta; s += 256) {
+            const int b = b0 + s;
+            if (b < a.batch && (a.latent_len[b] > a.lat_cover || a.raw_len[b] > a.raw_cover))
+                report(a.status, SLIMKV_DEVICE_BAD_LENGTH);
+        }
+    }
 
     // 1. U_k column chunk -> shared (fp16).
 #pragma unroll

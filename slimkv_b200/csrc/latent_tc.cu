@@ -23,7 +23,9 @@
 //           per k-step); the softmax and the epilogue add the two halves.
 //   nq = 2: columns are (query, head); hi and lo accumulate into the same
 //           columns (two MMAs per k-step).
-// Raw pieces read exact bf16 query rows (no lo part) in row mode.
+// Raw pieces read exact bf16 query rows (no lo part): query l of head h of
+// the group is row / score column 8 l + h, so the softmax handles 16 columns,
+// and P^T holds hi in columns 0-15 and lo in 16-31 (one MMA per k-step).
 //
 // Streams.  K and V chunks (16 KB, [128 keys x 64 columns], 128-byte
 // swizzle, no multicast) flow through two rings so that V chunks waiting for
@@ -58,7 +60,9 @@ constexpr int kKeys = 128;
 constexpr int kThreads8 = 256;
 constexpr int kProducerV = 7;                        // warp of the V producer
 constexpr int kMaxChunks = 5;                        // ranks <= 320
-constexpr int kKRingMax = 5;
+constexpr int kKRingMax = 6;
+constexpr int kRawCols = 8;                          // raw score columns per query (group <= 8)
+constexpr int kRawS = 2 * kRawCols;                  // raw score columns (two queries)
 constexpr uint32_t kChunkBytes = 128 * 128;          // [128 keys x 64 bf16], 128-byte swizzle
 constexpr uint32_t kQChunkBytes = 64 * 128;          // [64 rows x 64 bf16]
 constexpr float kLazyLog2 = 8.f;
@@ -70,26 +74,31 @@ constexpr uint32_t kTileBytes = 224 * 1024;          // tile area of the largest
 
 struct Misc {
     uint64_t kfull[kKRingMax], kempty[kKRingMax], vfull[kMaxChunks], vempty[kMaxChunks];
-    uint64_t qfull[2], qempty[2], sfull[2], sempty[2], pfull, odone, oempty[2], final_mma;
+    uint64_t qfull[2], qempty[2], sfull[2], sempty[2], pfull[2], odone[2], oempty[2], final_mma;
     uint32_t tmem_base;
     int abort;
     float m_run[64], l_run[64], alpha[64];
     float red[4][64];
 };
-// Misc sits at the start of dynamic shared memory; the tiles start at the next
-// 1024-byte boundary (at most 1008 bytes later for a 16-byte aligned base).
-constexpr uint32_t kSmemBytes = sizeof(Misc) + 1008 + kTileBytes;
+// The tiles start at the first 1024-byte boundary of dynamic shared memory
+// (the base itself on this GPU; a base more than kMaxPad bytes short of a
+// boundary is reported as SLIMKV_DEVICE_MISALIGNED), Misc right after them.
+constexpr uint32_t kMaxPad = 960;
+constexpr uint32_t kSmemBytes = kMaxPad + kTileBytes + uint32_t(sizeof(Misc));
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 // Tile-area layout of a class: V ring | K ring | Q buffers | P buffers.
+// The raw class double-buffers P (pdbl: P(j) in buffer j & 1).
 struct Layout {
     int kring, vslots, qbufs, pbufs;
+    bool pdbl;
     uint32_t off_k, off_q, qbytes, off_p;
 };
-__device__ __forceinline__ Layout class_layout(int cls, int kc) {
+__host__ __device__ __forceinline__ Layout class_layout(int cls, int kc) {
     Layout L;
     L.vslots = cls == 2 ? 4 : kMaxChunks;
-    L.kring = cls == 1 ? 2 : kKRingMax;
+    L.kring = cls == 1 ? 2 : cls == 0 ? kMaxChunks : kKRingMax;
+    L.pdbl = cls == 2;
     L.qbufs = cls == 2 ? 2 : 1;
     L.pbufs = cls == 0 ? 1 : 2;
     L.off_k = uint32_t(L.vslots) * kChunkBytes;
@@ -119,6 +128,25 @@ __device__ __forceinline__ bool named_bar_or(int id, int count, bool pred) {
     return r != 0;
 }
 
+// 16 columns: after this, lanes l and l + 16 hold the reduction of column
+// v[l & 15] over the warp's 32 lanes (15 shuffles, then one across halves).
+template <bool MAX>
+__device__ __forceinline__ float warp_transpose_reduce16(float (&v)[16], int lane) {
+#pragma unroll
+    for (int half = 8; half >= 1; half >>= 1) {
+        const bool upper = lane & half;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            const float recv = __shfl_xor_sync(0xffffffffu, send, half);
+            v[i] = MAX ? fmaxf(keep, recv) : keep + recv;
+        }
+    }
+    const float other = __shfl_xor_sync(0xffffffffu, v[0], 16);
+    return MAX ? fmaxf(v[0], other) : v[0] + other;
+}
+
 // After this, lane `l` holds the reduction of column v[l] over the warp's 32
 // lanes (a transpose-reduce: 31 shuffles for 32 columns).
 template <bool MAX>
@@ -138,7 +166,8 @@ __device__ __forceinline__ float warp_transpose_reduce(float (&v)[32], int lane)
 }
 
 // Eight packed bf16 pairs of (hi, lo) for p[8u .. 8u+8).
-__device__ __forceinline__ void split_hilo(const float (&p)[32], int u, uint4& hi, uint4& lo) {
+template <int N>
+__device__ __forceinline__ void split_hilo(const float (&p)[N], int u, uint4& hi, uint4& lo) {
     uint32_t h[4], l[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -193,10 +222,13 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                  const __grid_constant__ CUtensorMap rvmap, const __grid_constant__ CUtensorMap rqmap,
                  const __grid_constant__ TcJob jl, const __grid_constant__ TcJob jr, const int32_t* __restrict__ plan,
                  const TcPlanLayout PL, int lat_pieces) {
-    extern __shared__ uint8_t smem_raw[];
-    Misc* ms = reinterpret_cast<Misc*>(smem_raw);
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + sizeof(Misc) + 1023) &
-                                               ~uintptr_t(1023));
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    if (smem - smem_raw > int(kMaxPad)) {                     // uniform over the CTA, before any barrier
+        if (threadIdx.x == 0) report(jl.status, SLIMKV_DEVICE_MISALIGNED);
+        return;
+    }
+    Misc* ms = reinterpret_cast<Misc*>(smem + kTileBytes);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     // ---- class and range of this CTA ----
@@ -238,7 +270,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
     const Layout LY = class_layout(cls, kc);
     const int kring = LY.kring;
     const int total_tiles = int(R.r1 - R.r0);
-    const int total_k = total_tiles * kc, total_v = total_tiles * vc;
     const uint64_t wait_ns = J.wait_ns;
     // V chunk n -> (CTA tile T = n / vc, chunk c = n % vc) in V slot c; with
     // <= 2 chunks per tile (raw) tiles alternate between slot pairs (0,1) and
@@ -264,8 +295,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
             mbar_init(&ms->sempty[s], 4);
             mbar_init(&ms->oempty[s], 4);
         }
-        mbar_init(&ms->pfull, 4);
-        mbar_init(&ms->odone, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&ms->pfull[s], 4);
+            mbar_init(&ms->odone[s], 1);
+        }
         mbar_init(&ms->final_mma, 2);
         ms->abort = 0;
         fence_barrier_init();
@@ -331,13 +364,13 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                 uint8_t* qdst = smem + LY.off_q + qb * LY.qbytes;
                 const int nq = J.qlens ? J.qlens[p.b] : J.length;
                 if (J.q_rows) {
-                    // The group's query heads of query l -> rows 32 l + j (the
-                    // other rows of the chunk stay zero from the start).
+                    // The group's query heads of query l -> rows kRawCols l + j
+                    // (the other rows of the chunk stay zero from the start).
                     mbar_expect_tx(&ms->qfull[qb], uint32_t(kc * nq * J.group) * 128u);
                     for (int c = 0; c < kc; ++c)
                         for (int l = 0; l < nq; ++l)
-                            tma_load_4d(qdst + c * kQChunkBytes + l * 32 * 128, qmap, &ms->qfull[qb], c * 64, 0,
-                                        p.g * J.group, p.b * J.length + l);
+                            tma_load_4d(qdst + c * kQChunkBytes + l * kRawCols * 128, qmap, &ms->qfull[qb], c * 64,
+                                        0, p.g * J.group, p.b * J.length + l);
                 } else {
                     // [hi | lo] x 32 * nq rows: one 64-row box per chunk for
                     // nq = 1, hi and lo boxes for nq = 2.
@@ -427,9 +460,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
             const int ob = k & 1;
             const uint32_t o_tmem = tbase + uint32_t(ob) * kOBufCols;
             const int nq = J.qlens ? J.qlens[p.b] : J.length;
-            const bool cols = nq == 1;
+            const bool cols = nq == 1 || J.q_rows;            // hi and lo in separate columns of one P
             for (int t = p.t0; t < p.t1; ++t, ++j) {
-                if (!(ok = wait_or_abort(&ms->pfull, j & 1, ms, J.status, wait_ns))) break;
+                if (!(ok = wait_or_abort(&ms->pfull[j & 1], (j >> 1) & 1, ms, J.status, wait_ns))) break;
+                const uint32_t pb = LY.pdbl ? p0 + uint32_t(j & 1) * kChunkBytes : p0;
                 // The first tile of a piece overwrites the O buffer the
                 // epilogue of piece k - 2 read.
                 if (t == p.t0 && k >= 2 && !(ok = wait_or_abort(&ms->oempty[ob], ((k >> 1) - 1) & 1, ms, J.status,
@@ -450,7 +484,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
 #pragma unroll
                     for (int ks = 0; ks < kKeys / 16; ++ks) {
                         const uint64_t ad = umma_desc_sw128(va + ks * 2048, kChunkBytes, 1024);
-                        umma_bf16(o_b, ad, umma_desc_sw128(p0 + ks * 2048, kChunkBytes, 1024), idesc,
+                        umma_bf16(o_b, ad, umma_desc_sw128(pb + ks * 2048, kChunkBytes, 1024), idesc,
                                   (t > p.t0 || ks > 0) ? 1u : 0u);
                         if (!cols) umma_bf16(o_b, ad, umma_desc_sw128(p1 + ks * 2048, kChunkBytes, 1024), idesc, 1u);
                     }
@@ -458,12 +492,12 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     if (pair) umma_commit(&ms->vempty[s0 + 1]);
                 }
                 if (!ok) break;
-                umma_commit(&ms->odone);
+                umma_commit(&ms->odone[j & 1]);
             }
         }
         umma_commit(&ms->final_mma);
-    } else if (warp >= 3 && warp <= 6) {
-        // ---- softmax and epilogue: thread <-> key (TMEM lane) ----
+    } else if (warp >= 3 && warp <= 6 && cls < 2) {
+        // ---- latent softmax and epilogue: thread <-> key (TMEM lane) ----
         const int quarter = warp & 3;
         const int t_local = 32 * quarter + lane;
         const uint32_t lane_addr = uint32_t(32 * quarter) << 16;
@@ -554,7 +588,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                 }
                 // P(j) overwrites the buffer P.V(j-1) reads: wait for it.
                 if (j > 0) {
-                    ok = wait_or_abort(&ms->odone, (j - 1) & 1, ms, J.status, wait_ns);
+                    ok = wait_or_abort(&ms->odone[(j - 1) & 1], ((j - 1) >> 1) & 1, ms, J.status, wait_ns);
                     if (named_bar_or(1, 128, !ok)) { failed = true; break; }
                     tc_fence_after();
                 }
@@ -625,12 +659,12 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                 if (st < rows)
                     ms->l_run[st] += ms->red[0][st] + ms->red[1][st] + ms->red[2][st] + ms->red[3][st];
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&ms->pfull);
+                if (lane == 0) mbar_arrive(&ms->pfull[j & 1]);
             }
             if (failed) break;
             // ---- epilogue of the piece: normalised partial output and LSE ----
             {
-                const bool ok = wait_or_abort(&ms->odone, (j - 1) & 1, ms, J.status, wait_ns);
+                const bool ok = wait_or_abort(&ms->odone[(j - 1) & 1], ((j - 1) >> 1) & 1, ms, J.status, wait_ns);
                 if (named_bar_or(1, 128, !ok)) { failed = true; break; }
             }
             tc_fence_after();
@@ -675,6 +709,189 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                 const float lsum = ms->l_run[st];
                 J.part_lse[(int64_t)piece * J.rows_alloc + (st >> 5) * rg + (st & 31)] =
                     lsum > 0.f ? (ms->m_run[st] + log2f(lsum)) * 0.69314718055994530942f : -INFINITY;
+            }
+            named_bar(1, 128);                     // m_run / l_run / alpha are reset by the next piece
+        }
+    } else if (warp >= 3 && warp <= 6) {
+        // ---- raw softmax and epilogue: thread <-> key, 16 score columns ----
+        // Column l * kRawCols + h holds query l of head h of the group (Q rows
+        // in that order); P^T carries the bf16 hi parts in columns 0-15 and
+        // the lo parts in 16-31 of buffer j & 1, so P(j) is written while
+        // P.V(j - 1) still reads the other buffer.
+        const int quarter = warp & 3;
+        const int t_local = 32 * quarter + lane;
+        const uint32_t lane_addr = uint32_t(32 * quarter) << 16;
+        const int st = tid - 96;                      // 0..127
+        const int rg = J.group;
+        bool failed = false;
+        int s = R.s0;
+        long long pos = R.r0;
+        int j = 0;
+        for (int k = 0; pos < R.r1 && !failed; ++k) {
+            Piece p;
+            next_piece(R, k, s, pos, J.kv_heads, p);
+            const int ob = k & 1;
+            const uint32_t o_tmem = tbase + uint32_t(ob) * kOBufCols;
+            const int n_keys = J.seqlens[p.b];
+            const int nq = J.qlens ? J.qlens[p.b] : J.length;
+            const int n_tiles = (max(n_keys, 0) + kKeys - 1) / kKeys;
+            if (st < kRawS) {
+                ms->m_run[st] = -INFINITY;
+                ms->l_run[st] = 0.f;
+            }
+            named_bar(1, 128);
+            for (int t = p.t0; t < p.t1; ++t, ++j) {
+                const int sb = j & 1;
+                const uint32_t s_tmem = tbase + kSCol + uint32_t(sb * kN);
+                const int key = t * kKeys + t_local;
+                bool ok = wait_or_abort(&ms->sfull[sb], (j >> 1) & 1, ms, J.status, wait_ns);
+                if (named_bar_or(1, 128, !ok)) { failed = true; break; }
+                tc_fence_after();
+                float v[kRawS];
+                tmem_ld16(s_tmem + lane_addr, v);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ms->sempty[sb]);
+#pragma unroll
+                for (int c = 0; c < kRawS; ++c) v[c] = key < n_keys ? v[c] * J.scale_log2 : -INFINITY;
+                bool over = t == p.t0;
+                if (!over) {
+#pragma unroll
+                    for (int c = 0; c < kRawS; ++c) over |= v[c] > ms->m_run[c] + kLazyLog2;
+                }
+                const bool rescan = named_bar_or(1, 128, over);
+                bool need_fix = false;
+                if (rescan) {
+                    float tmp[kRawS];
+#pragma unroll
+                    for (int c = 0; c < kRawS; ++c) tmp[c] = v[c];
+                    const float r = warp_transpose_reduce16<true>(tmp, lane);
+                    if (lane < kRawS) ms->red[quarter][lane] = r;
+                    named_bar(1, 128);
+                    if (st < kRawS) {
+                        const float tm =
+                            fmaxf(fmaxf(ms->red[0][st], ms->red[1][st]), fmaxf(ms->red[2][st], ms->red[3][st]));
+                        const float mo = ms->m_run[st];
+                        float mn = mo, alpha = 1.f;
+                        if (tm != -INFINITY && (mo == -INFINITY || tm > mo + kLazyLog2)) {
+                            mn = fmaxf(mo, tm);
+                            alpha = mo == -INFINITY ? 0.f : exp2f(mo - mn);
+                        }
+                        ms->alpha[st] = alpha;
+                        ms->m_run[st] = mn;
+                        ms->l_run[st] *= alpha;
+                    }
+                    need_fix = named_bar_or(1, 128, st < kRawS && t > p.t0 && ms->alpha[st] != 1.f);
+                }
+                // P(j) overwrites the buffer P.V(j - 2) read; rescaling O needs
+                // P.V(j - 1) done (a commit covers every earlier MMA).
+                {
+                    const int w = need_fix ? j - 1 : j - 2;
+                    if (w >= 0) {
+                        ok = wait_or_abort(&ms->odone[w & 1], (w >> 1) & 1, ms, J.status, wait_ns);
+                        if (named_bar_or(1, 128, !ok)) { failed = true; break; }
+                        tc_fence_after();
+                    }
+                }
+                // The partial last tile: clear the V rows past the length (see
+                // the latent branch).
+                if (t == n_tiles - 1 && (n_keys & (kKeys - 1)) != 0) {
+                    bool okc = true;
+                    if (key >= n_keys) {
+                        for (int c = 0; c < vc && okc; ++c) {
+                            const int slot = v_slot(j, c);
+                            okc = wait_or_abort(&ms->vfull[slot], v_use(j) & 1, ms, J.status, wait_ns);
+                            if (okc) {
+                                uint4* row = reinterpret_cast<uint4*>(smem + slot * kChunkBytes + t_local * 128);
+#pragma unroll
+                                for (int u = 0; u < 8; ++u) row[u] = make_uint4(0, 0, 0, 0);
+                            }
+                        }
+                    }
+                    if (named_bar_or(1, 128, !okc)) { failed = true; break; }
+                }
+                if (need_fix) {
+                    // O^T columns c (hi) and 16 + c (lo) belong to score column c.
+                    for (int blk = 0; blk < vblocks; ++blk) {
+                        float o[32];
+                        const uint32_t addr = o_tmem + lane_addr + uint32_t(blk * kN);
+                        tmem_ld32(addr, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int c = 0; c < 32; ++c) o[c] *= ms->alpha[c & (kRawS - 1)];
+                        tmem_st32(addr, o);
+                    }
+                    tmem_wait_st();
+                }
+                uint8_t* prow = smem + LY.off_p + uint32_t(j & 1) * kChunkBytes + t_local * 128;
+                float pr[kRawS];
+#pragma unroll
+                for (int c = 0; c < kRawS; ++c) {
+                    const float m = ms->m_run[c];
+                    pr[c] = (v[c] == -INFINITY || m == -INFINITY) ? 0.f : exp2f(v[c] - m);
+                }
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    uint4 hi, lo;
+                    split_hilo(pr, u, hi, lo);
+                    *reinterpret_cast<uint4*>(prow + ((u ^ (t_local & 7)) << 4)) = hi;
+                    *reinterpret_cast<uint4*>(prow + (((u + 2) ^ (t_local & 7)) << 4)) = lo;
+                }
+                {
+                    const float r = warp_transpose_reduce16<false>(pr, lane);
+                    if (lane < kRawS) ms->red[quarter][lane] = r;
+                }
+                fence_async_shared();
+                tc_fence_before();
+                named_bar(1, 128);
+                if (st < kRawS)
+                    ms->l_run[st] += ms->red[0][st] + ms->red[1][st] + ms->red[2][st] + ms->red[3][st];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ms->pfull[j & 1]);
+            }
+            if (failed) break;
+            // ---- epilogue of the piece ----
+            {
+                const bool ok = wait_or_abort(&ms->odone[(j - 1) & 1], ((j - 1) >> 1) & 1, ms, J.status, wait_ns);
+                if (named_bar_or(1, 128, !ok)) { failed = true; break; }
+            }
+            tc_fence_after();
+            named_bar(1, 128);                     // every thread's l_run update is in
+            if (st < kRawS) ms->alpha[st] = ms->l_run[st] > 0.f ? 1.f / ms->l_run[st] : 0.f;
+            named_bar(1, 128);
+            const int piece = piece_base + p.piece;
+            float* out = J.part_o + (int64_t)piece * J.rows_alloc * J.out_width;
+            for (int blk = 0; blk < vblocks; ++blk) {
+                const bool pair = 2 * blk + 1 < vc;
+                float o[32];
+                tmem_ld32(o_tmem + lane_addr + uint32_t(blk * kN), o);
+                tmem_wait_ld();
+                if (pair || lane < 16) {
+                    const int d = 128 * blk + (pair ? 32 * quarter + lane : 16 * quarter + lane);
+#pragma unroll
+                    for (int l = 0; l < 2; ++l) {
+                        if (l < nq) {
+#pragma unroll
+                            for (int h = 0; h < kRawCols; ++h) {
+                                const int c = l * kRawCols + h;
+                                if (h < rg) out[(l * rg + h) * J.out_width + d] = (o[c] + o[kRawS + c]) * ms->alpha[c];
+                            }
+                        }
+                    }
+                }
+            }
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ms->oempty[ob]);
+            if (st < kRawS) {
+                const int l = st / kRawCols, h = st % kRawCols;
+                if (l < nq && h < rg) {
+                    const float lsum = ms->l_run[st];
+                    J.part_lse[(int64_t)piece * J.rows_alloc + l * rg + h] =
+                        lsum > 0.f ? (ms->m_run[st] + log2f(lsum)) * 0.69314718055994530942f : -INFINITY;
+                }
             }
             named_bar(1, 128);                     // m_run / l_run / alpha are reset by the next piece
         }
@@ -740,6 +957,8 @@ int make_side(const TcSide& S, int batch, int length, float scale, const int32_t
                                 uint64_t(S.stride_row) * 2, uint64_t(S.stride_batch) * 2, kKeys)))
             return rc;
     }
+    if (S.q_rows && (S.group > kRawCols || S.causal || length > 2))
+        return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "tensor-core decode attention: raw branch needs group <= 8");
     if (S.q_rows) {
         // q_rot [B][L][H][dim] as (dim, 1, H, B * L), boxes of `group` rows.
         const uint64_t row = uint64_t(S.dim_k) * 2;
@@ -794,6 +1013,13 @@ int launch_decode_tc(const TcLaunch& L, cudaStream_t stream) {
     } else {
         jr = jl;
         rk = lk; rv = lv; rq = lq;
+    }
+    // Every class layout fits the tile area (latent K chunks for classes 0-1,
+    // two for raw).
+    for (int cls = 0; cls < kTcClasses; ++cls) {
+        const Layout LY = class_layout(cls, cls == 2 ? 2 : jl.kchunks);
+        if (LY.off_p + uint32_t(LY.pbufs) * kChunkBytes > kTileBytes)
+            return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "tensor-core decode attention: class %d layout too large", cls);
     }
     static bool configured[64] = {};
     const int dev = device_info().device;

@@ -72,12 +72,14 @@ struct PjTarget {
 
 // A group: rows j < rows of every sequence b read A row
 // (a_idx ? a_idx[j] : j) + (a_start ? a_start[b] : 0) (checked against
-// a_limit) of a + b * a_sb, times weight map `gi` ([n][k]).
+// a_limit) of a + b * a_sb, times weight map `gi` ([n][k]).  With a_count,
+// rows j >= a_count[b] of sequence b are neither read nor written.
 struct PjGroup {
     const uint16_t* a;
     int64_t a_sb, a_sr;
     const int32_t* a_idx;
     const int32_t* a_start;
+    const int32_t* a_count;
     int a_limit, rows, k, n, bn, tiles_m, tiles_n, tile_begin;
     int splits;                // K slices per output tile (1: no workspace)
     float* acc;                // [splits][tiles_m * tiles_n][kPjTileM][bn] fp32 partial tiles
@@ -170,6 +172,10 @@ __device__ __forceinline__ void store_piece(uint16_t* dst, uint4 v, int cnt) {
     for (int e = 0; e < cnt; ++e) dst[e] = static_cast<uint16_t>(w[e >> 1] >> ((e & 1) * 16));
 }
 
+__device__ __forceinline__ bool pj_row_live(const PjGroup& G, int b, int j) {
+    return !G.a_count || j < __ldg(G.a_count + b);
+}
+
 __global__ void __launch_bounds__(kPjThreads, 1)
 project_kernel(const __grid_constant__ PjMaps maps, const __grid_constant__ PjParams P) {
     extern __shared__ uint8_t smem_raw[];
@@ -192,6 +198,15 @@ project_kernel(const __grid_constant__ PjMaps maps, const __grid_constant__ PjPa
     const int nk_all = (G.k + 63) / 64;
     const int k0 = split * nk_all / G.splits;              // this CTA's K chunks [k0, k0 + nk)
     const int nk = (split + 1) * nk_all / G.splits - k0;
+    if (G.a_count) {
+        // A tile whose rows are all past their sequences' counts has no work
+        // (uniform over the CTA, before any barrier or TMEM allocation).
+        bool live = false;
+        const int b_first = m0 / G.rows, b_last = (min(m0 + kPjTileM, total_rows) - 1) / G.rows;
+        for (int b = b_first; b <= b_last && !live; ++b)
+            live = (b == b_first ? m0 % G.rows : 0) < __ldg(G.a_count + b);
+        if (!live) return;
+    }
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
@@ -221,7 +236,7 @@ project_kernel(const __grid_constant__ PjMaps maps, const __grid_constant__ PjPa
         for (int q = 0; q < 8; ++q) {
             const int grow = m0 + rslot + 32 * q;
             rowp[q] = G.a;
-            if (grow < total_rows) {
+            if (grow < total_rows && pj_row_live(G, grow / G.rows, grow % G.rows)) {
                 const int b = grow / G.rows, j = grow % G.rows;
                 const int ar = (G.a_idx ? __ldg(G.a_idx + j) : j) + (G.a_start ? __ldg(G.a_start + b) : 0);
                 if (ar >= 0 && ar < G.a_limit) {
@@ -286,7 +301,7 @@ project_kernel(const __grid_constant__ PjMaps maps, const __grid_constant__ PjPa
         }
         if (ok) {
             uint16_t* dst[kPjMaxTargets] = {nullptr, nullptr, nullptr};
-            if (grow < total_rows) {
+            if (grow < total_rows && pj_row_live(G, grow / G.rows, grow % G.rows)) {
                 const int b = grow / G.rows, j = grow % G.rows;
                 const int ar = (G.a_idx ? __ldg(G.a_idx + j) : j) + (G.a_start ? __ldg(G.a_start + b) : 0);
                 if (ar >= 0 && ar < G.a_limit) {
@@ -405,6 +420,7 @@ __global__ void __launch_bounds__(256) finalize_kernel(const __grid_constant__ P
         const int grow = m0 + r, n = n0 + c;
         if (grow >= total_rows || n >= G.n) continue;
         const int b = grow / G.rows, j = grow % G.rows;
+        if (!pj_row_live(G, b, j)) continue;
         const int ar = (G.a_idx ? __ldg(G.a_idx + j) : j) + (G.a_start ? __ldg(G.a_start + b) : 0);
         if (ar < 0 || ar >= G.a_limit) continue;
         const float* src = G.acc + (int64_t(tile) * kPjTileM + r) * G.bn + c;
@@ -605,7 +621,7 @@ struct Launch {
 // Append a group computing rows x weight[n][k]^T; no-op when it has no target.
 int add_group(Launch& L, const void* a, int64_t a_sb, int64_t a_sr, const int32_t* a_idx, const int32_t* a_start,
               int a_limit, int rows, const void* weight, int k, int n, const void* bias,
-              std::initializer_list<PjTarget> targets, int batch) {
+              std::initializer_list<PjTarget> targets, int batch, const int32_t* a_count = nullptr) {
     bool any = false;
     for (const PjTarget& t : targets) any |= t.kind != kTargetNone;
     if (!any || rows == 0 || batch == 0) return SLIMKV_OK;
@@ -620,6 +636,7 @@ int add_group(Launch& L, const void* a, int64_t a_sb, int64_t a_sr, const int32_
     G.a_sr = a_sr;
     G.a_idx = a_idx;
     G.a_start = a_start;
+    G.a_count = a_count;
     G.a_limit = a_limit;
     G.rows = rows;
     G.k = k;
@@ -873,13 +890,13 @@ int build_reconstruct(const slimkv_reconstruct_args* a, Launch& L) {
                         a->rows, a->w_k_up, a->rank_k, kvd, a->b_k_up,
                         {dense_target(a->key, a->out_stride_batch, a->out_stride_row, a->out_rows, nullptr,
                                       a->out_start)},
-                        a->batch)))
+                        a->batch, a->row_count)))
         return rc;
     return add_group(L, a->lat_v, a->lat_stride_batch, a->lat_stride_row, nullptr, nullptr, a->lat_capacity, a->rows,
                      a->w_v_up, a->rank_v, kvd, a->b_v_up,
                      {dense_target(a->value, a->out_stride_batch, a->out_stride_row, a->out_rows, nullptr,
                                    a->out_start)},
-                     a->batch);
+                     a->batch, a->row_count);
 }
 
 }  // namespace

@@ -29,12 +29,13 @@ from .kernels import _bf16_cuda, _ptr, _require, _stream, attention_forward
 
 
 def reconstruct_kv(lat_k, lat_v, w_k_up, w_v_up, key, value, rows, b_k_up=None, b_v_up=None, out_start=None,
-                   workspace=None, head_dim=None):
+                   workspace=None, head_dim=None, row_count=None):
     """``key[b, out_start[b] + r] = bf16(lat_k[b, r] @ w_k_up.T + b_k_up)`` for
-    ``r < rows`` (and the same for values).  ``lat_k / lat_v [B, cap, R]``
-    (rows contiguous, matching strides), ``key / value [B, out_rows, Hkv*D]``
-    with ``head_dim`` given (or ``[B, out_rows, Hkv, D]``) bf16, ``out_start``
-    int32 ``[B]`` on the device or ``None`` (0)."""
+    ``r < rows`` and ``r < row_count[b]`` (and the same for values).
+    ``lat_k / lat_v [B, cap, R]`` (rows contiguous, matching strides), ``key /
+    value [B, out_rows, Hkv*D]`` with ``head_dim`` given (or ``[B, out_rows,
+    Hkv, D]``) bf16, ``out_start`` and ``row_count`` int32 ``[B]`` on the
+    device or ``None`` (0, and no per-sequence limit)."""
     _bf16_cuda(lat_k, lat_v, w_k_up, w_v_up, key, value)
     _require(lat_k.stride() == lat_v.stride() and lat_k.stride(-1) == 1 and lat_v.stride(-1) == 1,
              'latent caches [B, cap, R] need matching strides and contiguous rows')
@@ -48,9 +49,10 @@ def reconstruct_kv(lat_k, lat_v, w_k_up, w_v_up, key, value, rows, b_k_up=None, 
     for b in (b_k_up, b_v_up):
         if b is not None:
             _bf16_cuda(b)
-    if out_start is not None:
-        _require(out_start.is_cuda and out_start.dtype == torch.int32 and out_start.numel() == batch,
-                 'out_start must be int32 [B] on the device')
+    for t, name in ((out_start, 'out_start'), (row_count, 'row_count')):
+        if t is not None:
+            _require(t.is_cuda and t.dtype == torch.int32 and t.numel() == batch and t.is_contiguous(),
+                     f'{name} must be int32 [B] on the device')
     a = _lib.ReconstructArgs()
     a.batch, a.rows, a.rank_k, a.rank_v = batch, int(rows), lat_k.shape[-1], lat_v.shape[-1]
     a.head_dim = key.shape[-1] if key.dim() == 4 else int(head_dim or 0)
@@ -64,6 +66,7 @@ def reconstruct_kv(lat_k, lat_v, w_k_up, w_v_up, key, value, rows, b_k_up=None, 
     a.key, a.value = key.data_ptr(), value.data_ptr()
     a.out_stride_batch, a.out_stride_row, a.out_rows = flat_k.stride(0), flat_k.stride(1), flat_k.shape[1]
     a.out_start = 0 if out_start is None else out_start.data_ptr()
+    a.row_count = 0 if row_count is None else row_count.data_ptr()
     lib = _lib.load()
     if workspace is not None:
         a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel()
@@ -94,6 +97,8 @@ class ReconstructDecode:
         self.raw_len, self.latent_len, self.query_len = raw_len, latent_len, query_len
         self.key_full, self.value_full = key_full, value_full
         self.scale = scale if scale is not None else 1.0 / math.sqrt(dim)
+        # Every row a sequence can hold; each sequence rebuilds only its
+        # latent_len rows (the rest of the capacity is skipped on the device).
         self.rows = int(latent_rows if latent_rows is not None else lat_k.shape[1])
         self.raw_cap = raw_cap
         self.seq0 = torch.zeros(B, dtype=torch.int32, device=raw_len.device)
@@ -105,7 +110,7 @@ class ReconstructDecode:
         self.key_full[:, :self.raw_cap].copy_(self.raw_k_rot)
         self.value_full[:, :self.raw_cap].copy_(self.raw_v)
         reconstruct_kv(self.lat_k, self.lat_v, w_k, w_v, self.key_full, self.value_full, self.rows, b_k, b_v,
-                       out_start=self.raw_len)
+                       out_start=self.raw_len, row_count=self.latent_len)
         total = self.raw_len + self.latent_len
         two = (self.query_len == 2).to(torch.int32)
         torch.sub(total, two, out=self.seq0)              # the raw token's query skips this step's Beacon

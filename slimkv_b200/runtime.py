@@ -299,7 +299,9 @@ class LatentDecodeRuntime:
         self.logits = torch.zeros(B, cfg.vocab, dtype=torch.float32, device=device)
         z = self.z
         q = z[:, :, :qd].unflatten(-1, (cfg.heads, cfg.head_dim))          # [B, 2, H, D]
-        lat_max = int(hist.max()) + per_window + 64
+        # Every call covers the whole latent capacity: a sequence may grow up to
+        # it during a run (the append checks the capacity on the device).
+        lat_max = self.lat_capacity
         self.calls = []
         self.merges = []
         sp = self.split
@@ -313,7 +315,6 @@ class LatentDecodeRuntime:
             call_lat_len = sp['latent_len']
             if not sp['last']:
                 call_raw_len = torch.zeros(B, **i32)
-            lat_max = lat_max - int(sp['offset'].min()) if sp['last'] else int(sp['rows'].max())
         for c, layer in zip(self.caches, weights.layers):
             pages = (c['pages'], self.layout, self.tables) if paged else None
             shard = sp is not None and not sp['last']
@@ -333,7 +334,7 @@ class LatentDecodeRuntime:
                 new_k=None if shard else z[:, 0, qd:qd + kvd], new_v=None if shard else z[:, 0, qd + kvd:qd + 2 * kvd],
                 new_lat_k=None if shard else z[:, 1, qd:qd + cfg.rank_k],
                 new_lat_v=None if shard else z[:, 1, qd + cfg.rank_k:qd + cfg.rank_k + cfg.rank_v],
-                latent_len_max=min(lat_max, self.lat_capacity), raw_len_max=self.raw_capacity,
+                latent_len_max=lat_max, raw_len_max=self.raw_capacity,
                 latent_splits=latent_splits, raw_splits=raw_splits))
         self.call_latent_len, self.call_raw_len = call_lat_len, call_raw_len
         self.recon = []
@@ -348,8 +349,7 @@ class LatentDecodeRuntime:
                     raw_k_rot=c['raw_k_rot'], raw_v=c['raw_v'], lat_k=c['lat_k'], lat_v=c['lat_v'],
                     w_k_up=layer['uk'], w_v_up=layer['uv'], b_k_up=layer.get('uk_bias'), b_v_up=layer.get('uv_bias'),
                     raw_len=self.raw_len, latent_len=self.latent_len, query_len=self.query_len,
-                    key_full=self.key_full, value_full=self.value_full,
-                    latent_rows=min(lat_max, self.lat_capacity)))
+                    key_full=self.key_full, value_full=self.value_full))
         self.graph = None
 
     # ------------------------------------------------------------------

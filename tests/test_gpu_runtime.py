@@ -72,10 +72,14 @@ def test_qwen_geometry_runtime_steps():
 def test_reconstruct_backend_runtime_follows_latent_backend(geometry):
     """The reconstruct backend (Beacon K/V rebuilt each step, then attention)
     against the latent backend on the same caches, through steps that insert
-    Beacons and graph replays.  One layer, so both backends see identical
-    attention inputs each step: the attention rows differ only by the bf16
-    rounding of the rebuilt keys and values (norm-wise 1e-2); the caches the
-    backends append must stay bit-identical."""
+    Beacons and graph replays, and after one sequence has grown past every
+    length seen at construction (the rebuild covers each sequence's current
+    latent count, up to the capacity).  One layer, so both backends see
+    identical attention inputs each step: the attention rows differ only by
+    the bf16 rounding of the rebuilt keys and values (norm-wise 1e-2); the
+    caches the backends append must stay bit-identical, and the second query
+    row of a sequence that inserts no Beacon (zero keys) comes out zero."""
+    from slimkv_b200 import _lib
     from slimkv_b200.runtime import LatentDecodeRuntime, LatentLlamaConfig, RandomWeights, qwen25_14b_r2
     dev = torch.device('cuda', 0)
     if geometry == 'llama':
@@ -86,8 +90,8 @@ def test_reconstruct_backend_runtime_follows_latent_backend(geometry):
     w = RandomWeights(cfg, dev, seed=9)
     per_window = cfg.window // cfg.ratio
     history, tails = [per_window * 4, per_window * 9, per_window], [1013, 300, 7]
-    lat = LatentDecodeRuntime(cfg, w, history, tails, dev)
-    rec = LatentDecodeRuntime(cfg, w, history, tails, dev, backend='reconstruct')
+    lat = LatentDecodeRuntime(cfg, w, history, tails, dev, extra_windows=2)
+    rec = LatentDecodeRuntime(cfg, w, history, tails, dev, extra_windows=2, backend='reconstruct')
     for cl, cr in zip(lat.caches, rec.caches):
         for name in ('raw_k_rot', 'raw_k_pre', 'raw_v', 'lat'):
             cr[name].copy_(cl[name])
@@ -100,6 +104,8 @@ def test_reconstruct_backend_runtime_follows_latent_backend(geometry):
             for l in range(q):
                 x, y = lat.attn[bb, l].double(), rec.attn[bb, l].double()
                 assert ((x - y).norm() / x.norm()).item() < 1e-2
+            if q == 1:
+                assert torch.count_nonzero(rec.attn[bb, 1]).item() == 0
         d = (a.float() - b.float()).abs()
         assert d.mean().item() < 5e-3 and d.max().item() <= 0.125
         for cl, cr in zip(lat.caches, rec.caches):
@@ -120,4 +126,17 @@ def test_reconstruct_backend_runtime_follows_latent_backend(geometry):
         tokens = lat.next_tokens().clone()
         lat.tokens.copy_(tokens)
         rec.tokens.copy_(tokens)
+    # Sequence 2 jumps to 11 windows of history: more latents than the
+    # longest sequence at construction plus a window (within the capacity).
+    grown = per_window * 11
+    assert grown + per_window > max(history) + per_window + 64
+    for rt in (lat, rec):
+        rt.history[2] = grown
+    for _ in range(2):
+        compare(lat.step().clone(), rec.step().clone())
+        assert int(lat.latent_len[2].item()) > max(history) + per_window + 64
+        tokens = lat.next_tokens().clone()
+        lat.tokens.copy_(tokens)
+        rec.tokens.copy_(tokens)
+    assert _lib.device_status(clear=True) == 0
     assert inserted >= 2

@@ -108,10 +108,13 @@ def test_reconstruct_kv_matches_reference_golden():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize('rank,kv_heads,batch', [(512, 8, 3), (320, 8, 2), (160, 8, 1), (64, 2, 4)])
-def test_reconstruct_kv_matches_oracle_at_offsets(rank, kv_heads, batch):
+@pytest.mark.parametrize('rank,kv_heads,batch,counted', [(512, 8, 3, False), (320, 8, 2, False), (160, 8, 1, False),
+                                                         (64, 2, 4, False), (320, 8, 4, True), (512, 8, 3, True)])
+def test_reconstruct_kv_matches_oracle_at_offsets(rank, kv_heads, batch, counted):
     """Rows land at per-sequence starts (after each sequence's raw rows); rows
-    past out_rows are skipped, never written."""
+    past out_rows are skipped, never written.  With per-sequence row counts
+    (the latent lengths of a ragged batch, one of them 0) only each
+    sequence's first count rows are rebuilt; the rest stay untouched."""
     torch = _cuda()
     from gpu_util import to_bf16
     from slimkv_b200.reconstruct import reconstruct_kv
@@ -125,17 +128,23 @@ def test_reconstruct_kv_matches_oracle_at_offsets(rank, kv_heads, batch):
     lat_t = to_bf16(lat)
     key = torch.full((batch, out_rows, kv_heads, 128), float('nan'), dtype=torch.bfloat16, device='cuda')
     value = torch.full_like(key, float('nan'))
+    counts = np.full(batch, rows, np.int32)
+    if counted:
+        counts = rng.integers(1, rows + 1, size=batch).astype(np.int32)
+        counts[1] = 0
     reconstruct_kv(lat_t[..., :rank], lat_t[..., rank:], to_bf16(wk), to_bf16(wv), key, value, rows, to_bf16(bk),
-                   None, out_start=torch.from_numpy(starts).cuda())
+                   None, out_start=torch.from_numpy(starts).cuda(),
+                   row_count=torch.from_numpy(counts).cuda() if counted else None)
     torch.cuda.synchronize()
     want_k = materialize(lat[:, :rows, :rank], wk, bk).reshape(batch, rows, kv_heads, 128)
     want_v = materialize(lat[:, :rows, rank:], wv, None).reshape(batch, rows, kv_heads, 128)
     k, v = key.float().cpu().numpy(), value.float().cpu().numpy()
     for b in range(batch):
-        s = int(starts[b])
+        s, n = int(starts[b]), int(counts[b])
         for got, want in ((k, want_k), (v, want_v)):
-            assert_near_bits(bf16_bits(got[b, s:s + rows]), bf16_bits(want[b]), 5e-3)
-            assert np.isnan(got[b, :s]).all() and np.isnan(got[b, s + rows:]).all()
+            if n:
+                assert_near_bits(bf16_bits(got[b, s:s + n]), bf16_bits(want[b, :n]), 5e-3)
+            assert np.isnan(got[b, :s]).all() and np.isnan(got[b, s + n:]).all()
 
 
 @pytest.mark.gpu
