@@ -202,6 +202,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
         "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
 }
+// Programmatic dependent launch.  grid_dependency_wait blocks until the grids
+// this one depends on programmatically have completed and their writes are
+// visible (at once for a launch without that dependency);
+// grid_launch_dependents lets the dependent launch start once every CTA of
+// this grid has issued it or exited.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 // Named barrier over `count` threads (ids 1..15; id 0 is __syncthreads).
 __device__ __forceinline__ void named_bar(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -418,8 +418,21 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         }
     }
     const dim3 mgrid(a->kv_heads, (a->batch + ma.seq_per_cta - 1) / ma.seq_per_cta);
-    decode_merge_kernel<<<mgrid, 256, msmem, stream>>>(ma);
-    e = cudaGetLastError();
+    // Programmatic dependent launch: the merge's set-up (plan ranges, U_v,
+    // LSE shifts) overlaps the attention launch's last CTAs; it reads the
+    // partials only after the attention grid has completed.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = mgrid;
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = msmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, decode_merge_kernel, ma);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "merge launch failed: %s", cudaGetErrorString(e));
     return SLIMKV_OK;
 }

@@ -115,14 +115,16 @@ __device__ __forceinline__ uint4 widen8(uint4 v) {
 // into latent columns [cc*64, cc*64 + 64); the cc == 0 CTAs also write q_rot
 // and append this step's raw token (and, for g == 0, the Beacon latents).
 __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
-    __shared__ __align__(1024) uint8_t s_a[kProRows * 128 * 2];   // rope(q): 2 chunks [64 x 64] fp16
-    __shared__ __align__(1024) uint8_t s_b[128 * 64 * 2];         // U_k[g][:, cc*64 : +64] fp16
+    __shared__ __align__(1024) uint8_t s_ab[kProRows * 128 * 2 + 128 * 64 * 2];
+    uint8_t* s_a = s_ab;                                // rope(q): 2 chunks [64 x 64] fp16
+    uint8_t* s_b = s_ab + kProRows * 128 * 2;           // U_k[g][:, cc*64 : +64] fp16
     const int g = blockIdx.x, cc = blockIdx.y, bb = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (a.do_plan && bb == int(gridDim.z) - 1) {
         // The last z-slice only plans the attention (one block, in parallel
-        // with the absorb blocks).
-        if (g == 0 && cc == 0) plan_tc_work(a.plan);
+        // with the absorb blocks), in this block's shared memory when it fits.
+        if (g == 0 && cc == 0)
+            plan_tc_work(a.plan, reinterpret_cast<int32_t*>(s_ab), int(sizeof(s_ab) / sizeof(int32_t)));
         return;
     }
     const int rps = a.length * a.group;                 // rows per sequence
@@ -295,14 +297,58 @@ struct MergeArgs {
     float* out_lse;                // [B][L][H] merged LSE (nullable)
 };
 
-// Partials per row and branch that decode_merge_kernel combines (5 per lane).
+// Most CTAs of a split-KV attention launch (the tensor-memory route sizes its
+// launch below this).
 constexpr int kMergeMaxSplits = 160;
 
 // Dynamic shared memory of decode_merge_kernel for a padded value rank:
 // U_v[g] bf16 [128 x rvp], o_lat hi and lo bf16 [16 x rvp] each, raw rows
-// fp32 [16 x dim], LSEs [2][16], split weights [2][16][kMergeMaxSplits].
+// fp32 [16 x dim], LSEs [2][16], latent LSE shifts [16].
 __host__ __device__ constexpr size_t merge_smem_bytes(int rank_v_pad, int dim) {
-    return 1024 + size_t(128 + 32) * rank_v_pad * 2 + size_t(16) * dim * 4 + 32 * 4 + 2 * 16 * kMergeMaxSplits * 4;
+    return 1024 + size_t(128 + 32) * rank_v_pad * 2 + size_t(16) * dim * 4 + 48 * 4;
+}
+
+// out[c:c+4] = sum_s w_s part_s[c:c+4] / sum_s w_s with w_s = exp(lse_s - max
+// lse), over the n partials at src + s * pitch (LSE at lse + s * lse_pitch),
+// in one pass (running max); *row_lse = log sum_s exp(lse_s) (-inf if none).
+__device__ __forceinline__ float4 combine_partials(const float* src, int64_t pitch, const float* lse, int64_t lse_pitch,
+                                                   int n, float* row_lse) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float m = -INFINITY, tot = 0.f;
+    for (int s0 = 0; s0 < n; s0 += 8) {
+        float4 x[8];
+        float ls[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            ls[u] = -INFINITY;
+            if (s0 + u < n) {
+                x[u] = __ldg(reinterpret_cast<const float4*>(src + (s0 + u) * pitch));
+                ls[u] = __ldg(lse + (s0 + u) * lse_pitch);
+            }
+        }
+        float mn = m;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mn = fmaxf(mn, ls[u]);
+        if (mn == -INFINITY) continue;
+        const float sc = m == -INFINITY ? 0.f : expf(m - mn);
+        acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+        tot *= sc;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            if (ls[u] == -INFINITY) continue;
+            const float w = expf(ls[u] - mn);
+            acc.x = fmaf(w, x[u].x, acc.x); acc.y = fmaf(w, x[u].y, acc.y);
+            acc.z = fmaf(w, x[u].z, acc.z); acc.w = fmaf(w, x[u].w, acc.w);
+            tot += w;
+        }
+        m = mn;
+    }
+    if (tot > 0.f) {
+        const float inv = 1.f / tot;
+        acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
+    }
+    *row_lse = tot > 0.f ? m + logf(tot) : -INFINITY;
+    return acc;
 }
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
@@ -317,10 +363,9 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // First partial and partial count of sequence b's latent branch.
 __device__ __forceinline__ void lat_parts(const MergeArgs& a, int b, int& p0, int& n) {
     if (a.plan) {
-        const int ls = a.plan[a.PL.lat_seg + b], cls = ls >> 24, s = ls & 0xffffff;
-        const int32_t* pc = a.plan + a.PL.seg_piece[cls];
-        p0 = pc[s] + (cls ? a.lat_pieces : 0);
-        n = pc[s + 1] - pc[s];
+        const int2 r = *reinterpret_cast<const int2*>(a.plan + a.PL.lat_range + 2 * b);
+        p0 = (r.x & 0xffffff) + ((r.x >> 24) ? a.lat_pieces : 0);
+        n = r.y;
     } else {
         p0 = b * a.lat_splits;
         n = a.lat_splits;
@@ -362,8 +407,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
     uint8_t* s_hi = s_b + 128 * rvp * 2;                // o_lat hi: rvp/64 chunks [16 x 64] bf16
     uint8_t* s_lo = s_hi + 16 * rvp * 2;                // o_lat lo
     float* s_raw = reinterpret_cast<float*>(s_lo + 16 * rvp * 2);   // [16][D]
-    float* s_lse = s_raw + 16 * a.dim;                  // [2][16]: latent, raw
-    float* s_w = s_lse + 32;                            // [2][16][kMergeMaxSplits] split weights: latent, raw
+    float* s_lse = s_raw + 16 * a.dim;                  // [2][16]: latent, raw (then [16] shifts)
     const int g = blockIdx.x, bb = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rps = a.length * a.group, b0 = bb * a.seq_per_cta;
@@ -379,9 +423,13 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
         return r < nrows && b < a.batch && l < (a.qlens ? a.qlens[b] : a.length);
     };
 
-    // 0. Each row's partial ranges (latent, raw) once, before any other
-    //    load depends on them.
+    // 0. (Before the attention launch completes.)  Each row's partial ranges
+    //    (latent, raw) from the plan, U_v[g] (rows d, columns c) -> shared
+    //    asynchronously with zero columns past the rank, the zero rows of the
+    //    A operand, and the latent LSE shift scale * q . b_k of each row
+    //    (fa2_decode.py:157-160) — none of it reads the attention's output.
     __shared__ int s_parts[16][4];
+    float* s_shift = s_lse + 32;                        // [16]
     if (tid < 16) {
         int b, l, h, rr, p0 = 0, n = 0, q0 = 0, m = 0;
         if (row_info(tid, b, l, h, rr)) {
@@ -390,8 +438,6 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
         }
         s_parts[tid][0] = p0; s_parts[tid][1] = n; s_parts[tid][2] = q0; s_parts[tid][3] = m;
     }
-    // 1. U_v[g] (rows d, columns c) -> shared, asynchronously; zero columns
-    //    past the rank.
     const int units = rvp / 8;
     for (int i = tid; i < 128 * units; i += 256) {
         const int d = i / units, u = i - d * units, col = u * 8;
@@ -400,60 +446,24 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
         else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
     cp_async_commit();
-    // Rows of the A operand that no query fills stay zero.
     for (int i = tid; i < 2 * 16 * rvp / 8; i += 256) reinterpret_cast<uint4*>(s_hi)[i] = make_uint4(0, 0, 0, 0);
-    __syncthreads();
-    // 2. Split weights and LSEs per row.
     for (int r = warp; r < 16; r += 8) {
         int b, l, h, rr;
-        const bool valid = row_info(r, b, l, h, rr);
-        float lse_br[2];
-#pragma unroll
-        for (int br = 0; br < 2; ++br) {
-            const int p0 = s_parts[r][2 * br], nsp = valid ? s_parts[r][2 * br + 1] : 0;
-            float my[kMergeMaxSplits / 32];
-            float m = -INFINITY;
-#pragma unroll
-            for (int k = 0; k < kMergeMaxSplits / 32; ++k) {
-                const int sp = lane + 32 * k;
-                my[k] = -INFINITY;
-                if (sp < nsp)
-                    my[k] = br ? __ldg(a.raw_lse + (int64_t)(p0 + sp) * a.raw_rows + rr)
-                               : __ldg(a.lat_lse + (int64_t)(p0 + sp) * a.lat_rows + l * a.heads + h);
-                m = fmaxf(m, my[k]);
-            }
-#pragma unroll
-            for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-            float total = 0.f;
-#pragma unroll
-            for (int k = 0; k < kMergeMaxSplits / 32; ++k) {
-                my[k] = (m == -INFINITY || my[k] == -INFINITY) ? 0.f : expf(my[k] - m);
-                total += my[k];
-            }
-#pragma unroll
-            for (int off = 16; off; off >>= 1) total += __shfl_xor_sync(0xffffffffu, total, off);
-#pragma unroll
-            for (int k = 0; k < kMergeMaxSplits / 32; ++k)
-                s_w[(br * 16 + r) * kMergeMaxSplits + lane + 32 * k] = total > 0.f ? my[k] / total : 0.f;
-            lse_br[br] = total > 0.f ? m + logf(total) : -INFINITY;
-        }
-        if (valid && a.uk_bias && lse_br[0] != -INFINITY) {
-            // Latent LSE shift by scale * q . b_k (fa2_decode.py:157-160).
+        float dot = 0.f;
+        if (a.uk_bias && row_info(r, b, l, h, rr)) {
             const __nv_bfloat16* q = a.q_rot + (((int64_t)b * a.length + l) * a.heads + h) * a.dim;
             const __nv_bfloat16* bk = a.uk_bias + (int64_t)g * a.dim;
-            float dot = 0.f;
             for (int d = lane; d < a.dim; d += 32) dot += __bfloat162float(q[d]) * __bfloat162float(bk[d]);
 #pragma unroll
             for (int off = 16; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-            lse_br[0] += dot * a.scale;
         }
-        if (lane == 0) {
-            s_lse[r] = lse_br[0];
-            s_lse[16 + r] = lse_br[1];
-        }
+        if (lane == 0) s_shift[r] = dot * a.scale;
     }
+    grid_dependency_wait();
     __syncthreads();
-    // 3a. Latent branch: o_lat[r, c:c+4] = sum_s w_s * part_s[r, c:c+4] -> bf16 hi / lo.
+    // 1. Latent branch: o_lat[r, c:c+4] combined over the row's pieces in one
+    //    pass -> bf16 hi / lo (fp32-level accuracy through the bf16 tensor
+    //    cores); the column-0 item also records the row's LSE (shifted).
     {
         const int c4n = rvp / 4;
         const int64_t pitch = (int64_t)a.lat_rows * a.lat_width;
@@ -461,26 +471,12 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
             const int r = it / c4n, c = (it - r * c4n) * 4;
             int b, l, h, rr;
             if (!row_info(r, b, l, h, rr) || c >= a.lat_width) continue;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             const int p0 = s_parts[r][0], nsp = s_parts[r][1];
-            const float* src = a.lat_o + ((int64_t)p0 * a.lat_rows + l * a.heads + h) * a.lat_width + c;
-            const float* w = s_w + r * kMergeMaxSplits;
-            int s = 0;
-            for (; s + 8 <= nsp; s += 8) {
-                float4 x[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) x[u] = __ldg(reinterpret_cast<const float4*>(src + (s + u) * pitch));
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    acc.x = fmaf(w[s + u], x[u].x, acc.x); acc.y = fmaf(w[s + u], x[u].y, acc.y);
-                    acc.z = fmaf(w[s + u], x[u].z, acc.z); acc.w = fmaf(w[s + u], x[u].w, acc.w);
-                }
-            }
-            for (; s < nsp; ++s) {
-                const float4 x = __ldg(reinterpret_cast<const float4*>(src + s * pitch));
-                acc.x = fmaf(w[s], x.x, acc.x); acc.y = fmaf(w[s], x.y, acc.y);
-                acc.z = fmaf(w[s], x.z, acc.z); acc.w = fmaf(w[s], x.w, acc.w);
-            }
+            const int64_t row = (int64_t)p0 * a.lat_rows + l * a.heads + h;
+            float lse;
+            const float4 acc = combine_partials(a.lat_o + row * a.lat_width + c, pitch, a.lat_lse + row, a.lat_rows,
+                                                nsp, &lse);
+            if (c == 0) s_lse[r] = lse == -INFINITY ? lse : lse + s_shift[r];
             const float hx = bf16_round(acc.x), hy = bf16_round(acc.y), hz = bf16_round(acc.z), hw = bf16_round(acc.w);
             const int off = (c >> 6) * (16 * 128) + sw128(r, c & 63);
             *reinterpret_cast<uint2*>(s_hi + off) = make_uint2(pack_bf16x2(hx, hy), pack_bf16x2(hz, hw));
@@ -488,7 +484,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
                 make_uint2(pack_bf16x2(acc.x - hx, acc.y - hy), pack_bf16x2(acc.z - hz, acc.w - hw));
         }
     }
-    // 3b. Raw branch: fp32 combined output rows.
+    // 2. Raw branch: fp32 combined output rows and their LSE.
     {
         const int c4n = a.dim / 4;
         const int64_t pitch = (int64_t)a.raw_rows * a.dim;
@@ -496,27 +492,13 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
             const int r = it / c4n, c = (it - r * c4n) * 4;
             int b, l, h, rr;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            float lse = -INFINITY;
             if (row_info(r, b, l, h, rr)) {
                 const int p0 = s_parts[r][2], nsp = s_parts[r][3];
-                const float* src = a.raw_o + ((int64_t)p0 * a.raw_rows + rr) * a.dim + c;
-                const float* w = s_w + (16 + r) * kMergeMaxSplits;
-                int s = 0;
-                for (; s + 8 <= nsp; s += 8) {
-                    float4 x[8];
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) x[u] = __ldg(reinterpret_cast<const float4*>(src + (s + u) * pitch));
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        acc.x = fmaf(w[s + u], x[u].x, acc.x); acc.y = fmaf(w[s + u], x[u].y, acc.y);
-                        acc.z = fmaf(w[s + u], x[u].z, acc.z); acc.w = fmaf(w[s + u], x[u].w, acc.w);
-                    }
-                }
-                for (; s < nsp; ++s) {
-                    const float4 x = __ldg(reinterpret_cast<const float4*>(src + s * pitch));
-                    acc.x = fmaf(w[s], x.x, acc.x); acc.y = fmaf(w[s], x.y, acc.y);
-                    acc.z = fmaf(w[s], x.z, acc.z); acc.w = fmaf(w[s], x.w, acc.w);
-                }
+                const int64_t row = (int64_t)p0 * a.raw_rows + rr;
+                acc = combine_partials(a.raw_o + row * a.dim + c, pitch, a.raw_lse + row, a.raw_rows, nsp, &lse);
             }
+            if (c == 0) s_lse[16 + r] = lse;
             *reinterpret_cast<float4*>(s_raw + r * a.dim + c) = acc;
         }
     }

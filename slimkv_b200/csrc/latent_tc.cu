@@ -923,6 +923,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
         tc_fence_after();
         tmem_dealloc(tbase, kTmemCols);
     }
+    // Every CTA issues this at its end, so the merge launch (which waits for
+    // this grid's completion before reading its partials) can be set up while
+    // the last CTAs finish, never ahead of a CTA that has not started.
+    if (tid == 0) grid_launch_dependents();
 }
 
 namespace {

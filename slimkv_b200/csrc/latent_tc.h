@@ -31,11 +31,13 @@ constexpr int kTcClasses = 3;
 //   seg_piece[k] : [segments + 1] first piece of each segment (prefix)
 //   seg_id[k]    : [segments] sequence b (latent) or b * Hkv + g (raw)
 //   lat_seg[b]   : (class << 24) | segment of sequence b's latent segment
+//   lat_range[b] : {(class << 24) | first piece in its class, pieces} of
+//                  sequence b's latent segment (the merge's one lookup)
 struct TcPlanLayout {
     int max_lat_segs;      // batch
     int max_raw_segs;      // batch * kv_heads
     // Word offsets inside the plan array.
-    int hdr, seg_start[kTcClasses], seg_piece[kTcClasses], seg_id[kTcClasses], lat_seg;
+    int hdr, seg_start[kTcClasses], seg_piece[kTcClasses], seg_id[kTcClasses], lat_seg, lat_range;
     int words;
 };
 
@@ -52,6 +54,8 @@ __host__ __device__ inline TcPlanLayout tc_plan_layout(int batch, int kv_heads) 
         L.seg_id[k] = at; at += n;
     }
     L.lat_seg = at; at += batch;
+    at = (at + 1) & ~1;                      // int2 entries
+    L.lat_range = at; at += 2 * batch;
     L.words = at;
     return L;
 }

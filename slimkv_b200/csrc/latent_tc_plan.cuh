@@ -64,11 +64,31 @@ __device__ __host__ inline long long tc_cta_start(int tiles, int ctas, int i) {
     return (long long)tiles * i / ctas;
 }
 
-__device__ inline void plan_tc_work(const TcPlanArgs& a) {
+// Relative cost of a tile by class, in 16 KB latent chunks streamed: a
+// class-0 tile counts its chunks; the two-query layout (class 1, a K ring of
+// two chunks) streams them more slowly; a raw tile (64 KB, with a Q load and
+// an epilogue every few tiles) costs less than a latent tile but more than
+// its bytes.  Measured per-tile times on config 2 set the values.
+#ifndef SLIMKV_TC_W_TWO_QUERY
+#define SLIMKV_TC_W_TWO_QUERY 1.4f
+#endif
+#ifndef SLIMKV_TC_W_RAW_TILE
+#define SLIMKV_TC_W_RAW_TILE 7.5f
+#endif
+
+// `scratch` (shared memory, `scratch_words` ints): when the whole plan fits,
+// it is built there — every prefix, binary search and atomic stays on chip —
+// and copied to `a.plan` at the end; otherwise it is built in place.
+__device__ inline void plan_tc_work(const TcPlanArgs& a, int32_t* scratch, int scratch_words) {
     __shared__ int s_warp[32];
     const TcPlanLayout L = tc_plan_layout(a.batch, a.kv_heads);
-    int32_t* P = a.plan;
+    const bool on_chip = L.words <= scratch_words;
+    int32_t* P = on_chip ? scratch : a.plan;
     const int tid = threadIdx.x;
+    if (on_chip) {
+        for (int i = tid; i < L.words; i += blockDim.x) P[i] = 0;
+        __syncthreads();
+    }
     // 1. Latent segments of both classes, raw tile prefix.
     int carry[5] = {0, 0, 0, 0, 0};      // segments / tiles of class 0, 1; raw tiles
     for (int b0 = 0; b0 < a.batch; b0 += blockDim.x) {
@@ -104,11 +124,8 @@ __device__ inline void plan_tc_work(const TcPlanArgs& a) {
     if (tid < 3) P[L.seg_start[tid] + nseg[tid]] = tiles[tid];
     // 2. CTAs per class (thread 0).
     if (tid == 0) {
-        // Relative cost of a tile: its 16 KB chunks, x1.25 for the two-query
-        // layout (a K ring of two chunks) and x2 for raw tiles (the same
-        // per-tile softmax and MMA work as a latent tile for 2/5 of the bytes,
-        // short segments with a Q load and an epilogue every few tiles).
-        const float w[3] = {float(tiles[0]) * a.lat_chunks, 1.25f * tiles[1] * a.lat_chunks, 2.0f * tiles[2] * 4};
+        const float w[3] = {float(tiles[0]) * a.lat_chunks, SLIMKV_TC_W_TWO_QUERY * tiles[1] * a.lat_chunks,
+                            SLIMKV_TC_W_RAW_TILE * tiles[2]};
         // A raw CTA count given by the caller is kept; the other classes share
         // the rest by weight, at least one CTA each and at most one per tile.
         const bool fixed2 = a.raw_ctas > 0 && tiles[2] > 0;
@@ -173,6 +190,16 @@ __device__ inline void plan_tc_work(const TcPlanArgs& a) {
         if (tid == 0) piece[ns] = carry_p;
         __syncthreads();
     }
+    // 4. Each sequence's latent piece range.
+    for (int b = tid; b < a.batch; b += blockDim.x) {
+        const int ls = P[L.lat_seg + b], cls = ls >> 24, s = ls & 0xffffff;
+        const int32_t* pc = P + L.seg_piece[cls];
+        P[L.lat_range + 2 * b] = (cls << 24) | pc[s];
+        P[L.lat_range + 2 * b + 1] = pc[s + 1] - pc[s];
+    }
+    __syncthreads();
+    if (on_chip)
+        for (int i = tid; i < L.words; i += blockDim.x) a.plan[i] = P[i];
 }
 
 }  // namespace slimkv
