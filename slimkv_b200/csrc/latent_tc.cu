@@ -46,6 +46,7 @@
 // SLIMKV_DEVICE_TIMEOUT, drains its copies and MMAs (bounded), frees TMEM and
 // returns.
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "host_utils.h"
@@ -498,220 +499,231 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
         umma_commit(&ms->final_mma);
     } else if (warp >= 3 && warp <= 6 && cls < 2) {
         // ---- latent softmax and epilogue: thread <-> key (TMEM lane) ----
-        const int quarter = warp & 3;
-        const int t_local = 32 * quarter + lane;
-        const uint32_t lane_addr = uint32_t(32 * quarter) << 16;
-        const int st = tid - 96;                      // 0..127
-        bool failed = false;
-        int s = R.s0;
-        long long pos = R.r0;
-        int j = 0;
-        for (int k = 0; pos < R.r1 && !failed; ++k) {
-            Piece p;
-            next_piece(R, k, s, pos, J.kv_heads, p);
-            const int ob = k & 1;
-            const uint32_t o_tmem = tbase + uint32_t(ob) * kOBufCols;
-            const int n_keys = J.seqlens[p.b];
-            const int nq = J.qlens ? J.qlens[p.b] : J.length;
-            const bool cols = nq == 1;
-            const int rows = 32 * nq;
-            const int n_tiles = (max(n_keys, 0) + kKeys - 1) / kKeys;
-            if (st < 64) {
-                ms->m_run[st] = -INFINITY;
-                ms->l_run[st] = 0.f;
-            }
-            named_bar(1, 128);
-            for (int t = p.t0; t < p.t1; ++t, ++j) {
-                const int sb = j & 1;
-                const uint32_t s_tmem = tbase + kSCol + uint32_t(sb * kN);
-                const int key = t * kKeys + t_local;
-                bool ok = wait_or_abort(&ms->sfull[sb], (j >> 1) & 1, ms, J.status, wait_ns);
-                if (named_bar_or(1, 128, !ok)) { failed = true; break; }
-                tc_fence_after();
-                float v[2][32];
-                tmem_ld32(s_tmem + lane_addr, v[0]);
-                tmem_ld32(s_tmem + lane_addr + 32, v[1]);
-                tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&ms->sempty[sb]);
-                if (cols && !J.q_rows) {
-#pragma unroll
-                    for (int h = 0; h < 32; ++h) v[0][h] += v[1][h];       // hi + lo products
+        // Instantiated per query count (class 0: one query, class 1: two), so
+        // a CTA runs straight-line code for its own layout only.
+        auto latent_softmax = [&](auto nq_tag) {
+            constexpr int NQ = decltype(nq_tag)::value;
+            const int quarter = warp & 3;
+            const int t_local = 32 * quarter + lane;
+            const uint32_t lane_addr = uint32_t(32 * quarter) << 16;
+            const int st = tid - 96;                      // 0..127
+            bool failed = false;
+            int s = R.s0;
+            long long pos = R.r0;
+            int j = 0;
+            for (int k = 0; pos < R.r1 && !failed; ++k) {
+                Piece p;
+                next_piece(R, k, s, pos, J.kv_heads, p);
+                const int ob = k & 1;
+                const uint32_t o_tmem = tbase + uint32_t(ob) * kOBufCols;
+                const int n_keys = J.seqlens[p.b];
+                constexpr bool cols = NQ == 1;
+                constexpr int rows = 32 * NQ;
+                const int n_tiles = (max(n_keys, 0) + kKeys - 1) / kKeys;
+                if (st < 64) {
+                    ms->m_run[st] = -INFINITY;
+                    ms->l_run[st] = 0.f;
                 }
-                // scale and mask (an insertion step's raw query excludes the new Beacon)
-#pragma unroll
-                for (int l = 0; l < 2; ++l) {
-                    const int limit = (J.causal && nq == 2 && l == 0) ? n_keys - 1 : n_keys;
-#pragma unroll
-                    for (int h = 0; h < 32; ++h) v[l][h] = key < limit ? v[l][h] * J.scale_log2 : -INFINITY;
-                }
-                // Column maxima only when some score exceeds its row's running
-                // max by more than the lazy threshold (always on a piece's first
-                // tile): otherwise the max stays and every p <= 2^8.
-                bool over = t == p.t0;
-                if (!over) {
-#pragma unroll
-                    for (int l = 0; l < 2; ++l)
-                        if (l < nq) {
-#pragma unroll
-                            for (int h = 0; h < 32; ++h) over |= v[l][h] > ms->m_run[32 * l + h] + kLazyLog2;
-                        }
-                }
-                const bool rescan = named_bar_or(1, 128, over);
-                bool need_fix = false;
-                if (rescan) {
-#pragma unroll
-                    for (int l = 0; l < 2; ++l) {
-                        if (l < nq) {
-                            float tmp[32];
-#pragma unroll
-                            for (int h = 0; h < 32; ++h) tmp[h] = v[l][h];
-                            ms->red[quarter][32 * l + lane] = warp_transpose_reduce<true>(tmp, lane);
-                        }
-                    }
-                    named_bar(1, 128);
-                    if (st < rows) {
-                        const float tm =
-                            fmaxf(fmaxf(ms->red[0][st], ms->red[1][st]), fmaxf(ms->red[2][st], ms->red[3][st]));
-                        const float mo = ms->m_run[st];
-                        float mn = mo, alpha = 1.f;
-                        if (tm != -INFINITY && (mo == -INFINITY || tm > mo + kLazyLog2)) {
-                            mn = fmaxf(mo, tm);
-                            alpha = mo == -INFINITY ? 0.f : exp2f(mo - mn);
-                        }
-                        ms->alpha[st] = alpha;
-                        ms->m_run[st] = mn;
-                        ms->l_run[st] *= alpha;
-                    }
-                    need_fix = named_bar_or(1, 128, st < rows && t > p.t0 && ms->alpha[st] != 1.f);
-                }
-                // P(j) overwrites the buffer P.V(j-1) reads: wait for it.
-                if (j > 0) {
-                    ok = wait_or_abort(&ms->odone[(j - 1) & 1], ((j - 1) >> 1) & 1, ms, J.status, wait_ns);
+                named_bar(1, 128);
+                for (int t = p.t0; t < p.t1; ++t, ++j) {
+                    const int sb = j & 1;
+                    const uint32_t s_tmem = tbase + kSCol + uint32_t(sb * kN);
+                    const int key = t * kKeys + t_local;
+                    bool ok = wait_or_abort(&ms->sfull[sb], (j >> 1) & 1, ms, J.status, wait_ns);
                     if (named_bar_or(1, 128, !ok)) { failed = true; break; }
                     tc_fence_after();
-                }
-                // The sequence's partial last tile: V rows past the length hold
-                // whatever the cache has there; P is zero for them, and zeroing
-                // the rows too keeps a non-finite stale value from turning 0 * x
-                // into NaN.  Each thread clears its own key row once the chunk
-                // has landed (P.V(j) does not start before P(j) is released).
-                if (t == n_tiles - 1 && (n_keys & (kKeys - 1)) != 0) {
-                    bool okc = true;
-                    if (key >= n_keys) {
-                        for (int c = 0; c < vc && okc; ++c) {
-                            const int slot = v_slot(j, c);
-                            okc = wait_or_abort(&ms->vfull[slot], v_use(j) & 1, ms, J.status, wait_ns);
-                            if (okc) {
-                                uint4* row = reinterpret_cast<uint4*>(smem + slot * kChunkBytes + t_local * 128);
+                    float v[2][32];
+                    tmem_ld32(s_tmem + lane_addr, v[0]);
+                    tmem_ld32(s_tmem + lane_addr + 32, v[1]);
+                    tmem_wait_ld();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&ms->sempty[sb]);
+                    if constexpr (cols) {
 #pragma unroll
-                                for (int u = 0; u < 8; ++u) row[u] = make_uint4(0, 0, 0, 0);
+                        for (int h = 0; h < 32; ++h) v[0][h] += v[1][h];       // hi + lo products
+                    }
+                    // scale and mask (an insertion step's raw query excludes the new Beacon)
+#pragma unroll
+                    for (int l = 0; l < 2; ++l) {
+                        const int limit = (J.causal && NQ == 2 && l == 0) ? n_keys - 1 : n_keys;
+#pragma unroll
+                        for (int h = 0; h < 32; ++h) v[l][h] = key < limit ? v[l][h] * J.scale_log2 : -INFINITY;
+                    }
+                    // Column maxima only when some score exceeds its row's running
+                    // max by more than the lazy threshold (always on a piece's first
+                    // tile): otherwise the max stays and every p <= 2^8.
+                    bool over = t == p.t0;
+                    if (!over) {
+#pragma unroll
+                        for (int l = 0; l < 2; ++l)
+                            if (l < NQ) {
+#pragma unroll
+                                for (int h = 0; h < 32; ++h) over |= v[l][h] > ms->m_run[32 * l + h] + kLazyLog2;
+                            }
+                    }
+                    const bool rescan = named_bar_or(1, 128, over);
+                    bool need_fix = false;
+                    if (rescan) {
+#pragma unroll
+                        for (int l = 0; l < 2; ++l) {
+                            if (l < NQ) {
+                                float tmp[32];
+#pragma unroll
+                                for (int h = 0; h < 32; ++h) tmp[h] = v[l][h];
+                                ms->red[quarter][32 * l + lane] = warp_transpose_reduce<true>(tmp, lane);
                             }
                         }
+                        named_bar(1, 128);
+                        if (st < rows) {
+                            const float tm =
+                                fmaxf(fmaxf(ms->red[0][st], ms->red[1][st]), fmaxf(ms->red[2][st], ms->red[3][st]));
+                            const float mo = ms->m_run[st];
+                            float mn = mo, alpha = 1.f;
+                            if (tm != -INFINITY && (mo == -INFINITY || tm > mo + kLazyLog2)) {
+                                mn = fmaxf(mo, tm);
+                                alpha = mo == -INFINITY ? 0.f : exp2f(mo - mn);
+                            }
+                            ms->alpha[st] = alpha;
+                            ms->m_run[st] = mn;
+                            ms->l_run[st] *= alpha;
+                        }
+                        need_fix = named_bar_or(1, 128, st < rows && t > p.t0 && ms->alpha[st] != 1.f);
                     }
-                    if (named_bar_or(1, 128, !okc)) { failed = true; break; }
-                }
-                if (need_fix) {
-                    // O^T column group k2 (32 columns) belongs to row k2*32 + h,
-                    // or to row h for the single-query hi | lo layout.
-                    for (int blk = 0; blk < vblocks; ++blk)
-                        for (int k2 = 0; k2 < 2; ++k2) {
-                            float o[32];
-                            const uint32_t addr = o_tmem + lane_addr + uint32_t(blk * kN + 32 * k2);
-                            tmem_ld32(addr, o);
-                            tmem_wait_ld();
-                            const float* al = ms->alpha + (cols ? 0 : 32 * k2);
-#pragma unroll
-                            for (int h = 0; h < 32; ++h) o[h] *= al[h];
-                            tmem_st32(addr, o);
-                        }
-                    tmem_wait_st();
-                }
-                // probabilities -> P^T rows (hi and lo), row sums
-                uint8_t* prow = smem + LY.off_p + t_local * 128;
-#pragma unroll
-                for (int l = 0; l < 2; ++l) {
-                    if (l < nq) {
-                        float pr[32];
-#pragma unroll
-                        for (int h = 0; h < 32; ++h) {
-                            const float m = ms->m_run[32 * l + h];
-                            pr[h] = (v[l][h] == -INFINITY || m == -INFINITY) ? 0.f : exp2f(v[l][h] - m);
-                        }
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            uint4 hi, lo;
-                            split_hilo(pr, u, hi, lo);
-                            // nq = 1: units 0-3 hi, 4-7 lo of one buffer; nq = 2:
-                            // unit 4l + u of the hi and of the lo buffer.
-                            const int uh = cols ? u : 4 * l + u, ul = cols ? 4 + u : 4 * l + u;
-                            uint8_t* lrow = cols ? prow : prow + kChunkBytes;
-                            *reinterpret_cast<uint4*>(prow + ((uh ^ (t_local & 7)) << 4)) = hi;
-                            *reinterpret_cast<uint4*>(lrow + ((ul ^ (t_local & 7)) << 4)) = lo;
-                        }
-                        ms->red[quarter][32 * l + lane] = warp_transpose_reduce<false>(pr, lane);
+                    // P(j) overwrites the buffer P.V(j-1) reads: wait for it.
+                    if (j > 0) {
+                        ok = wait_or_abort(&ms->odone[(j - 1) & 1], ((j - 1) >> 1) & 1, ms, J.status, wait_ns);
+                        if (named_bar_or(1, 128, !ok)) { failed = true; break; }
+                        tc_fence_after();
                     }
+                    // The sequence's partial last tile: V rows past the length hold
+                    // whatever the cache has there; P is zero for them, and zeroing
+                    // the rows too keeps a non-finite stale value from turning 0 * x
+                    // into NaN.  Each thread clears its own key row once the chunk
+                    // has landed (P.V(j) does not start before P(j) is released).
+                    if (t == n_tiles - 1 && (n_keys & (kKeys - 1)) != 0) {
+                        bool okc = true;
+                        if (key >= n_keys) {
+                            for (int c = 0; c < vc && okc; ++c) {
+                                const int slot = v_slot(j, c);
+                                okc = wait_or_abort(&ms->vfull[slot], v_use(j) & 1, ms, J.status, wait_ns);
+                                if (okc) {
+                                    uint4* row = reinterpret_cast<uint4*>(smem + slot * kChunkBytes + t_local * 128);
+#pragma unroll
+                                    for (int u = 0; u < 8; ++u) row[u] = make_uint4(0, 0, 0, 0);
+                                }
+                            }
+                        }
+                        if (named_bar_or(1, 128, !okc)) { failed = true; break; }
+                    }
+                    if (need_fix) {
+                        // O^T column group k2 (32 columns) belongs to row k2*32 + h,
+                        // or to row h for the single-query hi | lo layout.
+                        for (int blk = 0; blk < vblocks; ++blk)
+                            for (int k2 = 0; k2 < 2; ++k2) {
+                                float o[32];
+                                const uint32_t addr = o_tmem + lane_addr + uint32_t(blk * kN + 32 * k2);
+                                tmem_ld32(addr, o);
+                                tmem_wait_ld();
+                                const float* al = ms->alpha + (cols ? 0 : 32 * k2);
+#pragma unroll
+                                for (int h = 0; h < 32; ++h) o[h] *= al[h];
+                                tmem_st32(addr, o);
+                            }
+                        tmem_wait_st();
+                    }
+                    // probabilities -> P^T rows (hi and lo), row sums
+                    uint8_t* prow = smem + LY.off_p + t_local * 128;
+#pragma unroll
+                    for (int l = 0; l < 2; ++l) {
+                        if (l < NQ) {
+                            float pr[32];
+#pragma unroll
+                            for (int h = 0; h < 32; ++h) {
+                                const float m = ms->m_run[32 * l + h];
+                                pr[h] = (v[l][h] == -INFINITY || m == -INFINITY) ? 0.f : exp2f(v[l][h] - m);
+                            }
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                uint4 hi, lo;
+                                split_hilo(pr, u, hi, lo);
+                                // nq = 1: units 0-3 hi, 4-7 lo of one buffer; nq = 2:
+                                // unit 4l + u of the hi and of the lo buffer.
+                                const int uh = cols ? u : 4 * l + u, ul = cols ? 4 + u : 4 * l + u;
+                                uint8_t* lrow = cols ? prow : prow + kChunkBytes;
+                                *reinterpret_cast<uint4*>(prow + ((uh ^ (t_local & 7)) << 4)) = hi;
+                                *reinterpret_cast<uint4*>(lrow + ((ul ^ (t_local & 7)) << 4)) = lo;
+                            }
+                            ms->red[quarter][32 * l + lane] = warp_transpose_reduce<false>(pr, lane);
+                        }
+                    }
+                    fence_async_shared();
+                    tc_fence_before();
+                    named_bar(1, 128);
+                    if (st < rows)
+                        ms->l_run[st] += ms->red[0][st] + ms->red[1][st] + ms->red[2][st] + ms->red[3][st];
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&ms->pfull[j & 1]);
                 }
-                fence_async_shared();
-                tc_fence_before();
+                if (failed) break;
+                // ---- epilogue of the piece: normalised partial output and LSE ----
+                {
+                    const bool ok = wait_or_abort(&ms->odone[(j - 1) & 1], ((j - 1) >> 1) & 1, ms, J.status, wait_ns);
+                    if (named_bar_or(1, 128, !ok)) { failed = true; break; }
+                }
+                tc_fence_after();
+                named_bar(1, 128);                     // every thread's l_run update is in
+                if (st < 64) ms->alpha[st] = (st < rows && ms->l_run[st] > 0.f) ? 1.f / ms->l_run[st] : 0.f;
                 named_bar(1, 128);
-                if (st < rows)
-                    ms->l_run[st] += ms->red[0][st] + ms->red[1][st] + ms->red[2][st] + ms->red[3][st];
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&ms->pfull[j & 1]);
-            }
-            if (failed) break;
-            // ---- epilogue of the piece: normalised partial output and LSE ----
-            {
-                const bool ok = wait_or_abort(&ms->odone[(j - 1) & 1], ((j - 1) >> 1) & 1, ms, J.status, wait_ns);
-                if (named_bar_or(1, 128, !ok)) { failed = true; break; }
-            }
-            tc_fence_after();
-            named_bar(1, 128);                     // every thread's l_run update is in
-            if (st < 64) ms->alpha[st] = (st < rows && ms->l_run[st] > 0.f) ? 1.f / ms->l_run[st] : 0.f;
-            named_bar(1, 128);
-            const int piece = piece_base + p.piece;
-            float* out = J.part_o + (int64_t)piece * J.rows_alloc * J.out_width;
-            // Output row of (query l, head column h): l * rg + h for h < rg (rg
-            // = all 32 heads for the latent branch, the group for raw rows).
-            const int rg = J.q_rows ? J.group : 32;
-            for (int blk = 0; blk < vblocks; ++blk) {
-                const bool pair = 2 * blk + 1 < vc;
-                float o[2][32];
-                tmem_ld32(o_tmem + lane_addr + uint32_t(blk * kN), o[0]);
-                tmem_ld32(o_tmem + lane_addr + uint32_t(blk * kN + 32), o[1]);
-                tmem_wait_ld();
-                // An M=128 block holds dim 32q + L of its chunk pair in lane L
-                // of quarter q; the M=64 block holds dim 16q + L in lane L < 16.
-                if (pair || lane < 16) {
-                    const int d = 128 * blk + (pair ? 32 * quarter + lane : 16 * quarter + lane);
-                    if (cols) {
+                const int piece = piece_base + p.piece;
+                float* out = J.part_o + (int64_t)piece * J.rows_alloc * J.out_width;
+                // Output row of (query l, head column h): l * rg + h for h < rg (rg
+                // = all 32 heads for the latent branch, the group for raw rows).
+                constexpr int rg = 32;
+                // The row scales in registers: read between the global stores
+                // through a generic pointer they would be reloaded every time.
+                float al[rows];
 #pragma unroll
-                        for (int h = 0; h < 32; ++h)
-                            if (h < rg) out[h * J.out_width + d] = (o[0][h] + o[1][h]) * ms->alpha[h];
-                    } else {
+                for (int h = 0; h < rows; ++h) al[h] = ms->alpha[h];
+                for (int blk = 0; blk < vblocks; ++blk) {
+                    const bool pair = 2 * blk + 1 < vc;
+                    float o[2][32];
+                    tmem_ld32(o_tmem + lane_addr + uint32_t(blk * kN), o[0]);
+                    tmem_ld32(o_tmem + lane_addr + uint32_t(blk * kN + 32), o[1]);
+                    tmem_wait_ld();
+                    // An M=128 block holds dim 32q + L of its chunk pair in lane L
+                    // of quarter q; the M=64 block holds dim 16q + L in lane L < 16.
+                    if (pair || lane < 16) {
+                        const int d = 128 * blk + (pair ? 32 * quarter + lane : 16 * quarter + lane);
+                        if constexpr (cols) {
 #pragma unroll
-                        for (int h = 0; h < 32; ++h) {
-                            if (h < rg) {
-                                out[h * J.out_width + d] = o[0][h] * ms->alpha[h];
-                                out[(rg + h) * J.out_width + d] = o[1][h] * ms->alpha[32 + h];
+                            for (int h = 0; h < 32; ++h)
+                                if (h < rg) out[h * J.out_width + d] = (o[0][h] + o[1][h]) * al[h];
+                        } else {
+#pragma unroll
+                            for (int h = 0; h < 32; ++h) {
+                                if (h < rg) {
+                                    out[h * J.out_width + d] = o[0][h] * al[h];
+                                    out[(rg + h) * J.out_width + d] = o[1][h] * al[32 + h];
+                                }
                             }
                         }
                     }
                 }
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ms->oempty[ob]);
+                if (st < rows && (st & 31) < rg) {
+                    const float lsum = ms->l_run[st];
+                    J.part_lse[(int64_t)piece * J.rows_alloc + (st >> 5) * rg + (st & 31)] =
+                        lsum > 0.f ? (ms->m_run[st] + log2f(lsum)) * 0.69314718055994530942f : -INFINITY;
+                }
+                named_bar(1, 128);                     // m_run / l_run / alpha are reset by the next piece
             }
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ms->oempty[ob]);
-            if (st < rows && (st & 31) < rg) {
-                const float lsum = ms->l_run[st];
-                J.part_lse[(int64_t)piece * J.rows_alloc + (st >> 5) * rg + (st & 31)] =
-                    lsum > 0.f ? (ms->m_run[st] + log2f(lsum)) * 0.69314718055994530942f : -INFINITY;
-            }
-            named_bar(1, 128);                     // m_run / l_run / alpha are reset by the next piece
-        }
+        };
+        if (cls == 0) latent_softmax(std::integral_constant<int, 1>{});
+        else latent_softmax(std::integral_constant<int, 2>{});
     } else if (warp >= 3 && warp <= 6) {
         // ---- raw softmax and epilogue: thread <-> key, 16 score columns ----
         // Column l * kRawCols + h holds query l of head h of the group (Q rows
@@ -862,6 +874,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
             named_bar(1, 128);
             const int piece = piece_base + p.piece;
             float* out = J.part_o + (int64_t)piece * J.rows_alloc * J.out_width;
+            float al[kRawS];
+#pragma unroll
+            for (int c = 0; c < kRawS; ++c) al[c] = ms->alpha[c];
             for (int blk = 0; blk < vblocks; ++blk) {
                 const bool pair = 2 * blk + 1 < vc;
                 float o[32];
@@ -875,7 +890,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
 #pragma unroll
                             for (int h = 0; h < kRawCols; ++h) {
                                 const int c = l * kRawCols + h;
-                                if (h < rg) out[(l * rg + h) * J.out_width + d] = (o[c] + o[kRawS + c]) * ms->alpha[c];
+                                if (h < rg) out[(l * rg + h) * J.out_width + d] = (o[c] + o[kRawS + c]) * al[c];
                             }
                         }
                     }
