@@ -236,11 +236,30 @@ typedef struct {
      * cache [B, Hkv, raw_capacity, D] passes raw_stride_token = head_dim and
      * raw_stride_head = raw_capacity * head_dim. */
     int64_t raw_stride_head;
+    /* The step's work plan from slimkv_decode_plan (int32 words on the
+     * device), shared by the step's layers: the call then skips planning and
+     * its attention launch starts while its prologue finishes (the tensor-core
+     * route; ignored elsewhere).  NULL: the call plans in its workspace.  It
+     * must have been computed from this call's raw_len / latent_len /
+     * query_len values. */
+    const int32_t* plan;
 } slimkv_latent_decode_args;
 
 SLIMKV_API size_t slimkv_latent_decode_workspace_size(const slimkv_latent_decode_args* args);
 SLIMKV_API int slimkv_latent_decode(const slimkv_latent_decode_args* args, void* workspace,
                          size_t workspace_bytes, void* stream);
+
+/* The work plan of a fused decode step (the split of the latent and raw rows
+ * of every sequence over the attention CTAs), from the device lengths in
+ * `args` (raw_len, latent_len, query_len and the shapes; other pointers are
+ * not read).  Every layer of a step has the same lengths, so one plan serves
+ * all of them (slimkv_latent_decode_args.plan); it replaces the planning that
+ * each call otherwise does on its own.  `plan` holds slimkv_decode_plan_words
+ * int32 words; on the split-KV route nothing is written and the plan is
+ * ignored.  No counterpart in the reference: its decode has no batched
+ * device schedule. */
+SLIMKV_API size_t slimkv_decode_plan_words(const slimkv_latent_decode_args* args);
+SLIMKV_API int slimkv_decode_plan(const slimkv_latent_decode_args* args, int32_t* plan, void* stream);
 
 /* ------------------------------------------------------------------------
  * BF16-exact decode RoPE — drop-in for `decode_ops.fused_rope`

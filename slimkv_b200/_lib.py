@@ -64,7 +64,7 @@ class LatentDecodeArgs(ctypes.Structure):
         ('lat_sink_elements', ctypes.c_int), ('lat_table', ctypes.c_void_p), ('lat_table_stride', ctypes.c_int64),
         ('lat_num_pages', ctypes.c_int),
         ('out_lse', ctypes.c_void_p), ('latent_shard', ctypes.c_int), ('wait_limit_ns', ctypes.c_uint64),
-        ('raw_stride_head', ctypes.c_int64),
+        ('raw_stride_head', ctypes.c_int64), ('plan', ctypes.c_void_p),
     ]
 
 
@@ -148,6 +148,8 @@ SIGNATURES = {
     'slimkv_attention_forward_noalloc': (_I, [ctypes.POINTER(AttentionArgs), _P]),
     'slimkv_latent_decode_workspace_size': (ctypes.c_size_t, [ctypes.POINTER(LatentDecodeArgs)]),
     'slimkv_latent_decode': (_I, [ctypes.POINTER(LatentDecodeArgs), _P, ctypes.c_size_t, _P]),
+    'slimkv_decode_plan_words': (ctypes.c_size_t, [ctypes.POINTER(LatentDecodeArgs)]),
+    'slimkv_decode_plan': (_I, [ctypes.POINTER(LatentDecodeArgs), _P, _P]),
     'slimkv_rope_decode': (_I, [_P, ctypes.POINTER(ctypes.c_int64), _P, ctypes.POINTER(ctypes.c_int64), _P, _P,
                                 _I, _P, ctypes.c_int64, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
     'slimkv_decode_schedule': (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),

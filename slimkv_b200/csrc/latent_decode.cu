@@ -119,7 +119,7 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
         // and raw_splits, when given, set the CTA count of the launch and of
         // the raw class.
         const int sms = std::max(device_info().sm_count, 1);
-        const int cap = std::min(sms, kMergeMaxSplits - 1);
+        const int cap = std::min({sms, kMergeMaxSplits - 1, kTcMaxCtas});
         p.ctas = std::max(3, std::min(a->latent_splits > 0 ? a->latent_splits : sms, cap));
         p.raw_ctas = a->raw_splits > 0 ? std::min(a->raw_splits, p.ctas - 2) : 0;
         p.lat_rows = 64;
@@ -293,13 +293,14 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     pa.lat_page_stride = a->lat_page_stride; pa.lat_table_stride = a->lat_table_stride;
     pa.lat_slots = a->lat_slots; pa.lat_sink = a->lat_sink_elements; pa.lat_num_pages = a->lat_num_pages;
     pa.lat_table = a->lat_table;
+    int32_t* plan = a->plan ? const_cast<int32_t*>(a->plan) : w.plan;
     if (p.tc) {
-        pa.do_plan = 1;
+        pa.do_plan = a->plan ? 0 : 1;
         TcPlanArgs& pl = pa.plan;
         pl.batch = a->batch; pl.kv_heads = a->kv_heads; pl.length = a->length;
         pl.latent_len = a->latent_len; pl.raw_len = a->raw_len; pl.query_len = a->query_len;
         pl.lat_chunks = (a->rank_k + 63) / 64 + (a->rank_v + 63) / 64;
-        pl.ctas = p.ctas; pl.raw_ctas = p.raw_ctas; pl.with_raw = 1; pl.plan = w.plan;
+        pl.ctas = p.ctas; pl.raw_ctas = p.raw_ctas; pl.with_raw = 1; pl.plan = plan;
     }
     pa.status = status;
     const dim3 pgrid(a->kv_heads, p.wl / 64, (a->batch + pa.seq_per_cta - 1) / pa.seq_per_cta + (p.tc ? 1 : 0));
@@ -346,8 +347,12 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         TcLaunch tl{};
         tl.batch = a->batch; tl.length = a->length; tl.scale = a->scale;
         tl.query_len = a->query_len; tl.status = status; tl.with_raw = 1;
-        tl.kv_heads = a->kv_heads; tl.ctas = p.ctas; tl.plan = w.plan; tl.lat_pieces = p.lat_pieces;
+        tl.kv_heads = a->kv_heads; tl.ctas = p.ctas; tl.plan = plan; tl.lat_pieces = p.lat_pieces;
         tl.wait_ns = a->wait_limit_ns;
+        // With the plan ready the attention may start before the prologue
+        // ends — not when its duration is being timed (the begin event would
+        // come after its start).
+        tl.early = a->plan && !a->attn_event_begin ? 1 : 0;
         TcSide& L = tl.lat;
         L.k = a->lat_k; L.v = a->lat_v; L.dim_k = a->rank_k; L.dim_v = a->rank_v;
         L.kv_heads = 1; L.capacity = a->lat_capacity;
@@ -391,7 +396,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     ma.lat_o = w.lat_o; ma.lat_lse = w.lat_lse; ma.lat_splits = p.lat_splits; ma.lat_rows = p.lat_rows;
     ma.lat_width = p.wl;
     if (p.tc) {
-        ma.plan = w.plan;
+        ma.plan = plan;
         ma.PL = tc_plan_layout(a->batch, a->kv_heads);
         ma.lat_pieces = p.lat_pieces;
     }
@@ -434,5 +439,41 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     e = cudaLaunchKernelEx(&cfg, decode_merge_kernel, ma);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "merge launch failed: %s", cudaGetErrorString(e));
+    return SLIMKV_OK;
+}
+
+namespace slimkv {
+namespace {
+
+// One block: the step plan of the tensor-core route (plan_tc_work), built in
+// this block's shared memory when it fits.
+__global__ void __launch_bounds__(256) decode_plan_kernel(TcPlanArgs pl) {
+    __shared__ int32_t scratch[8192];
+    plan_tc_work(pl, scratch, 8192);
+}
+
+}  // namespace
+}  // namespace slimkv
+
+extern "C" size_t slimkv_decode_plan_words(const slimkv_latent_decode_args* a) {
+    DecodePlan p;
+    if (plan_decode(a, p) != SLIMKV_OK) return 0;
+    return p.tc ? size_t(tc_plan_layout(a->batch, a->kv_heads).words) : 1;
+}
+
+extern "C" int slimkv_decode_plan(const slimkv_latent_decode_args* a, int32_t* plan, void* stream_ptr) {
+    DecodePlan p;
+    if (int rc = plan_decode(a, p)) return rc;
+    if (!p.tc) return SLIMKV_OK;                    // the split-KV route plans on the host
+    if (!plan || !a->raw_len || !a->latent_len)
+        return fail(SLIMKV_ERR_INVALID_ARGUMENT, "decode plan: null plan or length pointer");
+    TcPlanArgs pl{};
+    pl.batch = a->batch; pl.kv_heads = a->kv_heads; pl.length = a->length;
+    pl.latent_len = a->latent_len; pl.raw_len = a->raw_len; pl.query_len = a->query_len;
+    pl.lat_chunks = (a->rank_k + 63) / 64 + (a->rank_v + 63) / 64;
+    pl.ctas = p.ctas; pl.raw_ctas = p.raw_ctas; pl.with_raw = 1; pl.plan = plan;
+    decode_plan_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream_ptr)>>>(pl);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "decode plan launch failed: %s", cudaGetErrorString(e));
     return SLIMKV_OK;
 }

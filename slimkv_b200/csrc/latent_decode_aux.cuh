@@ -120,6 +120,11 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
     uint8_t* s_b = s_ab + kProRows * 128 * 2;           // U_k[g][:, cc*64 : +64] fp16
     const int g = blockIdx.x, cc = blockIdx.y, bb = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // An attention launch that depends on this one may start as soon as every
+    // block here has started (it waits for this grid's end before reading
+    // what it writes): all of this grid is resident by then, so it can only
+    // take SMs these blocks leave.
+    if (tid == 0) grid_launch_dependents();
     if (a.do_plan && bb == int(gridDim.z) - 1) {
         // The last z-slice only plans the attention (one block, in parallel
         // with the absorb blocks), in this block's shared memory when it fits.
@@ -426,8 +431,8 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
     // 0. (Before the attention launch completes.)  Each row's partial ranges
     //    (latent, raw) from the plan, U_v[g] (rows d, columns c) -> shared
     //    asynchronously with zero columns past the rank, the zero rows of the
-    //    A operand, and the latent LSE shift scale * q . b_k of each row
-    //    (fa2_decode.py:157-160) — none of it reads the attention's output.
+    //    A operand; then (after the attention grid) the latent LSE shift
+    //    scale * q . b_k of each row (fa2_decode.py:157-160).
     __shared__ int s_parts[16][4];
     float* s_shift = s_lse + 32;                        // [16]
     if (tid < 16) {
@@ -447,6 +452,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
     }
     cp_async_commit();
     for (int i = tid; i < 2 * 16 * rvp / 8; i += 256) reinterpret_cast<uint4*>(s_hi)[i] = make_uint4(0, 0, 0, 0);
+    grid_dependency_wait();
     for (int r = warp; r < 16; r += 8) {
         int b, l, h, rr;
         float dot = 0.f;
@@ -459,7 +465,6 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
         }
         if (lane == 0) s_shift[r] = dot * a.scale;
     }
-    grid_dependency_wait();
     __syncthreads();
     // 1. Latent branch: o_lat[r, c:c+4] combined over the row's pieces in one
     //    pass -> bf16 hi / lo (fp32-level accuracy through the bf16 tensor

@@ -222,7 +222,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                  const __grid_constant__ CUtensorMap lqmap, const __grid_constant__ CUtensorMap rkmap,
                  const __grid_constant__ CUtensorMap rvmap, const __grid_constant__ CUtensorMap rqmap,
                  const __grid_constant__ TcJob jl, const __grid_constant__ TcJob jr, const int32_t* __restrict__ plan,
-                 const TcPlanLayout PL, int lat_pieces) {
+                 const TcPlanLayout PL, int lat_pieces, int early) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     if (smem - smem_raw > int(kMaxPad)) {                     // uniform over the CTA, before any barrier
@@ -233,14 +233,12 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     // ---- class and range of this CTA ----
-    int cls = -1, idx = 0, nctas = 1, tiles = 0;
+    int cls = -1, idx = 0;
     for (int k = 0; k < kTcClasses; ++k) {
         const int n = plan[PL.hdr + 4 * k], base = plan[PL.hdr + 4 * k + 1];
         if (int(blockIdx.x) >= base && int(blockIdx.x) < base + n) {
             cls = k;
             idx = int(blockIdx.x) - base;
-            nctas = n;
-            tiles = plan[PL.hdr + 4 * k + 3];
         }
     }
     if (cls < 0) return;                                      // an idle CTA (before any barrier or TMEM)
@@ -254,14 +252,15 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
     R.pieces = plan + PL.seg_piece[cls];
     R.ids = plan + PL.seg_id[cls];
     R.nseg = plan[PL.hdr + 4 * cls + 2];
-    R.r0 = tc_cta_start(tiles, nctas, idx);
-    R.r1 = tc_cta_start(tiles, nctas, idx + 1);
+    const int32_t* cta_start = plan + PL.cta_start[cls];
+    R.r0 = cta_start[idx];
+    R.r1 = cta_start[idx + 1];
     if (R.r0 >= R.r1) return;
     R.s0 = tc_segment_of(R.start, R.nseg, R.r0);
     {
         int cnt = 0;                                          // CTAs <= idx starting strictly inside s0
         for (int j = idx; j >= 1; --j) {
-            if (tc_cta_start(tiles, nctas, j) > R.start[R.s0]) ++cnt;
+            if (cta_start[j] > R.start[R.s0]) ++cnt;
             else break;
         }
         R.first_piece = R.pieces[R.s0] + cnt;
@@ -270,7 +269,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
     const int kc = J.kchunks, vc = J.vchunks;
     const Layout LY = class_layout(cls, kc);
     const int kring = LY.kring;
-    const int total_tiles = int(R.r1 - R.r0);
     const uint64_t wait_ns = J.wait_ns;
     // V chunk n -> (CTA tile T = n / vc, chunk c = n % vc) in V slot c; with
     // <= 2 chunks per tile (raw) tiles alternate between slot pairs (0,1) and
@@ -353,15 +351,29 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
         long long pos = R.r0;
         bool ok = true;
         int j = 0;                                           // CTA tile
+        // An early launch waits for the prologue before its first copy of
+        // something the prologue writes: Q, and a segment's last tile (this
+        // step's raw token or Beacon row).  Copies before that overlap it.
+        bool waited = !early;
+        auto await_prologue = [&]() {
+            if (!waited) {
+                grid_dependency_wait();
+                waited = true;
+            }
+        };
         for (int k = 0; pos < R.r1 && ok; ++k) {
             Piece p;
             next_piece(R, k, s, pos, J.kv_heads, p);
-            if (kq) {
-                // Q of the piece, into a buffer S has finished with.
+            const int last_tile = (max(J.seqlens[p.b], 1) - 1) / kKeys;
+            // Q of the piece, issued once the first K chunks of the piece that
+            // fit the ring are on their way (S of the piece needs Q before it
+            // frees a K slot).
+            auto load_q = [&]() {
+                await_prologue();
                 const int qb = k % LY.qbufs;
                 if (k >= LY.qbufs &&
                     !(ok = wait_or_abort(&ms->qempty[qb], ((k / LY.qbufs) - 1) & 1, ms, J.status, wait_ns)))
-                    break;
+                    return;
                 uint8_t* qdst = smem + LY.off_q + qb * LY.qbytes;
                 const int nq = J.qlens ? J.qlens[p.b] : J.length;
                 if (J.q_rows) {
@@ -381,8 +393,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                             tma_load_4d(qdst + (hl * kMaxChunks + c) * kQChunkBytes, qmap, &ms->qfull[qb], c * 64, 0,
                                         hl * 64, p.b);
                 }
-            }
+            };
             for (int t = p.t0; t < p.t1 && ok; ++t, ++j) {
+                if (t == last_tile) await_prologue();
                 if (kq) {
                     for (int c = 0; c < kc; ++c) {
                         const int n = j * kc + c, slot = n % kring;
@@ -391,6 +404,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                             break;
                         mbar_expect_tx(&ms->kfull[slot], kChunkBytes);
                         load_chunk(smem + LY.off_k + slot * kChunkBytes, kmap, &ms->kfull[slot], c * 64, p, t);
+                        if (t == p.t0 && c == min(kc, kring) - 1) {
+                            load_q();
+                            if (!ok) break;
+                        }
                     }
                 } else {
                     for (int c = 0; c < vc; ++c) {
@@ -525,20 +542,31 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     ms->l_run[st] = 0.f;
                 }
                 named_bar(1, 128);
-                for (int t = p.t0; t < p.t1; ++t, ++j) {
+                // An early launch starts its first piece with a dry tile (t = t0 - 1):
+                // the tile code runs once on zero scores while the prologue finishes, so
+                // the real tiles find it in the instruction cache.  It waits on and
+                // signals nothing; its row state is reset after it and its P write lands
+                // in a buffer no MMA reads yet.
+                for (int t = p.t0 - (k == 0 && early ? 1 : 0); t < p.t1; ++t) {
+                    const bool dry = t < p.t0;
                     const int sb = j & 1;
                     const uint32_t s_tmem = tbase + kSCol + uint32_t(sb * kN);
                     const int key = t * kKeys + t_local;
-                    bool ok = wait_or_abort(&ms->sfull[sb], (j >> 1) & 1, ms, J.status, wait_ns);
+                    bool ok = dry || wait_or_abort(&ms->sfull[sb], (j >> 1) & 1, ms, J.status, wait_ns);
                     if (named_bar_or(1, 128, !ok)) { failed = true; break; }
                     tc_fence_after();
                     float v[2][32];
-                    tmem_ld32(s_tmem + lane_addr, v[0]);
-                    tmem_ld32(s_tmem + lane_addr + 32, v[1]);
+                    if (dry) {
+#pragma unroll
+                        for (int h = 0; h < 32; ++h) v[0][h] = v[1][h] = 0.f;
+                    } else {
+                        tmem_ld32(s_tmem + lane_addr, v[0]);
+                        tmem_ld32(s_tmem + lane_addr + 32, v[1]);
+                    }
                     tmem_wait_ld();
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&ms->sempty[sb]);
+                    if (lane == 0 && !dry) mbar_arrive(&ms->sempty[sb]);
                     if constexpr (cols) {
 #pragma unroll
                         for (int h = 0; h < 32; ++h) v[0][h] += v[1][h];       // hi + lo products
@@ -553,7 +581,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     // Column maxima only when some score exceeds its row's running
                     // max by more than the lazy threshold (always on a piece's first
                     // tile): otherwise the max stays and every p <= 2^8.
-                    bool over = t == p.t0;
+                    bool over = t <= p.t0;
                     if (!over) {
 #pragma unroll
                         for (int l = 0; l < 2; ++l)
@@ -601,7 +629,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     // the rows too keeps a non-finite stale value from turning 0 * x
                     // into NaN.  Each thread clears its own key row once the chunk
                     // has landed (P.V(j) does not start before P(j) is released).
-                    if (t == n_tiles - 1 && (n_keys & (kKeys - 1)) != 0) {
+                    if (!dry && t == n_tiles - 1 && (n_keys & (kKeys - 1)) != 0) {
                         bool okc = true;
                         if (key >= n_keys) {
                             for (int c = 0; c < vc && okc; ++c) {
@@ -663,7 +691,16 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     if (st < rows)
                         ms->l_run[st] += ms->red[0][st] + ms->red[1][st] + ms->red[2][st] + ms->red[3][st];
                     __syncwarp();
+                    if (dry) {
+                        if (st < 64) {
+                            ms->m_run[st] = -INFINITY;
+                            ms->l_run[st] = 0.f;
+                        }
+                        named_bar(1, 128);
+                        continue;
+                    }
                     if (lane == 0) mbar_arrive(&ms->pfull[j & 1]);
+                    ++j;
                 }
                 if (failed) break;
                 // ---- epilogue of the piece: normalised partial output and LSE ----
@@ -752,22 +789,29 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                 ms->l_run[st] = 0.f;
             }
             named_bar(1, 128);
-            for (int t = p.t0; t < p.t1; ++t, ++j) {
+            // A dry first tile on an early launch, as in the latent branch.
+            for (int t = p.t0 - (k == 0 && early ? 1 : 0); t < p.t1; ++t) {
+                const bool dry = t < p.t0;
                 const int sb = j & 1;
                 const uint32_t s_tmem = tbase + kSCol + uint32_t(sb * kN);
                 const int key = t * kKeys + t_local;
-                bool ok = wait_or_abort(&ms->sfull[sb], (j >> 1) & 1, ms, J.status, wait_ns);
+                bool ok = dry || wait_or_abort(&ms->sfull[sb], (j >> 1) & 1, ms, J.status, wait_ns);
                 if (named_bar_or(1, 128, !ok)) { failed = true; break; }
                 tc_fence_after();
                 float v[kRawS];
-                tmem_ld16(s_tmem + lane_addr, v);
+                if (dry) {
+#pragma unroll
+                    for (int c = 0; c < kRawS; ++c) v[c] = 0.f;
+                } else {
+                    tmem_ld16(s_tmem + lane_addr, v);
+                }
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&ms->sempty[sb]);
+                if (lane == 0 && !dry) mbar_arrive(&ms->sempty[sb]);
 #pragma unroll
                 for (int c = 0; c < kRawS; ++c) v[c] = key < n_keys ? v[c] * J.scale_log2 : -INFINITY;
-                bool over = t == p.t0;
+                bool over = t <= p.t0;
                 if (!over) {
 #pragma unroll
                     for (int c = 0; c < kRawS; ++c) over |= v[c] > ms->m_run[c] + kLazyLog2;
@@ -800,7 +844,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                 // P.V(j - 1) done (a commit covers every earlier MMA).
                 {
                     const int w = need_fix ? j - 1 : j - 2;
-                    if (w >= 0) {
+                    if (w >= 0 && !dry) {
                         ok = wait_or_abort(&ms->odone[w & 1], (w >> 1) & 1, ms, J.status, wait_ns);
                         if (named_bar_or(1, 128, !ok)) { failed = true; break; }
                         tc_fence_after();
@@ -808,7 +852,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                 }
                 // The partial last tile: clear the V rows past the length (see
                 // the latent branch).
-                if (t == n_tiles - 1 && (n_keys & (kKeys - 1)) != 0) {
+                if (!dry && t == n_tiles - 1 && (n_keys & (kKeys - 1)) != 0) {
                     bool okc = true;
                     if (key >= n_keys) {
                         for (int c = 0; c < vc && okc; ++c) {
@@ -860,7 +904,16 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                 if (st < kRawS)
                     ms->l_run[st] += ms->red[0][st] + ms->red[1][st] + ms->red[2][st] + ms->red[3][st];
                 __syncwarp();
+                if (dry) {
+                    if (st < kRawS) {
+                        ms->m_run[st] = -INFINITY;
+                        ms->l_run[st] = 0.f;
+                    }
+                    named_bar(1, 128);
+                    continue;
+                }
                 if (lane == 0) mbar_arrive(&ms->pfull[j & 1]);
+                ++j;
             }
             if (failed) break;
             // ---- epilogue of the piece ----
@@ -1049,9 +1102,21 @@ int launch_decode_tc(const TcLaunch& L, cudaStream_t stream) {
         configured[dev] = true;
     }
     const TcPlanLayout PL = tc_plan_layout(L.batch, L.kv_heads);
-    decode_tc_kernel<<<L.ctas, kThreads8, kSmemBytes, stream>>>(lk, lv, lq, rk, rv, rq, jl, jr, L.plan, PL,
-                                                                 L.lat_pieces);
-    const cudaError_t e = cudaGetLastError();
+    // An early launch may start before the previous kernel (the prologue)
+    // ends; the kernel waits for it before reading what it writes.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(L.ctas);
+    cfg.blockDim = dim3(kThreads8);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = L.early ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, decode_tc_kernel, lk, lv, lq, rk, rv, rq, jl, jr, L.plan, PL,
+                                       L.lat_pieces, L.early);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "decode tc launch failed: %s", cudaGetErrorString(e));
     return SLIMKV_OK;
 }

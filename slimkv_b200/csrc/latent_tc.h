@@ -24,6 +24,7 @@ namespace slimkv {
 
 constexpr int kTcTileKeys = 128;
 constexpr int kTcClasses = 3;
+constexpr int kTcMaxCtas = 160;          // CTAs of one launch (at most)
 
 // Device-written plan (int32 words in the workspace), header then arrays.
 //   hdr[4k + 0..3] = CTAs, first CTA, segments, tiles of class k
@@ -33,11 +34,14 @@ constexpr int kTcClasses = 3;
 //   lat_seg[b]   : (class << 24) | segment of sequence b's latent segment
 //   lat_range[b] : {(class << 24) | first piece in its class, pieces} of
 //                  sequence b's latent segment (the merge's one lookup)
+//   cta_start[k] : [CTAs + 1] first tile of each CTA of class k (then the
+//                  class's tile count)
 struct TcPlanLayout {
     int max_lat_segs;      // batch
     int max_raw_segs;      // batch * kv_heads
     // Word offsets inside the plan array.
     int hdr, seg_start[kTcClasses], seg_piece[kTcClasses], seg_id[kTcClasses], lat_seg, lat_range;
+    int cta_start[kTcClasses];
     int words;
 };
 
@@ -56,6 +60,10 @@ __host__ __device__ inline TcPlanLayout tc_plan_layout(int batch, int kv_heads) 
     L.lat_seg = at; at += batch;
     at = (at + 1) & ~1;                      // int2 entries
     L.lat_range = at; at += 2 * batch;
+    for (int k = 0; k < kTcClasses; ++k) {
+        L.cta_start[k] = at;
+        at += kTcMaxCtas + 1;
+    }
     L.words = at;
     return L;
 }
@@ -138,6 +146,11 @@ struct TcLaunch {
     const int32_t* plan;       // device plan written by plan_tc_work
     int lat_pieces;            // pieces reserved per latent class (class 1 starts after class 0's)
     uint64_t wait_ns;
+    // The plan was written before the prologue: the launch may start while
+    // the prologue finishes (programmatic dependent launch); the kernel waits
+    // for it only before reading what the prologue writes (Q rows, the new
+    // raw and Beacon rows).
+    int early;
 };
 
 // Shared memory of the launch (same for every class).

@@ -72,6 +72,10 @@ __device__ __host__ inline long long tc_cta_start(int tiles, int ctas, int i) {
 #ifndef SLIMKV_TC_W_TWO_QUERY
 #define SLIMKV_TC_W_TWO_QUERY 1.4f
 #endif
+// CTA boundaries move to a segment edge within (tiles per CTA) / this.
+#ifndef SLIMKV_TC_SNAP_DIV
+#define SLIMKV_TC_SNAP_DIV 4
+#endif
 #ifndef SLIMKV_TC_W_RAW_TILE
 #define SLIMKV_TC_W_RAW_TILE 7.5f
 #endif
@@ -164,16 +168,40 @@ __device__ inline void plan_tc_work(const TcPlanArgs& a, int32_t* scratch, int s
         }
     }
     __syncthreads();
-    // 3. Pieces of every segment: zero for an empty one, else one plus the
+    // 3. CTA ranges: equal shares of the class's tiles, each boundary moved to
+    // a segment boundary within a quarter share of it (a piece costs a query
+    // load and an epilogue; a boundary on a segment edge adds none).  Then
+    // the pieces of every segment: zero for an empty one, else one plus the
     // CTA boundaries strictly inside it.
+    if (tid < 3) {
+        const int k = tid, n = P[L.hdr + 4 * k], ns = nseg[k];
+        const int32_t* start = P + L.seg_start[k];
+        int32_t* cs = P + L.cta_start[k];
+        const long long snap = n > 0 && SLIMKV_TC_SNAP_DIV > 0 ? (long long)tiles[k] / n / SLIMKV_TC_SNAP_DIV : 0;
+        long long prev = 0;
+        cs[0] = 0;
+        for (int i = 1; i < n; ++i) {
+            long long r = tc_cta_start(tiles[k], n, i);
+            const int s = tc_segment_of(start, ns, r);
+            if (r - start[s] <= snap) r = start[s];
+            else if (start[s + 1] - r <= snap) r = start[s + 1];
+            r = max(r, prev);
+            cs[i] = int(r);
+            prev = r;
+        }
+        if (n > 0) cs[n] = tiles[k];
+    }
+    __syncthreads();
     for (int k = 0; k < 3; ++k) {
         const int n = P[L.hdr + 4 * k], ns = nseg[k];
         int32_t* start = P + L.seg_start[k];
         int32_t* piece = P + L.seg_piece[k];
+        const int32_t* cs = P + L.cta_start[k];
         for (int s = tid; s < ns; s += blockDim.x) piece[s] = start[s + 1] > start[s] ? 1 : 0;
         __syncthreads();
         for (int i = 1 + tid; i < n; i += blockDim.x) {
-            const long long r = tc_cta_start(tiles[k], n, i);
+            const long long r = cs[i];
+            if (r == cs[i - 1] || r >= tiles[k]) continue;     // an empty CTA adds no boundary
             const int s = tc_segment_of(start, ns, r);
             if (r > start[s]) atomicAdd(piece + s, 1);
         }

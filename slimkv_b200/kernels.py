@@ -189,7 +189,7 @@ class LatentDecodeCall:
     def __init__(self, *, q, raw_k_rot, raw_v, lat_k=None, lat_v=None, raw_len, latent_len, qpos, uk, uv, cos, sin,
                  out, query_len=None, raw_k_pre=None, new_k=None, new_v=None, new_lat_k=None, new_lat_v=None,
                  uk_bias=None, uv_bias=None, scale=None, latent_len_max=0, raw_len_max=0, latent_splits=0,
-                 raw_splits=0, lat_pages=None, out_lse=None, latent_shard=False, wait_limit_ns=0):
+                 raw_splits=0, lat_pages=None, out_lse=None, latent_shard=False, wait_limit_ns=0, plan=None):
         """``lat_pages = (pages, layout, tables)`` replaces ``lat_k / lat_v``
         with the vLLM plugin's Beacon pages: ``pages [num_pages, >=
         layout.page_elements]`` bf16 (a ``pages.BeaconPageLayout`` layout) and
@@ -203,7 +203,11 @@ class LatentDecodeCall:
 
         ``wait_limit_ns`` bounds every pipeline wait of the attention kernel
         (0: 2 s); a wait that runs out sets ``SLIMKV_DEVICE_TIMEOUT`` in the
-        device status word and the kernel returns early."""
+        device status word and the kernel returns early.
+
+        ``plan``: an int32 device tensor that :meth:`compute_plan` (of this or
+        another call with the same lengths) fills before this call runs; the
+        call then skips planning and starts its attention early."""
         paged = lat_pages is not None
         _require(paged or (lat_k is not None and lat_v is not None), 'lat_k / lat_v or lat_pages required')
         _bf16_cuda(q, raw_k_rot, raw_v, uk, uv, *(() if paged else (lat_k, lat_v)))
@@ -282,15 +286,38 @@ class LatentDecodeCall:
         a.out_lse = 0 if out_lse is None else out_lse.data_ptr()
         a.latent_shard = int(bool(latent_shard))
         a.wait_limit_ns = int(wait_limit_ns)
+        if plan is not None:
+            _require(plan.is_cuda and plan.dtype == torch.int32 and plan.is_contiguous(), 'plan: int32 CUDA tensor')
+            a.plan = plan.data_ptr()
         self.args = a
         self.device = q.device
         self._keep = (q, raw_k_rot, raw_v, raw_k_pre, lat_k, lat_v, lat_pages, raw_len, latent_len, query_len, qpos,
-                      new_k, new_v, new_lat_k, new_lat_v, uk, uv, uk_bias, uv_bias, cos, sin, out_lse, out)
+                      new_k, new_v, new_lat_k, new_lat_v, uk, uv, uk_bias, uv_bias, cos, sin, out_lse, plan, out)
         lib = _lib.load()
         size = lib.slimkv_latent_decode_workspace_size(ctypes.byref(a))
         if size == 0:
             _lib.check(lib.slimkv_latent_decode(ctypes.byref(a), None, 0, None))
         self.workspace = torch.empty(size, dtype=torch.uint8, device=q.device)
+
+    def plan_words(self):
+        """int32 words of this call's step plan (``slimkv_decode_plan_words``)."""
+        return int(_lib.load().slimkv_decode_plan_words(ctypes.byref(self.args)))
+
+    def use_plan(self, plan):
+        """Run with the step plan in ``plan`` (filled by :meth:`compute_plan`
+        before each launch) instead of planning per call."""
+        _require(plan.is_cuda and plan.dtype == torch.int32 and plan.numel() >= self.plan_words(), 'plan buffer')
+        self.args.plan = plan.data_ptr()
+        self._plan = plan
+
+    def compute_plan(self, plan):
+        """Fill ``plan`` (int32, >= :meth:`plan_words` words) with the step's
+        work plan from this call's current device lengths
+        (``slimkv_decode_plan``), on the current stream."""
+        _require(plan.is_cuda and plan.dtype == torch.int32 and plan.numel() >= self.plan_words(), 'plan buffer')
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.load().slimkv_decode_plan(ctypes.byref(self.args), _ptr(plan), _stream()))
+        return plan
 
     def __call__(self, attn_events=None):
         """Launch; ``attn_events`` = (begin, end) ``torch.cuda.Event`` pair

@@ -337,6 +337,12 @@ class LatentDecodeRuntime:
                 latent_len_max=lat_max, raw_len_max=self.raw_capacity,
                 latent_splits=latent_splits, raw_splits=raw_splits))
         self.call_latent_len, self.call_raw_len = call_lat_len, call_raw_len
+        # One work plan per step serves every layer (same lengths): computed
+        # once after the schedule, it lets each layer's attention start while
+        # its prologue finishes.
+        self.plan = torch.zeros(max(self.calls[0].plan_words(), 1), **i32)
+        for call in self.calls:
+            call.use_plan(self.plan)
         self.recon = []
         if backend == 'reconstruct':
             from .reconstruct import ReconstructDecode
@@ -420,6 +426,8 @@ class LatentDecodeRuntime:
         sp = self.split
         if sp is not None and sp['last']:
             torch.sub(self.latent_len, sp['offset'], out=sp['latent_len'])
+        if not self.recon:
+            self.calls[0].compute_plan(self.plan)
         x = self.x
         x[:, 0].copy_(w.embed.index_select(0, self.tokens))
         x[:, 1].copy_(w.beacon_embed.expand(B, -1))

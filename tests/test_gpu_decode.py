@@ -32,12 +32,14 @@ def tables(positions=16384):
 
 
 def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False, stale=0.0, paged=False, wait_limit_ns=0,
-              positions=16384):
+              positions=16384, step_plan=False):
     """Stage the caches without this step's entries, run the fused step.
 
     Cache rows past each sequence's staged length hold ``stale``.  With
     ``paged`` the latent cache lives in Beacon pages (vLLM plugin layout,
-    48 slots per page, disjoint shuffled block tables) instead.
+    48 slots per page, disjoint shuffled block tables) instead.  With
+    ``step_plan`` the work plan is computed first by ``compute_plan`` (as the
+    runtime does once per step) and the call starts its attention early.
     """
     from slimkv_b200 import kernels
     cos, sin, cos_t, sin_t = tables(positions)
@@ -94,7 +96,13 @@ def run_fused(c, query_len, extra_cap=3, pre=True, fp32=False, stale=0.0, paged=
         P.beacon_append(backing, layout, block_tables, np.zeros(B, np.int32), t['lat_k'], t['lat_v'])
         t['lat_pages'] = (backing, layout, block_tables)
         t['lat_k_dense'], t['lat_v_dense'] = t.pop('lat_k'), t.pop('lat_v')
-    kernels.latent_decode(**{k: v for k, v in t.items() if not k.endswith('_dense')}, wait_limit_ns=wait_limit_ns)
+    call = kernels.LatentDecodeCall(**{k: v for k, v in t.items() if not k.endswith('_dense')},
+                                    wait_limit_ns=wait_limit_ns)
+    if step_plan:
+        plan = torch.zeros(call.plan_words(), dtype=torch.int32, device='cuda')
+        call.use_plan(plan)
+        call.compute_plan(plan)
+    call()
     torch.cuda.synchronize()
     if paged:
         # The appended Beacon rows, read back from the pages.
@@ -232,6 +240,21 @@ def test_paged_decode_is_bit_identical_to_dense(length):
     dense = run_fused(c, query_len, fp32=True)
     paged = run_fused(c, query_len, fp32=True, paged=True)
     assert torch.equal(dense['out'], paged['out'])
+
+
+@pytest.mark.parametrize('paged', [False, True])
+def test_step_plan_and_early_attention_are_bit_identical(paged):
+    """A plan computed before the call (the runtime's one per step) and the
+    attention launch that overlaps the prologue give the same outputs and
+    cache writes, bit for bit, as per-call planning."""
+    c = decode_case(2101, batch=9, length=2, history=700, tail=300, ragged=True, bias=True)
+    query_len = np.array([2, 1, 2, 1, 1, 2, 1, 2, 1])
+    a = run_fused(c, query_len, fp32=True, paged=paged)
+    b = run_fused(c, query_len, fp32=True, paged=paged, step_plan=True)
+    for key in ('out', 'raw_k_rot', 'raw_v', 'raw_k_pre', 'lat_k', 'lat_v'):
+        assert torch.equal(a[key].view(torch.int32) if a[key].dtype == torch.float32 else a[key].view(torch.int16),
+                           b[key].view(torch.int32) if b[key].dtype == torch.float32 else b[key].view(torch.int16)), key
+    check(c, query_len, b)
 
 
 def test_mixed_query_lengths_in_one_batch():
