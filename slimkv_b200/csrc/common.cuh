@@ -278,5 +278,12 @@ __device__ __forceinline__ uint32_t sw128(int row, int col) {
 }
 
 __device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
+// 2^x by the special-function unit (ex2.approx.ftz: relative error ~2^-22,
+// far below the bf16 hi + lo probabilities it feeds); 2^-inf = 0.
+__device__ __forceinline__ float sfu_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 }  // namespace slimkv

@@ -669,7 +669,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
 #pragma unroll
                             for (int h = 0; h < 32; ++h) {
                                 const float m = ms->m_run[32 * l + h];
-                                pr[h] = (v[l][h] == -INFINITY || m == -INFINITY) ? 0.f : exp2f(v[l][h] - m);
+                                pr[h] = v[l][h] == -INFINITY ? 0.f : sfu_exp2(v[l][h] - m);     // finite v => finite m
                             }
 #pragma unroll
                             for (int u = 0; u < 4; ++u) {
@@ -885,7 +885,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
 #pragma unroll
                 for (int c = 0; c < kRawS; ++c) {
                     const float m = ms->m_run[c];
-                    pr[c] = (v[c] == -INFINITY || m == -INFINITY) ? 0.f : exp2f(v[c] - m);
+                    pr[c] = v[c] == -INFINITY ? 0.f : sfu_exp2(v[c] - m);     // finite v => finite m
                 }
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
