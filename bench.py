@@ -577,20 +577,32 @@ def own_launches_per_step(rt):
 
 
 def kernel_only(args):
-    """One layer of the bench workload (same batch, history, tails): the
-    fused decode call repeated; prints the attention kernel's time.  Small
-    device footprint, for ncu captures of the dominant kernel."""
+    """One layer of the bench workload (same batch, history, tails; config 2
+    or, with ``--config 5``, the Qwen geometry): the fused decode call
+    repeated; prints the attention kernel's time.  Small device footprint,
+    for ncu captures of the dominant kernel."""
     import numpy as np
     import torch
     from slimkv_b200 import _lib
     from slimkv_b200.runtime import LatentDecodeRuntime, LatentLlamaConfig, RandomWeights
     device = torch.device('cuda', 0)
-    cfg = LatentLlamaConfig(layers=1)
-    weights = RandomWeights(cfg, device, seed=0)
     rng = np.random.default_rng(1234)
-    tails = rng.integers(0, cfg.window, size=BATCH)
-    rt = LatentDecodeRuntime(cfg, weights, [HISTORY] * BATCH, tails, device, extra_windows=1)
-    rt.tokens.copy_(torch.from_numpy(rng.integers(0, cfg.vocab, size=BATCH)).to(device))
+    if args.config == 5:
+        import dataclasses
+        from slimkv_b200.runtime import qwen25_14b_r2
+        cfg = dataclasses.replace(qwen25_14b_r2(), layers=1)
+        batch = C5_BATCH
+        history = [131072 // cfg.window * (cfg.window // cfg.ratio)] * batch
+        extra = dict(raw_pre=False)
+    else:
+        cfg = LatentLlamaConfig(layers=1)
+        batch = BATCH
+        history = [HISTORY] * batch
+        extra = {}
+    weights = RandomWeights(cfg, device, seed=0)
+    tails = rng.integers(0, cfg.window, size=batch)
+    rt = LatentDecodeRuntime(cfg, weights, history, tails, device, extra_windows=1, **extra)
+    rt.tokens.copy_(torch.from_numpy(rng.integers(0, cfg.vocab, size=batch)).to(device))
     rt.step_eager()
     for _ in range(max(args.warmup, 1)):
         rt.calls[0]()
@@ -906,7 +918,7 @@ def main():
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
                      'peak_source': f'{peak_kind} (MEASURED_PEAKS.json hbm_gbs)' if peak_kind == 'measured'
                      else 'fallback 6650 GB/s',
-                     'traffic': traffic_per_launch(kernel_bytes) if args.config == 2 else None, 'kernel': ('decode_tc_kernel' if args.config != 5 else 'decode_attention_kernel<512>') +
+                     'traffic': traffic_per_launch(kernel_bytes) if args.config == 2 else None, 'kernel': ('decode_tc_kernel' if args.config != 5 else 'decode_tc_kernel<wide> (40 heads, ranks 512)') +
                      ' (latent + raw branches, one launch per layer)', 'bytes_per_launch': kernel_bytes, 'us_per_launch': attn_ms * 1000.0,
                      'fused_step_per_layer': {'us': layer_ms * 1000.0, 'bytes': layer_bytes,
                                               'gbs': layer_bytes / (layer_ms / 1000.0) / 1e9}},

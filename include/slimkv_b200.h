@@ -562,6 +562,22 @@ typedef struct {
 
 SLIMKV_API int slimkv_merge_partials(const slimkv_merge_partials_args* args, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Decoder-layer element-wise steps of the batched decode runtime.
+ * slimkv_rms_norm replaces LlamaRMSNorm.forward (slimkv/llama3/
+ * modeling_llama.py:79-95): out = weight * bf16(x * rsqrt(mean(x^2) + eps)),
+ * the mean in fp32, bf16 rows x / out with row strides in elements, weight
+ * [hidden] bf16; hidden a multiple of 8, at most 8192; 16-byte aligned rows.
+ * slimkv_silu_mul replaces act_fn(gate_proj(x)) * up_proj(x) of
+ * LlamaMLP.forward (modeling_llama.py:97-113) with the two projections as
+ * one row [gate (intermediate) | up (intermediate)]: out = bf16(silu(gate))
+ * * up, rounded to bf16; intermediate a multiple of 8, 16-byte aligned rows.
+ * ---------------------------------------------------------------------- */
+SLIMKV_API int slimkv_rms_norm(const void* x, int64_t x_row_stride, const void* weight, void* out,
+                               int64_t out_row_stride, int rows, int hidden, float eps, void* stream);
+SLIMKV_API int slimkv_silu_mul(const void* gate_up, int64_t gate_up_row_stride, void* out, int64_t out_row_stride,
+                               int rows, int intermediate, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

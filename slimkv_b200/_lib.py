@@ -169,6 +169,8 @@ SIGNATURES = {
     'slimkv_merge_partials': (_I, [ctypes.POINTER(MergePartialsArgs), _P]),
     'slimkv_reconstruct_kv_workspace_size': (ctypes.c_size_t, [ctypes.POINTER(ReconstructArgs)]),
     'slimkv_reconstruct_kv': (_I, [ctypes.POINTER(ReconstructArgs), _P]),
+    'slimkv_rms_norm': (_I, [_P, _L, _P, _P, _L, _I, _I, ctypes.c_float, _P]),
+    'slimkv_silu_mul': (_I, [_P, _L, _P, _L, _I, _I, _P]),
 }
 
 _lib = None

@@ -202,6 +202,23 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
         "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
 }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+    const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+// NC (a multiple of 16) consecutive columns: loads of 32, then one of 16.
+template <int NC>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
+    static_assert(NC % 16 == 0, "whole 16-column loads");
+#pragma unroll
+    for (int c = 0; c + 32 <= NC; c += 32) tmem_ld32(taddr + c, v + c);
+    if constexpr (NC % 32 != 0) tmem_ld16(taddr + (NC - 16), v + (NC - 16));
+}
 // Programmatic dependent launch.  grid_dependency_wait blocks until the grids
 // this one depends on programmatically have completed and their writes are
 // visible (at once for a launch without that dependency);

@@ -61,7 +61,8 @@ namespace {
 struct DecodePlan {
     int wl = 0, mtl = 0, lat_row_blocks = 0, lat_rows = 0, lat_splits = 0, lat_tps = 0;
     int raw_rows = 0, raw_splits = 0, raw_tps = 0, group = 0, rvp = 0;
-    bool tc = false;   // both branches on the persistent tensor-memory kernel (32 query heads)
+    bool tc = false;   // both branches on the persistent tensor-memory kernel (32 or 40 query heads)
+    bool wide = false; // its 40-head layout (latent ranks <= 512, one query per latent CTA)
     int ctas = 0, raw_ctas = 0, lat_pieces = 0;          // tensor-memory route
     int lat_cover = 0, raw_cover = 0;                    // rows per sequence the launch attends to
     size_t q_rot = 0, q_lat = 0, lat_o = 0, lat_lse = 0, raw_o = 0, raw_lse = 0, plan = 0;
@@ -112,7 +113,10 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
     p.lat_cover = std::min(a->lat_capacity, p.lat_splits * p.lat_tps * lt);
     p.raw_cover = std::min(a->raw_capacity, p.raw_splits * p.raw_tps * kTile);
     const size_t B = a->batch, L = a->length, H = a->heads;
-    p.tc = a->heads == 32 && p.wl <= 320 && p.group <= 8;   // 8: the raw score columns per query
+    // 8: the raw score columns per query.  The 40-head layout cycles V
+    // chunk pairs through a ring: an even number of 64-column V chunks.
+    p.wide = a->heads == kTcWideHeads && p.wl <= 512 && p.group <= 8 && ((a->rank_v + 63) / 64) % 2 == 0;
+    p.tc = (a->heads == kTcHeads && p.wl <= 320 && p.group <= 8) || p.wide;
     if (p.tc) {
         // One persistent launch: CTAs (at most one per SM) split the latent and
         // raw work by volume on the device (latent_tc_plan.cuh).  latent_splits
@@ -122,18 +126,18 @@ int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
         const int cap = std::min({sms, kMergeMaxSplits - 1, kTcMaxCtas});
         p.ctas = std::max(3, std::min(a->latent_splits > 0 ? a->latent_splits : sms, cap));
         p.raw_ctas = a->raw_splits > 0 ? std::min(a->raw_splits, p.ctas - 2) : 0;
-        p.lat_rows = 64;
+        p.lat_rows = 2 * a->heads;
         p.raw_rows = 2 * p.group;
-        p.lat_pieces = tc_max_pieces(a->batch, p.ctas);
+        p.lat_pieces = tc_max_pieces(p.wide ? 2 * a->batch : a->batch, p.ctas);
         // The device plan tiles every sequence to its own length.
         p.lat_cover = a->lat_capacity;
         p.raw_cover = a->raw_capacity;
     }
     p.q_rot = B * L * H * a->head_dim;
-    p.q_lat = p.tc ? B * 128 * p.wl : B * L * H * p.wl;
+    p.q_lat = p.tc ? B * (p.wide ? kTcWideRows : 128) * p.wl : B * L * H * p.wl;
     if (p.tc) {
         const size_t raw_pieces = tc_max_pieces(a->batch * a->kv_heads, p.ctas);
-        p.plan = tc_plan_layout(a->batch, a->kv_heads).words;
+        p.plan = tc_plan_layout(a->batch, a->kv_heads, p.wide).words;
         p.lat_o = 2 * size_t(p.lat_pieces) * p.lat_rows * p.wl;
         p.lat_lse = 2 * size_t(p.lat_pieces) * p.lat_rows;
         p.raw_o = raw_pieces * p.raw_rows * 128;
@@ -234,7 +238,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     if (!paged && a->lat_stride_row < std::max(a->rank_k, a->rank_v))
         return fail(SLIMKV_ERR_INVALID_ARGUMENT, "cache row stride smaller than a row");
     if (paged) {
-        if (!p.tc) return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "paged latent caches need 32 query heads");
+        if (!p.tc) return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "paged latent caches need 32 or 40 query heads");
         if (!a->lat_table || a->lat_slots <= 0 || a->lat_slots % 16 || a->lat_num_pages <= 0 ||
             a->lat_table_stride <= 0 || a->lat_sink_elements < 0 || a->lat_sink_elements % 8 ||
             a->lat_page_stride % 8 || !aligned16(a->lat_pages) ||
@@ -271,6 +275,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     pa.uk = static_cast<const __nv_bfloat16*>(a->uk);
     pa.q_rot = w.q_rot; pa.q_lat = w.q_lat;
     pa.q_hilo = reinterpret_cast<__nv_bfloat16*>(w.q_lat); pa.hilo = p.tc ? 1 : 0;
+    pa.hilo_rows = p.wide ? kTcWideRows : 128; pa.hilo_split = p.wide ? 1 : 0;
     pa.new_k = static_cast<const __nv_bfloat16*>(a->new_k);
     pa.new_v = static_cast<const __nv_bfloat16*>(a->new_v);
     pa.new_stride = a->new_stride > 0 ? a->new_stride : (int64_t)a->kv_heads * a->head_dim;
@@ -301,6 +306,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         pl.latent_len = a->latent_len; pl.raw_len = a->raw_len; pl.query_len = a->query_len;
         pl.lat_chunks = (a->rank_k + 63) / 64 + (a->rank_v + 63) / 64;
         pl.ctas = p.ctas; pl.raw_ctas = p.raw_ctas; pl.with_raw = 1; pl.plan = plan;
+        pl.split_queries = p.wide ? 1 : 0;
     }
     pa.status = status;
     const dim3 pgrid(a->kv_heads, p.wl / 64, (a->batch + pa.seq_per_cta - 1) / pa.seq_per_cta + (p.tc ? 1 : 0));
@@ -348,6 +354,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         tl.batch = a->batch; tl.length = a->length; tl.scale = a->scale;
         tl.query_len = a->query_len; tl.status = status; tl.with_raw = 1;
         tl.kv_heads = a->kv_heads; tl.ctas = p.ctas; tl.plan = plan; tl.lat_pieces = p.lat_pieces;
+        tl.wide = p.wide ? 1 : 0;
         tl.wait_ns = a->wait_limit_ns;
         // With the plan ready the attention may start before the prologue
         // ends — not when its duration is being timed (the begin event would
@@ -397,7 +404,7 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     ma.lat_width = p.wl;
     if (p.tc) {
         ma.plan = plan;
-        ma.PL = tc_plan_layout(a->batch, a->kv_heads);
+        ma.PL = tc_plan_layout(a->batch, a->kv_heads, p.wide);
         ma.lat_pieces = p.lat_pieces;
     }
     ma.raw_o = w.raw_o; ma.raw_lse = w.raw_lse; ma.raw_splits = p.raw_splits; ma.raw_rows = p.raw_rows;
@@ -458,7 +465,7 @@ __global__ void __launch_bounds__(256) decode_plan_kernel(TcPlanArgs pl) {
 extern "C" size_t slimkv_decode_plan_words(const slimkv_latent_decode_args* a) {
     DecodePlan p;
     if (plan_decode(a, p) != SLIMKV_OK) return 0;
-    return p.tc ? size_t(tc_plan_layout(a->batch, a->kv_heads).words) : 1;
+    return p.tc ? size_t(tc_plan_layout(a->batch, a->kv_heads, p.wide).words) : 1;
 }
 
 extern "C" int slimkv_decode_plan(const slimkv_latent_decode_args* a, int32_t* plan, void* stream_ptr) {
@@ -472,6 +479,7 @@ extern "C" int slimkv_decode_plan(const slimkv_latent_decode_args* a, int32_t* p
     pl.latent_len = a->latent_len; pl.raw_len = a->raw_len; pl.query_len = a->query_len;
     pl.lat_chunks = (a->rank_k + 63) / 64 + (a->rank_v + 63) / 64;
     pl.ctas = p.ctas; pl.raw_ctas = p.raw_ctas; pl.with_raw = 1; pl.plan = plan;
+    pl.split_queries = p.wide ? 1 : 0;
     decode_plan_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream_ptr)>>>(pl);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "decode plan launch failed: %s", cudaGetErrorString(e));

@@ -29,8 +29,10 @@ struct PrologueArgs {
     const __nv_bfloat16* uk;
     __nv_bfloat16* q_rot;   // [B, L, H, D]
     __half* q_lat;          // [B, L, H, width] fp16 (split-KV path), or
-    __nv_bfloat16* q_hilo;  // [B][128][width] bf16 hi/lo rows (tensor-memory path)
+    __nv_bfloat16* q_hilo;  // [B][hilo_rows][width] bf16 hi/lo rows (tensor-memory path)
     int hilo;
+    int hilo_rows;          // 128: row hl*H*nq + l*H + h; 160 (split): row l*2H + hl*H + h
+    int hilo_split;
     const __nv_bfloat16* new_k;
     const __nv_bfloat16* new_v;
     int64_t new_stride;
@@ -200,8 +202,9 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
         }
     }
     // 4. q_lat for the valid rows: fp16, or a bf16 hi/lo pair (q = hi + lo)
-    //    at rows l*32 + h (hi) and 32*nq + l*32 + h (lo) of the sequence's
-    //    block, nq being the sequence's query count.
+    //    at rows l*H + h (hi) and H*nq + l*H + h (lo) of the sequence's
+    //    block, nq being the sequence's query count; split: l*2H + h (hi) and
+    //    l*2H + H + h (lo), each query's pair contiguous.
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
         const int r = 16 * mt + (lane >> 2) + 8 * hh;
@@ -212,8 +215,10 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(PrologueArgs a) {
         if (l >= nq) continue;
         const int col = cc * 64 + nh * 32 + (lane & 3) * 2;
         if (a.hilo) {
-            __nv_bfloat16* hi = a.q_hilo + ((int64_t)b * 128 + l * 32 + g * a.group + j) * a.width + col;
-            __nv_bfloat16* lo = hi + 32 * nq * a.width;
+            const int h = g * a.group + j;
+            const int hrow = a.hilo_split ? l * 2 * a.heads + h : l * a.heads + h;
+            __nv_bfloat16* hi = a.q_hilo + ((int64_t)b * a.hilo_rows + hrow) * a.width + col;
+            __nv_bfloat16* lo = hi + int64_t(a.hilo_split ? a.heads : a.heads * nq) * a.width;
 #pragma unroll
             for (int n = 0; n < 4; ++n) {
                 const float x0 = acc[n][2 * hh], x1 = acc[n][2 * hh + 1];

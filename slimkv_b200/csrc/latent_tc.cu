@@ -88,22 +88,50 @@ constexpr uint32_t kMaxPad = 960;
 constexpr uint32_t kSmemBytes = kMaxPad + kTileBytes + uint32_t(sizeof(Misc));
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
-// Tile-area layout of a class: V ring | K ring | Q buffers | P buffers.
+// Tile-area layout of a class: V ring | K ring | Q buffers | P buffers,
+// and its TMEM map: `obufs` O accumulators of `o_cols` columns from column
+// 0, two S buffers of `n` columns (the MMA N) from `s_col`.
 // The raw class double-buffers P (pdbl: P(j) in buffer j & 1).
+//
+// 40-head latent layout (wide): N = 80 (hi | lo of one query), Q [80 rows x
+// 64] per chunk (10 KB, 8 chunks), P^T [128 keys x 80] as two 64-column
+// swizzle atoms (32 KB), a V ring of 4 slots that a tile's 8 chunks cycle
+// through and a K ring of 3: 224 KB.  TMEM: one O of 4 x 80 columns (its
+// epilogue finishes before the next piece's first P.V), S at 320 and 400.
 struct Layout {
-    int kring, vslots, qbufs, pbufs;
+    int kring, vslots, qbufs, pbufs, obufs, n;
     bool pdbl;
-    uint32_t off_k, off_q, qbytes, off_p;
+    uint32_t off_k, off_q, qbytes, qchunk, off_p, o_cols, s_col;
 };
+template <bool WIDE>
 __host__ __device__ __forceinline__ Layout class_layout(int cls, int kc) {
     Layout L;
-    L.vslots = cls == 2 ? 4 : kMaxChunks;
-    L.kring = cls == 1 ? 2 : cls == 0 ? kMaxChunks : kKRingMax;
-    L.pdbl = cls == 2;
-    L.qbufs = cls == 2 ? 2 : 1;
-    L.pbufs = cls == 0 ? 1 : 2;
+    if (WIDE && cls < 2) {
+        L.vslots = 4;
+        L.kring = 3;
+        L.pdbl = false;
+        L.qbufs = 1;
+        L.pbufs = 2;                                   // the two N atoms of one P
+        L.n = 2 * kTcWideHeads;
+        L.qchunk = uint32_t(L.n) * 128;
+        L.qbytes = 8 * L.qchunk;
+        L.obufs = 1;
+        L.o_cols = 4 * uint32_t(L.n);
+        L.s_col = L.o_cols;
+    } else {
+        L.vslots = cls == 2 ? 4 : kMaxChunks;
+        L.kring = cls == 1 ? 2 : cls == 0 ? kMaxChunks : kKRingMax;
+        L.pdbl = cls == 2;
+        L.qbufs = cls == 2 ? 2 : 1;
+        L.pbufs = cls == 0 ? 1 : 2;
+        L.n = kN;
+        L.qchunk = kQChunkBytes;
+        L.qbytes = uint32_t(cls == 1 ? 2 : 1) * uint32_t(cls == 2 ? kc : kMaxChunks) * kQChunkBytes;
+        L.obufs = 2;
+        L.o_cols = kOBufCols;
+        L.s_col = kSCol;
+    }
     L.off_k = uint32_t(L.vslots) * kChunkBytes;
-    L.qbytes = uint32_t(cls == 1 ? 2 : 1) * uint32_t(cls == 2 ? kc : kMaxChunks) * kQChunkBytes;
     L.off_q = L.off_k + uint32_t(L.kring) * kChunkBytes;
     L.off_p = L.off_q + uint32_t(L.qbufs) * L.qbytes;
     return L;
@@ -166,6 +194,29 @@ __device__ __forceinline__ float warp_transpose_reduce(float (&v)[32], int lane)
     return v[0];
 }
 
+// Column reductions of x[0 .. NS) over the warp's 32 lanes into dst[0 ..
+// NS): 32-column transpose-reduces, then one of 16 for a remainder of at
+// most 16 columns (padded with the identity).
+template <bool MAX, int NS>
+__device__ __forceinline__ void transpose_reduce_to(const float* x, int lane, float* dst) {
+#pragma unroll
+    for (int g = 0; g < NS / 32; ++g) {
+        float t[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) t[i] = x[32 * g + i];
+        dst[32 * g + lane] = warp_transpose_reduce<MAX>(t, lane);
+    }
+    if constexpr (NS % 32 != 0) {
+        static_assert(NS % 32 <= 16, "remainder of at most 16 columns");
+        constexpr int R = NS % 32, G = NS - R;
+        float t[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) t[i] = i < R ? x[G + i] : (MAX ? -INFINITY : 0.f);
+        const float r = warp_transpose_reduce16<MAX>(t, lane);
+        if (lane < R) dst[G + lane] = r;
+    }
+}
+
 // Eight packed bf16 pairs of (hi, lo) for p[8u .. 8u+8).
 template <int N>
 __device__ __forceinline__ void split_hilo(const float (&p)[N], int u, uint4& hi, uint4& lo) {
@@ -191,14 +242,15 @@ struct Range {
     int s0, first_piece;
 };
 
-// One piece: segment s, its local tiles [t0, t1), and where its output goes.
+// One piece: segment s, its local tiles [t0, t1), and where its output goes
+// (sequence b, KV head g of a raw segment, query l of a split latent one).
 struct Piece {
-    int s, t0, t1, piece, b, g;
+    int s, t0, t1, piece, b, g, l;
 };
 
 // Piece k of the walk (k = 0, 1, ... while pos < r1); `s` and `pos` carry
 // the walk's position.
-__device__ __forceinline__ void next_piece(const Range& R, int k, int& s, long long& pos, int kv_heads,
+__device__ __forceinline__ void next_piece(const Range& R, int k, int& s, long long& pos, int kv_heads, int split,
                                            Piece& p) {
     while (R.start[s + 1] <= pos) ++s;                 // skip segments without tiles
     const long long seg0 = R.start[s], seg1 = R.start[s + 1];
@@ -207,8 +259,15 @@ __device__ __forceinline__ void next_piece(const Range& R, int k, int& s, long l
     p.t1 = int(min(R.r1, seg1) - seg0);
     p.piece = k == 0 ? R.first_piece : R.pieces[s];
     const int id = R.ids[s];
-    p.b = id / kv_heads;
-    p.g = id - p.b * kv_heads;
+    if (split) {
+        p.b = id >> 1;
+        p.l = id & 1;
+        p.g = 0;
+    } else {
+        p.b = id / kv_heads;
+        p.g = id - p.b * kv_heads;
+        p.l = 0;
+    }
     pos = seg0 + p.t1;
     ++s;
 }
@@ -216,7 +275,8 @@ __device__ __forceinline__ void next_piece(const Range& R, int k, int& s, long l
 }  // namespace
 
 // Kernel parameters: the K / V / Q maps of both branches (latent, raw), both
-// jobs, the plan and its layout.
+// jobs, the plan and its layout.  WIDE: the 40-head latent layout.
+template <bool WIDE>
 __global__ void __launch_bounds__(kThreads8, 1)
 decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constant__ CUtensorMap lvmap,
                  const __grid_constant__ CUtensorMap lqmap, const __grid_constant__ CUtensorMap rkmap,
@@ -267,15 +327,29 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
     }
     const int piece_base = J.piece_base + (cls == 1 ? lat_pieces : 0);
     const int kc = J.kchunks, vc = J.vchunks;
-    const Layout LY = class_layout(cls, kc);
+    const Layout LY = class_layout<WIDE>(cls, kc);
     const int kring = LY.kring;
     const uint64_t wait_ns = J.wait_ns;
-    // V chunk n -> (CTA tile T = n / vc, chunk c = n % vc) in V slot c; with
-    // <= 2 chunks per tile (raw) tiles alternate between slot pairs (0,1) and
-    // (2,3), so two tiles of V are in flight.
+    // V chunk c of CTA tile T: in V slot c; with <= 2 chunks per tile (raw)
+    // tiles alternate between slot pairs (0,1) and (2,3), so two tiles of V
+    // are in flight; with more chunks than slots (the wide layout, an even
+    // chunk count) chunk n = T * vc + c cycles through the ring, so a chunk
+    // pair always takes two adjacent slots.
+    // The TMEM map, MMA N and Q chunk: compile-time constants outside the
+    // wide layout.
+    const int n_mma = WIDE ? LY.n : kN;
+    const int obufs = WIDE ? LY.obufs : 2;
+    const uint32_t o_cols = WIDE ? LY.o_cols : kOBufCols;
+    const uint32_t s_col = WIDE ? LY.s_col : kSCol;
+    const uint32_t qchunk = WIDE ? LY.qchunk : kQChunkBytes;
     const bool dbl = vc <= 2;
-    auto v_slot = [&](int T, int c) -> int { return dbl ? 2 * (T & 1) + c : c; };
-    auto v_use = [&](int T) -> int { return dbl ? T >> 1 : T; };       // earlier uses of the slot
+    const bool vring = WIDE && vc > LY.vslots;
+    auto v_slot = [&](int T, int c) -> int {
+        return vring ? (T * vc + c) % LY.vslots : dbl ? 2 * (T & 1) + c : c;
+    };
+    auto v_use = [&](int T, int c) -> int {                             // earlier uses of the slot
+        return vring ? (T * vc + c) / LY.vslots : dbl ? T >> 1 : T;
+    };
 
     if (J.q_rows) {
         // Row-mode Q fills only the query rows of each chunk; the rest must
@@ -363,7 +437,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
         };
         for (int k = 0; pos < R.r1 && ok; ++k) {
             Piece p;
-            next_piece(R, k, s, pos, J.kv_heads, p);
+            next_piece(R, k, s, pos, J.kv_heads, J.split, p);
             const int last_tile = (max(J.seqlens[p.b], 1) - 1) / kKeys;
             // Q of the piece, issued once the first K chunks of the piece that
             // fit the ring are on their way (S of the piece needs Q before it
@@ -384,6 +458,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                         for (int l = 0; l < nq; ++l)
                             tma_load_4d(qdst + c * kQChunkBytes + l * kRawCols * 128, qmap, &ms->qfull[qb], c * 64,
                                         0, p.g * J.group, p.b * J.length + l);
+                } else if (J.split) {
+                    // [hi | lo] x 40 rows of query l: one 80-row box per chunk.
+                    mbar_expect_tx(&ms->qfull[qb], uint32_t(kc) * qchunk);
+                    for (int c = 0; c < kc; ++c)
+                        tma_load_4d(qdst + c * qchunk, qmap, &ms->qfull[qb], c * 64, 0, p.l * n_mma, p.b);
                 } else {
                     // [hi | lo] x 32 * nq rows: one 64-row box per chunk for
                     // nq = 1, hi and lo boxes for nq = 2.
@@ -411,7 +490,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     }
                 } else {
                     for (int c = 0; c < vc; ++c) {
-                        const int slot = v_slot(j, c), use = v_use(j);
+                        const int slot = v_slot(j, c), use = v_use(j, c);
                         if (use > 0 && !(ok = wait_or_abort(&ms->vempty[slot], (use - 1) & 1, ms, J.status, wait_ns)))
                             break;
                         mbar_expect_tx(&ms->vfull[slot], kChunkBytes);
@@ -422,22 +501,22 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
         }
     } else if (warp == 2 && lane == 0) {
         // ---- S issuer: S(j) = K(j) . Q^T as K chunks land ----
-        const uint32_t idesc_s = umma_idesc_bf16(128, kN, 0, 0);
+        const uint32_t idesc_s = umma_idesc_bf16(128, n_mma, 0, 0);
         int s = R.s0;
         long long pos = R.r0;
         bool ok = true;
         int j = 0;
         for (int k = 0; pos < R.r1 && ok; ++k) {
             Piece p;
-            next_piece(R, k, s, pos, J.kv_heads, p);
+            next_piece(R, k, s, pos, J.kv_heads, J.split, p);
             const int qb = k % LY.qbufs;
             const uint32_t q0 = sbase + LY.off_q + qb * LY.qbytes, q1 = q0 + kMaxChunks * kQChunkBytes;
             const int nq = J.qlens ? J.qlens[p.b] : J.length;
-            const bool two = nq == 2 && !J.q_rows;            // hi and lo into the same columns
+            const bool two = nq == 2 && !J.q_rows && !J.split;   // hi and lo into the same columns
             if (!(ok = wait_or_abort(&ms->qfull[qb], (k / LY.qbufs) & 1, ms, J.status, wait_ns))) break;
             for (int t = p.t0; t < p.t1; ++t, ++j) {
                 const int sb = j & 1;
-                const uint32_t s_tmem = tbase + kSCol + uint32_t(sb * kN);
+                const uint32_t s_tmem = tbase + s_col + uint32_t(sb * n_mma);
                 if (j >= 2 && !(ok = wait_or_abort(&ms->sempty[sb], ((j - 2) >> 1) & 1, ms, J.status, wait_ns)))
                     break;
                 tc_fence_after();
@@ -449,7 +528,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint64_t ad = umma_desc_sw128(ka + kk * 32, 16, 1024);
-                        umma_bf16(s_tmem, ad, umma_desc_sw128(q0 + c * kQChunkBytes + kk * 32, 16, 1024), idesc_s,
+                        umma_bf16(s_tmem, ad, umma_desc_sw128(q0 + c * qchunk + kk * 32, 16, 1024), idesc_s,
                                   (c | kk) != 0);
                         if (two)
                             umma_bf16(s_tmem, ad, umma_desc_sw128(q1 + c * kQChunkBytes + kk * 32, 16, 1024), idesc_s,
@@ -463,10 +542,18 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
             if (ok) umma_commit(&ms->qempty[qb]);            // the piece's last MMA read Q
         }
         umma_commit(&ms->final_mma);
-    } else if (warp == 1 && lane == 0) {
+    } else if (warp == 1 && (WIDE || lane == 0)) {
         // ---- P.V issuer: O^T += V(j)^T . P(j)^T once P(j) is written ----
-        const uint32_t idesc_pair = umma_idesc_bf16(128, kN, 1, 1);
-        const uint32_t idesc_one = umma_idesc_bf16(64, kN, 1, 1);
+        // Lane 0 issues.  In the wide layout a tile's V chunks only land as
+        // the ring turns, after P(j) is released, so the whole warp follows
+        // lane 0 and clears the V rows past a sequence's length in its partial
+        // last tile before their MMA (the cache may hold non-finite values
+        // there, and 0 * inf would poison O).
+        const unsigned wm = WIDE ? 0xffffffffu : 1u;       // the lanes taking part
+        const bool leader = lane == 0;
+        const bool clear_v = WIDE && is_lat;
+        const uint32_t idesc_pair = umma_idesc_bf16(128, n_mma, 1, 1);
+        const uint32_t idesc_one = umma_idesc_bf16(64, n_mma, 1, 1);
         const uint32_t p0 = sbase + LY.off_p, p1 = p0 + kChunkBytes;
         int s = R.s0;
         long long pos = R.r0;
@@ -474,52 +561,82 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
         int j = 0;
         for (int k = 0; pos < R.r1 && ok; ++k) {
             Piece p;
-            next_piece(R, k, s, pos, J.kv_heads, p);
-            const int ob = k & 1;
-            const uint32_t o_tmem = tbase + uint32_t(ob) * kOBufCols;
+            next_piece(R, k, s, pos, J.kv_heads, J.split, p);
+            const int ob = k % obufs;
+            const uint32_t o_tmem = tbase + uint32_t(ob) * o_cols;
             const int nq = J.qlens ? J.qlens[p.b] : J.length;
-            const bool cols = nq == 1 || J.q_rows;            // hi and lo in separate columns of one P
+            const bool cols = nq == 1 || J.q_rows || J.split;   // hi and lo in separate columns of one P
+            const int n_keys = J.seqlens[p.b];
+            const int valid_last = n_keys & (kKeys - 1);        // keys of a partial last tile (0: none)
+            const int last_tile = (max(n_keys, 1) - 1) / kKeys;
             for (int t = p.t0; t < p.t1; ++t, ++j) {
-                if (!(ok = wait_or_abort(&ms->pfull[j & 1], (j >> 1) & 1, ms, J.status, wait_ns))) break;
+                ok = __all_sync(wm, wait_or_abort(&ms->pfull[j & 1], (j >> 1) & 1, ms, J.status, wait_ns));
+                if (!ok) break;
                 const uint32_t pb = LY.pdbl ? p0 + uint32_t(j & 1) * kChunkBytes : p0;
                 // The first tile of a piece overwrites the O buffer the
-                // epilogue of piece k - 2 read.
-                if (t == p.t0 && k >= 2 && !(ok = wait_or_abort(&ms->oempty[ob], ((k >> 1) - 1) & 1, ms, J.status,
-                                                                wait_ns)))
-                    break;
+                // epilogue of piece k - obufs read.
+                if (t == p.t0 && k >= obufs) {
+                    ok = __all_sync(wm, wait_or_abort(&ms->oempty[ob], ((k / obufs) - 1) & 1, ms,
+                                                               J.status, wait_ns));
+                    if (!ok) break;
+                }
                 tc_fence_after();
+                const bool clear = clear_v && t == last_tile && valid_last != 0;
                 for (int blk = 0; blk < vblocks; ++blk) {
                     const int c0 = 2 * blk, s0 = v_slot(j, c0);
                     const bool pair = c0 + 1 < vc;
                     for (int c = c0; c <= c0 + (pair ? 1 : 0); ++c)
-                        if (!(ok = wait_or_abort(&ms->vfull[v_slot(j, c)], v_use(j) & 1, ms, J.status, wait_ns)))
+                        if (!(ok = wait_or_abort(&ms->vfull[v_slot(j, c)], v_use(j, c) & 1, ms, J.status, wait_ns)))
                             break;
+                    ok = __all_sync(wm, ok);
                     if (!ok) break;
-                    tc_fence_after();
-                    const uint32_t va = sbase + s0 * kChunkBytes;
-                    const uint32_t o_b = o_tmem + uint32_t(blk * kN);
-                    const uint32_t idesc = pair ? idesc_pair : idesc_one;
-#pragma unroll
-                    for (int ks = 0; ks < kKeys / 16; ++ks) {
-                        const uint64_t ad = umma_desc_sw128(va + ks * 2048, kChunkBytes, 1024);
-                        umma_bf16(o_b, ad, umma_desc_sw128(pb + ks * 2048, kChunkBytes, 1024), idesc,
-                                  (t > p.t0 || ks > 0) ? 1u : 0u);
-                        if (!cols) umma_bf16(o_b, ad, umma_desc_sw128(p1 + ks * 2048, kChunkBytes, 1024), idesc, 1u);
+                    if (clear) {
+                        for (int c = c0; c <= c0 + (pair ? 1 : 0); ++c) {
+                            uint4* rows = reinterpret_cast<uint4*>(smem + v_slot(j, c) * kChunkBytes);
+                            for (int i = valid_last * 8 + lane; i < kKeys * 8; i += 32) rows[i] = make_uint4(0, 0, 0, 0);
+                        }
+                        fence_async_shared();
+                        __syncwarp(wm);
                     }
-                    umma_commit(&ms->vempty[s0]);
-                    if (pair) umma_commit(&ms->vempty[s0 + 1]);
+                    tc_fence_after();
+                    if (leader) {
+                        const uint32_t va = sbase + s0 * kChunkBytes;
+                        const uint32_t o_b = o_tmem + uint32_t(blk * n_mma);
+                        const uint32_t idesc = pair ? idesc_pair : idesc_one;
+#pragma unroll
+                        for (int ks = 0; ks < kKeys / 16; ++ks) {
+                            const uint64_t ad = umma_desc_sw128(va + ks * 2048, kChunkBytes, 1024);
+                            umma_bf16(o_b, ad, umma_desc_sw128(pb + ks * 2048, kChunkBytes, 1024), idesc,
+                                      (t > p.t0 || ks > 0) ? 1u : 0u);
+                            if (!cols)
+                                umma_bf16(o_b, ad, umma_desc_sw128(p1 + ks * 2048, kChunkBytes, 1024), idesc, 1u);
+                        }
+                        umma_commit(&ms->vempty[s0]);
+                        if (pair) umma_commit(&ms->vempty[v_slot(j, c0 + 1)]);
+                    }
+                    __syncwarp(wm);
                 }
                 if (!ok) break;
-                umma_commit(&ms->odone[j & 1]);
+                if (leader) umma_commit(&ms->odone[j & 1]);
+                __syncwarp(wm);
             }
         }
-        umma_commit(&ms->final_mma);
+        if (leader) umma_commit(&ms->final_mma);
     } else if (warp >= 3 && warp <= 6 && cls < 2) {
         // ---- latent softmax and epilogue: thread <-> key (TMEM lane) ----
         // Instantiated per query count (class 0: one query, class 1: two), so
-        // a CTA runs straight-line code for its own layout only.
+        // a CTA runs straight-line code for its own layout only.  S has NC =
+        // 2 HQ columns per key: hi | lo products of one query (added here),
+        // or (query, head) with hi and lo accumulated by the MMA (two queries
+        // of 32 heads); NS scores per key, one running row state per score
+        // column.
         auto latent_softmax = [&](auto nq_tag) {
             constexpr int NQ = decltype(nq_tag)::value;
+            constexpr int HQ = WIDE ? kTcWideHeads : kTcHeads;
+            constexpr int NC = 2 * HQ;
+            constexpr int NS = NQ * HQ;
+            constexpr bool cols = NQ == 1;
+            static_assert(NS <= 64 && (NQ == 1 || HQ == 32), "latent score columns per CTA");
             const int quarter = warp & 3;
             const int t_local = 32 * quarter + lane;
             const uint32_t lane_addr = uint32_t(32 * quarter) << 16;
@@ -530,12 +647,16 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
             int j = 0;
             for (int k = 0; pos < R.r1 && !failed; ++k) {
                 Piece p;
-                next_piece(R, k, s, pos, J.kv_heads, p);
-                const int ob = k & 1;
-                const uint32_t o_tmem = tbase + uint32_t(ob) * kOBufCols;
+                next_piece(R, k, s, pos, J.kv_heads, J.split, p);
+                const int ob = k % obufs;
+                const uint32_t o_tmem = tbase + uint32_t(ob) * o_cols;
                 const int n_keys = J.seqlens[p.b];
-                constexpr bool cols = NQ == 1;
-                constexpr int rows = 32 * NQ;
+                const int nq_seq = J.qlens ? J.qlens[p.b] : J.length;
+                // Keys of the first query's rows: an insertion step's raw query
+                // excludes the new Beacon (the sequence's last key).
+                const bool excl = J.causal && nq_seq == 2 && (NQ == 2 || (J.split && p.l == 0));
+                const int lim0 = excl ? n_keys - 1 : n_keys;
+                const int row0 = J.split ? p.l * HQ : 0;          // output row of head 0
                 const int n_tiles = (max(n_keys, 0) + kKeys - 1) / kKeys;
                 if (st < 64) {
                     ms->m_run[st] = -INFINITY;
@@ -550,18 +671,17 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                 for (int t = p.t0 - (k == 0 && early ? 1 : 0); t < p.t1; ++t) {
                     const bool dry = t < p.t0;
                     const int sb = j & 1;
-                    const uint32_t s_tmem = tbase + kSCol + uint32_t(sb * kN);
+                    const uint32_t s_tmem = tbase + s_col + uint32_t(sb * n_mma);
                     const int key = t * kKeys + t_local;
                     bool ok = dry || wait_or_abort(&ms->sfull[sb], (j >> 1) & 1, ms, J.status, wait_ns);
                     if (named_bar_or(1, 128, !ok)) { failed = true; break; }
                     tc_fence_after();
-                    float v[2][32];
+                    float v[NC];
                     if (dry) {
 #pragma unroll
-                        for (int h = 0; h < 32; ++h) v[0][h] = v[1][h] = 0.f;
+                        for (int c = 0; c < NC; ++c) v[c] = 0.f;
                     } else {
-                        tmem_ld32(s_tmem + lane_addr, v[0]);
-                        tmem_ld32(s_tmem + lane_addr + 32, v[1]);
+                        tmem_ld_cols<NC>(s_tmem + lane_addr, v);
                     }
                     tmem_wait_ld();
                     tc_fence_before();
@@ -569,41 +689,25 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     if (lane == 0 && !dry) mbar_arrive(&ms->sempty[sb]);
                     if constexpr (cols) {
 #pragma unroll
-                        for (int h = 0; h < 32; ++h) v[0][h] += v[1][h];       // hi + lo products
+                        for (int h = 0; h < HQ; ++h) v[h] += v[HQ + h];       // hi + lo products
                     }
-                    // scale and mask (an insertion step's raw query excludes the new Beacon)
+                    // scale and mask
 #pragma unroll
-                    for (int l = 0; l < 2; ++l) {
-                        const int limit = (J.causal && NQ == 2 && l == 0) ? n_keys - 1 : n_keys;
-#pragma unroll
-                        for (int h = 0; h < 32; ++h) v[l][h] = key < limit ? v[l][h] * J.scale_log2 : -INFINITY;
-                    }
+                    for (int i = 0; i < NS; ++i) v[i] = key < (i < HQ ? lim0 : n_keys) ? v[i] * J.scale_log2 : -INFINITY;
                     // Column maxima only when some score exceeds its row's running
                     // max by more than the lazy threshold (always on a piece's first
                     // tile): otherwise the max stays and every p <= 2^8.
                     bool over = t <= p.t0;
                     if (!over) {
 #pragma unroll
-                        for (int l = 0; l < 2; ++l)
-                            if (l < NQ) {
-#pragma unroll
-                                for (int h = 0; h < 32; ++h) over |= v[l][h] > ms->m_run[32 * l + h] + kLazyLog2;
-                            }
+                        for (int i = 0; i < NS; ++i) over |= v[i] > ms->m_run[i] + kLazyLog2;
                     }
                     const bool rescan = named_bar_or(1, 128, over);
                     bool need_fix = false;
                     if (rescan) {
-#pragma unroll
-                        for (int l = 0; l < 2; ++l) {
-                            if (l < NQ) {
-                                float tmp[32];
-#pragma unroll
-                                for (int h = 0; h < 32; ++h) tmp[h] = v[l][h];
-                                ms->red[quarter][32 * l + lane] = warp_transpose_reduce<true>(tmp, lane);
-                            }
-                        }
+                        transpose_reduce_to<true, NS>(v, lane, ms->red[quarter]);
                         named_bar(1, 128);
-                        if (st < rows) {
+                        if (st < NS) {
                             const float tm =
                                 fmaxf(fmaxf(ms->red[0][st], ms->red[1][st]), fmaxf(ms->red[2][st], ms->red[3][st]));
                             const float mo = ms->m_run[st];
@@ -616,7 +720,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                             ms->m_run[st] = mn;
                             ms->l_run[st] *= alpha;
                         }
-                        need_fix = named_bar_or(1, 128, st < rows && t > p.t0 && ms->alpha[st] != 1.f);
+                        need_fix = named_bar_or(1, 128, st < NS && t > p.t0 && ms->alpha[st] != 1.f);
                     }
                     // P(j) overwrites the buffer P.V(j-1) reads: wait for it.
                     if (j > 0) {
@@ -629,66 +733,73 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     // the rows too keeps a non-finite stale value from turning 0 * x
                     // into NaN.  Each thread clears its own key row once the chunk
                     // has landed (P.V(j) does not start before P(j) is released).
-                    if (!dry && t == n_tiles - 1 && (n_keys & (kKeys - 1)) != 0) {
-                        bool okc = true;
-                        if (key >= n_keys) {
-                            for (int c = 0; c < vc && okc; ++c) {
-                                const int slot = v_slot(j, c);
-                                okc = wait_or_abort(&ms->vfull[slot], v_use(j) & 1, ms, J.status, wait_ns);
-                                if (okc) {
-                                    uint4* row = reinterpret_cast<uint4*>(smem + slot * kChunkBytes + t_local * 128);
+                    // The wide layout's P.V warp does this instead.
+                    if constexpr (!WIDE) {
+                        if (!dry && t == n_tiles - 1 && (n_keys & (kKeys - 1)) != 0) {
+                            bool okc = true;
+                            if (key >= n_keys) {
+                                for (int c = 0; c < vc && okc; ++c) {
+                                    const int slot = v_slot(j, c);
+                                    okc = wait_or_abort(&ms->vfull[slot], v_use(j, c) & 1, ms, J.status, wait_ns);
+                                    if (okc) {
+                                        uint4* row = reinterpret_cast<uint4*>(smem + slot * kChunkBytes + t_local * 128);
 #pragma unroll
-                                    for (int u = 0; u < 8; ++u) row[u] = make_uint4(0, 0, 0, 0);
+                                        for (int u = 0; u < 8; ++u) row[u] = make_uint4(0, 0, 0, 0);
+                                    }
+                                }
+                            }
+                            if (named_bar_or(1, 128, !okc)) { failed = true; break; }
+                        }
+                    }
+                    if (need_fix) {
+                        // O^T column c of a block belongs to row c mod HQ (hi | lo)
+                        // or to row c (two queries).
+                        for (int blk = 0; blk < vblocks; ++blk) {
+#pragma unroll
+                            for (int c0 = 0; c0 < NC; c0 += 32) {
+                                const uint32_t addr = o_tmem + lane_addr + uint32_t(blk * n_mma + c0);
+                                if (c0 + 32 <= NC) {
+                                    float o[32];
+                                    tmem_ld32(addr, o);
+                                    tmem_wait_ld();
+#pragma unroll
+                                    for (int i = 0; i < 32; ++i) o[i] *= ms->alpha[cols ? (c0 + i) % HQ : c0 + i];
+                                    tmem_st32(addr, o);
+                                } else {
+                                    float o[16];
+                                    tmem_ld16(addr, o);
+                                    tmem_wait_ld();
+#pragma unroll
+                                    for (int i = 0; i < 16; ++i) o[i] *= ms->alpha[cols ? (c0 + i) % HQ : c0 + i];
+                                    tmem_st16(addr, o);
                                 }
                             }
                         }
-                        if (named_bar_or(1, 128, !okc)) { failed = true; break; }
-                    }
-                    if (need_fix) {
-                        // O^T column group k2 (32 columns) belongs to row k2*32 + h,
-                        // or to row h for the single-query hi | lo layout.
-                        for (int blk = 0; blk < vblocks; ++blk)
-                            for (int k2 = 0; k2 < 2; ++k2) {
-                                float o[32];
-                                const uint32_t addr = o_tmem + lane_addr + uint32_t(blk * kN + 32 * k2);
-                                tmem_ld32(addr, o);
-                                tmem_wait_ld();
-                                const float* al = ms->alpha + (cols ? 0 : 32 * k2);
-#pragma unroll
-                                for (int h = 0; h < 32; ++h) o[h] *= al[h];
-                                tmem_st32(addr, o);
-                            }
                         tmem_wait_st();
                     }
-                    // probabilities -> P^T rows (hi and lo), row sums
+                    // Probabilities -> P^T row of this key: column 8u of the hi part
+                    // and HQ + 8u (hi | lo) or 64 + 8u (two queries: the lo buffer)
+                    // of the lo part, in 64-column swizzle atoms kChunkBytes apart.
                     uint8_t* prow = smem + LY.off_p + t_local * 128;
+                    float pr[NS];
 #pragma unroll
-                    for (int l = 0; l < 2; ++l) {
-                        if (l < NQ) {
-                            float pr[32];
-#pragma unroll
-                            for (int h = 0; h < 32; ++h) {
-                                const float m = ms->m_run[32 * l + h];
-                                pr[h] = v[l][h] == -INFINITY ? 0.f : sfu_exp2(v[l][h] - m);     // finite v => finite m
-                            }
-#pragma unroll
-                            for (int u = 0; u < 4; ++u) {
-                                uint4 hi, lo;
-                                split_hilo(pr, u, hi, lo);
-                                // nq = 1: units 0-3 hi, 4-7 lo of one buffer; nq = 2:
-                                // unit 4l + u of the hi and of the lo buffer.
-                                const int uh = cols ? u : 4 * l + u, ul = cols ? 4 + u : 4 * l + u;
-                                uint8_t* lrow = cols ? prow : prow + kChunkBytes;
-                                *reinterpret_cast<uint4*>(prow + ((uh ^ (t_local & 7)) << 4)) = hi;
-                                *reinterpret_cast<uint4*>(lrow + ((ul ^ (t_local & 7)) << 4)) = lo;
-                            }
-                            ms->red[quarter][32 * l + lane] = warp_transpose_reduce<false>(pr, lane);
-                        }
+                    for (int i = 0; i < NS; ++i) {
+                        const float m = ms->m_run[i];
+                        pr[i] = v[i] == -INFINITY ? 0.f : sfu_exp2(v[i] - m);     // finite v => finite m
                     }
+#pragma unroll
+                    for (int u = 0; u < NS / 8; ++u) {
+                        uint4 hi, lo;
+                        split_hilo(pr, u, hi, lo);
+                        const int ch = 8 * u, cl = (cols ? HQ : 64) + 8 * u;
+                        *reinterpret_cast<uint4*>(prow + (ch >> 6) * kChunkBytes + ((((ch & 63) >> 3) ^ (t_local & 7)) << 4)) = hi;
+                        *reinterpret_cast<uint4*>(prow + (cl >> 6) * kChunkBytes + ((((cl & 63) >> 3) ^ (t_local & 7)) << 4)) = lo;
+                    }
+                    transpose_reduce_to<false, NS>(pr, lane, ms->red[quarter]);
                     fence_async_shared();
                     tc_fence_before();
                     named_bar(1, 128);
-                    if (st < rows)
+                    if (st < NS)
                         ms->l_run[st] += ms->red[0][st] + ms->red[1][st] + ms->red[2][st] + ms->red[3][st];
                     __syncwarp();
                     if (dry) {
@@ -710,40 +821,31 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                 }
                 tc_fence_after();
                 named_bar(1, 128);                     // every thread's l_run update is in
-                if (st < 64) ms->alpha[st] = (st < rows && ms->l_run[st] > 0.f) ? 1.f / ms->l_run[st] : 0.f;
+                if (st < 64) ms->alpha[st] = (st < NS && ms->l_run[st] > 0.f) ? 1.f / ms->l_run[st] : 0.f;
                 named_bar(1, 128);
                 const int piece = piece_base + p.piece;
                 float* out = J.part_o + (int64_t)piece * J.rows_alloc * J.out_width;
-                // Output row of (query l, head column h): l * rg + h for h < rg (rg
-                // = all 32 heads for the latent branch, the group for raw rows).
-                constexpr int rg = 32;
                 // The row scales in registers: read between the global stores
                 // through a generic pointer they would be reloaded every time.
-                float al[rows];
+                float al[NS];
 #pragma unroll
-                for (int h = 0; h < rows; ++h) al[h] = ms->alpha[h];
+                for (int i = 0; i < NS; ++i) al[i] = ms->alpha[i];
                 for (int blk = 0; blk < vblocks; ++blk) {
                     const bool pair = 2 * blk + 1 < vc;
-                    float o[2][32];
-                    tmem_ld32(o_tmem + lane_addr + uint32_t(blk * kN), o[0]);
-                    tmem_ld32(o_tmem + lane_addr + uint32_t(blk * kN + 32), o[1]);
+                    float o[NC];
+                    tmem_ld_cols<NC>(o_tmem + lane_addr + uint32_t(blk * n_mma), o);
                     tmem_wait_ld();
                     // An M=128 block holds dim 32q + L of its chunk pair in lane L
                     // of quarter q; the M=64 block holds dim 16q + L in lane L < 16.
                     if (pair || lane < 16) {
                         const int d = 128 * blk + (pair ? 32 * quarter + lane : 16 * quarter + lane);
                         if constexpr (cols) {
+                            float* dst = out + (int64_t)row0 * J.out_width + d;
 #pragma unroll
-                            for (int h = 0; h < 32; ++h)
-                                if (h < rg) out[h * J.out_width + d] = (o[0][h] + o[1][h]) * al[h];
+                            for (int h = 0; h < HQ; ++h) dst[h * J.out_width] = (o[h] + o[HQ + h]) * al[h];
                         } else {
 #pragma unroll
-                            for (int h = 0; h < 32; ++h) {
-                                if (h < rg) {
-                                    out[h * J.out_width + d] = o[0][h] * al[h];
-                                    out[(rg + h) * J.out_width + d] = o[1][h] * al[32 + h];
-                                }
-                            }
+                            for (int c = 0; c < NC; ++c) out[c * J.out_width + d] = o[c] * al[c];
                         }
                     }
                 }
@@ -751,15 +853,20 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&ms->oempty[ob]);
-                if (st < rows && (st & 31) < rg) {
+                // Output row of score column i: row0 + i (head h of query l at l * HQ + h).
+                if (st < NS) {
                     const float lsum = ms->l_run[st];
-                    J.part_lse[(int64_t)piece * J.rows_alloc + (st >> 5) * rg + (st & 31)] =
+                    J.part_lse[(int64_t)piece * J.rows_alloc + row0 + st] =
                         lsum > 0.f ? (ms->m_run[st] + log2f(lsum)) * 0.69314718055994530942f : -INFINITY;
                 }
+                // A split sequence's other query has no keys in this piece.
+                if (J.split && nq_seq == 2 && st < HQ)
+                    J.part_lse[(int64_t)piece * J.rows_alloc + (HQ - row0) + st] = -INFINITY;
                 named_bar(1, 128);                     // m_run / l_run / alpha are reset by the next piece
             }
         };
-        if (cls == 0) latent_softmax(std::integral_constant<int, 1>{});
+        if constexpr (WIDE) latent_softmax(std::integral_constant<int, 1>{});
+        else if (cls == 0) latent_softmax(std::integral_constant<int, 1>{});
         else latent_softmax(std::integral_constant<int, 2>{});
     } else if (warp >= 3 && warp <= 6) {
         // ---- raw softmax and epilogue: thread <-> key, 16 score columns ----
@@ -778,9 +885,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
         int j = 0;
         for (int k = 0; pos < R.r1 && !failed; ++k) {
             Piece p;
-            next_piece(R, k, s, pos, J.kv_heads, p);
+            next_piece(R, k, s, pos, J.kv_heads, J.split, p);
             const int ob = k & 1;
-            const uint32_t o_tmem = tbase + uint32_t(ob) * kOBufCols;
+            const uint32_t o_tmem = tbase + uint32_t(ob) * o_cols;
             const int n_keys = J.seqlens[p.b];
             const int nq = J.qlens ? J.qlens[p.b] : J.length;
             const int n_tiles = (max(n_keys, 0) + kKeys - 1) / kKeys;
@@ -793,7 +900,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
             for (int t = p.t0 - (k == 0 && early ? 1 : 0); t < p.t1; ++t) {
                 const bool dry = t < p.t0;
                 const int sb = j & 1;
-                const uint32_t s_tmem = tbase + kSCol + uint32_t(sb * kN);
+                const uint32_t s_tmem = tbase + s_col + uint32_t(sb * n_mma);
                 const int key = t * kKeys + t_local;
                 bool ok = dry || wait_or_abort(&ms->sfull[sb], (j >> 1) & 1, ms, J.status, wait_ns);
                 if (named_bar_or(1, 128, !ok)) { failed = true; break; }
@@ -857,7 +964,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     if (key >= n_keys) {
                         for (int c = 0; c < vc && okc; ++c) {
                             const int slot = v_slot(j, c);
-                            okc = wait_or_abort(&ms->vfull[slot], v_use(j) & 1, ms, J.status, wait_ns);
+                            okc = wait_or_abort(&ms->vfull[slot], v_use(j, c) & 1, ms, J.status, wait_ns);
                             if (okc) {
                                 uint4* row = reinterpret_cast<uint4*>(smem + slot * kChunkBytes + t_local * 128);
 #pragma unroll
@@ -871,7 +978,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     // O^T columns c (hi) and 16 + c (lo) belong to score column c.
                     for (int blk = 0; blk < vblocks; ++blk) {
                         float o[32];
-                        const uint32_t addr = o_tmem + lane_addr + uint32_t(blk * kN);
+                        const uint32_t addr = o_tmem + lane_addr + uint32_t(blk * n_mma);
                         tmem_ld32(addr, o);
                         tmem_wait_ld();
 #pragma unroll
@@ -933,7 +1040,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
             for (int blk = 0; blk < vblocks; ++blk) {
                 const bool pair = 2 * blk + 1 < vc;
                 float o[32];
-                tmem_ld32(o_tmem + lane_addr + uint32_t(blk * kN), o);
+                tmem_ld32(o_tmem + lane_addr + uint32_t(blk * n_mma), o);
                 tmem_wait_ld();
                 if (pair || lane < 16) {
                     const int d = 128 * blk + (pair ? 32 * quarter + lane : 16 * quarter + lane);
@@ -1000,9 +1107,14 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
 namespace {
 
 int make_side(const TcSide& S, int batch, int length, float scale, const int32_t* qlens, unsigned* status,
-              uint64_t wait_ns, TcJob& J, CUtensorMap& km, CUtensorMap& vm, CUtensorMap& qm) {
-    if (S.dim_k > 320 || S.dim_v > 320 || S.width < 64 || S.width % 64 || S.rows_alloc < 2 * std::min(S.group, 32) ||
-        (reinterpret_cast<uintptr_t>(S.part_o) & 15) || S.group > 32)
+              uint64_t wait_ns, bool wide, TcJob& J, CUtensorMap& km, CUtensorMap& vm, CUtensorMap& qm) {
+    // The wide latent branch: 40 heads, ranks <= 512 with an even number of
+    // 64-column V chunks (a chunk pair takes two adjacent ring slots).
+    const bool wide_lat = wide && !S.q_rows;
+    const int max_dim = wide_lat ? 512 : 320;
+    if (S.dim_k > max_dim || S.dim_v > max_dim || S.width < 64 || S.width % 64 || S.rows_alloc < 2 * S.group ||
+        (reinterpret_cast<uintptr_t>(S.part_o) & 15) || (wide_lat ? S.group != kTcWideHeads : S.group > kTcHeads) ||
+        (wide_lat && ((S.dim_v + 63) / 64) % 2))
         return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "tensor-core decode attention: unsupported branch shape");
     int rc, box_rows = 128;
     if (S.pages) {
@@ -1037,6 +1149,12 @@ int make_side(const TcSide& S, int batch, int length, float scale, const int32_t
         if ((rc = encode_map_4d(&qm, S.q, S.dim_k, 1, S.heads, uint64_t(batch) * length, row, row, row * S.heads,
                                 S.group)))
             return rc;
+    } else if (wide_lat) {
+        // q_hilo [B][160][width]: boxes of one query's 80 rows.
+        const uint64_t row = uint64_t(S.width) * 2;
+        if ((rc = encode_map_4d(&qm, S.q, S.width, 1, kTcWideRows, batch, row, row, row * kTcWideRows,
+                                2 * kTcWideHeads)))
+            return rc;
     } else {
         const uint64_t row = uint64_t(S.width) * 2;
         if ((rc = encode_map_4d(&qm, S.q, S.width, 1, 128, batch, row, row, row * 128, 64))) return rc;
@@ -1048,6 +1166,7 @@ int make_side(const TcSide& S, int batch, int length, float scale, const int32_t
     J.group = S.group;
     J.causal = S.causal;
     J.q_rows = S.q_rows;
+    J.split = wide_lat ? 1 : 0;
     J.seqlens = S.seqlens;
     J.qlens = qlens;
     J.length = length;
@@ -1071,37 +1190,29 @@ int make_side(const TcSide& S, int batch, int length, float scale, const int32_t
 
 size_t tc_smem_bytes() { return kSmemBytes; }
 
-int launch_decode_tc(const TcLaunch& L, cudaStream_t stream) {
-    CUtensorMap lk, lv, lq, rk, rv, rq;
-    TcJob jl, jr;
-    int rc;
-    const uint64_t wait_ns = L.wait_ns ? L.wait_ns : 2000000000ull;
-    if ((rc = make_side(L.lat, L.batch, L.length, L.scale, L.query_len, L.status, wait_ns, jl, lk, lv, lq))) return rc;
-    if (L.with_raw) {
-        if ((rc = make_side(L.raw, L.batch, L.length, L.scale, L.query_len, L.status, wait_ns, jr, rk, rv, rq)))
-            return rc;
-        if (jr.kchunks > 2 || jr.vchunks > 2)
-            return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "tensor-core decode attention: raw head dim above 128");
-    } else {
-        jr = jl;
-        rk = lk; rv = lv; rq = lq;
-    }
+namespace {
+
+template <bool WIDE>
+int launch_tc(const TcLaunch& L, const CUtensorMap& lk, const CUtensorMap& lv, const CUtensorMap& lq,
+              const CUtensorMap& rk, const CUtensorMap& rv, const CUtensorMap& rq, const TcJob& jl, const TcJob& jr,
+              cudaStream_t stream) {
     // Every class layout fits the tile area (latent K chunks for classes 0-1,
     // two for raw).
     for (int cls = 0; cls < kTcClasses; ++cls) {
-        const Layout LY = class_layout(cls, cls == 2 ? 2 : jl.kchunks);
-        if (LY.off_p + uint32_t(LY.pbufs) * kChunkBytes > kTileBytes)
+        const Layout LY = class_layout<WIDE>(cls, cls == 2 ? 2 : jl.kchunks);
+        if (LY.off_p + uint32_t(LY.pbufs) * kChunkBytes > kTileBytes ||
+            (cls < 2 && uint32_t(jl.kchunks) * LY.qchunk > LY.qbytes))
             return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "tensor-core decode attention: class %d layout too large", cls);
     }
+    auto kernel = decode_tc_kernel<WIDE>;
     static bool configured[64] = {};
     const int dev = device_info().device;
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        if (cudaFuncSetAttribute(decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) != cudaSuccess)
             return fail(SLIMKV_ERR_CUDA, "cudaFuncSetAttribute (decode tc) failed");
         configured[dev] = true;
     }
-    const TcPlanLayout PL = tc_plan_layout(L.batch, L.kv_heads);
+    const TcPlanLayout PL = tc_plan_layout(L.batch, L.kv_heads, WIDE ? 1 : 0);
     // An early launch may start before the previous kernel (the prologue)
     // ends; the kernel waits for it before reading what it writes.
     cudaLaunchConfig_t cfg{};
@@ -1114,11 +1225,33 @@ int launch_decode_tc(const TcLaunch& L, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = L.early ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, decode_tc_kernel, lk, lv, lq, rk, rv, rq, jl, jr, L.plan, PL,
-                                       L.lat_pieces, L.early);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, lk, lv, lq, rk, rv, rq, jl, jr, L.plan, PL, L.lat_pieces, L.early);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SLIMKV_ERR_CUDA, "decode tc launch failed: %s", cudaGetErrorString(e));
     return SLIMKV_OK;
+}
+
+}  // namespace
+
+int launch_decode_tc(const TcLaunch& L, cudaStream_t stream) {
+    CUtensorMap lk, lv, lq, rk, rv, rq;
+    TcJob jl, jr;
+    int rc;
+    const uint64_t wait_ns = L.wait_ns ? L.wait_ns : 2000000000ull;
+    const bool wide = L.wide != 0;
+    if ((rc = make_side(L.lat, L.batch, L.length, L.scale, L.query_len, L.status, wait_ns, wide, jl, lk, lv, lq)))
+        return rc;
+    if (L.with_raw) {
+        if ((rc = make_side(L.raw, L.batch, L.length, L.scale, L.query_len, L.status, wait_ns, wide, jr, rk, rv, rq)))
+            return rc;
+        if (jr.kchunks > 2 || jr.vchunks > 2)
+            return fail(SLIMKV_ERR_UNSUPPORTED_SHAPE, "tensor-core decode attention: raw head dim above 128");
+    } else {
+        jr = jl;
+        rk = lk; rv = lv; rq = lq;
+    }
+    return wide ? launch_tc<true>(L, lk, lv, lq, rk, rv, rq, jl, jr, stream)
+                : launch_tc<false>(L, lk, lv, lq, rk, rv, rq, jl, jr, stream);
 }
 
 }  // namespace slimkv

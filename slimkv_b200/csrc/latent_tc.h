@@ -27,6 +27,9 @@ constexpr int kTcClasses = 3;
 constexpr int kTcMaxCtas = 160;          // CTAs of one launch (at most)
 
 // Device-written plan (int32 words in the workspace), header then arrays.
+// In the split-query plan (the 40-head layout, whose Q buffer holds one
+// query) a latent segment is one (sequence, query): class 0 carries them all,
+// id 2b + l, the two of a sequence adjacent; class 1 stays empty.
 //   hdr[4k + 0..3] = CTAs, first CTA, segments, tiles of class k
 //   seg_start[k] : [segments + 1] tile prefix of the class's segments
 //   seg_piece[k] : [segments + 1] first piece of each segment (prefix)
@@ -45,9 +48,9 @@ struct TcPlanLayout {
     int words;
 };
 
-__host__ __device__ inline TcPlanLayout tc_plan_layout(int batch, int kv_heads) {
+__host__ __device__ inline TcPlanLayout tc_plan_layout(int batch, int kv_heads, int split = 0) {
     TcPlanLayout L{};
-    L.max_lat_segs = batch;
+    L.max_lat_segs = split ? 2 * batch : batch;
     L.max_raw_segs = batch * kv_heads;
     int at = 16;
     L.hdr = 0;
@@ -82,6 +85,7 @@ struct TcPlanArgs {
     int ctas;                        // CTAs of the launch
     int raw_ctas;                    // > 0: CTAs of the raw class (else by volume)
     int with_raw;
+    int split_queries;               // one latent segment per (sequence, query)
     int32_t* plan;
 };
 
@@ -92,6 +96,7 @@ struct TcJob {
     int group;                // query heads per KV head (rows of a Q box in row mode)
     int causal;               // two queries: the first excludes the last key (the new Beacon)
     int q_rows;               // Q read per query from [B*L][H][dim] rows (exact bf16: no lo part)
+    int split;                // latent segments per (sequence, query): segment id 2b + l
     const int32_t* seqlens;   // keys per sequence
     const int32_t* qlens;     // queries per sequence (1 or 2), nullable
     int length;
@@ -118,7 +123,8 @@ struct TcSide {
     int kv_heads, capacity;
     int64_t stride_batch, stride_row, stride_head;   // elements
     // Latent: q_hilo [B][128][width] bf16 with row hl*32*nq + l*32 + head
-    // (hl 0 = hi, 1 = lo).  Raw: q_rot [B][L][H][dim] bf16.
+    // (hl 0 = hi, 1 = lo); 40 heads: [B][160][width] with row l*80 + hl*40 +
+    // head.  Raw: q_rot [B][L][H][dim] bf16.
     const void* q;
     int q_rows, heads, group, causal;
     const int32_t* seqlens;
@@ -142,6 +148,7 @@ struct TcLaunch {
     TcSide lat, raw;
     int with_raw;
     int kv_heads;              // the plan's KV heads (raw segments per sequence)
+    int wide;                  // 40 query heads, latent ranks <= 512 (split-query plan)
     int ctas;                  // grid size (persistent CTAs)
     const int32_t* plan;       // device plan written by plan_tc_work
     int lat_pieces;            // pieces reserved per latent class (class 1 starts after class 0's)
@@ -152,6 +159,13 @@ struct TcLaunch {
     // raw and Beacon rows).
     int early;
 };
+
+// Query heads of the latent branch the kernel is built for: 32 (ranks <=
+// 320, both query counts in one CTA) or 40 (ranks <= 512 with an even
+// number of 64-column V chunks, one query per CTA).
+constexpr int kTcHeads = 32;
+constexpr int kTcWideHeads = 40;
+constexpr int kTcWideRows = 4 * kTcWideHeads;     // q_hilo rows per sequence (2 queries x hi, lo)
 
 // Shared memory of the launch (same for every class).
 size_t tc_smem_bytes();

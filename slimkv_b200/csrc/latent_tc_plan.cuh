@@ -3,7 +3,8 @@
 // Run by one thread block (the prologue's first block, so it needs no launch
 // of its own) from this step's device lengths:
 //   1. segments: the latent rows of every sequence (class 0 for one query,
-//      class 1 for two) and the raw rows of every (sequence, KV head)
+//      class 1 for two; with split queries, one class-0 segment per
+//      (sequence, query)) and the raw rows of every (sequence, KV head)
 //      (class 2), in sequence order, with the tile prefix of each class;
 //   2. CTAs per class in proportion to the bytes the class streams, weighted
 //      by how fast its layout streams them;
@@ -85,7 +86,7 @@ __device__ __host__ inline long long tc_cta_start(int tiles, int ctas, int i) {
 // and copied to `a.plan` at the end; otherwise it is built in place.
 __device__ inline void plan_tc_work(const TcPlanArgs& a, int32_t* scratch, int scratch_words) {
     __shared__ int s_warp[32];
-    const TcPlanLayout L = tc_plan_layout(a.batch, a.kv_heads);
+    const TcPlanLayout L = tc_plan_layout(a.batch, a.kv_heads, a.split_queries);
     const bool on_chip = L.words <= scratch_words;
     int32_t* P = on_chip ? scratch : a.plan;
     const int tid = threadIdx.x;
@@ -99,20 +100,23 @@ __device__ inline void plan_tc_work(const TcPlanArgs& a, int32_t* scratch, int s
         const int b = b0 + tid;
         const bool ok = b < a.batch;
         const int nq = ok ? (a.query_len ? a.query_len[b] : a.length) : 1;
-        const int cls = nq == 2 ? 1 : 0;
+        const int cls = nq == 2 && !a.split_queries ? 1 : 0;
+        const int ns = a.split_queries ? nq : 1;        // latent segments of sequence b
         const int tl = ok ? tc_tiles_of(a.latent_len[b]) : 0;
         const int tr = ok && a.with_raw ? tc_tiles_of(a.raw_len[b]) : 0;
         int tot[5];
-        const int seg0 = block_exclusive_scan(ok && cls == 0, &tot[0], s_warp);
-        const int til0 = block_exclusive_scan(ok && cls == 0 ? tl : 0, &tot[1], s_warp);
+        const int seg0 = block_exclusive_scan(ok && cls == 0 ? ns : 0, &tot[0], s_warp);
+        const int til0 = block_exclusive_scan(ok && cls == 0 ? ns * tl : 0, &tot[1], s_warp);
         const int seg1 = block_exclusive_scan(ok && cls == 1, &tot[2], s_warp);
         const int til1 = block_exclusive_scan(ok && cls == 1 ? tl : 0, &tot[3], s_warp);
         const int rawp = block_exclusive_scan(tr, &tot[4], s_warp);
         if (ok) {
             const int seg = cls ? carry[2] + seg1 : carry[0] + seg0;
             const int til = cls ? carry[3] + til1 : carry[1] + til0;
-            P[L.seg_start[cls] + seg] = til;
-            P[L.seg_id[cls] + seg] = b;
+            for (int q = 0; q < ns; ++q) {
+                P[L.seg_start[cls] + seg + q] = til + q * tl;
+                P[L.seg_id[cls] + seg + q] = a.split_queries ? 2 * b + q : b;
+            }
             P[L.lat_seg + b] = (cls << 24) | seg;
             // Raw segments (b, g): tile prefix Hkv * (raw tiles before b) + g * tr.
             const int rbase = a.kv_heads * (carry[4] + rawp);
@@ -218,12 +222,14 @@ __device__ inline void plan_tc_work(const TcPlanArgs& a, int32_t* scratch, int s
         if (tid == 0) piece[ns] = carry_p;
         __syncthreads();
     }
-    // 4. Each sequence's latent piece range.
+    // 4. Each sequence's latent piece range (both query segments of a split
+    // sequence: they are adjacent).
     for (int b = tid; b < a.batch; b += blockDim.x) {
         const int ls = P[L.lat_seg + b], cls = ls >> 24, s = ls & 0xffffff;
+        const int ns = a.split_queries ? (a.query_len ? a.query_len[b] : a.length) : 1;
         const int32_t* pc = P + L.seg_piece[cls];
         P[L.lat_range + 2 * b] = (cls << 24) | pc[s];
-        P[L.lat_range + 2 * b + 1] = pc[s + 1] - pc[s];
+        P[L.lat_range + 2 * b + 1] = pc[s + ns] - pc[s];
     }
     __syncthreads();
     if (on_chip)

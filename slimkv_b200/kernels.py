@@ -163,6 +163,40 @@ def rope_rows(x, positions, cos, sin, counts=None, out=None):
     return out
 
 
+def rms_norm(x, weight, eps, out=None):
+    """``LlamaRMSNorm`` of the rows of ``x [..., hidden]`` (bf16, rows with a
+    contiguous last dimension): ``weight * bf16(x * rsqrt(mean(x^2) + eps))``
+    (``slimkv_rms_norm``; slimkv/llama3/modeling_llama.py:79-95)."""
+    _bf16_cuda(x, weight)
+    H = x.shape[-1]
+    rows = x.view(-1, H)
+    _require(rows.stride(1) == 1 and weight.is_contiguous() and weight.numel() == H, 'rows [N, hidden], weight [hidden]')
+    if out is None:
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    orows = out.view(-1, H)
+    _require(orows.shape == rows.shape and orows.stride(1) == 1, 'out like x')
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.load().slimkv_rms_norm(_ptr(rows), rows.stride(0), _ptr(weight), _ptr(orows), orows.stride(0),
+                                              rows.shape[0], H, float(eps), _stream()))
+    return out
+
+
+def silu_mul(gate_up, out=None):
+    """``silu(gate) * up`` of rows ``gate_up [N, 2I]`` = ``[gate | up]`` (bf16),
+    each product rounded as the bf16 modules round it (``slimkv_silu_mul``;
+    ``LlamaMLP.forward``, modeling_llama.py:97-113).  Returns ``[N, I]``."""
+    _bf16_cuda(gate_up)
+    _require(gate_up.dim() == 2 and gate_up.stride(1) == 1 and gate_up.shape[1] % 2 == 0, 'gate_up [N, 2I]')
+    n, inter = gate_up.shape[0], gate_up.shape[1] // 2
+    if out is None:
+        out = torch.empty((n, inter), dtype=gate_up.dtype, device=gate_up.device)
+    _require(out.shape == (n, inter) and out.stride(1) == 1, 'out [N, I]')
+    with torch.cuda.device(gate_up.device):
+        _lib.check(_lib.load().slimkv_silu_mul(_ptr(gate_up), gate_up.stride(0), _ptr(out), out.stride(0), n, inter,
+                                              _stream()))
+    return out
+
+
 def merge(raw, raw_lse, latent, latent_lse):
     """LSE merge of BHQD bf16 outputs (``decode_ops.fused_merge`` contract)."""
     _bf16_cuda(raw, latent)

@@ -24,7 +24,6 @@ import math
 from dataclasses import dataclass, field
 
 import torch
-import torch.nn.functional as F
 
 from . import kernels
 from .rope import LLAMA3_SCALING, rope_tables
@@ -296,6 +295,10 @@ class LatentDecodeRuntime:
         self.x = torch.zeros(B, 2, H, **bf)
         self.z = torch.zeros(B, 2, self.width, **bf)            # projection outputs per row
         self.attn = torch.zeros(B, 2, qd, **bf)
+        self.h = torch.zeros(B, 2, H, **bf)                      # normalised rows
+        self.gu = torch.zeros(2 * B, 2 * cfg.intermediate, **bf)
+        self.act = torch.zeros(2 * B, cfg.intermediate, **bf)
+        self.h_final = torch.zeros(B, H, **bf)
         self.logits = torch.zeros(B, cfg.vocab, dtype=torch.float32, device=device)
         z = self.z
         q = z[:, :, :qd].unflatten(-1, (cfg.heads, cfg.head_dim))          # [B, 2, H, D]
@@ -418,7 +421,7 @@ class LatentDecodeRuntime:
     def step_eager(self):
         """One decode step on the current stream (what the graph captures)."""
         cfg, w = self.cfg, self.w
-        B, H, I = self.batch, cfg.hidden, cfg.intermediate
+        B, H = self.batch, cfg.hidden
         qd = cfg.heads * cfg.head_dim
         nb = qd + cfg.rank_k + cfg.rank_v
         kernels.decode_schedule(self.history, self.tail, self.raw_len, self.latent_len, self.query_len,
@@ -431,8 +434,9 @@ class LatentDecodeRuntime:
         x = self.x
         x[:, 0].copy_(w.embed.index_select(0, self.tokens))
         x[:, 1].copy_(w.beacon_embed.expand(B, -1))
+        x2d, h = x.view(2 * B, H), self.h
         for i, (layer, call) in enumerate(zip(w.layers, self.calls)):
-            h = F.rms_norm(x, (H,), layer['norm1'], cfg.rms_eps)
+            kernels.rms_norm(x, layer['norm1'], cfg.rms_eps, out=h)
             if cfg.qkv_bias:
                 torch.addmm(layer['b_raw'], h[:, 0], layer['w_raw'].t(), out=self.z[:, 0])
                 torch.addmm(layer['b_beacon'], h[:, 1], layer['w_beacon'].t(), out=self.z[:, 1, :nb])
@@ -445,12 +449,13 @@ class LatentDecodeRuntime:
                 call()
             if self.merges:
                 self.merges[i]()                     # all-gather of the partials + N-part merge -> self.attn
-            x.add_((self.attn.view(2 * B, qd) @ layer['w_o'].t()).view(B, 2, H))
-            h2 = F.rms_norm(x, (H,), layer['norm2'], cfg.rms_eps)
-            gu = h2.view(2 * B, H) @ layer['w_gate_up'].t()
-            act = F.silu(gu[:, :I]) * gu[:, I:]
-            x.add_((act @ layer['w_down'].t()).view(B, 2, H))
-        final = F.rms_norm(x[:, 0], (H,), w.final_norm, cfg.rms_eps)
+            # Residual adds in the GEMMs' accumulate (beta = 1, one bf16 rounding).
+            x2d.addmm_(self.attn.view(2 * B, qd), layer['w_o'].t())
+            kernels.rms_norm(x, layer['norm2'], cfg.rms_eps, out=h)
+            torch.mm(h.view(2 * B, H), layer['w_gate_up'].t(), out=self.gu)
+            kernels.silu_mul(self.gu, out=self.act)
+            x2d.addmm_(self.act, layer['w_down'].t())
+        final = kernels.rms_norm(x[:, 0], w.final_norm, cfg.rms_eps, out=self.h_final)
         # bf16 operands, the fp32 accumulator kept as the logits (no bf16
         # rounding of the output: same weight traffic, exact to the GEMM).
         torch.mm(final, w.lm_head.t(), torch.float32, out=self.logits)

@@ -206,16 +206,39 @@ def test_fused_decode_matches_oracle(length, history, tail, rank, bias, ragged):
 
 
 @pytest.mark.parametrize('length,heads,rank,ragged', [
-    (1, 40, 512, True), (2, 40, 512, False), (2, 32, 384, True), (1, 40, 320, False), (2, 40, 160, True)])
+    (1, 40, 512, True), (2, 40, 512, False), (2, 32, 384, True), (1, 40, 320, False), (2, 40, 160, True),
+    (2, 40, 384, True), (1, 40, 256, True)])
 def test_qwen_geometry_and_wide_latents(length, heads, rank, ragged):
     """40 query heads over 8 KV heads (Qwen2.5-14B) and latent ranks up to 512
-    (r2), with up-projection biases: the split-KV route with 32-key tiles for
-    ranks above 320."""
+    (r2), with up-projection biases.  An even number of 64-column V chunks
+    (ranks 256, 384, 512) runs the tensor-memory kernel's 40-head layout (one
+    query per latent CTA, V chunks cycling through a 4-slot ring); odd ones
+    (160, 320) and 32 heads above rank 320 the split-KV route."""
     c = decode_case(500 + rank + length, batch=3, length=length, history=700, tail=300, heads=heads, kv_heads=8,
                     rk=rank, rv=rank, bias=True, ragged=ragged)
     query_len = np.full(3, length)
     check(c, query_len, run_fused(c, query_len))
     check(c, query_len, run_fused(c, query_len, fp32=True))
+
+
+@pytest.mark.parametrize('paged', [False, True])
+def test_wide_layout_mixed_queries_stale_rows_and_early_start(paged):
+    """The 40-head layout at rank 512: sequences with and without a Beacon in
+    one batch (each query its own latent segment, the merge combining both
+    segments' pieces), NaN in the cache rows past every length (cleared by the
+    P.V warp in the partial last tile), dense or paged latents; a step plan
+    with the early attention start gives the same bits."""
+    c = decode_case(2140, batch=7, length=2, history=900, tail=300, heads=40, kv_heads=8, rk=512, rv=512,
+                    bias=True, ragged=True)
+    query_len = np.array([2, 1, 1, 2, 1, 2, 2])
+    c['n_lat'] = c['n_lat'] - (query_len == 1)
+    a = run_fused(c, query_len, extra_cap=150, fp32=True, paged=paged, stale=float('nan'))
+    assert torch.isfinite(a['out']).all()
+    check(c, query_len, a)
+    b = run_fused(c, query_len, extra_cap=150, fp32=True, paged=paged, stale=float('nan'), step_plan=True)
+    for key in ('out', 'lat_k', 'lat_v'):
+        x, y = a[key], b[key]
+        assert torch.equal(torch.nan_to_num(x.float(), nan=7.0), torch.nan_to_num(y.float(), nan=7.0)), key
 
 
 @pytest.mark.parametrize('paged', [False, True])
