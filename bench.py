@@ -28,6 +28,7 @@ install it times the numpy restatement in ``oracle/cpu_decode.py``.
 """
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -499,6 +500,102 @@ def prefill_window_step(device, steps, warmup):
             'kernels': 'project_kernel (tcgen05, gathered rows) + finalize_kernel when split', 'device_status': status}
 
 
+def prefill_chunk_attention(device, steps, warmup):
+    """BASELINE config 4, the attention of one layer at the last 4096-token
+    chunk of the 32768-token prompts: B=4 x 5120 chunk rows (4 windows of
+    1024 raw + 256 Beacon rows), 4 sinks, 7168 history Beacon latents (ranks
+    320), Llama-3.1-8B heads (32 / 8, dim 128).  Times (CUDA graphs) the
+    absorbed-history attention (``prefill_attention.latent_history_attention``:
+    two ``slimkv_prefill_attention`` launches, the absorb and up-projection
+    GEMMs, the LSE merge), the materialised recipe on this library's kernels
+    and the reference's recipe on the same GPU through torch: the history up-
+    projected by ``nn.Linear`` each chunk, concatenated with the sinks and the
+    chunk, then a causal (bottom-right) scaled-dot-product attention."""
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention.bias import causal_lower_right
+    from slimkv_b200 import _lib
+    from slimkv_b200 import prefill_attention as PA
+    g = torch.Generator(device=device)
+    g.manual_seed(44)
+    B, T, P, N, H, Hkv, D, R = PREFILL_BATCH, 5120, 4, 7168, 32, 8, 128, 320
+    bf = lambda *s, std=1.0: (torch.randn(*s, generator=g, device=device) * std).to(torch.bfloat16)
+    q, k_cur, v_cur = bf(B, T, H, D), bf(B, T, Hkv, D), bf(B, T, Hkv, D)
+    sink_k, sink_v = bf(B, P, Hkv, D), bf(B, P, Hkv, D)
+    lat = bf(B, N, 2 * R, std=1.3)
+    lat_k, lat_v = lat[..., :R], lat[..., R:]
+    uk, uv = bf(Hkv * D, R, std=0.05), bf(Hkv * D, R, std=0.05)
+    lat_len = torch.full((B,), N, dtype=torch.int32, device=device)
+    scale = 1.0 / math.sqrt(D)
+    mask = causal_lower_right(T, P + N + T)
+
+    def absorbed():
+        return PA.latent_history_attention(q, sink_k, sink_v, lat_k, lat_v, lat_len, uk, uv, k_cur, v_cur, scale)
+
+    def materialized():
+        return PA.materialized_history_attention(q, sink_k, sink_v, lat_k, lat_v, N, uk, uv, k_cur, v_cur, scale)
+
+    def recipe():
+        hk = (lat_k @ uk.t()).view(B, N, Hkv, D)
+        hv = (lat_v @ uv.t()).view(B, N, Hkv, D)
+        keys = torch.cat([sink_k, hk, k_cur], 1).transpose(1, 2)
+        vals = torch.cat([sink_v, hv, v_cur], 1).transpose(1, 2)
+        return F.scaled_dot_product_attention(q.transpose(1, 2), keys, vals, attn_mask=mask, scale=scale,
+                                              enable_gqa=True)
+
+    def graph_us(fn):
+        fn()
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream(device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        for _ in range(max(warmup, 3)):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps * 1000.0
+
+    _lib.device_status(clear=True)
+    t_abs, t_mat = graph_us(absorbed), graph_us(materialized)
+    try:
+        t_ref = graph_us(recipe)
+    except RuntimeError as e:                                  # no SDPA backend for this mask on this build
+        t_ref = None
+        ref_error = str(e).splitlines()[0]
+    status = _lib.device_status(clear=True)
+    # FLOPs: 2 per multiply-add of S and of P.V (causal chunk part: the visible half).
+    chunk_keys = B * H * (T * P + T * (T + 1) // 2)
+    hist_pairs = B * H * T * N
+    f_hist_abs = 2 * hist_pairs * 2 * R
+    f_hist_mat = 2 * hist_pairs * 2 * D
+    f_chunk = 2 * chunk_keys * 2 * D
+    out = {'workload': 'BASELINE config 4 prefill attention, one layer at the last chunk: B=4 x 5120 rows '
+                       '(4096 raw + 1024 Beacon), 4 sinks, 7168 history latents (ranks 320), heads 32/8 dim 128',
+           'absorbed_us': t_abs, 'absorbed_tflops': (f_hist_abs + f_chunk) / (t_abs / 1e6) / 1e12,
+           'absorbed_flops': f_hist_abs + f_chunk,
+           'materialized_us': t_mat, 'materialized_tflops': (f_hist_mat + f_chunk) / (t_mat / 1e6) / 1e12,
+           'materialized_flops': f_hist_mat + f_chunk,
+           'reference_recipe_gpu_us': t_ref,
+           'kernels': 'prefill_attention_kernel (tcgen05, twice) + cuBLAS absorb / up-projection + merge_kernel; '
+                      'materialized: project_kernel (reconstruct) + prefill_attention_kernel',
+           'device_status': status}
+    if t_ref is None:
+        out['reference_recipe_error'] = ref_error
+    else:
+        out['speedup_vs_reference_recipe'] = t_ref / min(t_abs, t_mat)
+    return out
+
+
 def attention_kernel_time(rt, reps):
     """Average device time of the attention launch (both branches) alone:
     CUDA events recorded by the library right around that kernel, on the
@@ -748,7 +845,8 @@ def main():
     if args.prefill_only:
         import torch
         device = torch.device('cuda', 0)
-        print(json.dumps({'prefill_only': True, **prefill_window_step(device, max(args.steps, 1), args.warmup)}),
+        print(json.dumps({'prefill_only': True, **prefill_window_step(device, max(args.steps, 1), args.warmup),
+                          'chunk_attention': prefill_chunk_attention(device, max(args.steps, 1), args.warmup)}),
               flush=True)
         return
     import numpy as np

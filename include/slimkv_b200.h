@@ -563,6 +563,47 @@ typedef struct {
 SLIMKV_API int slimkv_merge_partials(const slimkv_merge_partials_args* args, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Prefill attention (tcgen05 flash attention forward) — the attention of a
+ * prefill chunk when the history stays in latent form, replacing the
+ * materialisation of every history latent (ReconstructionCache.materialize,
+ * slimkv/llama3/memory.py:26-48, joined at modeling_llama.py:1650-1681)
+ * followed by one flash attention.  One call attends one part:
+ *   out[b, t, g*R + j, :] = softmax_k(scale q[b, t, g*R + j, :] . k[b, k, g, :]) v[b, k, g, :]
+ * over keys k < kv_len[b] (and k <= causal_offset + t when causal), R =
+ * rows_per_token query heads per KV head g.  The history part passes the
+ * queries absorbed into latent space with every head of the chunk as rows
+ * of the one latent head (kv_heads 1, R = H) and the latents as k / v; the
+ * chunk part passes the rotated queries, keys and values of the sinks and
+ * the chunk (causal, bottom-right: causal_offset = keys before the chunk).
+ * q [B][tokens][kv_heads*R][dim_qk], k [B][kv_capacity][kv_heads][dim_qk],
+ * v likewise with dim_v: bf16, element strides {batch, token, head}
+ * (multiples of 8, last dimension contiguous, 16-byte aligned); out bf16
+ * [B][tokens][heads][dim_v] strides out_stride; lse fp32 natural log at
+ * lse[b*lse_stride[0] + t*lse_stride[1] + head] (nullable; -inf for a row
+ * without keys).  dims multiples of 8 up to 320; R at most 128.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    int batch, kv_heads, rows_per_token, tokens;
+    int dim_qk, dim_v;
+    const void* q;
+    int64_t q_stride[3];
+    const void* k;
+    const void* v;
+    int64_t kv_stride[3];
+    int kv_capacity;
+    const int32_t* kv_len;
+    int causal, causal_offset;
+    float scale;
+    void* out;
+    int64_t out_stride[3];
+    float* lse;
+    int64_t lse_stride[2];
+    uint64_t wait_limit_ns;    /* bound of every pipeline wait (0: 2 s) */
+} slimkv_prefill_attention_args;
+
+SLIMKV_API int slimkv_prefill_attention(const slimkv_prefill_attention_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
  * Decoder-layer element-wise steps of the batched decode runtime.
  * slimkv_rms_norm replaces LlamaRMSNorm.forward (slimkv/llama3/
  * modeling_llama.py:79-95): out = weight * bf16(x * rsqrt(mean(x^2) + eps)),

@@ -137,6 +137,16 @@ class MergePartialsArgs(ctypes.Structure):
     ]
 
 
+class PrefillAttentionArgs(ctypes.Structure):
+    """Mirror of ``slimkv_prefill_attention_args``."""
+    _fields_ = [
+        ('batch', _I), ('kv_heads', _I), ('rows_per_token', _I), ('tokens', _I), ('dim_qk', _I), ('dim_v', _I),
+        ('q', _P), ('q_stride', _L * 3), ('k', _P), ('v', _P), ('kv_stride', _L * 3), ('kv_capacity', _I),
+        ('kv_len', _P), ('causal', _I), ('causal_offset', _I), ('scale', ctypes.c_float), ('out', _P),
+        ('out_stride', _L * 3), ('lse', _P), ('lse_stride', _L * 2), ('wait_limit_ns', ctypes.c_uint64),
+    ]
+
+
 _PL = ctypes.POINTER(ctypes.c_int64)
 
 SIGNATURES = {
@@ -169,6 +179,7 @@ SIGNATURES = {
     'slimkv_merge_partials': (_I, [ctypes.POINTER(MergePartialsArgs), _P]),
     'slimkv_reconstruct_kv_workspace_size': (ctypes.c_size_t, [ctypes.POINTER(ReconstructArgs)]),
     'slimkv_reconstruct_kv': (_I, [ctypes.POINTER(ReconstructArgs), _P]),
+    'slimkv_prefill_attention': (_I, [ctypes.POINTER(PrefillAttentionArgs), _P]),
     'slimkv_rms_norm': (_I, [_P, _L, _P, _P, _L, _I, _I, ctypes.c_float, _P]),
     'slimkv_silu_mul': (_I, [_P, _L, _P, _L, _I, _I, _P]),
 }

@@ -54,11 +54,16 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 int encode_map_4d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                   uint64_t d3, uint64_t s1, uint64_t s2, uint64_t s3, uint32_t box_rows) {
+    return encode_map_4d_box(map, base, d0, d1, d2, d3, s1, s2, s3, 1, box_rows);
+}
+
+int encode_map_4d_box(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3,
+                      uint64_t s1, uint64_t s2, uint64_t s3, uint32_t box1, uint32_t box2) {
     auto fn = encode_fn();
     if (!fn) return fail(SLIMKV_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled is unavailable");
     cuuint64_t dims[4] = {d0, d1, d2, d3};
     cuuint64_t strides[3] = {s1, s2, s3};
-    cuuint32_t box[4] = {64, 1, box_rows, 1};
+    cuuint32_t box[4] = {64, box1, box2, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box,
                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

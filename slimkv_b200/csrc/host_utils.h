@@ -30,6 +30,9 @@ const DeviceInfo& device_info();
 // swizzle.  Returns SLIMKV_OK or SLIMKV_ERR_TENSOR_MAP (text in last error).
 int encode_map_4d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                   uint64_t d3, uint64_t s1, uint64_t s2, uint64_t s3, uint32_t box_rows);
+// The same with box {64, box1, box2, 1}: box1 x box2 rows of 128 bytes.
+int encode_map_4d_box(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3,
+                      uint64_t s1, uint64_t s2, uint64_t s3, uint32_t box1, uint32_t box2);
 // fp32 3-D map without swizzle (row-major [d2][d1][d0], strides in bytes),
 // box {box0, box1, 1}: the target of bulk tensor stores of staged tiles.
 int encode_map_f32_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,

@@ -480,13 +480,76 @@ def gen_reconstruct(out):
             out[f'{name}_full_{kind}'] = full.transpose(1, 2).contiguous().view(torch.int16).numpy()
 
 
+def gen_prefill_attention(out):
+    """The keys and values a prefill chunk attends over when its history is
+    latent: ``ReconstructionCache.materialize(attention, current)``
+    (slimkv/llama3/memory.py:26-48; the join of modeling_llama.py:1676-1681)
+    with bf16 up-projections, then the chunk's causal attention over them in
+    fp32 (torch SDPA with the bottom-right mask flash attention applies when
+    the queries are the last tokens of the keys)."""
+    import types
+    import torch
+    from slimkv.llama3.memory import ReconstructionCache
+    for name, (seed, batch, sink, n, tokens, rank, heads, kv_heads, dim, bias) in {
+            'llama_r4': (41, 2, 4, 200, 72, 320, 8, 2, 128, False),
+            'qwen_r2': (42, 1, 4, 97, 40, 512, 10, 2, 128, True)}.items():
+        rng = np.random.default_rng(seed)
+        f32 = np.float32
+        bf = lambda x: torch.from_numpy(np.ascontiguousarray(x, f32)).to(torch.bfloat16)
+        q = bf(rng.standard_normal((batch, heads, tokens, dim), dtype=f32))
+        sink_k = bf(rng.standard_normal((batch, kv_heads, sink, dim), dtype=f32))
+        sink_v = bf(rng.standard_normal((batch, kv_heads, sink, dim), dtype=f32))
+        cur_k = bf(rng.standard_normal((batch, kv_heads, tokens, dim), dtype=f32))
+        cur_v = bf(rng.standard_normal((batch, kv_heads, tokens, dim), dtype=f32))
+        lat = {kind: bf(rng.standard_normal((batch, 1, n, rank), dtype=f32) * 1.3) for kind in 'kv'}
+        mods = {}
+        for kind in 'kv':
+            lin = torch.nn.Linear(rank, kv_heads * dim, bias=bias, dtype=torch.bfloat16)
+            with torch.no_grad():
+                lin.weight.copy_(torch.from_numpy(rng.standard_normal((kv_heads * dim, rank), dtype=f32) * 0.05))
+                if bias:
+                    lin.bias.copy_(torch.from_numpy(rng.standard_normal(kv_heads * dim, dtype=f32) * 0.1))
+            mods[kind] = lin
+        attn = types.SimpleNamespace(beacon_k_up_proj=mods['k'], beacon_v_up_proj=mods['v'],
+                                     num_key_value_heads=kv_heads, head_dim=dim)
+        full = {}
+        for kind, sink_t, cur in (('k', sink_k, cur_k), ('v', sink_v, cur_v)):
+            cache = ReconstructionCache(sink_t, lat[kind], None, None, None, kv_heads, dim, kind)
+            with torch.no_grad():
+                full[kind] = cache.materialize(attn, cur)                     # [B, Hkv, S + N + T, D] bf16
+        keys = full['k'].shape[2]
+        group = heads // kv_heads
+        kf = full['k'].float().repeat_interleave(group, dim=1)
+        vf = full['v'].float().repeat_interleave(group, dim=1)
+        visible = torch.arange(keys)[None, :] <= (keys - tokens) + torch.arange(tokens)[:, None]
+        scale = 1.0 / math.sqrt(dim)
+        s = torch.einsum('bhtd,bhkd->bhtk', q.float(), kf) * scale
+        s = s.masked_fill(~visible, float('-inf'))
+        o = torch.softmax(s, -1) @ vf
+        lse = torch.logsumexp(s, -1)
+        i16 = lambda t: t.contiguous().view(torch.int16).numpy()
+        out[f'{name}_q'] = i16(q.transpose(1, 2))                             # [B, T, H, D]
+        out[f'{name}_sink_k'] = i16(sink_k.transpose(1, 2))                   # [B, S, Hkv, D]
+        out[f'{name}_sink_v'] = i16(sink_v.transpose(1, 2))
+        out[f'{name}_cur_k'] = i16(cur_k.transpose(1, 2))                     # [B, T, Hkv, D]
+        out[f'{name}_cur_v'] = i16(cur_v.transpose(1, 2))
+        for kind in 'kv':
+            out[f'{name}_lat_{kind}'] = i16(lat[kind][:, 0])                  # [B, N, R]
+            out[f'{name}_w_{kind}'] = i16(mods[kind].weight.detach())
+            if bias:
+                out[f'{name}_b_{kind}'] = i16(mods[kind].bias.detach())
+        out[f'{name}_out'] = o.transpose(1, 2).numpy()                        # [B, T, H, D] fp32
+        out[f'{name}_lse'] = lse.transpose(1, 2).numpy()                      # [B, T, H]
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument('--reference', required=True, help='path to a SlimKV source checkout')
     p.add_argument('--output', default=str(HERE / 'reference_golden.npz'))
     p.add_argument('--prefill-output', default=str(HERE / 'prefill_golden.npz'))
     p.add_argument('--reconstruct-output', default=str(HERE / 'reconstruct_golden.npz'))
-    p.add_argument('--only', choices=['decode', 'prefill', 'reconstruct'], default=None,
+    p.add_argument('--prefill-attention-output', default=str(HERE / 'prefill_attention_golden.npz'))
+    p.add_argument('--only', choices=['decode', 'prefill', 'reconstruct', 'prefill_attention'], default=None,
                    help='write only the decode-side or only the prefill-side fixture file')
     args = p.parse_args()
     ref = Path(args.reference).resolve()
@@ -494,6 +557,13 @@ def main():
     import torch
     torch.set_num_threads(4)
     from cases import config1_layer
+    if args.only in (None, 'prefill_attention'):
+        pa = {}
+        gen_prefill_attention(pa)
+        np.savez_compressed(args.prefill_attention_output, **pa)
+        print('wrote', args.prefill_attention_output, sum(v.nbytes for v in pa.values()), 'bytes raw')
+        if args.only == 'prefill_attention':
+            return
     if args.only in (None, 'reconstruct'):
         rec = {}
         gen_reconstruct(rec)
