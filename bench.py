@@ -565,7 +565,19 @@ def prefill_chunk_attention(device, steps, warmup):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / steps * 1000.0
 
+    # The two kernel launches alone (inputs as latent_history_attention makes them).
+    q_lat = torch.einsum('btgjd,gdr->btgjr', q.view(B, T, Hkv, H // Hkv, D), uk.view(Hkv, D, R)).reshape(B, T, H, R)
+    keys_k, keys_v = torch.cat([sink_k, k_cur], 1), torch.cat([sink_v, v_cur], 1)
+    chunk_len = torch.full((B,), P + T, dtype=torch.int32, device=device)
+
+    def history_kernel():
+        return PA.attention(q_lat, lat_k.unsqueeze(2), lat_v.unsqueeze(2), lat_len, scale, H)
+
+    def chunk_kernel():
+        return PA.attention(q, keys_k, keys_v, chunk_len, scale, H // Hkv, causal=True, causal_offset=P)
+
     _lib.device_status(clear=True)
+    t_hist_k, t_chunk_k = graph_us(history_kernel), graph_us(chunk_kernel)
     t_abs, t_mat = graph_us(absorbed), graph_us(materialized)
     try:
         t_ref = graph_us(recipe)
@@ -585,6 +597,8 @@ def prefill_chunk_attention(device, steps, warmup):
            'absorbed_flops': f_hist_abs + f_chunk,
            'materialized_us': t_mat, 'materialized_tflops': (f_hist_mat + f_chunk) / (t_mat / 1e6) / 1e12,
            'materialized_flops': f_hist_mat + f_chunk,
+           'history_kernel_us': t_hist_k, 'history_kernel_tflops': f_hist_abs / (t_hist_k / 1e6) / 1e12,
+           'chunk_kernel_us': t_chunk_k, 'chunk_kernel_tflops': f_chunk / (t_chunk_k / 1e6) / 1e12,
            'reference_recipe_gpu_us': t_ref,
            'kernels': 'prefill_attention_kernel (tcgen05, twice) + cuBLAS absorb / up-projection + merge_kernel; '
                       'materialized: project_kernel (reconstruct) + prefill_attention_kernel',
@@ -687,12 +701,12 @@ def kernel_only(args):
     if args.config == 5:
         import dataclasses
         from slimkv_b200.runtime import qwen25_14b_r2
-        cfg = dataclasses.replace(qwen25_14b_r2(), layers=1)
+        cfg = dataclasses.replace(qwen25_14b_r2(), layers=1, vocab=1024)
         batch = C5_BATCH
         history = [131072 // cfg.window * (cfg.window // cfg.ratio)] * batch
         extra = dict(raw_pre=False)
     else:
-        cfg = LatentLlamaConfig(layers=1)
+        cfg = LatentLlamaConfig(layers=1, vocab=1024)
         batch = BATCH
         history = [HISTORY] * batch
         extra = {}
