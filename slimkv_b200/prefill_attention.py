@@ -94,19 +94,19 @@ def latent_history_attention(q, prefix_k, prefix_v, lat_k, lat_v, lat_len, uk, u
     P = prefix_k.shape[1]
     rk, rv = lat_k.shape[-1], lat_v.shape[-1]
     dev = q.device
-    # 1. absorb: q_lat[b, t, h] = q[b, t, h] . U_k[g(h)]  (U_k[g] = uk[g*D:(g+1)*D].T : [D, R])
-    uk_g = uk.view(kv_heads, D, rk)
-    q_lat = torch.matmul(q.view(B, T, kv_heads, group, D), uk_g).view(B, T, H, rk)
+    # 1. absorb: q_lat[b, t, h] = q[b, t, h] . U_k[g(h)]  (U_k[g] = uk[g*D:(g+1)*D] : [D, R]), one GEMM
+    #    per KV head over all the chunk's rows of its group.
+    q5 = q.view(B, T, kv_heads, group, D)
+    q_lat = torch.einsum('btgjd,gdr->btgjr', q5, uk.view(kv_heads, D, rk)).reshape(B, T, H, rk)
     # 2. history in latent space: all H heads are rows of the one latent head.
     o_lat, lse_h = attention(q_lat, lat_k.unsqueeze(2), lat_v.unsqueeze(2), lat_len, scale, H)
     if uk_bias is not None:
         # every history key carries the bias: its score adds q . b_k[g], a row constant
-        shift = torch.matmul(q.float().view(B, T, kv_heads, group, D),
-                             uk_bias.float().view(kv_heads, D, 1)).view(B, T, H)
+        shift = torch.einsum('btgjd,gd->btgj', q5.float(), uk_bias.float().view(kv_heads, D)).reshape(B, T, H)
         lse_h = lse_h + shift * scale
     # 3. up-project the latent output: o[b, t, h] = o_lat[b, t, h] . U_v[g]^T (+ b_v)
-    uv_g = uv.view(kv_heads, D, rv).transpose(1, 2)                      # [Hkv, R, D]
-    o_hist = torch.matmul(o_lat.view(B, T, kv_heads, group, rv), uv_g).view(B, T, H, D)
+    o_hist = torch.einsum('btgjr,gdr->btgjd', o_lat.view(B, T, kv_heads, group, rv),
+                          uv.view(kv_heads, D, rv)).reshape(B, T, H, D)
     if uv_bias is not None:
         o_hist = o_hist + uv_bias.view(kv_heads, 1, D).expand(kv_heads, group, D).reshape(H, D)
     # 4. prefix + chunk, causal bottom-right (the chunk's rows are the last P + T keys' queries)
