@@ -636,6 +636,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
             constexpr int NC = 2 * HQ;
             constexpr int NS = NQ * HQ;
             constexpr bool cols = NQ == 1;
+            // One query: each thread keeps partial row sums of its own keys
+            // across the piece's tiles, reduced across the CTA once, in the
+            // epilogue (no per-tile reduction or barrier for them); two
+            // queries (64 columns) reduce per tile.
+            constexpr bool thread_sums = NQ == 1;
             static_assert(NS <= 64 && (NQ == 1 || HQ == 32), "latent score columns per CTA");
             const int quarter = warp & 3;
             const int t_local = 32 * quarter + lane;
@@ -662,6 +667,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     ms->m_run[st] = -INFINITY;
                     ms->l_run[st] = 0.f;
                 }
+                float lsum[thread_sums ? NS : 1];
+#pragma unroll
+                for (int i = 0; i < (thread_sums ? NS : 1); ++i) lsum[i] = 0.f;
                 named_bar(1, 128);
                 // An early launch starts its first piece with a dry tile (t = t0 - 1):
                 // the tile code runs once on zero scores while the prologue finishes, so
@@ -721,6 +729,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                             ms->l_run[st] *= alpha;
                         }
                         need_fix = named_bar_or(1, 128, st < NS && t > p.t0 && ms->alpha[st] != 1.f);
+                        if constexpr (thread_sums) {
+#pragma unroll
+                            for (int i = 0; i < NS; ++i) lsum[i] *= ms->alpha[i];
+                        }
                     }
                     // P(j) overwrites the buffer P.V(j-1) reads: wait for it.
                     if (j > 0) {
@@ -795,18 +807,27 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                         *reinterpret_cast<uint4*>(prow + (ch >> 6) * kChunkBytes + ((((ch & 63) >> 3) ^ (t_local & 7)) << 4)) = hi;
                         *reinterpret_cast<uint4*>(prow + (cl >> 6) * kChunkBytes + ((((cl & 63) >> 3) ^ (t_local & 7)) << 4)) = lo;
                     }
-                    transpose_reduce_to<false, NS>(pr, lane, ms->red[quarter]);
+                    if constexpr (thread_sums) {
+#pragma unroll
+                        for (int i = 0; i < NS; ++i) lsum[i] += pr[i];
+                    } else {
+                        transpose_reduce_to<false, NS>(pr, lane, ms->red[quarter]);
+                    }
                     fence_async_shared();
                     tc_fence_before();
-                    named_bar(1, 128);
-                    if (st < NS)
-                        ms->l_run[st] += ms->red[0][st] + ms->red[1][st] + ms->red[2][st] + ms->red[3][st];
+                    if constexpr (!thread_sums) {
+                        named_bar(1, 128);
+                        if (st < NS)
+                            ms->l_run[st] += ms->red[0][st] + ms->red[1][st] + ms->red[2][st] + ms->red[3][st];
+                    }
                     __syncwarp();
                     if (dry) {
                         if (st < 64) {
                             ms->m_run[st] = -INFINITY;
                             ms->l_run[st] = 0.f;
                         }
+#pragma unroll
+                        for (int i = 0; i < (thread_sums ? NS : 1); ++i) lsum[i] = 0.f;
                         named_bar(1, 128);
                         continue;
                     }
@@ -820,6 +841,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap lkmap, const __grid_constan
                     if (named_bar_or(1, 128, !ok)) { failed = true; break; }
                 }
                 tc_fence_after();
+                if constexpr (thread_sums) {
+                    transpose_reduce_to<false, NS>(lsum, lane, ms->red[quarter]);
+                    named_bar(1, 128);
+                    if (st < NS) ms->l_run[st] = ms->red[0][st] + ms->red[1][st] + ms->red[2][st] + ms->red[3][st];
+                }
                 named_bar(1, 128);                     // every thread's l_run update is in
                 if (st < 64) ms->alpha[st] = (st < NS && ms->l_run[st] > 0.f) ? 1.f / ms->l_run[st] : 0.f;
                 named_bar(1, 128);
