@@ -20,9 +20,11 @@
 //            alignment of a causal attention whose queries are the last
 //            tokens of the key sequence).
 //
-// One CTA per (128-row tile, KV head, sequence): Q staged once by TMA; keys
-// in 128-key tiles through K and V rings of 16 KB chunks ([128 keys x 64
-// columns], 128-byte swizzle, no multicast);
+// One CTA per (one or two 128-row Q tiles, KV head, sequence): Q staged once
+// by TMA; keys in 128-key tiles through K and V rings of 16 KB chunks ([128
+// keys x 64 columns], 128-byte swizzle, no multicast), each key / value tile
+// used by every Q tile of the CTA (two when both dims are <= 128: the chunk
+// part, with one softmax warpgroup per Q tile);
 //   S [128 rows x 128 keys] = Q . K^T   (tcgen05, M=128, N=128, fp32 in TMEM)
 //   O [128 rows x dim_v]   += P . V     (M=128, N=64 per V chunk)
 // with P in bf16 (as flash attention keeps it).  Softmax: one thread per row
@@ -31,7 +33,8 @@
 // more than 2^8).  Warp roles: 0 = Q and K producer, 3 = V producer, 1 = MMA
 // issuer (lane 0; the warp zeroes the V rows past a sequence's keys in its
 // last tile, whose contents the cache does not define), 2 = TMEM owner,
-// 4-7 = softmax and epilogue.  Every wait is bounded.
+// 4-7 (and 8-11) = softmax and epilogue of Q tile 0 (1).  Every wait is
+// bounded.
 #include <algorithm>
 
 #include "common.cuh"
@@ -42,7 +45,6 @@ namespace {
 
 constexpr int kRows = 128;
 constexpr int kKeys = 128;
-constexpr int kThreads = 256;
 constexpr uint32_t kChunk = 128 * 128;           // [128 x 64] bf16
 constexpr uint32_t kTileArea = 224 * 1024;
 constexpr int kMaxChunks = 5;                    // dims <= 320
@@ -51,7 +53,8 @@ constexpr float kLazyLog2 = 8.f;
 
 struct Bars {
     uint64_t kfull[kMaxRing], kempty[kMaxRing], vfull[kMaxRing], vempty[kMaxRing];
-    uint64_t qfull, sfull[2], sempty[2], pfull[2], odone[2], final_mma;
+    // [Q tile][buffer]
+    uint64_t qfull, sfull[2][2], sempty[2][2], pfull[2][2], odone[2][2], final_mma;
     uint32_t tmem_base;
     int abort;
 };
@@ -61,7 +64,7 @@ static_assert(kSmemBytes <= 232448, "shared memory budget");
 struct Job {
     int kc, vc;                 // 64-column chunks of a key / value row
     int dim_v;
-    int kring, vring, sbufs;    // ring slots, S buffers in TMEM
+    int kring, vring, sbufs;    // ring slots, S buffers per Q tile in TMEM
     int rpt;                    // query rows per token (per CTA's KV head)
     int tokens;                 // query tokens per sequence
     int kv_heads;
@@ -85,34 +88,41 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Bars* b
     return false;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+// NQ Q tiles of 128 rows per CTA (2: dims <= 128, every key / value tile
+// feeds twice the MMA work; one softmax warpgroup per Q tile).
+template <int NQ>
+__global__ void __launch_bounds__(128 + 128 * NQ, 1)
 prefill_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                          const __grid_constant__ CUtensorMap vmap, const __grid_constant__ Job J) {
+    constexpr int kThreadsNQ = 128 + 128 * NQ;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Bars* bs = reinterpret_cast<Bars*>(smem + kTileArea);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // Heaviest (last, for a causal job) row tiles first.
-    const int tile = int(gridDim.x) - 1 - int(blockIdx.x);
+    const int pair = int(gridDim.x) - 1 - int(blockIdx.x);
     const int g = blockIdx.y, b = blockIdx.z;
-    // A tile is tpt whole tokens: rows r < tpt * rpt (token t_first + r / rpt,
-    // head r % rpt of the KV group); the rows past them are idle.
+    // A Q tile is tpt whole tokens: rows r < tpt * rpt (token t_first + r / rpt,
+    // head r % rpt of the KV group); the rows past them are idle.  Q tile q of
+    // the CTA starts at token (pair * NQ + q) * tpt.
     const int tpt = kRows / J.rpt, tile_rows = tpt * J.rpt;
-    const int t_first = tile * tpt, t_last = t_first + tpt - 1;
+    const int t_first = pair * NQ * tpt, t_last = t_first + NQ * tpt - 1;
     const int n_keys = min(max(J.kv_len[b], 0), J.kv_capacity);
     const int vis_keys = J.causal ? min(n_keys, max(J.causal_offset + t_last + 1, 0)) : n_keys;
     const int tiles = (vis_keys + kKeys - 1) / kKeys;
-    // Layout: Q (kc chunks) | P (2 chunks) | K ring | V ring.
-    const uint32_t off_p = uint32_t(J.kc) * kChunk;
-    const uint32_t off_k = off_p + 2 * kChunk;
+    // Layout: Q (NQ x kc chunks) | P (NQ x 2 chunks) | K ring | V ring.
+    const uint32_t off_p = uint32_t(NQ * J.kc) * kChunk;
+    const uint32_t off_k = off_p + uint32_t(NQ * 2) * kChunk;
     const uint32_t off_v = off_k + uint32_t(J.kring) * kChunk;
+    // TMEM: O of Q tile q at q * o_cols, then its S buffers.
     const uint32_t o_cols = 64u * uint32_t(J.vc);
-    const uint32_t s_col = o_cols;
+    auto s_col = [&](int q, int sb) -> uint32_t { return NQ * o_cols + uint32_t((q * J.sbufs + sb) * kKeys); };
 
     if (tile_rows < kRows) {
         // The idle rows of Q read as zero (the TMA box fills the rest).
-        for (int i = tid; i < J.kc * (kRows - tile_rows) * 8; i += kThreads) {
-            const int c = i / ((kRows - tile_rows) * 8), w = i - c * (kRows - tile_rows) * 8;
+        const int per = (kRows - tile_rows) * 8;
+        for (int i = tid; i < NQ * J.kc * per; i += kThreadsNQ) {
+            const int c = i / per, w = i - c * per;
             reinterpret_cast<uint4*>(smem + c * kChunk + tile_rows * 128)[w] = make_uint4(0, 0, 0, 0);
         }
         fence_async_shared();
@@ -123,12 +133,13 @@ prefill_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_
             mbar_init(&bs->vfull[s], 1); mbar_init(&bs->vempty[s], 1);
         }
         mbar_init(&bs->qfull, 1);
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(&bs->sfull[s], 1);
-            mbar_init(&bs->sempty[s], 4);
-            mbar_init(&bs->pfull[s], 4);
-            mbar_init(&bs->odone[s], 1);
-        }
+        for (int q = 0; q < 2; ++q)
+            for (int s = 0; s < 2; ++s) {
+                mbar_init(&bs->sfull[q][s], 1);
+                mbar_init(&bs->sempty[q][s], 4);
+                mbar_init(&bs->pfull[q][s], 4);
+                mbar_init(&bs->odone[q][s], 1);
+            }
         mbar_init(&bs->final_mma, 1);
         bs->abort = 0;
         fence_barrier_init();
@@ -145,9 +156,11 @@ prefill_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_
 
     if (warp == 0 && lane == 0 && tiles > 0) {
         // ---- Q, then the K chunks of every tile ----
-        mbar_expect_tx(&bs->qfull, uint32_t(J.kc) * uint32_t(tile_rows) * 128u);
-        for (int c = 0; c < J.kc; ++c)
-            tma_load_4d(smem + c * kChunk, &qmap, &bs->qfull, c * 64, g * J.rpt, t_first, b);
+        mbar_expect_tx(&bs->qfull, uint32_t(NQ * J.kc) * uint32_t(tile_rows) * 128u);
+        for (int q = 0; q < NQ; ++q)
+            for (int c = 0; c < J.kc; ++c)
+                tma_load_4d(smem + (q * J.kc + c) * kChunk, &qmap, &bs->qfull, c * 64, g * J.rpt, t_first + q * tpt,
+                            b);
         bool ok = true;
         for (int n = 0; n < tiles * J.kc && ok; ++n) {
             const int j = n / J.kc, c = n - j * J.kc, slot = n % J.kring;
@@ -165,47 +178,55 @@ prefill_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_
             tma_load_4d(smem + off_v + slot * kChunk, &vmap, &bs->vfull[slot], c * 64, g, j * kKeys, b);
         }
     } else if (warp == 1) {
-        // ---- MMA issuer: S(j), then P.V(j - 1) (overlapping softmax(j)) ----
+        // ---- MMA issuer: S(j) of every Q tile, then P.V(j - 1) of each Q
+        // tile as its probabilities land (overlapping the softmax of tile j) ----
         const bool leader = lane == 0;
         const uint32_t idesc_s = umma_idesc_bf16(128, kKeys, 0, 0);
         const uint32_t idesc_o = umma_idesc_bf16(128, 64, 0, 1);
         bool ok = tiles == 0 || __all_sync(0xffffffffu, wait_bar(&bs->qfull, 0, bs, J));
         auto issue_pv = [&](int jj) {
-            ok = __all_sync(0xffffffffu, wait_bar(&bs->pfull[jj & 1], (jj >> 1) & 1, bs, J));
-            if (!ok) return;
-            tc_fence_after();
             const int valid = n_keys - jj * kKeys;          // < 128 only in the sequence's last tile
-            for (int c = 0; c < J.vc && ok; ++c) {
-                const int n = jj * J.vc + c, slot = n % J.vring;
-                ok = __all_sync(0xffffffffu, wait_bar(&bs->vfull[slot], (n / J.vring) & 1, bs, J));
-                if (!ok) break;
-                if (valid < kKeys) {
-                    uint4* rows = reinterpret_cast<uint4*>(smem + off_v + slot * kChunk);
-                    for (int i = max(valid, 0) * 8 + lane; i < kKeys * 8; i += 32) rows[i] = make_uint4(0, 0, 0, 0);
-                    fence_async_shared();
+            for (int q = 0; q < NQ && ok; ++q) {
+                ok = __all_sync(0xffffffffu, wait_bar(&bs->pfull[q][jj & 1], (jj >> 1) & 1, bs, J));
+                if (!ok) return;
+                tc_fence_after();
+                const uint32_t pbase = sbase + off_p + uint32_t(q * 2) * kChunk;
+                for (int c = 0; c < J.vc && ok; ++c) {
+                    const int n = jj * J.vc + c, slot = n % J.vring;
+                    if (q == 0) {
+                        ok = __all_sync(0xffffffffu, wait_bar(&bs->vfull[slot], (n / J.vring) & 1, bs, J));
+                        if (!ok) break;
+                        if (valid < kKeys) {
+                            uint4* rows = reinterpret_cast<uint4*>(smem + off_v + slot * kChunk);
+                            for (int i = max(valid, 0) * 8 + lane; i < kKeys * 8; i += 32)
+                                rows[i] = make_uint4(0, 0, 0, 0);
+                            fence_async_shared();
+                            __syncwarp();
+                        }
+                        tc_fence_after();
+                    }
+                    if (leader) {
+                        const uint32_t va = sbase + off_v + slot * kChunk;
+#pragma unroll
+                        for (int ks = 0; ks < kKeys / 16; ++ks)
+                            umma_bf16(tbase + q * o_cols + 64u * c,
+                                      umma_desc_sw128(pbase + (ks >> 2) * kChunk + (ks & 3) * 32, 16, 1024),
+                                      umma_desc_sw128(va + ks * 2048, kChunk, 1024), idesc_o,
+                                      (jj > 0 || ks > 0) ? 1u : 0u);
+                        if (q == NQ - 1) umma_commit(&bs->vempty[slot]);
+                    }
                     __syncwarp();
                 }
-                tc_fence_after();
-                if (leader) {
-                    const uint32_t va = sbase + off_v + slot * kChunk;
-#pragma unroll
-                    for (int ks = 0; ks < kKeys / 16; ++ks)
-                        umma_bf16(tbase + 64u * c,
-                                  umma_desc_sw128(sbase + off_p + (ks >> 2) * kChunk + (ks & 3) * 32, 16, 1024),
-                                  umma_desc_sw128(va + ks * 2048, kChunk, 1024), idesc_o, (jj > 0 || ks > 0) ? 1u : 0u);
-                    umma_commit(&bs->vempty[slot]);
-                }
+                if (ok && leader) umma_commit(&bs->odone[q][jj & 1]);
                 __syncwarp();
             }
-            if (ok && leader) umma_commit(&bs->odone[jj & 1]);
-            __syncwarp();
         };
         for (int j = 0; j < tiles && ok; ++j) {
             const int sb = j % J.sbufs;
-            if (j >= J.sbufs) {
-                ok = __all_sync(0xffffffffu, wait_bar(&bs->sempty[sb], ((j / J.sbufs) - 1) & 1, bs, J));
-                if (!ok) break;
-            }
+            if (j >= J.sbufs)
+                for (int q = 0; q < NQ && ok; ++q)
+                    ok = __all_sync(0xffffffffu, wait_bar(&bs->sempty[q][sb], ((j / J.sbufs) - 1) & 1, bs, J));
+            if (!ok) break;
             tc_fence_after();
             for (int c = 0; c < J.kc && ok; ++c) {
                 const int n = j * J.kc + c, slot = n % J.kring;
@@ -215,27 +236,32 @@ prefill_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_
                 if (leader) {
                     const uint32_t ka = sbase + off_k + slot * kChunk;
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        umma_bf16(tbase + s_col + uint32_t(sb * kKeys),
-                                  umma_desc_sw128(sbase + c * kChunk + kk * 32, 16, 1024),
-                                  umma_desc_sw128(ka + kk * 32, 16, 1024), idesc_s, (c | kk) != 0);
+                    for (int q = 0; q < NQ; ++q)
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            umma_bf16(tbase + s_col(q, sb),
+                                      umma_desc_sw128(sbase + (q * J.kc + c) * kChunk + kk * 32, 16, 1024),
+                                      umma_desc_sw128(ka + kk * 32, 16, 1024), idesc_s, (c | kk) != 0);
                     umma_commit(&bs->kempty[slot]);
                 }
                 __syncwarp();
             }
             if (!ok) break;
-            if (leader) umma_commit(&bs->sfull[sb]);
+            if (leader)
+                for (int q = 0; q < NQ; ++q) umma_commit(&bs->sfull[q][sb]);
             __syncwarp();
             if (j >= 1) issue_pv(j - 1);
         }
         if (ok && tiles > 0) issue_pv(tiles - 1);
         if (leader) umma_commit(&bs->final_mma);
     } else if (warp >= 4) {
-        // ---- softmax and epilogue: thread <-> query row (TMEM lane) ----
+        // ---- softmax and epilogue of Q tile qt: thread <-> query row (TMEM lane) ----
+        const int qt = (warp - 4) >> 2;
         const int quarter = warp & 3;
         const int r = 32 * quarter + lane;
         const uint32_t lane_addr = uint32_t(32 * quarter) << 16;
-        const int t = t_first + r / J.rpt, jh = r % J.rpt;
+        const uint32_t o_base = tbase + lane_addr + uint32_t(qt) * o_cols;
+        const int t = t_first + qt * tpt + r / J.rpt, jh = r % J.rpt;
         const bool live = r < tile_rows && t < J.tokens;
         // Keys this row may see.
         const int row_keys = J.causal ? min(n_keys, max(J.causal_offset + t + 1, 0)) : n_keys;
@@ -243,23 +269,38 @@ prefill_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_
         bool failed = false;
         for (int j = 0; j < tiles; ++j) {
             const int sb = j % J.sbufs;
-            const bool ok = wait_bar(&bs->sfull[sb], (j / J.sbufs) & 1, bs, J);
+            const bool ok = wait_bar(&bs->sfull[qt][sb], (j / J.sbufs) & 1, bs, J);
             if (!__all_sync(0xffffffffu, ok)) { failed = true; break; }
             tc_fence_after();
-            float v[kKeys];
-#pragma unroll
-            for (int c = 0; c < kKeys / 32; ++c) tmem_ld32(tbase + lane_addr + s_col + uint32_t(sb * kKeys + 32 * c), v + 32 * c);
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bs->sempty[sb]);
+            // One Q tile: the row's 128 scores held in registers.  Two (384
+            // threads, 168 registers each): two passes over them in TMEM, 32 at a
+            // time, the row max and then the probabilities.
+            const uint32_t s_addr = tbase + lane_addr + s_col(qt, sb);
             const int lim = row_keys - j * kKeys;
+            float vall[NQ == 1 ? kKeys : 1];
             float mx = -INFINITY;
+            if constexpr (NQ == 1) {
 #pragma unroll
-            for (int i = 0; i < kKeys; ++i) {
-                v[i] = i < lim ? v[i] * J.scale_log2 : -INFINITY;
-                mx = fmaxf(mx, v[i]);
+                for (int c = 0; c < kKeys / 32; ++c) tmem_ld32(s_addr + uint32_t(32 * c), vall + 32 * c);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bs->sempty[qt][sb]);
+#pragma unroll
+                for (int i = 0; i < kKeys; ++i)
+                    if (i < lim) mx = fmaxf(mx, vall[i]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < kKeys / 32; ++c) {
+                    float v[32];
+                    tmem_ld32(s_addr + uint32_t(32 * c), v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (32 * c + i < lim) mx = fmaxf(mx, v[i]);
+                }
             }
+            mx *= J.scale_log2;                                // scale > 0: the max of the scaled scores
             float alpha = 1.f;
             if (mx != -INFINITY && (m_run == -INFINITY || mx > m_run + kLazyLog2)) {
                 const float mn = fmaxf(m_run, mx);
@@ -269,50 +310,65 @@ prefill_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_
             }
             // P(j) overwrites the P that P.V(j - 1) reads; a rescale of O needs it done.
             if (j > 0) {
-                const bool okd = wait_bar(&bs->odone[(j - 1) & 1], ((j - 1) >> 1) & 1, bs, J);
+                const bool okd = wait_bar(&bs->odone[qt][(j - 1) & 1], ((j - 1) >> 1) & 1, bs, J);
                 if (!__all_sync(0xffffffffu, okd)) { failed = true; break; }
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, alpha != 1.f)) {
                     for (int c = 0; c < 2 * J.vc; ++c) {
                         float o[32];
-                        tmem_ld32(tbase + lane_addr + uint32_t(32 * c), o);
+                        tmem_ld32(o_base + uint32_t(32 * c), o);
                         tmem_wait_ld();
 #pragma unroll
                         for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                        tmem_st32(tbase + lane_addr + uint32_t(32 * c), o);
+                        tmem_st32(o_base + uint32_t(32 * c), o);
                     }
                     tmem_wait_st();
                 }
             }
             float sum = 0.f;
-            uint8_t* prow = smem + off_p + r * 128;
+            uint8_t* prow = smem + off_p + uint32_t(qt * 2) * kChunk + r * 128;
 #pragma unroll
-            for (int u = 0; u < kKeys / 8; ++u) {
-                float p[8];
+            for (int c = 0; c < kKeys / 32; ++c) {
+                float v[32];
+                if constexpr (NQ == 1) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float x = v[8 * u + e];
-                    p[e] = x == -INFINITY ? 0.f : sfu_exp2(x - m_run);
+                    for (int i = 0; i < 32; ++i) v[i] = vall[32 * c + i];
+                } else {
+                    tmem_ld32(s_addr + uint32_t(32 * c), v);
+                    tmem_wait_ld();
                 }
-                // The row sum of the probabilities as the MMA sees them (bf16).
-                uint4 w;
-                w.x = pack_bf16x2(p[0], p[1]); w.y = pack_bf16x2(p[2], p[3]);
-                w.z = pack_bf16x2(p[4], p[5]); w.w = pack_bf16x2(p[6], p[7]);
-                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    sum += __uint_as_float(ws[e] << 16) + __uint_as_float(ws[e] & 0xffff0000u);
-                *reinterpret_cast<uint4*>(prow + (u >> 3) * kChunk + (((u & 7) ^ (r & 7)) << 4)) = w;
+                for (int uu = 0; uu < 4; ++uu) {
+                    const int u = 4 * c + uu;                  // 8-key unit of the row
+                    float p[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        p[e] = 8 * u + e < lim ? sfu_exp2(v[8 * uu + e] * J.scale_log2 - m_run) : 0.f;
+                    // The row sum of the probabilities as the MMA sees them (bf16).
+                    uint4 w;
+                    w.x = pack_bf16x2(p[0], p[1]); w.y = pack_bf16x2(p[2], p[3]);
+                    w.z = pack_bf16x2(p[4], p[5]); w.w = pack_bf16x2(p[6], p[7]);
+                    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        sum += __uint_as_float(ws[e] << 16) + __uint_as_float(ws[e] & 0xffff0000u);
+                    *reinterpret_cast<uint4*>(prow + (u >> 3) * kChunk + (((u & 7) ^ (r & 7)) << 4)) = w;
+                }
+            }
+            if constexpr (NQ != 1) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bs->sempty[qt][sb]);
             }
             l_run += sum;
             fence_async_shared();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bs->pfull[j & 1]);
+            if (lane == 0) mbar_arrive(&bs->pfull[qt][j & 1]);
         }
         // ---- epilogue: O / l in bf16, the row's natural-log LSE ----
         if (!failed && tiles > 0) {
-            const bool okd = wait_bar(&bs->odone[(tiles - 1) & 1], ((tiles - 1) >> 1) & 1, bs, J);
+            const bool okd = wait_bar(&bs->odone[qt][(tiles - 1) & 1], ((tiles - 1) >> 1) & 1, bs, J);
             failed = !__all_sync(0xffffffffu, okd);
             tc_fence_after();
         }
@@ -322,7 +378,7 @@ prefill_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_
             for (int c = 0; c < 2 * J.vc; ++c) {
                 float o[32];
                 if (tiles > 0) {
-                    tmem_ld32(tbase + lane_addr + uint32_t(32 * c), o);
+                    tmem_ld32(o_base + uint32_t(32 * c), o);
                     tmem_wait_ld();
                 } else {
 #pragma unroll
@@ -368,6 +424,23 @@ prefill_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_
     }
 }
 
+template <int NQ>
+int launch_prefill_attention(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Job& J,
+                             dim3 grid, cudaStream_t stream) {
+    auto kernel = prefill_attention_kernel<NQ>;
+    static bool configured[64] = {};
+    const int dev = device_info().device;
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) != cudaSuccess)
+            return fail(SLIMKV_ERR_CUDA, "cudaFuncSetAttribute (prefill attention) failed");
+        configured[dev] = true;
+    }
+    kernel<<<grid, 128 + 128 * NQ, kSmemBytes, stream>>>(qm, km, vm, J);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? SLIMKV_OK
+                            : fail(SLIMKV_ERR_CUDA, "prefill attention launch failed: %s", cudaGetErrorString(e));
+}
+
 }  // namespace
 }  // namespace slimkv
 
@@ -406,10 +479,14 @@ extern "C" int slimkv_prefill_attention(const slimkv_prefill_attention_args* a, 
     J.kc = (a->dim_qk + 63) / 64;
     J.vc = (a->dim_v + 63) / 64;
     J.dim_v = a->dim_v;
-    const int slots = int((kTileArea - uint32_t(J.kc + 2) * kChunk) / kChunk);
+    // Two Q tiles per CTA when both dims fit two chunks (their Q, P, O and S
+    // then fill shared memory and TMEM: O 2 x 128, S 2 x 128 columns) and the
+    // chunk has more than one tile of tokens.
+    const int nq = (J.kc <= 2 && J.vc <= 2 && a->tokens > tpt) ? 2 : 1;
+    const int slots = int((kTileArea - uint32_t(nq * (J.kc + 2)) * kChunk) / kChunk);
     J.kring = std::min(kMaxRing, slots / 2);
     J.vring = std::min(kMaxRing, slots - J.kring);
-    J.sbufs = 64 * J.vc + 2 * kKeys <= 512 ? 2 : 1;
+    J.sbufs = nq * (64 * J.vc + 2 * kKeys) <= 512 ? 2 : 1;
     J.rpt = a->rows_per_token;
     J.tokens = a->tokens;
     J.kv_heads = a->kv_heads;
@@ -424,17 +501,8 @@ extern "C" int slimkv_prefill_attention(const slimkv_prefill_attention_args* a, 
     J.l_sb = a->lse_stride[0]; J.l_st = a->lse_stride[1];
     J.status = status_word();
     J.wait_ns = a->wait_limit_ns ? a->wait_limit_ns : 2000000000ull;
-    static bool configured[64] = {};
-    const int dev = device_info().device;
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
-        if (cudaFuncSetAttribute(prefill_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 int(kSmemBytes)) != cudaSuccess)
-            return fail(SLIMKV_ERR_CUDA, "cudaFuncSetAttribute (prefill attention) failed");
-        configured[dev] = true;
-    }
-    const dim3 grid((a->tokens + tpt - 1) / tpt, a->kv_heads, a->batch);
-    prefill_attention_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(qm, km, vm, J);
-    const cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? SLIMKV_OK
-                            : fail(SLIMKV_ERR_CUDA, "prefill attention launch failed: %s", cudaGetErrorString(e));
+    const dim3 grid((a->tokens + nq * tpt - 1) / (nq * tpt), a->kv_heads, a->batch);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return nq == 2 ? launch_prefill_attention<2>(qm, km, vm, J, grid, st)
+                   : launch_prefill_attention<1>(qm, km, vm, J, grid, st);
 }
