@@ -411,9 +411,7 @@ def prefill_window_step(device, steps, warmup):
     same GPU through torch/cuBLAS: every row through both weight sets,
     torch.where, index_select and the page write by advanced indexing
     (modeling_llama.py:1291-1367, paged_cache.py:78-87)."""
-    import numpy as np
     import torch
-    import oracle
     from slimkv_b200 import prefill, _lib
     from slimkv_b200.pages import BeaconPageLayout, BeaconPages
     g = torch.Generator(device=device)
@@ -425,10 +423,10 @@ def prefill_window_step(device, steps, warmup):
 
     W = prefill.BeaconProjectionWeights(q=w(qd, H), k=w(kvd, H), v=w(kvd, H), bq=w(qd, H), k_down=w(R, H),
                                         v_down=w(R, H), k_up=w(kvd, R), v_up=w(kvd, R))
-    roles, _, _ = oracle.interleave_roles(PREFILL_WINDOW, 0, 4)
+    roles, _, _ = prefill.window_roles(PREFILL_WINDOW, 0, 4)
     n = len(roles)
     hidden = w(B, n, H, std=1.0)
-    meta = prefill.metadata_from_roles(torch.from_numpy(roles).to(device), n)
+    meta = prefill.metadata_from_roles(roles.to(device), n)
     meta.raw_indices, meta.beacon_indices = meta.raw_indices.int(), meta.beacon_indices.int()
     layout = BeaconPageLayout(192, 4, R, R, kvd)
     per_seq = 32 * 1024 // 192 + 2                        # a 32k prompt's Beacon pages

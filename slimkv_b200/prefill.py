@@ -41,6 +41,18 @@ class PrefillMetadata:
     replicas: bool
 
 
+def window_roles(input_size, remainder, ratio):
+    """Roles of one interleaved chunk (``Memory._step``, slimkv/memory.py:
+    491-567, indices 579-589): ``(input_size + remainder) // ratio`` Beacons
+    among ``input_size`` raw tokens, position ``i`` of the interleaved chunk a
+    Beacon iff ``i % (ratio + 1) == ratio - remainder``.  Returns ``(roles
+    int64 tensor (0 raw, 1 Beacon), beacon_count, new_remainder)`` on the CPU."""
+    beacons = (input_size + remainder) // ratio
+    i = torch.arange(input_size + beacons)
+    roles = ((i % (ratio + 1)) == (ratio - remainder)).long() if beacons > 0 else torch.zeros_like(i)
+    return roles, beacons, (input_size + remainder) % ratio
+
+
 def metadata_from_roles(roles, chunk_rows, positions=None):
     """The index lists ``prepare_metadata`` builds (prefill_ops.py:31-36):
     the chunk is the last ``chunk_rows`` window roles; role 0 rows are raw,

@@ -391,3 +391,13 @@ def test_prefill_rope_llama_window_matches_oracle():
                                  sin.cpu().numpy(), pos.cpu().numpy(), roles, 4)
     assert np.array_equal(_bits(qo), bf16_bits(wq))
     assert np.array_equal(_bits(ko), bf16_bits(wk))
+
+
+def test_window_roles_match_the_oracle_interleave():
+    """The product's role list (bench and callers) is the reference's interleave rule."""
+    from oracle.schedule import interleave_roles
+    from slimkv_b200.prefill import window_roles
+    for size, rem, ratio in [(1024, 0, 4), (1000, 3, 4), (7, 1, 8), (3, 0, 4), (4096, 2, 8)]:
+        roles, nb, new_rem = window_roles(size, rem, ratio)
+        want, wnb, wrem = interleave_roles(size, rem, ratio)
+        assert np.array_equal(roles.numpy(), want) and nb == wnb and new_rem == wrem
