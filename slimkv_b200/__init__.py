@@ -12,8 +12,10 @@ thin torch bindings that mirror the reference's Python entry points:
 * ``slimkv_b200.pages``      — GPU drop-in for the plugin's page classes
 * ``slimkv_b200.runtime``    — CUDA-graph batched decode step of a SlimKV Llama
 * ``slimkv_b200.prefill``    — prefill window projection and Beacon append
+* ``slimkv_b200.prefill_attention`` — a prefill chunk's attention over its latent history
 * ``slimkv_b200.reconstruct``— the reconstruct decode backend
 * ``slimkv_b200.parallel``   — sequence split across GPUs, max-over-ranks timing
+* ``slimkv_b200.tensor_parallel`` — decode split by KV head and by sequence across GPUs
 * ``slimkv_b200.rope``       — RoPE tables built exactly like the reference
 """
 __version__ = '0.2.0'
