@@ -956,16 +956,13 @@ def main():
     # ---- end to end through the runtime API: host tokens in, host tokens out -
     host_in = torch.from_numpy(rng.integers(0, cfg.vocab, size=batch)).pin_memory()
     host_out = torch.empty(batch, dtype=torch.int64).pin_memory()
+    rt.capture_host_io(host_in, host_out)               # token copy in, step, greedy tokens out: one replay
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        rt.tokens.copy_(host_in, non_blocking=True)
-        rt.step()
-        host_out.copy_(rt.next_tokens(), non_blocking=True)
-        torch.cuda.current_stream().synchronize()      # the next step needs these tokens
-        host_in.copy_(host_out)
+        host_in.copy_(rt.step_host())                   # the next step needs these tokens
     e1.record()
     torch.cuda.synchronize()
     barrier()
@@ -1009,6 +1006,7 @@ def main():
     peak, peak_kind = peaks()
     status = _lib.device_status(clear=True)
     rt.graph = None
+    rt.graph_host = None
     prefill = None
     if not args.no_prefill and args.config == 2:
         prefill = prefill_window_step(device, max(args.steps, 10), args.warmup)

@@ -429,7 +429,11 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
             configured[dev] = true;
         }
     }
-    const dim3 mgrid(a->kv_heads, (a->batch + ma.seq_per_cta - 1) / ma.seq_per_cta);
+    // Row split of each (KV head, sequence) merge over SLIMKV_MERGE_ROW_SPLIT CTAs.
+#ifndef SLIMKV_MERGE_ROW_SPLIT
+#define SLIMKV_MERGE_ROW_SPLIT 2
+#endif
+    const dim3 mgrid(a->kv_heads, (a->batch + ma.seq_per_cta - 1) / ma.seq_per_cta, SLIMKV_MERGE_ROW_SPLIT);
     // Programmatic dependent launch: the merge's set-up (plan ranges, U_v,
     // LSE shifts) overlaps the attention launch's last CTAs; it reads the
     // partials only after the attention grid has completed.

@@ -394,9 +394,10 @@ __device__ __forceinline__ void raw_parts(const MergeArgs& a, int b, int g, int&
     }
 }
 
-// grid (Hkv, ceil(B / seq_per_cta)), 256 threads, merge_smem_bytes() of
-// dynamic shared memory.  CTA (g, bb) merges the (<= 16) query rows
-// (seq_per_cta sequences x L x group) of KV head g.
+// grid (Hkv, ceil(B / seq_per_cta), row split), 256 threads,
+// merge_smem_bytes() of dynamic shared memory.  CTAs (g, bb, *) merge the
+// (<= 16) query rows (seq_per_cta sequences x L x group) of KV head g, each
+// CTA an equal share of them.
 //   1. U_v[g] -> shared with asynchronous copies (bf16 as stored, the MMA's
 //      column-major B operand), overlapping steps 2-3.
 //   2. One warp per row: lane s holds the LSEs of splits s, s+32, s+64 and
@@ -422,15 +423,19 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rps = a.length * a.group, b0 = bb * a.seq_per_cta;
     const int nrows = min(16, a.seq_per_cta * rps);
+    // gridDim.z CTAs share the rows: this one takes [row0, row0 + part) as its
+    // local rows 0 .. part - 1.
+    const int part = (nrows + int(gridDim.z) - 1) / int(gridDim.z), row0 = int(blockIdx.z) * part;
     // rr: the row's index in the raw branch partials.
     auto row_info = [&](int r, int& b, int& l, int& h, int& rr) -> bool {
-        const int s = r / rps, rs = r - s * rps;
+        const int rg = r + row0;
+        const int s = rg / rps, rs = rg - s * rps;
         l = rs / a.group;
         b = b0 + s;
         const int j = rs - l * a.group;
         h = g * a.group + j;
         rr = l * a.raw_l_pitch + j;
-        return r < nrows && b < a.batch && l < (a.qlens ? a.qlens[b] : a.length);
+        return r < part && rg < nrows && b < a.batch && l < (a.qlens ? a.qlens[b] : a.length);
     };
 
     // 0. (Before the attention launch completes.)  Each row's partial ranges
@@ -477,7 +482,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(MergeArgs a) {
     {
         const int c4n = rvp / 4;
         const int64_t pitch = (int64_t)a.lat_rows * a.lat_width;
-        for (int it = tid; it < nrows * c4n; it += 256) {
+        for (int it = tid; it < part * c4n; it += 256) {
             const int r = it / c4n, c = (it - r * c4n) * 4;
             int b, l, h, rr;
             if (!row_info(r, b, l, h, rr) || c >= a.lat_width) continue;

@@ -360,6 +360,7 @@ class LatentDecodeRuntime:
                     raw_len=self.raw_len, latent_len=self.latent_len, query_len=self.query_len,
                     key_full=self.key_full, value_full=self.value_full))
         self.graph = None
+        self.graph_host = None
 
     # ------------------------------------------------------------------
     def load_memory(self, layers, window_raw_indices=None):
@@ -504,6 +505,32 @@ class LatentDecodeRuntime:
             return self.step_eager()
         self.graph.replay()
         return self.logits
+
+    def capture_host_io(self, host_tokens, host_next):
+        """Capture a second graph for serving from host memory: this step's
+        token ids copied in from ``host_tokens`` (pinned int64 [B]), the step,
+        the greedy next tokens copied out to ``host_next`` (pinned int64 [B]),
+        all in one replay (``step_host``)."""
+        if not (host_tokens.is_pinned() and host_next.is_pinned() and host_tokens.numel() == self.batch and
+                host_next.numel() == self.batch):
+            raise ValueError('host_tokens / host_next must be pinned int64 [batch]')
+        stream = torch.cuda.Stream(self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        self.graph_host = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph_host, stream=stream):
+            self.tokens.copy_(host_tokens, non_blocking=True)
+            self.step_eager()
+            host_next.copy_(self.logits.argmax(-1), non_blocking=True)
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        self._host_next = host_next
+        return self.graph_host
+
+    def step_host(self):
+        """One decode step from and to host memory (``capture_host_io``):
+        returns the pinned next-token buffer once it holds this step's tokens."""
+        self.graph_host.replay()
+        torch.cuda.current_stream(self.device).synchronize()
+        return self._host_next
 
     def next_tokens(self):
         return self.logits.argmax(-1)

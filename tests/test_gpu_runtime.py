@@ -140,3 +140,34 @@ def test_reconstruct_backend_runtime_follows_latent_backend(geometry):
         rec.tokens.copy_(tokens)
     assert _lib.device_status(clear=True) == 0
     assert inserted >= 2
+
+
+@pytest.mark.gpu
+def test_host_io_graph_matches_device_steps():
+    """``capture_host_io`` / ``step_host``: token ids in from pinned host memory,
+    the step, greedy tokens out, one replay — the same tokens and logits as
+    the device-resident graph steps of a twin runtime."""
+    from slimkv_b200.runtime import LatentDecodeRuntime, LatentLlamaConfig, RandomWeights
+    dev = torch.device('cuda', 0)
+    cfg = LatentLlamaConfig(layers=2, vocab=512, hidden=1024, intermediate=2048)
+    w = RandomWeights(cfg, dev, seed=11)
+    per_window = cfg.window // cfg.ratio
+    history, tails = [per_window * 3, per_window], [5, 1000]
+    a = LatentDecodeRuntime(cfg, w, history, tails, dev)
+    b = LatentDecodeRuntime(cfg, w, history, tails, dev)
+    start = torch.tensor([7, 300], dtype=torch.int64)
+    for rt in (a, b):
+        rt.tokens.copy_(start.to(dev))
+        rt.capture(warmup=1)
+    host_in = start.clone().pin_memory()
+    host_out = torch.empty(2, dtype=torch.int64).pin_memory()
+    b.capture_host_io(host_in, host_out)
+    tokens = start.to(dev)
+    for _ in range(4):
+        a.tokens.copy_(tokens)
+        logits = a.step().clone()
+        tokens = a.next_tokens()
+        got = b.step_host()
+        assert torch.equal(got.cuda(), tokens)
+        assert torch.equal(b.logits, logits)
+        host_in.copy_(got)
