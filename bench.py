@@ -686,8 +686,8 @@ def own_launches_per_step(rt):
 
 
 def kernel_only(args):
-    """One layer of the bench workload (same batch, history, tails; config 2
-    or, with ``--config 5``, the Qwen geometry): the fused decode call
+    """One layer of the bench workload (same batch, history, tails; config 2,
+    or config 3 / 5 with ``--config``): the fused decode call
     repeated; prints the attention kernel's time.  Small device footprint,
     for ncu captures of the dominant kernel."""
     import numpy as np
@@ -703,13 +703,19 @@ def kernel_only(args):
         batch = C5_BATCH
         history = [131072 // cfg.window * (cfg.window // cfg.ratio)] * batch
         extra = dict(raw_pre=False)
+    elif args.config == 3:
+        cfg = LatentLlamaConfig(rank_k=160, rank_v=160, ratio=8, layers=1, vocab=1024)
+        batch = C3_BATCH
+        ctx = rng.integers(2048, 131072 + 1, size=batch)
+        history = (ctx // cfg.window) * (cfg.window // cfg.ratio)
+        extra = dict(paged=True, raw_pre=False)
     else:
         cfg = LatentLlamaConfig(layers=1, vocab=1024)
         batch = BATCH
         history = [HISTORY] * batch
         extra = {}
     weights = RandomWeights(cfg, device, seed=0)
-    tails = rng.integers(0, cfg.window, size=batch)
+    tails = ctx % cfg.window if args.config == 3 else rng.integers(0, cfg.window, size=batch)
     rt = LatentDecodeRuntime(cfg, weights, history, tails, device, extra_windows=1, **extra)
     rt.tokens.copy_(torch.from_numpy(rng.integers(0, cfg.vocab, size=batch)).to(device))
     rt.step_eager()
