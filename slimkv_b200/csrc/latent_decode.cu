@@ -68,6 +68,20 @@ struct DecodePlan {
     size_t q_rot = 0, q_lat = 0, lat_o = 0, lat_lse = 0, raw_o = 0, raw_lse = 0, plan = 0;
 };
 
+// Prologue CTAs resident at once on this device (one wave).
+int prologue_wave() {
+    static int wave[64] = {};
+    const int dev = device_info().device;
+    if (dev < 0 || dev >= 64) return 0;
+    if (!wave[dev]) {
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_prologue_kernel, 256, 0) != cudaSuccess)
+            per_sm = 1;
+        wave[dev] = std::max(per_sm, 1) * std::max(device_info().sm_count, 1);
+    }
+    return wave[dev];
+}
+
 int plan_decode(const slimkv_latent_decode_args* a, DecodePlan& p) {
     if (!a) return fail(SLIMKV_ERR_INVALID_ARGUMENT, "null arguments");
     if (a->batch <= 0 || a->heads <= 0 || a->kv_heads <= 0 || a->heads % a->kv_heads)
@@ -359,7 +373,11 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
         // With the plan ready the attention may start before the prologue
         // ends — not when its duration is being timed (the begin event would
         // come after its start).
-        tl.early = a->plan && !a->attn_event_begin ? 1 : 0;
+        // Only for a prologue of at most three waves: with more, the early
+        // attention CTAs hold whole SMs while the prologue drains (config 3,
+        // 4.2 waves: 1132 us against 903 us started after it; config 5, 2.85
+        // waves, still gains 2 % from the early start).
+        tl.early = a->plan && !a->attn_event_begin && int(pgrid.x * pgrid.y * pgrid.z) <= 3 * prologue_wave() ? 1 : 0;
         TcSide& L = tl.lat;
         L.k = a->lat_k; L.v = a->lat_v; L.dim_k = a->rank_k; L.dim_v = a->rank_v;
         L.kv_heads = 1; L.capacity = a->lat_capacity;
@@ -415,7 +433,15 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
     ma.uv_bias = static_cast<const __nv_bfloat16*>(a->uv_bias);
     ma.qlens = a->query_len; ma.batch = a->batch; ma.length = a->length; ma.heads = a->heads;
     ma.kv_heads = a->kv_heads; ma.dim = a->head_dim; ma.rank_v = a->rank_v; ma.rank_v_pad = p.rvp;
-    ma.group = p.group; ma.seq_per_cta = 1; ma.scale = a->scale;
+    ma.group = p.group; ma.scale = a->scale;
+    // Merge CTAs: one per (KV head, sequence), its rows split over two CTAs
+    // while that still fits one wave (two merge CTAs per SM); for a batch
+    // larger than that, as many sequences per CTA as fill its 16 rows.
+    {
+        const int sms = std::max(device_info().sm_count, 1);
+        const int rps_m = a->length * p.group;
+        ma.seq_per_cta = a->kv_heads * a->batch <= sms ? 1 : std::max(1, 16 / rps_m);
+    }
     ma.out = a->out; ma.out_fp32 = a->out_fp32; ma.o_sb = a->out_stride[0]; ma.o_sl = a->out_stride[1];
     ma.out_lse = a->out_lse;
     const size_t msmem = merge_smem_bytes(p.rvp, a->head_dim);
@@ -429,11 +455,9 @@ extern "C" int slimkv_latent_decode(const slimkv_latent_decode_args* a, void* wo
             configured[dev] = true;
         }
     }
-    // Row split of each (KV head, sequence) merge over SLIMKV_MERGE_ROW_SPLIT CTAs.
-#ifndef SLIMKV_MERGE_ROW_SPLIT
-#define SLIMKV_MERGE_ROW_SPLIT 2
-#endif
-    const dim3 mgrid(a->kv_heads, (a->batch + ma.seq_per_cta - 1) / ma.seq_per_cta, SLIMKV_MERGE_ROW_SPLIT);
+    const int units = a->kv_heads * ((a->batch + ma.seq_per_cta - 1) / ma.seq_per_cta);
+    const int row_split = ma.seq_per_cta == 1 && units <= std::max(device_info().sm_count, 1) ? 2 : 1;
+    const dim3 mgrid(a->kv_heads, (a->batch + ma.seq_per_cta - 1) / ma.seq_per_cta, row_split);
     // Programmatic dependent launch: the merge's set-up (plan ranges, U_v,
     // LSE shifts) overlaps the attention launch's last CTAs; it reads the
     // partials only after the attention grid has completed.

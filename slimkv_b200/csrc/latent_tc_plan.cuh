@@ -68,8 +68,8 @@ __device__ __host__ inline long long tc_cta_start(int tiles, int ctas, int i) {
 // Relative cost of a tile by class, in 16 KB latent chunks streamed: a
 // class-0 tile counts its chunks; the two-query layout (class 1, a K ring of
 // two chunks) streams them more slowly; a raw tile (64 KB, with a Q load and
-// an epilogue every few tiles) costs less than a latent tile but more than
-// its bytes.  Measured per-tile times on config 2 set the values.
+// an epilogue every few tiles) costs TcPlanArgs::raw_weight, which the host
+// sets from measured launch times (raw_tile_weight()).
 #ifndef SLIMKV_TC_W_TWO_QUERY
 #define SLIMKV_TC_W_TWO_QUERY 1.4f
 #endif
@@ -77,9 +77,19 @@ __device__ __host__ inline long long tc_cta_start(int tiles, int ctas, int i) {
 #ifndef SLIMKV_TC_SNAP_DIV
 #define SLIMKV_TC_SNAP_DIV 4
 #endif
-#ifndef SLIMKV_TC_W_RAW_TILE
-#define SLIMKV_TC_W_RAW_TILE 7.5f
+#ifndef SLIMKV_TC_W_RAW_FRACTION
+#define SLIMKV_TC_W_RAW_FRACTION 0.75f
 #endif
+#ifndef SLIMKV_TC_W_RAW_WIDE
+#define SLIMKV_TC_W_RAW_WIDE 7.5f
+#endif
+// The raw tile's weight: 0.75 of a class-0 tile in the 32-head layout (the
+// best of the fractions tried at config 2, 10 chunks per latent tile, and at
+// config 3, 6 chunks in pages); 7.5 chunks in the 40-head layout (config 5,
+// 16 chunks per latent tile: 706 us against 731 us at 0.75 x 16).
+__host__ __device__ inline float raw_tile_weight(int lat_chunks, bool wide) {
+    return wide ? SLIMKV_TC_W_RAW_WIDE : SLIMKV_TC_W_RAW_FRACTION * float(lat_chunks);
+}
 
 // `scratch` (shared memory, `scratch_words` ints): when the whole plan fits,
 // it is built there — every prefix, binary search and atomic stays on chip —
@@ -133,7 +143,7 @@ __device__ inline void plan_tc_work(const TcPlanArgs& a, int32_t* scratch, int s
     // 2. CTAs per class (thread 0).
     if (tid == 0) {
         const float w[3] = {float(tiles[0]) * a.lat_chunks, SLIMKV_TC_W_TWO_QUERY * tiles[1] * a.lat_chunks,
-                            SLIMKV_TC_W_RAW_TILE * tiles[2]};
+                            raw_tile_weight(a.lat_chunks, a.split_queries != 0) * tiles[2]};
         // A raw CTA count given by the caller is kept; the other classes share
         // the rest by weight, at least one CTA each and at most one per tile.
         const bool fixed2 = a.raw_ctas > 0 && tiles[2] > 0;
