@@ -25,7 +25,7 @@ import math
 import torch
 
 from . import _lib
-from .kernels import _bf16_cuda, _ptr, _require, _stream, attention_forward
+from .kernels import _bf16_cuda, _require, _stream, attention_forward
 
 
 def reconstruct_kv(lat_k, lat_v, w_k_up, w_v_up, key, value, rows, b_k_up=None, b_v_up=None, out_start=None,

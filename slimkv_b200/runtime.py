@@ -20,7 +20,6 @@ unit-variance hidden states produce.  This is the reference's static decode
 (slimkv/llama3/static_decode.py:43-287) generalised to B > 1 and ragged
 lengths.
 """
-import math
 from dataclasses import dataclass, field
 
 import torch
