@@ -65,6 +65,7 @@ struct Job {
     int kc, vc;                 // 64-column chunks of a key / value row
     int dim_v;
     int kring, vring, sbufs;    // ring slots, S buffers per Q tile in TMEM
+    int vpair;                  // V chunk pairs in adjacent ring slots: one N=128 P.V MMA per pair
     int rpt;                    // query rows per token (per CTA's KV head)
     int tokens;                 // query tokens per sequence
     int kv_heads;
@@ -183,6 +184,7 @@ prefill_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_
         const bool leader = lane == 0;
         const uint32_t idesc_s = umma_idesc_bf16(128, kKeys, 0, 0);
         const uint32_t idesc_o = umma_idesc_bf16(128, 64, 0, 1);
+        const uint32_t idesc_pair = umma_idesc_bf16(128, 128, 0, 1);
         bool ok = tiles == 0 || __all_sync(0xffffffffu, wait_bar(&bs->qfull, 0, bs, J));
         auto issue_pv = [&](int jj) {
             const int valid = n_keys - jj * kKeys;          // < 128 only in the sequence's last tile
@@ -191,18 +193,24 @@ prefill_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_
                 if (!ok) return;
                 tc_fence_after();
                 const uint32_t pbase = sbase + off_p + uint32_t(q * 2) * kChunk;
-                for (int c = 0; c < J.vc && ok; ++c) {
+                // V chunks one at a time (N=64), or as adjacent pairs in the ring
+                // (N=128 over two 64-column atoms kChunk apart).
+                const int step = J.vpair ? 2 : 1;
+                for (int c = 0; c < J.vc && ok; c += step) {
                     const int n = jj * J.vc + c, slot = n % J.vring;
                     if (q == 0) {
-                        ok = __all_sync(0xffffffffu, wait_bar(&bs->vfull[slot], (n / J.vring) & 1, bs, J));
-                        if (!ok) break;
-                        if (valid < kKeys) {
-                            uint4* rows = reinterpret_cast<uint4*>(smem + off_v + slot * kChunk);
-                            for (int i = max(valid, 0) * 8 + lane; i < kKeys * 8; i += 32)
-                                rows[i] = make_uint4(0, 0, 0, 0);
-                            fence_async_shared();
-                            __syncwarp();
+                        for (int cc = 0; cc < step && ok; ++cc) {
+                            const int sl = (n + cc) % J.vring;
+                            ok = __all_sync(0xffffffffu, wait_bar(&bs->vfull[sl], ((n + cc) / J.vring) & 1, bs, J));
+                            if (ok && valid < kKeys) {
+                                uint4* rows = reinterpret_cast<uint4*>(smem + off_v + sl * kChunk);
+                                for (int i = max(valid, 0) * 8 + lane; i < kKeys * 8; i += 32)
+                                    rows[i] = make_uint4(0, 0, 0, 0);
+                                fence_async_shared();
+                                __syncwarp();
+                            }
                         }
+                        if (!ok) break;
                         tc_fence_after();
                     }
                     if (leader) {
@@ -211,9 +219,10 @@ prefill_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_
                         for (int ks = 0; ks < kKeys / 16; ++ks)
                             umma_bf16(tbase + q * o_cols + 64u * c,
                                       umma_desc_sw128(pbase + (ks >> 2) * kChunk + (ks & 3) * 32, 16, 1024),
-                                      umma_desc_sw128(va + ks * 2048, kChunk, 1024), idesc_o,
+                                      umma_desc_sw128(va + ks * 2048, kChunk, 1024), step == 2 ? idesc_pair : idesc_o,
                                       (jj > 0 || ks > 0) ? 1u : 0u);
-                        if (q == NQ - 1) umma_commit(&bs->vempty[slot]);
+                        if (q == NQ - 1)
+                            for (int cc = 0; cc < step; ++cc) umma_commit(&bs->vempty[(n + cc) % J.vring]);
                     }
                     __syncwarp();
                 }
@@ -486,6 +495,15 @@ extern "C" int slimkv_prefill_attention(const slimkv_prefill_attention_args* a, 
     const int slots = int((kTileArea - uint32_t(nq * (J.kc + 2)) * kChunk) / kChunk);
     J.kring = std::min(kMaxRing, slots / 2);
     J.vring = std::min(kMaxRing, slots - J.kring);
+#ifndef SLIMKV_PREFILL_VPAIR
+#define SLIMKV_PREFILL_VPAIR 1
+#endif
+    // An even V ring and chunk count keep every chunk pair in adjacent slots.
+    if (SLIMKV_PREFILL_VPAIR && J.vc % 2 == 0 && J.vring % 2) {
+        if (J.kring > 2) { --J.kring; ++J.vring; }
+        else --J.vring;
+    }
+    J.vpair = SLIMKV_PREFILL_VPAIR && J.vc % 2 == 0 && J.vring % 2 == 0 ? 1 : 0;
     J.sbufs = nq * (64 * J.vc + 2 * kKeys) <= 512 ? 2 : 1;
     J.rpt = a->rows_per_token;
     J.tokens = a->tokens;
