@@ -87,6 +87,20 @@ __device__ __host__ inline long long tc_cta_start(int tiles, int ctas, int i) {
 // best of the fractions tried at config 2, 10 chunks per latent tile, and at
 // config 3, 6 chunks in pages); 7.5 chunks in the 40-head layout (config 5,
 // 16 chunks per latent tile: 706 us against 731 us at 0.75 x 16).
+// Piece overhead, in tiles of its class, for placing CTA boundaries: every
+// piece (a segment, or the part of one, inside a CTA) pays a Q load, the
+// pipeline drain before its epilogue and the epilogue.  Globaltimer stamps of
+// a config-2 launch put it at ~4 us per raw piece against ~1.25 us per raw
+// tile, and at ~6 us per latent piece against ~4 us per latent tile; over
+// the round values tried, 3.2 / 1.5 made the launch 3 % faster at config 2
+// (79.3 -> 77.0 us) and 5 % faster at config 3 (851 -> 806 us).  The 40-head
+// layout keeps equal tile shares (every value tried there was slower).
+#ifndef SLIMKV_TC_BOUND_RAW
+#define SLIMKV_TC_BOUND_RAW 3.2f
+#endif
+#ifndef SLIMKV_TC_BOUND_LAT
+#define SLIMKV_TC_BOUND_LAT 1.5f
+#endif
 __host__ __device__ inline float raw_tile_weight(int lat_chunks, bool wide) {
     return wide ? SLIMKV_TC_W_RAW_WIDE : SLIMKV_TC_W_RAW_FRACTION * float(lat_chunks);
 }
@@ -192,10 +206,28 @@ __device__ inline void plan_tc_work(const TcPlanArgs& a, int32_t* scratch, int s
         const int32_t* start = P + L.seg_start[k];
         int32_t* cs = P + L.cta_start[k];
         const long long snap = n > 0 && SLIMKV_TC_SNAP_DIV > 0 ? (long long)tiles[k] / n / SLIMKV_TC_SNAP_DIV : 0;
+        // Equal shares of the class's cost: segment s starts at tile start[s]
+        // and at cost start[s] + c s, its piece overhead c (in tiles) paid
+        // before its first tile; a share boundary inside an overhead lands on
+        // the segment's first tile.
+        const float c = a.split_queries ? 0.f : (k == 2 ? SLIMKV_TC_BOUND_RAW : SLIMKV_TC_BOUND_LAT);
+        const double cost = double(tiles[k]) + double(c) * ns;
         long long prev = 0;
         cs[0] = 0;
         for (int i = 1; i < n; ++i) {
             long long r = tc_cta_start(tiles[k], n, i);
+            if (c > 0.f) {
+                const double rc = cost * i / n;
+                int lo = 0, hi = ns - 1;                 // last segment whose cost start is <= rc
+                while (lo < hi) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (double(start[mid]) + double(c) * mid <= rc) lo = mid;
+                    else hi = mid - 1;
+                }
+                const double off = rc - double(start[lo]) - double(c) * (lo + 1);
+                const long long len = start[lo + 1] - start[lo];
+                r = start[lo] + (off <= 0.0 ? 0 : min(len, (long long)(off + 0.5)));
+            }
             const int s = tc_segment_of(start, ns, r);
             if (r - start[s] <= snap) r = start[s];
             else if (start[s + 1] - r <= snap) r = start[s + 1];
