@@ -78,15 +78,17 @@ __device__ __host__ inline long long tc_cta_start(int tiles, int ctas, int i) {
 #define SLIMKV_TC_SNAP_DIV 4
 #endif
 #ifndef SLIMKV_TC_W_RAW_FRACTION
-#define SLIMKV_TC_W_RAW_FRACTION 0.75f
+#define SLIMKV_TC_W_RAW_FRACTION 0.65f
 #endif
 #ifndef SLIMKV_TC_W_RAW_WIDE
 #define SLIMKV_TC_W_RAW_WIDE 7.5f
 #endif
-// The raw tile's weight: 0.75 of a class-0 tile in the 32-head layout (the
+// The raw tile's weight: 0.65 of a class-0 tile in the 32-head layout (the
 // best of the fractions tried at config 2, 10 chunks per latent tile, and at
-// config 3, 6 chunks in pages); 7.5 chunks in the 40-head layout (config 5,
-// 16 chunks per latent tile: 706 us against 731 us at 0.75 x 16).
+// config 3, 6 chunks in pages, with the piece-aware boundaries below: 0.75
+// gave 77 / 807 us, 0.65 75.4 / 797 us, 0.55 74.2 / 874 us); 7.5 chunks in the
+// 40-head layout (config 5, 16 chunks per latent tile: 706 us against 731 us
+// at 0.75 x 16).
 // Piece overhead, in tiles of its class, for placing CTA boundaries: every
 // piece (a segment, or the part of one, inside a CTA) pays a Q load, the
 // pipeline drain before its epilogue and the epilogue.  Globaltimer stamps of
