@@ -69,7 +69,11 @@ __device__ __host__ inline long long tc_cta_start(int tiles, int ctas, int i) {
 // class-0 tile counts its chunks; the two-query layout (class 1, a K ring of
 // two chunks) streams them more slowly; a raw tile (64 KB, with a Q load and
 // an epilogue every few tiles) costs TcPlanArgs::raw_weight, which the host
-// sets from measured launch times (raw_tile_weight()).
+// sets from measured launch times (raw_tile_weight()).  With the piece-aware
+// shares, two-query weights of 1.3 / 1.5 / 1.6 against 1.4 gave 76 / 75 / 72.6
+// against 75.5 us at config 2 and 835 / 820 / 788 against 786 us at config 3
+// (kernel-only); 1.6 then measured 74.0 against 72.5 us per launch in the full
+// 32-layer bench, so 1.4 stays.
 #ifndef SLIMKV_TC_W_TWO_QUERY
 #define SLIMKV_TC_W_TWO_QUERY 1.4f
 #endif
